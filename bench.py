@@ -1,0 +1,375 @@
+#!/usr/bin/env python3
+"""Decode throughput of the LLaMA-3-8B-shape Q4_K continuous-batching step.
+
+Workload: 32 layers, d_model 4096, 32 query / 8 KV heads,
+head_dim 128, SwiGLU FFN 14336, vocab 128256, RoPE theta 5e5; Q4_K linear
+weights from N(0, 0.02), f32 embedding and LM head; 256 active sequences per
+GPU with ragged contexts.  A step = one continuous-batching decode step of all
+256 sequences through the engine's C ABI (slate_llama_batch_step_device, one
+CUDA graph); `value` = tokens/s over all ranks with inputs already in HBM,
+`e2e` = the same through slate_llama_batch_step with host buffers.
+
+Contexts: prompt U[128, 4096] plus a uniform offset of U[0, 256) already-decoded
+tokens (the steady state of 256-token budgets under continuous refill), seeded
+on the device as synthetic K/V.  The timed window is shorter than a budget, so
+no sequence finishes inside it.  The KV read per step (~75 GB f16) exceeds the
+126 MB L2, so no flush is needed between steps.
+
+Multi-GPU: sequences are independent, so each rank is a replica running its own
+256 sequences (weak scaling, no collective on the data path); torch.distributed
+(nccl) only provides the barrier and the max-over-ranks timing.
+
+--impl reference: the reference's own CPU path (oracle/_ref, the unmodified
+slate sources) on this host's cores, one slate_llama_decode_step session per
+thread, timed at a few context lengths and fitted per token as a + b*ctx.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG3 = dict(n_layers=32, d_model=4096, ffn_hidden=14336, n_heads=32, n_kv_heads=8, vocab=128256,
+            max_seq=4352, theta_base=500000.0, rms_eps=1e-5)
+METRIC = "decode tok/s (box), LLaMA-3-8B-shape Q4_K, 256 ragged seqs; p50 step latency"
+PROFILE_TRAFFIC = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--layers", type=int, default=CFG3["n_layers"],
+                    help="reduce only for debugging; the benchmark workload is 32")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    return ap.parse_args()
+
+
+def model_path(args, cfg) -> str:
+    tag = f"slate_b200_cfg3_L{cfg['n_layers']}_s{args.seed}.gguf"
+    need = 9 << 30
+    for d in (os.environ.get("SLATE_BENCH_DIR"), "/dev/shm", "/tmp"):
+        if d and os.path.isdir(d) and shutil.disk_usage(d).free > need:
+            return os.path.join(d, tag)
+    return os.path.join("/tmp", tag)
+
+
+def ensure_model(args, cfg, rank, barrier) -> str:
+    import slate_b200 as sb
+    path = model_path(args, cfg)
+    if int(os.environ.get("LOCAL_RANK", "0")) == 0 and not os.path.exists(path):
+        tmp = path + f".{os.getpid()}.tmp"
+        sb.synth_gguf(tmp, q4k=True, seed=args.seed, **cfg)
+        os.rename(tmp, path)
+    barrier()
+    return path
+
+
+def contexts(args, n, rank, steps):
+    rng = np.random.default_rng(args.seed * 1000 + rank)
+    prompt = rng.integers(128, 4097, n)
+    done = rng.integers(0, 256, n)
+    return np.minimum(prompt + done, CFG3["max_seq"] - steps - 1).astype(np.int64)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.p = None
+        self.out = ""
+
+    def __enter__(self):
+        if shutil.which("nvidia-smi"):
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                      text=True)
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.out, _ = self.p.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in self.gpus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# reference CPU baseline (oracle/_ref: the reference's own sources)
+# ---------------------------------------------------------------------------
+def reference_cpu(path, cfg, budget_s, threads=None):
+    """Per-token time of slate_llama_decode_step at a few context lengths, one
+    reference session per thread.  A session's dense KV cache is calloc'd by
+    the reference (llama_infer.c:225-226); to decode at context c its position
+    field (struct slate_llama_session, llama_infer.c:53-59: model, backend,
+    position, ...) is set to c, so attention reads c zero-initialised rows --
+    the same work as a real c-token history (the CPU attention has no
+    data-dependent shortcuts).  Fits t = a + b*ctx."""
+    import ctypes as C
+    import oracle as O
+    ref = O.Reference()
+    g, m = ref.open(path)
+    V = ref.config(m)["vocab"]
+    n_thr = threads or os.cpu_count() or 1
+    pts = [128, 2048, 4096]
+    per_pt = []
+    t_start = time.time()
+    for ctx in pts:
+        if time.time() - t_start > budget_s and per_pt:
+            break
+        times = [0.0] * n_thr
+
+        def work(i):
+            s = ref.lib.slate_llama_session_new(m)
+            C.c_int.from_address(s + 16).value = ctx        # position
+            out = np.zeros(V, np.float32)
+            t0 = time.perf_counter()
+            rc = ref.lib.slate_llama_decode_step(s, 1, out.ctypes.data_as(C.POINTER(C.c_float)))
+            times[i] = time.perf_counter() - t0 if rc == 0 else float("nan")
+            ref.lib.slate_llama_session_free(s)
+
+        th = [threading.Thread(target=work, args=(i,)) for i in range(n_thr)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        per_pt.append((ctx, float(np.nanmedian(times))))
+    ref.close(g, m)
+    x = np.array([p[0] for p in per_pt], float)
+    y = np.array([p[1] for p in per_pt], float)
+    b = float(np.polyfit(x, y, 1)[0]) if len(x) > 1 else 0.0
+    a = float(y.mean() - b * x.mean())
+    mean_ctx = (128 + 4096) / 2 + 128          # prompt U[128,4096] + half a 256-token budget
+    t_tok = a + b * mean_ctx
+    return {"value": n_thr / t_tok, "unit": "tok/s", "cores": n_thr, "kind": "reference",
+            "sample": (f"{n_thr} concurrent reference sessions (one per thread), 1 decode token each "
+                       f"at ctx {[p[0] for p in per_pt]}; per-token s {[round(p[1], 3) for p in per_pt]}; "
+                       f"extrapolated to mean ctx {mean_ctx:.0f} as t = a + b*ctx"),
+            "seconds": round(time.time() - t_start, 1)}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = dict(CFG3)
+    cfg["n_layers"] = args.layers
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        import oracle as O
+        if not O.Reference.available():
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "oracle/_ref/libslate_ref.so was not built (reference sources absent at build time)"}))
+            return 0
+        path = ensure_model(args, cfg, rank, lambda: None)
+        t0 = time.time()
+        cpu = reference_cpu(path, cfg, args.cpu_seconds)
+        line = {"metric": METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / (cpu["value"] / cpu["cores"]),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "impl": "reference",
+                "config": {"workload": "llama3-8b-shape q4k decode, reference CPU sessions", "seqs": cpu["cores"],
+                           "kv_dtype": "f32", "contexts": "sampled, extrapolated"},
+                "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "wall_s": round(time.time() - t0, 1)}
+        print(json.dumps(line))
+        return 0
+
+    import torch
+    import slate_b200 as sb
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+        def barrier():
+            dist.barrier()
+    else:
+        dist = None
+
+        def barrier():
+            pass
+
+    path = ensure_model(args, cfg, rank, barrier)
+    kv = sb.KV_F16 if args.kv == "f16" else sb.KV_F32
+    n = args.batch
+    total_steps = args.warmup + args.steps
+    ctx = contexts(args, n, rank, 3 * total_steps + 4)
+    eng = sb.LlamaBatch(path, device=local, max_batch=n, max_slots=n, kv_dtype=kv,
+                        max_seq=cfg["max_seq"])
+    slots = np.array([eng.open() for _ in range(n)], np.int32)
+    assert (slots >= 0).all(), sb.last_error()
+    for s, c in zip(slots, ctx):
+        rc = eng.seed_context(int(s), int(c), args.seed + int(s))
+        assert rc == 0, (rc, sb.last_error())
+    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+    d_slots = torch.tensor(slots, device="cuda")
+    rng = np.random.default_rng(args.seed + rank)
+    d_tok = [torch.tensor(rng.integers(0, cfg["vocab"], n).astype(np.int32), device="cuda"),
+             torch.zeros(n, dtype=torch.int32, device="cuda")]
+
+    def dstep(i):
+        rc = eng.step_device(d_slots.data_ptr(), n, d_tok[i & 1].data_ptr(), d_tok[(i + 1) & 1].data_ptr())
+        assert rc == 0, sb.last_error()
+
+    for i in range(args.warmup):
+        dstep(i)
+    assert eng.sync() == 0, "device rejected a warm-up step"
+    torch.cuda.synchronize()
+    barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler([local] if world == 1 else range(world)) as clk:
+        torch.cuda.synchronize()
+        barrier()
+        with torch.cuda.stream(stream):
+            ev[0].record(stream)
+            for i in range(args.steps):
+                dstep(args.warmup + i)
+                ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    assert eng.sync() == 0, "device rejected a timed step"
+    step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    tot_ms = ev[0].elapsed_time(ev[-1])
+    if dist:
+        t = torch.tensor([tot_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tot_ms = float(t.item())
+    value = n * world * args.steps / (tot_ms / 1000.0)
+
+    # per-kernel timing of the dominant kernels on the same state and stream
+    layer = cfg["n_layers"] // 2
+    kt = {name: eng.profile(k, n, layer, iters=10) for name, k in
+          [("attention", sb.PROF_ATTENTION), ("qkv", sb.PROF_QKV), ("wo", sb.PROF_WO),
+           ("gate_up", sb.PROF_GATE_UP), ("down", sb.PROF_DOWN), ("lm_head", sb.PROF_LM_HEAD)]}
+    esz = 2 if kv == sb.KV_F16 else 4
+    hd, nkv, L, D, F, V = 128, 8, cfg["n_layers"], 4096, 14336, cfg["vocab"]
+    ctx_now = ctx + total_steps                        # contexts seen by the profiled launch
+    attn_bytes = float(ctx_now.sum()) * 2 * nkv * hd * esz + n * 32 * hd * 4 * 3
+    q4k = 144 / 256
+    w_layer = (D * (D + 2 * nkv * hd) + D * D + 3 * D * F) * q4k
+    head = V * D * 4
+    kv_read_step = float((ctx + total_steps - args.steps // 2).sum()) * 2 * nkv * hd * esz * L
+    step_bytes = w_layer * L + head + kv_read_step + n * 2 * nkv * hd * esz * L
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak, peak_src = float(peaks["hbm_gbs"]), "measured"
+    except Exception:
+        peak, peak_src = 6650.0, "fallback"
+    achieved = attn_bytes / (kt["attention"] / 1000.0) / 1e9
+    traffic = None
+    try:
+        tr = json.load(open(PROFILE_TRAFFIC))
+        traffic = tr.get("attention_bytes_per_launch")
+    except Exception:
+        pass
+    step_s = tot_ms / 1000.0 / args.steps
+
+    # end to end through the host-buffer API: H2D slots+tokens, D2H greedy tokens
+    host_tok = d_tok[args.steps & 1 ^ (args.warmup & 1)].cpu().numpy()
+    e2e_steps = max(3, args.steps // 2)
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        rc, host_tok, _ = eng.step(slots, host_tok)
+        assert rc == 0, sb.last_error()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = n * world * e2e_steps / e2e_s
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle as O
+        if O.Reference.available():
+            cpu = reference_cpu(path, cfg, args.cpu_seconds)
+    launches = eng.launches_per_step(n) * args.steps
+    clocks = clk.summary()
+    eng.close()
+    if dist:
+        barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
+        "p50_step_ms": float(np.median(step_ms)), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama3-8b-shape q4k continuous-batching decode (BASELINE config 3)",
+                   "model": "llama3-8b-shape random N(0,0.02) Q4_K", "layers": cfg["n_layers"],
+                   "global_batch": n * world, "seqs_per_gpu": n, "kv_dtype": args.kv,
+                   "mean_ctx": float(ctx.mean()), "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2 (KV read per step >> 126 MB)"},
+        "roofline": {"bound": "hbm", "kernel": "attn_partial+attn_combine (paged GQA attention)",
+                     "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": kt["attention"]},
+        "step_roofline": {"bytes_per_step": step_bytes, "achieved_GBps": step_bytes / step_s / 1e9,
+                          "frac_of_measured": step_bytes / step_s / 1e9 / peak,
+                          "frac_of_8TBps": step_bytes / step_s / 8e12},
+        "kernel_ms": kt,
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": n * 4},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

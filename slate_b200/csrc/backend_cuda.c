@@ -1,0 +1,211 @@
+/*
+ * backend_cuda.c -- the CUDA implementation of Slate's compute-backend vtable
+ * (include/slate/backend.h:41-99), replacing src/backend/backend_cuda_stub.c.
+ *
+ * The reference vtable is a process-wide singleton of plain function pointers
+ * with no context argument and void returns, so this backend keeps one bound
+ * device and one stream; every entry enqueues on that stream and returns at
+ * once, and sync() waits (cudaStreamSynchronize).  copy_h2d / copy_d2h are
+ * synchronous like the CPU backend's memcpy.  Errors of the void entries are
+ * recorded for slate_cuda_last_error(); the appended entries return them.
+ */
+#define _GNU_SOURCE
+#include "sb_internal.h"
+#include "sb_kernels.h"
+
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+static slate_backend_cuda_t g_be;
+static cudaStream_t g_stream;
+static int g_device = -1;
+static pthread_mutex_t g_init = PTHREAD_MUTEX_INITIALIZER;
+
+static void note(int rc, const char* what) {
+    if (rc == 0) rc = sb_cuda_check(cudaGetLastError(), what);
+    else if (rc == -1) sb_set_error("%s: unsupported arguments", what);
+}
+
+static void* be_alloc(size_t bytes) {
+    if (bytes == 0) return NULL;   /* backend_cpu.c:23 returns NULL for 0 bytes */
+    void* p = NULL;
+    if (sb_cuda_check(cudaMalloc(&p, bytes), "alloc")) return NULL;
+    return p;
+}
+static void be_release(void* p) {
+    if (!p) return;
+    cudaStreamSynchronize(g_stream);
+    cudaFree(p);
+}
+static void be_h2d(void* dst, const void* src, size_t bytes) {
+    sb_cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, g_stream), "copy_h2d");
+    sb_cuda_check(cudaStreamSynchronize(g_stream), "copy_h2d");
+}
+static void be_d2h(void* dst, const void* src, size_t bytes) {
+    sb_cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, g_stream), "copy_d2h");
+    sb_cuda_check(cudaStreamSynchronize(g_stream), "copy_d2h");
+}
+
+static int aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+/* y[M] = A[M,K]·x  (backend_cpu.c:33-36) */
+static void be_matvec(float* y, const float* A, const float* x, int M, int K) {
+    int rc;
+    if (K % 128 == 0 && aligned16(A) && aligned16(x)) {
+        sb_matrix W = {SB_WT_F32, A, M, M, K, K};
+        rc = sb_gemm(&W, x, K, 1, y, M, SB_EPI_STORE, 0, g_stream);
+    } else {
+        rc = sb_matvec_f32_generic(y, A, x, M, K, g_stream);
+    }
+    note(rc, "matvec");
+}
+/* C[B,N] = X[B,K]·W[K,N]  (backend_cpu.c:38-42) */
+static void be_linear_batch(float* C, const float* X, const float* W, int B, int K, int N) {
+    note(sb_linear_batch_generic(C, X, W, B, K, N, g_stream), "linear_batch");
+}
+/* y[M] = Q4K(A)[M,K]·x  (backend_cpu.c:44-46) */
+static void be_matvec_q4k(float* y, const void* A, const float* x, int M, int K) {
+    note(sb_q4k_matmul_generic(y, A, x, 1, M, K, g_stream), "matvec_q4k");
+}
+static void be_rmsnorm_row(float* y, const float* x, const float* w, int D, float eps) {
+    note(sb_rmsnorm_rows(y, D, x, D, w, 1, D, eps, g_stream), "rmsnorm_row");
+}
+static void be_silu_mul(float* y, const float* g, const float* u, int H) {
+    note(sb_silu_mul(y, g, u, H, g_stream), "silu_mul");
+}
+static void be_add(float* y, const float* x, int D) {
+    note(sb_add_inplace(y, x, D, g_stream), "add_inplace");
+}
+static void be_embed(float* y, const float* W, int token, int D) {
+    note(sb_embed_lookup(y, W, token, D, g_stream), "embed_lookup");
+}
+static void be_attention_step(float* out, const float* q, const float* K, const float* V,
+                              float* scores, int L, int D) {
+    (void)scores;  /* the device kernel keeps scores in shared memory */
+    note(sb_attention_step(out, q, K, V, L, D, g_stream), "attention_step");
+}
+static void be_sync(void) { sb_cuda_check(cudaStreamSynchronize(g_stream), "sync"); }
+
+/* ---- appended, status-returning entries -------------------------------- */
+static int fin(int rc, const char* what) {
+    if (rc == -1) { sb_set_error("%s: unsupported arguments", what); return -1; }
+    return rc ? rc : sb_cuda_check(cudaGetLastError(), what);
+}
+static int be_matmul_q4k(float* Y, const void* A, const float* X, int B, int M, int K) {
+    return fin(sb_q4k_matmul_generic(Y, A, X, B, M, K, g_stream), "matmul_q4k_batch");
+}
+static int be_matmul_f32(float* Y, const float* A, const float* X, int B, int M, int K) {
+    if (K % 128 == 0 && aligned16(A) && aligned16(X)) {
+        sb_matrix W = {SB_WT_F32, A, M, M, K, K};
+        return fin(sb_gemm(&W, X, K, B, Y, M, SB_EPI_STORE, 0, g_stream), "matmul_f32_batch");
+    }
+    int rc = 0;
+    for (int b = 0; b < B && !rc; ++b)
+        rc = sb_matvec_f32_generic(Y + (size_t)b * M, A, X + (size_t)b * K, M, K, g_stream);
+    return fin(rc, "matmul_f32_batch");
+}
+static int be_rmsnorm_rows(float* Y, const float* X, const float* w, int B, int D, float eps) {
+    return fin(sb_rmsnorm_rows(Y, D, X, D, w, B, D, eps, g_stream), "rmsnorm_rows");
+}
+static int be_argmax_rows(int32_t* out, const float* logits, int B, int V) {
+    return fin(sb_argmax_rows(out, logits, V, B, V, g_stream), "argmax_rows");
+}
+static int be_rope_kv(float* q, float* k, const float* v, const int32_t* pos,
+                      const int32_t* row_slot, const int32_t* page_table, int max_pages,
+                      void* pool, int64_t n_pages, int layer, int B, int nq, int nkv, int hd,
+                      int kv_dtype, const float* rc, const float* rs) {
+    /* the kernel takes one [q | k | v] row per batch entry; these entries may
+     * live in separate buffers, so gather them into a scratch row block */
+    const int qd = nq * hd, kd = nkv * hd, ld = qd + 2 * kd;
+    float* tmp = NULL;
+    int rcode = sb_cuda_check(cudaMallocAsync((void**)&tmp, (size_t)B * ld * 4, g_stream), "scratch");
+    if (rcode) return rcode;
+    rcode = sb_cuda_check(cudaMemcpy2DAsync(tmp, (size_t)ld * 4, q, (size_t)qd * 4, (size_t)qd * 4, B,
+                                            cudaMemcpyDeviceToDevice, g_stream), "gather q");
+    if (!rcode) rcode = sb_cuda_check(cudaMemcpy2DAsync(tmp + qd, (size_t)ld * 4, k, (size_t)kd * 4,
+                                                        (size_t)kd * 4, B, cudaMemcpyDeviceToDevice,
+                                                        g_stream), "gather k");
+    if (!rcode) rcode = sb_cuda_check(cudaMemcpy2DAsync(tmp + qd + kd, (size_t)ld * 4, v,
+                                                        (size_t)kd * 4, (size_t)kd * 4, B,
+                                                        cudaMemcpyDeviceToDevice, g_stream), "gather v");
+    if (!rcode) rcode = fin(sb_rope_append(tmp, ld, B, nq, nkv, hd, pos, row_slot, page_table,
+                                           max_pages, pool, n_pages, layer, kv_dtype, rc, rs,
+                                           g_stream), "rope_kv_append_paged");
+    if (!rcode) rcode = sb_cuda_check(cudaMemcpy2DAsync(q, (size_t)qd * 4, tmp, (size_t)ld * 4,
+                                                        (size_t)qd * 4, B, cudaMemcpyDeviceToDevice,
+                                                        g_stream), "scatter q");
+    if (!rcode) rcode = sb_cuda_check(cudaMemcpy2DAsync(k, (size_t)kd * 4, tmp + qd, (size_t)ld * 4,
+                                                        (size_t)kd * 4, B, cudaMemcpyDeviceToDevice,
+                                                        g_stream), "scatter k");
+    cudaFreeAsync(tmp, g_stream);
+    return rcode;
+}
+static int be_attention_paged(float* out, const float* q, const int32_t* pos,
+                              const int32_t* row_slot, const int32_t* page_table, int max_pages,
+                              const void* pool, int64_t n_pages, int layer, int B, int nq, int nkv,
+                              int hd, int kv_dtype) {
+    int max_seq = max_pages * SB_PAGE_TOKENS;
+    size_t nf = sb_attention_scratch_floats(B, nq, hd, max_seq);
+    float* scr = NULL;
+    int rc = sb_cuda_check(cudaMallocAsync((void**)&scr, nf * 4, g_stream), "scratch");
+    if (rc) return rc;
+    rc = fin(sb_attention_paged(out, nq * hd, q, nq * hd, B, nq, nkv, hd, pos, row_slot, page_table,
+                                max_pages, pool, n_pages, layer, kv_dtype, max_seq, scr, g_stream),
+             "attention_paged_gqa");
+    cudaFreeAsync(scr, g_stream);
+    return rc;
+}
+
+const slate_backend_cuda_t* slate_backend_cuda_create(int device) {
+    pthread_mutex_lock(&g_init);
+    const slate_backend_cuda_t* r = NULL;
+    if (g_device >= 0) {
+        r = g_device == device ? &g_be : NULL;
+        if (!r) sb_set_error("backend already bound to device %d", g_device);
+    } else {
+        int n = 0;
+        if (!sb_cuda_check(cudaGetDeviceCount(&n), "cudaGetDeviceCount") && device >= 0 &&
+            device < n && !sb_cuda_check(cudaSetDevice(device), "cudaSetDevice") &&
+            !sb_cuda_check(cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking), "stream")) {
+            sb_gemm_prepare();
+            memset(&g_be, 0, sizeof g_be);
+            g_be.base.name = "cuda";
+            g_be.base.alloc = be_alloc;
+            g_be.base.release = be_release;
+            g_be.base.copy_h2d = be_h2d;
+            g_be.base.copy_d2h = be_d2h;
+            g_be.base.matvec = be_matvec;
+            g_be.base.linear_batch = be_linear_batch;
+            g_be.base.matvec_q4k = be_matvec_q4k;
+            g_be.base.rmsnorm_row = be_rmsnorm_row;
+            g_be.base.silu_mul = be_silu_mul;
+            g_be.base.add_inplace = be_add;
+            g_be.base.embed_lookup = be_embed;
+            g_be.base.attention_step = be_attention_step;
+            g_be.base.sync = be_sync;
+            g_be.abi_version = SLATE_CUDA_ABI_VERSION;
+            g_be.device = device;
+            g_be.matmul_q4k_batch = be_matmul_q4k;
+            g_be.matmul_f32_batch = be_matmul_f32;
+            g_be.rmsnorm_rows = be_rmsnorm_rows;
+            g_be.argmax_rows = be_argmax_rows;
+            g_be.rope_kv_append_paged = be_rope_kv;
+            g_be.attention_paged_gqa = be_attention_paged;
+            g_device = device;
+            r = &g_be;
+        } else if (device < 0 || device >= n) {
+            sb_set_error("no CUDA device %d (%d present)", device, n);
+        }
+    }
+    pthread_mutex_unlock(&g_init);
+    return r;
+}
+
+const slate_backend_t* slate_backend_cuda(void) {
+    const char* e = getenv("SLATE_CUDA_BACKEND");
+    if (!e || strcmp(e, "1") != 0) return NULL;
+    const char* d = getenv("SLATE_CUDA_DEVICE");
+    const slate_backend_cuda_t* b = slate_backend_cuda_create(d ? atoi(d) : 0);
+    return b ? &b->base : NULL;
+}

@@ -1,0 +1,754 @@
+/*
+ * llama_batch.c -- device-resident continuous-batching LLaMA decode engine.
+ *
+ * The reference decodes one session at a time (src/loader/llama_infer.c:
+ * 134-206) with a dense host KV cache per session (:225-226); its only
+ * batched step is the GPT engine's slate_infer_batch_step
+ * (src/infer/engine.c:543-642).  This engine runs the LLaMA step for n
+ * sequences at once on one GPU:
+ *
+ *   prologue   validate rows, allocate KV pages, gather embeddings    (1 kernel)
+ *   per layer  rmsnorm -> QKV GEMM -> RoPE + paged KV append ->
+ *              attention (partial + combine) -> Wo GEMM (+residual) ->
+ *              rmsnorm -> gate/up GEMM (+SiLU*up) -> down GEMM (+residual)
+ *                                                                  (9 kernels)
+ *   final      rmsnorm -> LM head GEMM -> argmax + position advance (3 kernels)
+ *
+ * Host responsibilities are only: argument checks against host mirrors of the
+ * positions, the per-step copy of (slot, token) metadata, and launching one
+ * captured CUDA graph per batch size.  Positions, page tables and the page
+ * free list live in device memory and are updated by the kernels.
+ */
+#define _GNU_SOURCE
+#include "sb_internal.h"
+#include "sb_kernels.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+typedef struct sb_layer {
+    float* attn_norm;
+    float* ffn_norm;
+    sb_matrix wqkv, wo, wgu, wdown;
+} sb_layer;
+
+struct slate_llama_batch {
+    int device;
+    cudaStream_t stream;
+    pthread_mutex_t lock;
+    /* model */
+    int L, D, F, nq, nkv, hd, V, kvd, qkv_dim, max_seq;
+    float theta, eps;
+    float *emb, *out_norm;
+    sb_matrix lm_head;
+    sb_layer* layers;
+    void** allocs;
+    int n_allocs, cap_allocs;
+    float *rope_cos, *rope_sin;
+    /* KV */
+    int kv_dtype, max_pages, max_slots;
+    int64_t n_pages;
+    void* pool;
+    int32_t *pos, *page_table, *free_stack, *free_top, *status;
+    /* activations */
+    int max_batch, gemm_path, use_graphs;
+    int ld_x, ld_qkv, ld_att, ld_h, ld_logits;
+    float *x, *xn, *qkv, *att, *h, *logits, *scratch;
+    int32_t *row_pos, *row_slot;
+    int32_t *d_io;        /* [slots | tokens | out_tokens] of max_batch each */
+    int32_t* h_io;        /* pinned mirror of d_io + one status word */
+    /* host mirrors */
+    int* h_pos;
+    unsigned char* h_open;
+    int pos_dirty;
+    int64_t pages_used;
+    /* graphs, one per batch size */
+    cudaGraphExec_t* graphs;
+};
+
+static int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+static void* dalloc(slate_llama_batch_t* b, size_t bytes) {
+    void* p = NULL;
+    if (sb_cuda_check(cudaMalloc(&p, bytes ? bytes : 16), "cudaMalloc")) return NULL;
+    if (b->n_allocs == b->cap_allocs) {
+        b->cap_allocs = b->cap_allocs ? 2 * b->cap_allocs : 64;
+        b->allocs = (void**)realloc(b->allocs, (size_t)b->cap_allocs * sizeof(void*));
+    }
+    b->allocs[b->n_allocs++] = p;
+    return p;
+}
+
+/* ---- weight packing ------------------------------------------------------ */
+
+/* Source rows of one logical matrix: `rows` rows of length K, dtype 0|18. */
+typedef struct { const void* p; int dtype; int rows; } src_part;
+
+static size_t q4k_row_bytes(int K) { return (size_t)(K / 256) * 144; }
+
+/* Host staging buffer (pinned) reused across matrices. */
+typedef struct { void* p; size_t cap; } stage_t;
+static void* stage_get(stage_t* s, size_t bytes) {
+    if (bytes > s->cap) {
+        if (s->p) cudaFreeHost(s->p);
+        s->p = NULL;
+        if (cudaHostAlloc(&s->p, bytes, cudaHostAllocDefault) != cudaSuccess) {
+            s->p = NULL;
+            s->cap = 0;
+            return NULL;
+        }
+        s->cap = bytes;
+    }
+    return s->p;
+}
+
+/* Packs parts (concatenated rows) into one device matrix.  interleave64 puts
+ * part 0 (gate) and part 1 (up) in alternating 64-row groups for the fused
+ * SwiGLU epilogue.  All-Q4_K groups stay Q4_K; any f32 part makes the whole
+ * matrix f32 (Q4_K parts dequantised exactly). */
+static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, const src_part* parts,
+                       int nparts, int K, int interleave64) {
+    int all_q4k = 1, M = 0;
+    for (int i = 0; i < nparts; ++i) {
+        if (parts[i].dtype != 0 && parts[i].dtype != 18) {
+            sb_set_error("unsupported weight dtype %d", parts[i].dtype);
+            return -1;
+        }
+        if (parts[i].dtype != 18) all_q4k = 0;
+        M += parts[i].rows;
+    }
+    if (all_q4k && K % 256) all_q4k = 0;
+    int per_part_pad = 0;
+    if (interleave64) {
+        per_part_pad = round_up(parts[0].rows, 64);
+        M = 2 * per_part_pad;
+    }
+    const int M_pad = round_up(M, 128);
+    out->wtype = all_q4k ? SB_WT_Q4K : SB_WT_F32;
+    out->M = M;
+    out->M_pad = M_pad;
+    out->K = K;
+    out->ldw = all_q4k ? 0 : round_up(K, 128);
+    const size_t row_bytes = all_q4k ? q4k_row_bytes(K) : (size_t)out->ldw * 4;
+    const size_t bytes = row_bytes * (size_t)M_pad;
+    if (nparts == 1 && !interleave64 && (all_q4k || (parts[0].dtype == 0 && out->ldw == K))) {
+        /* already in the device layout: copy rows straight from the source */
+        unsigned char* dptr = (unsigned char*)dalloc(b, bytes);
+        if (!dptr) return -5;
+        SB_CU(cudaMemcpy(dptr, parts[0].p, row_bytes * (size_t)M, cudaMemcpyHostToDevice));
+        if (M_pad > M) SB_CU(cudaMemset(dptr + row_bytes * (size_t)M, 0, row_bytes * (size_t)(M_pad - M)));
+        out->data = dptr;
+        return 0;
+    }
+    unsigned char* h = (unsigned char*)stage_get(st, bytes);
+    if (!h) {
+        sb_set_error("pinned staging of %zu bytes failed", bytes);
+        return -5;
+    }
+    memset(h, 0, bytes);
+    /* destination row of source row r of part i */
+    for (int i = 0, base = 0; i < nparts; ++i) {
+        const src_part* sp = &parts[i];
+        const size_t src_row = sp->dtype == 18 ? q4k_row_bytes(K) : (size_t)K * 4;
+        for (int r = 0; r < sp->rows; ++r) {
+            int dr;
+            if (interleave64) dr = (r / 64) * 128 + (i ? 64 : 0) + r % 64;
+            else dr = base + r;
+            const unsigned char* s = (const unsigned char*)sp->p + (size_t)r * src_row;
+            unsigned char* d = h + (size_t)dr * row_bytes;
+            if (all_q4k) memcpy(d, s, src_row);
+            else if (sp->dtype == 0) memcpy(d, s, (size_t)K * 4);
+            else sb_q4k_dequant_rows((float*)d, s, 1, K);
+        }
+        base += sp->rows;
+    }
+    void* dptr = dalloc(b, bytes);
+    if (!dptr) return -5;
+    SB_CU(cudaMemcpy(dptr, h, bytes, cudaMemcpyHostToDevice));
+    out->data = dptr;
+    return 0;
+}
+
+static int upload_f32(slate_llama_batch_t* b, float** dst, const void* src, size_t n) {
+    *dst = (float*)dalloc(b, n * 4);
+    if (!*dst) return -5;
+    SB_CU(cudaMemcpy(*dst, src, n * 4, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+/* ---- step enqueue ------------------------------------------------------- */
+
+static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
+    int rc = 0;
+    const int32_t* slots = b->d_io;
+    const int32_t* toks = b->d_io + b->max_batch;
+    int32_t* out = b->d_io + 2 * b->max_batch;
+    rc |= sb_step_prologue(slots, toks, n, b->pos, b->page_table, b->max_pages, b->free_stack,
+                           b->free_top, b->max_slots, b->max_seq, b->V, b->emb, b->D, b->x,
+                           b->ld_x, b->row_pos, b->row_slot, b->status, s);
+    for (int l = 0; l < b->L && !rc; ++l) {
+        const sb_layer* ly = &b->layers[l];
+        rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, ly->attn_norm, n, b->D, b->eps, s);
+        rc |= sb_gemm(&ly->wqkv, b->xn, b->ld_x, n, b->qkv, b->ld_qkv, SB_EPI_STORE, b->gemm_path, s);
+        rc |= sb_rope_append(b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, b->row_pos, b->row_slot,
+                             b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
+                             b->rope_cos, b->rope_sin, s);
+        rc |= sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
+                                 b->row_pos, b->row_slot, b->page_table, b->max_pages, b->pool,
+                                 b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch, s);
+        rc |= sb_gemm(&ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, SB_EPI_ADD, b->gemm_path, s);
+        rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, ly->ffn_norm, n, b->D, b->eps, s);
+        rc |= sb_gemm(&ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->gemm_path, s);
+        rc |= sb_gemm(&ly->wdown, b->h, b->ld_h, n, b->x, b->ld_x, SB_EPI_ADD, b->gemm_path, s);
+    }
+    rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, b->out_norm, n, b->D, b->eps, s);
+    rc |= sb_gemm(&b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE,
+                  b->gemm_path, s);
+    rc |= sb_step_epilogue(b->logits, b->ld_logits, b->V, n, b->row_slot, b->row_pos, b->pos,
+                           b->status, out, s);
+    if (rc) {
+        sb_set_error("kernel launch rejected its arguments");
+        return -1;
+    }
+    return sb_cuda_check(cudaGetLastError(), "step launch");
+}
+
+int slate_llama_batch_launches_per_step(const slate_llama_batch_t* b, int n) {
+    (void)n;
+    return b ? 4 + 9 * b->L : 0;
+}
+
+/* Runs the step for n rows whose metadata is already in d_io. */
+static int run_step(slate_llama_batch_t* b, int n) {
+    if (!b->use_graphs) return enqueue_step(b, n, b->stream);
+    if (!b->graphs[n]) {
+        cudaGraph_t g = NULL;
+        SB_CU(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue_step(b, n, b->stream);
+        cudaError_t e = cudaStreamEndCapture(b->stream, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        SB_CU(e);
+        e = cudaGraphInstantiate(&b->graphs[n], g, 0);
+        cudaGraphDestroy(g);
+        SB_CU(e);
+    }
+    SB_CU(cudaGraphLaunch(b->graphs[n], b->stream));
+    return 0;
+}
+
+/* ---- construction ------------------------------------------------------- */
+
+void slate_llama_batch_free(slate_llama_batch_t* b) {
+    if (!b) return;
+    cudaSetDevice(b->device);
+    if (b->stream) cudaStreamSynchronize(b->stream);
+    if (b->graphs) {
+        for (int i = 0; i <= b->max_batch; ++i)
+            if (b->graphs[i]) cudaGraphExecDestroy(b->graphs[i]);
+        free(b->graphs);
+    }
+    for (int i = 0; i < b->n_allocs; ++i) cudaFree(b->allocs[i]);
+    free(b->allocs);
+    if (b->h_io) cudaFreeHost(b->h_io);
+    if (b->stream) cudaStreamDestroy(b->stream);
+    free(b->layers);
+    free(b->h_pos);
+    free(b->h_open);
+    pthread_mutex_destroy(&b->lock);
+    free(b);
+}
+
+slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
+                                                const slate_cuda_opts_t* o) {
+    if (!m || !o) { sb_set_error("NULL model or options"); return NULL; }
+    const int L = m->n_layers, D = m->d_model, F = m->ffn_hidden, nq = m->n_heads,
+              nkv = m->n_kv_heads, hd = m->head_dim, V = m->vocab;
+    if (L < 1 || D < 1 || F < 1 || nq < 1 || nkv < 1 || nq % nkv || hd * nq != D || V < 1 ||
+        !m->token_embd || !m->output_norm || !m->output || !m->layers) {
+        sb_set_error("inconsistent model description");
+        return NULL;
+    }
+    if (hd != 16 && hd != 32 && hd != 64 && hd != 128) {
+        sb_set_error("head_dim %d unsupported (16, 32, 64, 128)", hd);
+        return NULL;
+    }
+    const int G = nq / nkv;
+    if (G != 1 && G != 2 && G != 4 && G != 8) {
+        sb_set_error("GQA group %d unsupported (1, 2, 4, 8)", G);
+        return NULL;
+    }
+    if (m->token_embd_dtype != 0) {
+        sb_set_error("token_embd must be f32 (llama_infer.c:149-150 reads it as f32)");
+        return NULL;
+    }
+    if (o->max_batch < 1 || o->max_batch > 1024) {
+        sb_set_error("max_batch %d out of range", o->max_batch);
+        return NULL;
+    }
+    slate_llama_batch_t* b = (slate_llama_batch_t*)calloc(1, sizeof(*b));
+    pthread_mutex_init(&b->lock, NULL);
+    b->device = o->device;
+    b->L = L; b->D = D; b->F = F; b->nq = nq; b->nkv = nkv; b->hd = hd; b->V = V;
+    b->kvd = nkv * hd;
+    b->qkv_dim = D + 2 * b->kvd;
+    b->theta = m->theta_base;
+    b->eps = m->rms_eps;
+    b->max_seq = o->max_seq > 0 ? o->max_seq : m->max_seq;
+    b->max_batch = o->max_batch;
+    b->max_slots = o->max_slots > 0 ? o->max_slots : o->max_batch;
+    b->kv_dtype = o->kv_dtype == SLATE_KV_F16 ? SLATE_KV_F16 : SLATE_KV_F32;
+    b->gemm_path = o->gemm_path;
+    b->use_graphs = o->use_graphs;
+    b->max_pages = (b->max_seq + SB_PAGE_TOKENS - 1) / SB_PAGE_TOKENS;
+    stage_t stg = {NULL, 0};
+
+    if (sb_cuda_check(cudaSetDevice(b->device), "cudaSetDevice") ||
+        sb_cuda_check(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking), "stream"))
+        goto fail;
+    sb_gemm_prepare();
+
+    /* weights */
+    if (upload_f32(b, &b->emb, m->token_embd, (size_t)V * D)) goto fail;
+    if (upload_f32(b, &b->out_norm, m->output_norm, (size_t)D)) goto fail;
+    if (m->output == m->token_embd && m->output_dtype == 0 && D % 128 == 0 && V % 128 == 0) {
+        b->lm_head = (sb_matrix){SB_WT_F32, b->emb, V, V, D, D};   /* tied: share the table */
+    } else {
+        src_part p = {m->output, m->output_dtype, V};
+        if (pack_matrix(b, &stg, &b->lm_head, &p, 1, D, 0)) goto fail;
+    }
+    b->layers = (sb_layer*)calloc((size_t)L, sizeof(sb_layer));
+    for (int l = 0; l < L; ++l) {
+        const slate_llama_layer_desc_t* s = m->layers[l];
+        sb_layer* ly = &b->layers[l];
+        if (!s) { sb_set_error("layer %d missing", l); goto fail; }
+        if (upload_f32(b, &ly->attn_norm, s->attn_norm, (size_t)D) ||
+            upload_f32(b, &ly->ffn_norm, s->ffn_norm, (size_t)D))
+            goto fail;
+        src_part qkv[3] = {{s->attn_q, s->attn_q_dtype, D},
+                           {s->attn_k, s->attn_k_dtype, b->kvd},
+                           {s->attn_v, s->attn_v_dtype, b->kvd}};
+        src_part wo = {s->attn_output, s->attn_output_dtype, D};
+        src_part gu[2] = {{s->ffn_gate, s->ffn_gate_dtype, F}, {s->ffn_up, s->ffn_up_dtype, F}};
+        src_part dn = {s->ffn_down, s->ffn_down_dtype, D};
+        if (pack_matrix(b, &stg, &ly->wqkv, qkv, 3, D, 0) ||
+            pack_matrix(b, &stg, &ly->wo, &wo, 1, D, 0) ||
+            pack_matrix(b, &stg, &ly->wgu, gu, 2, D, 1) ||
+            pack_matrix(b, &stg, &ly->wdown, &dn, 1, F, 0))
+            goto fail;
+    }
+    if (stg.p) cudaFreeHost(stg.p);
+    stg.p = NULL;
+
+    /* RoPE tables with the reference's exact f32 expressions (llama_infer.c:83-85). */
+    {
+        const int half = hd / 2;
+        size_t n = (size_t)b->max_seq * half;
+        float* c = (float*)malloc(n * 4);
+        float* sn = (float*)malloc(n * 4);
+        for (int p = 0; p < b->max_seq; ++p)
+            for (int i = 0; i < half; ++i) {
+                float inv_freq = powf(b->theta, -2.0f * (float)i / (float)hd);
+                float angle = (float)p * inv_freq;
+                c[(size_t)p * half + i] = cosf(angle);
+                sn[(size_t)p * half + i] = sinf(angle);
+            }
+        int rc = upload_f32(b, &b->rope_cos, c, n) | upload_f32(b, &b->rope_sin, sn, n);
+        free(c);
+        free(sn);
+        if (rc) goto fail;
+    }
+
+    /* activations */
+    {
+        const int Dp = round_up(D, 128);
+        const int B = b->max_batch;
+        b->ld_x = Dp;
+        b->ld_att = Dp;
+        b->ld_qkv = round_up(b->layers[0].wqkv.M_pad, 4);
+        b->ld_h = round_up(b->layers[0].wgu.M_pad / 2, 128);
+        b->ld_logits = round_up(b->lm_head.M_pad, 4);
+        size_t scr = sb_attention_scratch_floats(B, nq, hd, b->max_seq);
+        b->x = (float*)dalloc(b, (size_t)B * b->ld_x * 4);
+        b->xn = (float*)dalloc(b, (size_t)B * b->ld_x * 4);
+        b->att = (float*)dalloc(b, (size_t)B * b->ld_att * 4);
+        b->qkv = (float*)dalloc(b, (size_t)B * b->ld_qkv * 4);
+        b->h = (float*)dalloc(b, (size_t)B * b->ld_h * 4);
+        b->logits = (float*)dalloc(b, (size_t)B * b->ld_logits * 4);
+        b->scratch = (float*)dalloc(b, scr * 4);
+        b->row_pos = (int32_t*)dalloc(b, (size_t)B * 4);
+        b->row_slot = (int32_t*)dalloc(b, (size_t)B * 4);
+        b->d_io = (int32_t*)dalloc(b, (size_t)3 * B * 4);
+        b->status = (int32_t*)dalloc(b, 16);
+        if (!b->x || !b->xn || !b->att || !b->qkv || !b->h || !b->logits || !b->scratch ||
+            !b->row_pos || !b->row_slot || !b->d_io || !b->status)
+            goto fail;
+        /* zero padding columns are part of the GEMM contract */
+        if (sb_cuda_check(cudaMemset(b->x, 0, (size_t)B * b->ld_x * 4), "memset") ||
+            sb_cuda_check(cudaMemset(b->xn, 0, (size_t)B * b->ld_x * 4), "memset") ||
+            sb_cuda_check(cudaMemset(b->att, 0, (size_t)B * b->ld_att * 4), "memset") ||
+            sb_cuda_check(cudaMemset(b->h, 0, (size_t)B * b->ld_h * 4), "memset") ||
+            sb_cuda_check(cudaMemset(b->qkv, 0, (size_t)B * b->ld_qkv * 4), "memset") ||
+            sb_cuda_check(cudaMemset(b->status, 0, 16), "memset") ||
+            sb_cuda_check(cudaMemset(b->d_io, 0, (size_t)3 * B * 4), "memset"))
+            goto fail;
+        if (sb_cuda_check(cudaHostAlloc((void**)&b->h_io, (size_t)(3 * B + 4) * 4,
+                                        cudaHostAllocDefault), "cudaHostAlloc"))
+            goto fail;
+    }
+
+    /* KV pool, page tables, free list */
+    {
+        const size_t esz = b->kv_dtype == SLATE_KV_F16 ? 2 : 4;
+        const size_t page_bytes_all = (size_t)L * 2 * nkv * SB_PAGE_TOKENS * hd * esz;
+        int64_t pages = o->kv_pages;
+        if (pages <= 0) {
+            size_t budget = o->kv_bytes;
+            if (!budget) {
+                size_t fr = 0, tot = 0;
+                if (sb_cuda_check(cudaMemGetInfo(&fr, &tot), "cudaMemGetInfo")) goto fail;
+                size_t tables = (size_t)b->max_slots * b->max_pages * 4;
+                budget = fr > tables + (1u << 30) ? (size_t)((double)(fr - tables) * 0.90) : 0;
+            }
+            pages = (int64_t)(budget / page_bytes_all);
+            int64_t want = (int64_t)b->max_slots * b->max_pages;
+            if (pages > want) pages = want;
+        }
+        if (pages < 1 || pages > 0x7fffffff) {
+            sb_set_error("KV pool of %lld pages not possible", (long long)pages);
+            goto fail;
+        }
+        b->n_pages = pages;
+        b->pool = dalloc(b, (size_t)pages * page_bytes_all);
+        b->pos = (int32_t*)dalloc(b, (size_t)b->max_slots * 4);
+        b->page_table = (int32_t*)dalloc(b, (size_t)b->max_slots * b->max_pages * 4);
+        b->free_stack = (int32_t*)dalloc(b, (size_t)pages * 4);
+        b->free_top = (int32_t*)dalloc(b, 16);
+        if (!b->pool || !b->pos || !b->page_table || !b->free_stack || !b->free_top) goto fail;
+        if (sb_cuda_check(cudaMemset(b->pos, 0, (size_t)b->max_slots * 4), "memset") ||
+            sb_cuda_check(cudaMemset(b->page_table, 0xff, (size_t)b->max_slots * b->max_pages * 4),
+                          "memset"))
+            goto fail;
+        if (sb_init_free_list(b->free_stack, b->free_top, pages, b->stream)) goto fail;
+    }
+    b->h_pos = (int*)calloc((size_t)b->max_slots, sizeof(int));
+    b->h_open = (unsigned char*)calloc((size_t)b->max_slots, 1);
+    b->graphs = (cudaGraphExec_t*)calloc((size_t)b->max_batch + 1, sizeof(cudaGraphExec_t));
+    if (sb_cuda_check(cudaStreamSynchronize(b->stream), "init sync")) goto fail;
+    return b;
+fail:
+    if (stg.p) cudaFreeHost(stg.p);
+    slate_llama_batch_free(b);
+    return NULL;
+}
+
+slate_llama_batch_t* slate_llama_batch_new_gguf(const char* path, const slate_cuda_opts_t* o) {
+    slate_llama_desc_t d;
+    slate_gguf_model_t* g = slate_gguf_model_open(path, &d);
+    if (!g) return NULL;
+    slate_llama_batch_t* b = slate_llama_batch_new_desc(&d, o);
+    slate_gguf_model_close(g);
+    return b;
+}
+
+/* ---- accessors ---------------------------------------------------------- */
+int slate_llama_batch_vocab(const slate_llama_batch_t* b) { return b ? b->V : -1; }
+int slate_llama_batch_max_batch(const slate_llama_batch_t* b) { return b ? b->max_batch : -1; }
+int slate_llama_batch_max_seq(const slate_llama_batch_t* b) { return b ? b->max_seq : -1; }
+int64_t slate_llama_batch_free_pages(const slate_llama_batch_t* b) {
+    return b ? b->n_pages - b->pages_used : -1;
+}
+void* slate_llama_batch_stream(slate_llama_batch_t* b) { return b ? (void*)b->stream : NULL; }
+
+/* Pulls device positions into the host mirror after device-API steps. */
+static int refresh_positions(slate_llama_batch_t* b) {
+    if (!b->pos_dirty) return 0;
+    SB_CU(cudaMemcpyAsync(b->h_pos, b->pos, (size_t)b->max_slots * 4, cudaMemcpyDeviceToHost,
+                          b->stream));
+    SB_CU(cudaStreamSynchronize(b->stream));
+    int64_t used = 0;
+    for (int s = 0; s < b->max_slots; ++s)
+        if (b->h_open[s]) used += (b->h_pos[s] + SB_PAGE_TOKENS - 1) / SB_PAGE_TOKENS;
+    b->pages_used = used;
+    b->pos_dirty = 0;
+    return 0;
+}
+
+int slate_llama_batch_open(slate_llama_batch_t* b) {
+    if (!b) return -1;
+    pthread_mutex_lock(&b->lock);
+    int slot = -2;
+    for (int s = 0; s < b->max_slots; ++s)
+        if (!b->h_open[s]) {
+            b->h_open[s] = 1;
+            b->h_pos[s] = 0;
+            slot = s;
+            break;
+        }
+    pthread_mutex_unlock(&b->lock);
+    return slot;
+}
+
+int slate_llama_batch_close(slate_llama_batch_t* b, int slot) {
+    if (!b || slot < 0 || slot >= b->max_slots || !b->h_open[slot]) return -1;
+    pthread_mutex_lock(&b->lock);
+    int rc = refresh_positions(b);
+    if (!rc) {
+        cudaSetDevice(b->device);
+        rc = sb_release_slot(slot, b->pos, b->page_table, b->max_pages, b->free_stack,
+                             b->free_top, b->stream);
+        if (!rc) rc = sb_cuda_check(cudaGetLastError(), "release");
+        b->pages_used -= (b->h_pos[slot] + SB_PAGE_TOKENS - 1) / SB_PAGE_TOKENS;
+        b->h_open[slot] = 0;
+        b->h_pos[slot] = 0;
+    }
+    pthread_mutex_unlock(&b->lock);
+    return rc;
+}
+
+int slate_llama_batch_position(const slate_llama_batch_t* cb, int slot) {
+    slate_llama_batch_t* b = (slate_llama_batch_t*)cb;
+    if (!b || slot < 0 || slot >= b->max_slots || !b->h_open[slot]) return -1;
+    pthread_mutex_lock(&b->lock);
+    int rc = refresh_positions(b);
+    int p = rc ? rc : b->h_pos[slot];
+    pthread_mutex_unlock(&b->lock);
+    return p;
+}
+
+/* ---- steps --------------------------------------------------------------- */
+
+int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
+                           const int32_t* tokens, int32_t* out_tokens, float* out_logits) {
+    if (!b || !slots || !tokens || n < 1 || n > b->max_batch) return -1;
+    pthread_mutex_lock(&b->lock);
+    int rc = refresh_positions(b);
+    /* host-side validation, same order and codes as engine.c:557-559 */
+    int64_t new_pages = 0;
+    for (int r = 0; r < n && !rc; ++r) {
+        const int s = slots[r];
+        if (s < 0 || s >= b->max_slots || !b->h_open[s]) { rc = -1; break; }
+        for (int q = 0; q < r; ++q)
+            if (slots[q] == s) { rc = -1; break; }
+        if (rc) break;
+        if (b->h_pos[s] >= b->max_seq) { rc = -2; break; }
+        if (tokens[r] < 0 || tokens[r] >= b->V) { rc = -3; break; }
+        if (b->h_pos[s] % SB_PAGE_TOKENS == 0) ++new_pages;
+    }
+    if (!rc && b->pages_used + new_pages > b->n_pages) rc = -2;
+    if (rc) {
+        pthread_mutex_unlock(&b->lock);
+        return rc;
+    }
+    cudaSetDevice(b->device);
+    int32_t* h = b->h_io;
+    memcpy(h, slots, (size_t)n * 4);
+    memcpy(h + b->max_batch, tokens, (size_t)n * 4);
+    rc = sb_cuda_check(cudaMemcpyAsync(b->d_io, h, (size_t)2 * b->max_batch * 4,
+                                       cudaMemcpyHostToDevice, b->stream), "H2D metadata");
+    if (!rc) rc = run_step(b, n);
+    if (!rc)
+        rc = sb_cuda_check(cudaMemcpyAsync(h + 2 * b->max_batch, b->d_io + 2 * b->max_batch,
+                                           (size_t)n * 4, cudaMemcpyDeviceToHost, b->stream),
+                           "D2H tokens");
+    if (!rc)
+        rc = sb_cuda_check(cudaMemcpyAsync(h + 3 * b->max_batch, b->status, 4,
+                                           cudaMemcpyDeviceToHost, b->stream), "D2H status");
+    if (!rc && out_logits)
+        rc = sb_cuda_check(cudaMemcpy2DAsync(out_logits, (size_t)b->V * 4, b->logits,
+                                             (size_t)b->ld_logits * 4, (size_t)b->V * 4, (size_t)n,
+                                             cudaMemcpyDeviceToHost, b->stream), "D2H logits");
+    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(b->status, 0, 4, b->stream), "status reset");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(b->stream), "step");
+    if (!rc) {
+        const int st = h[3 * b->max_batch];
+        if (st) {
+            rc = st;
+            sb_set_error("device rejected the step (%d)", st);
+        } else {
+            for (int r = 0; r < n; ++r) {
+                if (b->h_pos[slots[r]] % SB_PAGE_TOKENS == 0) ++b->pages_used;
+                b->h_pos[slots[r]]++;
+            }
+            if (out_tokens) memcpy(out_tokens, h + 2 * b->max_batch, (size_t)n * 4);
+        }
+    }
+    pthread_mutex_unlock(&b->lock);
+    return rc;
+}
+
+int slate_llama_batch_step_device(slate_llama_batch_t* b, const int32_t* d_slots, int n,
+                                  const int32_t* d_tokens, int32_t* d_out_tokens,
+                                  float* d_out_logits, void* stream) {
+    if (!b || !d_slots || !d_tokens || n < 1 || n > b->max_batch) return -1;
+    pthread_mutex_lock(&b->lock);
+    cudaSetDevice(b->device);
+    cudaStream_t us = stream ? (cudaStream_t)stream : b->stream;
+    int rc = 0;
+    cudaEvent_t ev = NULL;
+    if (us != b->stream) {
+        /* order the engine stream after the caller's work and vice versa */
+        rc = sb_cuda_check(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event");
+        if (!rc) rc = sb_cuda_check(cudaEventRecord(ev, us), "event record");
+        if (!rc) rc = sb_cuda_check(cudaStreamWaitEvent(b->stream, ev, 0), "event wait");
+    }
+    if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(b->d_io, d_slots, (size_t)n * 4,
+                                                cudaMemcpyDeviceToDevice, b->stream), "slots");
+    if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(b->d_io + b->max_batch, d_tokens, (size_t)n * 4,
+                                                cudaMemcpyDeviceToDevice, b->stream), "tokens");
+    if (!rc) rc = run_step(b, n);
+    if (!rc && d_out_tokens)
+        rc = sb_cuda_check(cudaMemcpyAsync(d_out_tokens, b->d_io + 2 * b->max_batch, (size_t)n * 4,
+                                           cudaMemcpyDeviceToDevice, b->stream), "out tokens");
+    if (!rc && d_out_logits)
+        rc = sb_cuda_check(cudaMemcpy2DAsync(d_out_logits, (size_t)b->V * 4, b->logits,
+                                             (size_t)b->ld_logits * 4, (size_t)b->V * 4, (size_t)n,
+                                             cudaMemcpyDeviceToDevice, b->stream), "out logits");
+    if (!rc && ev) {
+        rc = sb_cuda_check(cudaEventRecord(ev, b->stream), "event record");
+        if (!rc) rc = sb_cuda_check(cudaStreamWaitEvent(us, ev, 0), "event wait");
+    }
+    if (ev) cudaEventDestroy(ev);
+    b->pos_dirty = 1;
+    pthread_mutex_unlock(&b->lock);
+    return rc;
+}
+
+int slate_llama_batch_sync(slate_llama_batch_t* b) {
+    if (!b) return -1;
+    pthread_mutex_lock(&b->lock);
+    cudaSetDevice(b->device);
+    int rc = sb_cuda_check(cudaMemcpyAsync(b->h_io + 3 * b->max_batch, b->status, 4,
+                                           cudaMemcpyDeviceToHost, b->stream), "D2H status");
+    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(b->status, 0, 4, b->stream), "status reset");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(b->stream), "sync");
+    if (!rc) rc = b->h_io[3 * b->max_batch];
+    pthread_mutex_unlock(&b->lock);
+    return rc;
+}
+
+int slate_llama_batch_prefill(slate_llama_batch_t* b, int slot, const int32_t* tokens,
+                              int n_tokens, float* out_logits) {
+    if (!b || !tokens || n_tokens <= 0) return -1;
+    int32_t s = slot;
+    for (int i = 0; i < n_tokens; ++i) {
+        int rc = slate_llama_batch_step(b, &s, 1, &tokens[i], NULL,
+                                        i == n_tokens - 1 ? out_logits : NULL);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
+int slate_llama_batch_seed_context(slate_llama_batch_t* b, int slot, int n_tokens, uint64_t seed) {
+    if (!b || slot < 0 || slot >= b->max_slots || !b->h_open[slot] || n_tokens < 0) return -1;
+    pthread_mutex_lock(&b->lock);
+    int rc = refresh_positions(b);
+    if (!rc && (b->h_pos[slot] != 0 || n_tokens > b->max_seq)) rc = -2;
+    const int64_t need = (n_tokens + SB_PAGE_TOKENS - 1) / SB_PAGE_TOKENS;
+    if (!rc && b->pages_used + need > b->n_pages) rc = -2;
+    if (!rc) {
+        cudaSetDevice(b->device);
+        rc = sb_seed_context(slot, n_tokens, seed, b->L, b->nkv, b->hd, b->pos, b->page_table,
+                             b->max_pages, b->free_stack, b->free_top, b->pool, b->n_pages,
+                             b->kv_dtype, b->status, b->stream);
+        if (!rc) rc = sb_cuda_check(cudaGetLastError(), "seed");
+        if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(b->h_io + 3 * b->max_batch, b->status, 4,
+                                                    cudaMemcpyDeviceToHost, b->stream), "status");
+        if (!rc) rc = sb_cuda_check(cudaMemsetAsync(b->status, 0, 4, b->stream), "status reset");
+        if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(b->stream), "seed sync");
+        if (!rc) rc = b->h_io[3 * b->max_batch];
+        if (!rc) {
+            b->h_pos[slot] = n_tokens;
+            b->pages_used += need;
+        }
+    }
+    pthread_mutex_unlock(&b->lock);
+    return rc;
+}
+
+int slate_llama_batch_read_kv(slate_llama_batch_t* b, int slot, int n, float* K, float* V) {
+    if (!b || !K || !V || slot < 0 || slot >= b->max_slots || !b->h_open[slot] || n < 1) return -1;
+    pthread_mutex_lock(&b->lock);
+    int rc = refresh_positions(b);
+    if (!rc && n > b->h_pos[slot]) rc = -1;
+    float *dk = NULL, *dv = NULL;
+    const size_t cnt = (size_t)b->L * n * b->kvd;
+    if (!rc) {
+        cudaSetDevice(b->device);
+        rc = sb_cuda_check(cudaMalloc((void**)&dk, cnt * 4), "cudaMalloc");
+        if (!rc) rc = sb_cuda_check(cudaMalloc((void**)&dv, cnt * 4), "cudaMalloc");
+        if (!rc) rc = sb_read_kv(slot, n, b->L, b->nkv, b->hd, b->page_table, b->max_pages, b->pool,
+                                 b->n_pages, b->kv_dtype, dk, dv, b->stream);
+        if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(K, dk, cnt * 4, cudaMemcpyDeviceToHost, b->stream), "K");
+        if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(V, dv, cnt * 4, cudaMemcpyDeviceToHost, b->stream), "V");
+        if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(b->stream), "read_kv");
+    }
+    if (dk) cudaFree(dk);
+    if (dv) cudaFree(dv);
+    pthread_mutex_unlock(&b->lock);
+    return rc;
+}
+
+/* ---- profiling ---------------------------------------------------------- */
+static int enqueue_kernel(slate_llama_batch_t* b, int kernel, int n, int layer, cudaStream_t s) {
+    const sb_layer* ly = &b->layers[layer];
+    float* scratch_y = b->logits;   /* [max_batch][ld_logits], >= any GEMM output row here */
+    switch (kernel) {
+        case SLATE_PROF_ATTENTION:
+            return sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
+                                      b->row_pos, b->row_slot, b->page_table, b->max_pages,
+                                      b->pool, b->n_pages, layer, b->kv_dtype, b->max_seq,
+                                      b->scratch, s);
+        case SLATE_PROF_QKV:
+            return sb_gemm(&ly->wqkv, b->xn, b->ld_x, n, scratch_y, b->ld_logits, SB_EPI_STORE,
+                           b->gemm_path, s);
+        case SLATE_PROF_WO:
+            return sb_gemm(&ly->wo, b->att, b->ld_att, n, scratch_y, b->ld_logits, SB_EPI_STORE,
+                           b->gemm_path, s);
+        case SLATE_PROF_GATE_UP:
+            return sb_gemm(&ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->gemm_path, s);
+        case SLATE_PROF_DOWN:
+            return sb_gemm(&ly->wdown, b->h, b->ld_h, n, scratch_y, b->ld_logits, SB_EPI_STORE,
+                           b->gemm_path, s);
+        case SLATE_PROF_LM_HEAD:
+            return sb_gemm(&b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE,
+                           b->gemm_path, s);
+        case SLATE_PROF_STEP:
+            return run_step(b, n);
+    }
+    return -1;
+}
+
+int slate_llama_batch_profile(slate_llama_batch_t* b, int kernel, int n, int layer, int iters,
+                              float* ms) {
+    if (!b || !ms || n < 1 || n > b->max_batch || layer < 0 || layer >= b->L || iters < 1 ||
+        kernel < 0 || kernel > SLATE_PROF_STEP)
+        return -1;
+    if (b->ld_logits < b->D || (kernel == SLATE_PROF_QKV && b->ld_logits < b->layers[0].wqkv.M)) {
+        sb_set_error("profile scratch too small for this model");
+        return -1;
+    }
+    pthread_mutex_lock(&b->lock);
+    cudaSetDevice(b->device);
+    cudaEvent_t e0 = NULL, e1 = NULL;
+    int rc = sb_cuda_check(cudaEventCreate(&e0), "event");
+    if (!rc) rc = sb_cuda_check(cudaEventCreate(&e1), "event");
+    if (!rc) rc = enqueue_kernel(b, kernel, n, layer, b->stream);   /* untimed */
+    if (!rc) rc = sb_cuda_check(cudaEventRecord(e0, b->stream), "record");
+    for (int i = 0; i < iters && !rc; ++i) rc = enqueue_kernel(b, kernel, n, layer, b->stream);
+    if (!rc) rc = sb_cuda_check(cudaEventRecord(e1, b->stream), "record");
+    if (!rc) rc = sb_cuda_check(cudaEventSynchronize(e1), "sync");
+    float t = 0.f;
+    if (!rc) rc = sb_cuda_check(cudaEventElapsedTime(&t, e0, e1), "elapsed");
+    if (!rc) *ms = t / (float)iters;
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (kernel == SLATE_PROF_STEP) b->pos_dirty = 1;
+    pthread_mutex_unlock(&b->lock);
+    return rc;
+}

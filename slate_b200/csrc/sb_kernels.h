@@ -1,0 +1,119 @@
+/*
+ * sb_kernels.h -- C-callable launchers for the sm_100a kernels (internal to
+ * libslate_cuda.so; the public ABI is include/slate_cuda.h).  Every launcher
+ * enqueues on the given stream and returns 0, or -1 for unsupported
+ * arguments (checked before anything is launched).
+ */
+#ifndef SB_KERNELS_H
+#define SB_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+#include "slate_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_WT_F32 0
+#define SB_WT_Q4K 18
+
+#define SB_EPI_STORE 0   /* Y[n][m]  = acc                                   */
+#define SB_EPI_ADD   1   /* Y[n][m] += acc (residual add, backend_cpu.c:99)  */
+#define SB_EPI_SILU  2   /* rows interleaved by 64 (gate | up) per 128-row
+                            tile: Y[n][t*64+r] = silu(g)*u (backend_cpu.c:78) */
+
+#define SB_PAGE_TOKENS 16
+
+/* Weight matrix as the GEMMs consume it (packed once at upload):
+ *   Q4_K: rows of K/256 super-blocks of 144 bytes (Slate's nibble order),
+ *         row stride K/256*144 bytes, M_pad rows (zero blocks past M).
+ *   f32 : row-major [M_pad][ldw] with ldw >= K, ldw % 32 == 0, zero padded. */
+typedef struct sb_matrix {
+    int wtype;
+    const void* data;
+    int M;       /* logical rows (for SILU: 2 * outputs, interleaved)      */
+    int M_pad;   /* physical rows, multiple of 128                         */
+    int K;       /* reduction length                                       */
+    int ldw;     /* f32 row stride (floats); ignored for Q4_K              */
+} sb_matrix;
+
+/* Y[n][·] (epi) X[n][0..K) · W[m][0..K)  for n < B.
+ * X row stride ldx (floats); for f32 weights X must be zero in [K, ldw).
+ * path: 0 = auto (GEMV for B <= 8, tiled otherwise), 1 = tiled only. */
+int sb_gemm(const sb_matrix* W, const float* X, int ldx, int B, float* Y, int ldy,
+            int epi, int path, cudaStream_t st);
+
+/* Generic (any shape / alignment) f32 kernels for the reference vtable. */
+int sb_matvec_f32_generic(float* y, const float* A, const float* x, int M, int K, cudaStream_t st);
+int sb_linear_batch_generic(float* C, const float* X, const float* W, int B, int K, int N,
+                            cudaStream_t st);
+int sb_q4k_matmul_generic(float* Y, const void* A, const float* X, int B, int M, int K,
+                          cudaStream_t st);
+
+/* Row-wise RMSNorm (backend_cpu.c:48-76): Y[b] = X[b]*w*inv_rms(X[b]). */
+int sb_rmsnorm_rows(float* Y, int ldy, const float* X, int ldx, const float* w, int B, int D,
+                    float eps, cudaStream_t st);
+int sb_silu_mul(float* y, const float* g, const float* u, int n, cudaStream_t st);
+int sb_add_inplace(float* y, const float* x, int n, cudaStream_t st);
+int sb_embed_lookup(float* y, const float* W, int token, int D, cudaStream_t st);
+int sb_argmax_rows(int32_t* out, const float* logits, int ld, int B, int V, cudaStream_t st);
+int sb_attention_step(float* out, const float* q, const float* K, const float* V, int L, int D,
+                      cudaStream_t st);
+
+/* Step prologue: validates rows, allocates KV pages on the device free list,
+ * records row_pos/row_slot and gathers embeddings x[b] = emb[token[b]].
+ * status (device int) receives -3 (bad token), -2 (position/pages) or -1
+ * (bad slot) on failure; rows are then left without effect. */
+int sb_step_prologue(const int32_t* slots, const int32_t* tokens, int B, int32_t* pos,
+                     int32_t* page_table, int max_pages, int32_t* free_stack,
+                     int32_t* free_top, int max_slots, int max_seq, int vocab,
+                     const float* emb, int D, float* x, int ldx, int32_t* row_pos,
+                     int32_t* row_slot, int32_t* status, cudaStream_t st);
+/* Step epilogue: out_tokens[b] = argmax(logits[b]) (first max), pos[slot]++
+ * for every row when *status == 0. */
+int sb_step_epilogue(const float* logits, int ldl, int V, int B, const int32_t* row_slot,
+                     const int32_t* row_pos, int32_t* pos, const int32_t* status,
+                     int32_t* out_tokens, cudaStream_t st);
+
+/* RoPE with host-built tables cos/sin[pos][hd/2] (llama_infer.c:83-85 values)
+ * on q and k in place, then K/V rows appended at row_pos into the paged pool
+ * pool[layer][page][2][nkv][16][hd].  qkv rows: [q(nq*hd) | k | v], stride ld. */
+int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd, const int32_t* row_pos,
+                   const int32_t* row_slot, const int32_t* page_table, int max_pages,
+                   void* pool, int64_t n_pages, int layer, int kv_dtype,
+                   const float* rope_cos, const float* rope_sin, cudaStream_t st);
+
+/* Paged GQA attention (llama_infer.c:97-129): att[b][hq*hd+d] for ctx =
+ * row_pos[b]+1.  Split over context chunks of SB_ATTN_CHUNK tokens into
+ * scratch partials (m, l, o[hd]) of size sb_attention_scratch_floats(), then
+ * combined. */
+#define SB_ATTN_CHUNK 256
+size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int max_seq);
+int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
+                       int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
+                       const int32_t* page_table, int max_pages, const void* pool,
+                       int64_t n_pages, int layer, int kv_dtype, int max_seq, float* scratch,
+                       cudaStream_t st);
+
+/* Fills positions [0, n) of one slot with deterministic pseudo-random K/V
+ * (benchmark stand-in for a prefilled prompt), allocating its pages. */
+int sb_seed_context(int slot, int n, uint64_t seed, int n_layers, int nkv, int hd, int32_t* pos,
+                    int32_t* page_table, int max_pages, int32_t* free_stack, int32_t* free_top,
+                    void* pool, int64_t n_pages, int kv_dtype, int32_t* status,
+                    cudaStream_t st);
+/* Copies the first n K/V rows of one slot into dense f32 [n_layers][n][nkv*hd]. */
+int sb_read_kv(int slot, int n, int n_layers, int nkv, int hd, const int32_t* page_table,
+               int max_pages, const void* pool, int64_t n_pages, int kv_dtype, float* K,
+               float* V, cudaStream_t st);
+/* Returns the slot's pages to the device free list and zeroes its position. */
+int sb_release_slot(int slot, int32_t* pos, int32_t* page_table, int max_pages,
+                    int32_t* free_stack, int32_t* free_top, cudaStream_t st);
+/* free_stack = [0, n_pages), free_top = n_pages. */
+int sb_init_free_list(int32_t* free_stack, int32_t* free_top, int64_t n_pages, cudaStream_t st);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

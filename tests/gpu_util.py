@@ -1,0 +1,93 @@
+"""GPU-test helpers: call the CUDA backend's vtable through its C function
+pointers (the same entry points a reference caller would use)."""
+import ctypes as C
+
+import numpy as np
+
+p, i32, i64, f32, sz = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
+
+SIGS = {
+    "alloc": (p, sz), "release": (None, p), "copy_h2d": (None, p, p, sz),
+    "copy_d2h": (None, p, p, sz), "matvec": (None, p, p, p, i32, i32),
+    "linear_batch": (None, p, p, p, i32, i32, i32), "matvec_q4k": (None, p, p, p, i32, i32),
+    "rmsnorm_row": (None, p, p, p, i32, f32), "silu_mul": (None, p, p, p, i32),
+    "add_inplace": (None, p, p, i32), "embed_lookup": (None, p, p, i32, i32),
+    "attention_step": (None, p, p, p, p, p, i32, i32), "sync": (None,),
+}
+EXT = {
+    "matmul_q4k_batch": (i32, p, p, p, i32, i32, i32),
+    "matmul_f32_batch": (i32, p, p, p, i32, i32, i32),
+    "rmsnorm_rows": (i32, p, p, p, i32, i32, f32),
+    "argmax_rows": (i32, p, p, i32, i32),
+    "rope_kv_append_paged": (i32, p, p, p, p, p, p, i32, p, i64, i32, i32, i32, i32, i32, i32, p, p),
+    "attention_paged_gqa": (i32, p, p, p, p, p, i32, p, i64, i32, i32, i32, i32, i32, i32),
+}
+
+
+class Backend:
+    def __init__(self, sb, device=0):
+        ptr = sb.F["slate_backend_cuda_create"](device)
+        if not ptr:
+            raise RuntimeError(sb.last_error())
+        self.sb = sb
+        s = ptr.contents
+        self.name = s.base.name.decode()
+        self.fn = {}
+        for n, sig in SIGS.items():
+            self.fn[n] = C.CFUNCTYPE(*sig)(getattr(s.base, n))
+        for n, sig in EXT.items():
+            self.fn[n] = C.CFUNCTYPE(*sig)(getattr(s, n))
+        self.live = []
+
+    def __getattr__(self, n):
+        return self.fn[n]
+
+    def dev(self, a):
+        a = np.ascontiguousarray(a)
+        d = self.fn["alloc"](max(a.nbytes, 4))
+        assert d
+        if a.nbytes:
+            self.fn["copy_h2d"](d, a.ctypes.data, a.nbytes)
+        self.live.append(d)
+        return d
+
+    def empty(self, nbytes):
+        d = self.fn["alloc"](max(nbytes, 4))
+        assert d
+        self.live.append(d)
+        return d
+
+    def host(self, d, shape, dtype=np.float32):
+        out = np.zeros(shape, dtype)
+        self.fn["sync"]()
+        self.fn["copy_d2h"](out.ctypes.data, d, out.nbytes)
+        return out
+
+    def free_all(self):
+        for d in self.live:
+            self.fn["release"](d)
+        self.live = []
+
+
+def rope_tables(max_seq, hd, theta):
+    """cos/sin[pos][hd/2] with the reference's f32 expressions (llama_infer.c:83-85)."""
+    half = hd // 2
+    i = np.arange(half, dtype=np.float32)
+    inv = np.power(np.float32(theta), np.float32(-2.0) * i / np.float32(hd)).astype(np.float32)
+    ang = (np.arange(max_seq, dtype=np.float32)[:, None] * inv[None, :]).astype(np.float32)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def scale_err(got, want):
+    """max |got - want| relative to the reference's largest magnitude."""
+    return float(np.max(np.abs(np.asarray(got, np.float64) - want)) / max(np.abs(want).max(), 1e-30))
+
+
+def greedy_agrees(engine_id, ref_logits, tol_abs):
+    """Exact match, or a near-tie: the reference's top-2 gap is below tol_abs and
+    the engine picked one of the tied candidates."""
+    top = int(np.argmax(ref_logits))
+    if engine_id == top:
+        return True, False
+    gap = ref_logits[top] - ref_logits[engine_id]
+    return bool(gap <= tol_abs), True

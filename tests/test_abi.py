@@ -1,0 +1,101 @@
+"""The C-ABI library loads without a GPU and exports every function declared in
+include/slate_cuda.h; the vtable prefix keeps the reference's layout
+(include/slate/backend.h:41-99).  No device calls are made here."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "slate_cuda.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = re.sub(r"typedef struct \w+ \{.*?\} \w+;", "", src, flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w \*]*?\b(slate_\w+)\s*\(", src, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    for must in ("slate_backend_cuda", "slate_backend_cuda_create", "slate_llama_batch_step",
+                 "slate_llama_batch_step_device", "slate_llama_scheduler_decode",
+                 "slate_synth_llama_gguf"):
+        assert must in names
+    assert len(names) >= 30
+
+
+def test_library_exports_every_declared_symbol(sb):
+    lib = C.CDLL(sb.LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    # and the Python mirror binds exactly the declared set
+    assert set(sb.EXPORTS) == set(declared_functions())
+
+
+def test_dynamic_symbols_are_c_abi(sb):
+    out = subprocess.run(["nm", "-D", "--defined-only", sb.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    for n in declared_functions():
+        assert n in exported, n           # unmangled, i.e. extern "C"
+
+
+def test_vtable_layout_matches_reference(sb):
+    # 1 name + 13 function pointers, pointer-sized, in the reference's order
+    assert C.sizeof(sb.BackendBase) == 14 * C.sizeof(C.c_void_p)
+    names = [f for f, _ in sb.BackendBase._fields_]
+    assert names == ["name", "alloc", "release", "copy_h2d", "copy_d2h", "matvec",
+                     "linear_batch", "matvec_q4k", "rmsnorm_row", "silu_mul", "add_inplace",
+                     "embed_lookup", "attention_step", "sync"]
+
+
+def test_header_compiles_with_reference_header_first(tmp_path):
+    """A translation unit that includes the reference's backend.h first and
+    then slate_cuda.h sees one struct slate_backend (the reference's)."""
+    ref_inc = "/root/reference/include"
+    if not os.path.isdir(ref_inc):
+        pytest.skip("reference headers unavailable")
+    src = tmp_path / "t.c"
+    src.write_text('#include "slate/backend.h"\n#include "slate_cuda.h"\n'
+                   "_Static_assert(sizeof(slate_backend_t) == 14 * sizeof(void*), \"layout\");\n"
+                   "int main(void) { const slate_backend_t* b = slate_backend_cuda(); return b != 0; }\n")
+    subprocess.run(["gcc", "-std=c11", "-c", str(src), "-I", ref_inc, "-I",
+                    os.path.join(ROOT, "include"), "-o", str(tmp_path / "t.o")], check=True)
+
+
+def test_cuda_backend_is_opt_in(sb):
+    """Without SLATE_CUDA_BACKEND=1 the accessor returns NULL like the stub
+    (backend_cuda_stub.c:33), so slate_backend_default() keeps the CPU."""
+    env = dict(os.environ)
+    env.pop("SLATE_CUDA_BACKEND", None)
+    code = ("import ctypes as C, slate_b200 as s; "
+            "print(bool(s.F['slate_backend_cuda']()))")
+    out = subprocess.run(["python", "-c", code], capture_output=True, text=True, env=env,
+                         cwd=ROOT, check=True).stdout.strip()
+    assert out == "False"
+
+
+def test_gguf_loader_fills_description(sb, oracle):
+    from conftest import golden
+    for name in ("slate_tiny_llama.gguf", "slate_tiny_llama_gqa.gguf", "slate_tiny_llama_q4k.gguf"):
+        d = sb.LlamaDesc()
+        h = sb.F["slate_gguf_model_open"](golden(name).encode(), C.byref(d))
+        assert h
+        m = oracle.open(golden(name))
+        for f in ("n_layers", "d_model", "ffn_hidden", "n_heads", "n_kv_heads", "head_dim",
+                  "max_seq", "vocab", "tied_output"):
+            assert getattr(d, f) == m.cfg[f], (name, f)
+        assert abs(d.theta_base - m.cfg["theta_base"]) == 0
+        # both readers mmap the file separately: compare offsets from token_embd
+        L0 = d.layers[0].contents
+        p, dt = m.tensor("blk.0.attn_q.weight")
+        e, _ = m.tensor("token_embd.weight")
+        assert L0.attn_q - d.token_embd == p - e and L0.attn_q_dtype == dt
+        m.close()
+        sb.F["slate_gguf_model_close"](h)

@@ -1,0 +1,295 @@
+"""Batch-engine parity through the C ABI (slate_llama_batch_*) against the
+oracle's independent per-sequence sessions (src/loader/llama_infer.c
+semantics), on the reference's golden models and on synthetic models.
+
+Tolerances (written here, applied to every logit of every step):
+  * f32 KV cache: max |engine - oracle| <= 1e-4 * max |oracle logits|
+  * f16 KV cache: <= 2e-3 * max |oracle logits|
+Greedy ids must equal the oracle's argmax; the only accepted difference is a
+near-tie, where the oracle's own top-2 gap is within that tolerance -- those
+are counted and reported, and every sequence is teacher-forced with the
+engine's token so a tie never cascades.
+"""
+import os
+import threading
+
+import numpy as np
+import pytest
+
+from conftest import golden
+from gpu_util import greedy_agrees, scale_err
+from test_golden import TINY, read_ref_logits
+
+pytestmark = pytest.mark.gpu
+
+
+def make_engine(sb, path, **kw):
+    return sb.LlamaBatch(path, **kw)
+
+
+@pytest.mark.parametrize("gguf,ref", TINY)
+def test_engine_prefill_matches_reference_fixture(sb, oracle, gguf, ref):
+    """test_llama_infer{,_gqa,_q4k}.c on the GPU engine: Linf < 1e-3 vs numpy."""
+    prompt, want = read_ref_logits(ref)
+    eng = make_engine(sb, golden(gguf), max_batch=4)
+    s = eng.open()
+    rc, lg = eng.prefill(s, prompt)
+    assert rc == 0 and eng.position(s) == len(prompt)
+    assert np.max(np.abs(lg - want)) < 1e-3
+    m = oracle.open(golden(gguf))
+    o, _ = m.decode_many(prompt[None, :])
+    assert scale_err(lg, o[0, -1]) < 1e-4
+    eng.close()
+
+
+def run_continuous(eng, requests, max_batch, rng):
+    """Continuous batching: requests (prompt, n_new) join when a batch row is
+    free and leave when done.  Returns per-request token streams and logits."""
+    waiting = list(range(len(requests)))
+    active = {}                                # req -> dict(slot, fed, stream, logits)
+    done = {}
+    while waiting or active:
+        while waiting and len(active) < max_batch:
+            r = waiting.pop(0)
+            slot = eng.open()
+            assert slot >= 0
+            active[r] = dict(slot=slot, fed=0, stream=[], logits=[])
+        reqs = list(active)
+        rng.shuffle(reqs)                       # row order must not matter
+        slots, toks = [], []
+        for r in reqs:
+            a, (prompt, _) = active[r], requests[r]
+            tok = prompt[a["fed"]] if a["fed"] < len(prompt) else a["stream"][-1]
+            slots.append(a["slot"])
+            toks.append(tok)
+        rc, out, lg = eng.step(slots, toks, want_logits=True)
+        assert rc == 0
+        for i, r in enumerate(reqs):
+            a, (prompt, n_new) = active[r], requests[r]
+            a["fed"] += 1
+            if a["fed"] >= len(prompt):
+                a["stream"].append(int(out[i]))
+                a["logits"].append(lg[i])
+            if len(a["stream"]) >= n_new:
+                assert eng.release(a["slot"]) == 0
+                done[r] = a
+                del active[r]
+    return done
+
+
+def check_against_oracle(oracle, path, requests, done, tol):
+    """Teacher-forced oracle sessions fed prompt + the engine's own tokens."""
+    m = oracle.open(path)
+    n_tie = 0
+    worst = 0.0
+    for r, (prompt, n_new) in enumerate(requests):
+        stream = done[r]["stream"]
+        feed = np.array(list(prompt) + stream[:-1], np.int32)
+        lg, _ = m.decode_many(feed[None, :])
+        ref = lg[0, len(prompt) - 1:]
+        got = np.stack(done[r]["logits"])
+        assert ref.shape == got.shape
+        scale = max(np.abs(ref).max(), 1e-30)
+        err = np.max(np.abs(got - ref)) / scale
+        worst = max(worst, err)
+        assert err <= tol, (r, err)
+        for t, tok in enumerate(stream):
+            ok, tie = greedy_agrees(tok, ref[t], tol * scale)
+            assert ok, (r, t, tok, int(np.argmax(ref[t])))
+            n_tie += tie
+    m.close()
+    return n_tie, worst
+
+
+def test_config1_continuous_batching(sb, oracle, workdir):
+    """tiny all-f32 GQA decoder, 16 requests, prompts
+    U{4..32}, 32 greedy tokens each, joining and leaving a batch of 8."""
+    path = os.path.join(str(workdir), "cfg1.gguf")
+    sb.synth_gguf(path, n_layers=2, d_model=64, ffn_hidden=172, n_heads=4, n_kv_heads=2,
+                  vocab=256, max_seq=128, q4k=False, seed=0)
+    rng = np.random.default_rng(0)
+    reqs = [(rng.integers(0, 256, rng.integers(4, 33)).astype(np.int32), 32) for _ in range(16)]
+    eng = make_engine(sb, path, max_batch=8, max_slots=8)
+    done = run_continuous(eng, reqs, 8, rng)
+    eng.close()
+    n_tie, worst = check_against_oracle(oracle, path, reqs, done, 1e-4)
+    print(f"config1: worst logit err {worst:.2e} of scale, near-ties {n_tie}")
+
+
+@pytest.mark.parametrize("kv_dtype,tol", [(0, 1e-4), (1, 2e-3)])
+@pytest.mark.parametrize("max_batch", [4, 24, 70])
+def test_gqa_q4k_continuous_batching(sb, oracle, workdir, kv_dtype, tol, max_batch):
+    """Q4_K GQA model through GEMV (<=8 rows), BN-64 and BN-128 tiled GEMMs."""
+    path = os.path.join(str(workdir), "gqa_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=2,
+                      vocab=512, max_seq=512, q4k=True, seed=7)
+    rng = np.random.default_rng(max_batch + kv_dtype)
+    n_req = max_batch + 6
+    reqs = [(rng.integers(0, 512, rng.integers(1, 40)).astype(np.int32), int(rng.integers(3, 12)))
+            for _ in range(n_req)]
+    eng = make_engine(sb, path, max_batch=max_batch, kv_dtype=kv_dtype)
+    done = run_continuous(eng, reqs, max_batch, rng)
+    eng.close()
+    check_against_oracle(oracle, path, reqs, done, tol)
+
+
+def test_graphs_and_eager_agree(sb, workdir):
+    path = os.path.join(str(workdir), "gqa_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=2,
+                      vocab=512, max_seq=512, q4k=True, seed=7)
+    outs = []
+    for graphs in (True, False):
+        eng = make_engine(sb, path, max_batch=8, use_graphs=graphs)
+        slots = [eng.open() for _ in range(5)]
+        toks = np.array([1, 2, 3, 4, 5], np.int32)
+        res = []
+        for _ in range(6):
+            rc, out, lg = eng.step(slots, toks, want_logits=True)
+            assert rc == 0
+            res.append(lg)
+            toks = out
+        outs.append(np.stack(res))
+        eng.close()
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_error_codes_leave_state_unchanged(sb, workdir):
+    path = os.path.join(str(workdir), "err.gguf")
+    sb.synth_gguf(path, n_layers=1, d_model=256, ffn_hidden=256, n_heads=4, n_kv_heads=2,
+                  vocab=300, max_seq=20, q4k=True, seed=3)
+    eng = make_engine(sb, path, max_batch=2, max_slots=2)
+    a, b = eng.open(), eng.open()
+    assert eng.open() == -2                                  # no free slot
+    assert eng.step([a], [300])[0] == -3                     # token == vocab
+    assert eng.step([a], [-1])[0] == -3
+    assert eng.step([a, a], [1, 2])[0] == -1                 # same slot twice
+    assert eng.step([5], [1])[0] == -1                       # slot never opened
+    assert eng.position(a) == 0
+    for i in range(20):
+        assert eng.step([a, b], [i, i])[0] == 0
+    assert eng.step([a], [1])[0] == -2                       # cache full (max_seq 20)
+    assert eng.position(a) == 20
+    assert eng.release(b) == 0 and eng.open() == b and eng.position(b) == 0
+    assert eng.step([b], [7])[0] == 0 and eng.position(b) == 1
+    eng.close()
+
+
+def test_page_pool_exhaustion(sb, workdir):
+    path = os.path.join(str(workdir), "err.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=1, d_model=256, ffn_hidden=256, n_heads=4, n_kv_heads=2,
+                      vocab=300, max_seq=20, q4k=True, seed=3)
+    eng = make_engine(sb, path, max_batch=4, max_slots=4, kv_pages=2)
+    a, b, c = eng.open(), eng.open(), eng.open()
+    assert eng.step([a, b], [1, 2])[0] == 0                  # two pages in use
+    assert eng.step([c], [3])[0] == -2                       # third page unavailable
+    assert eng.step([a, b], [4, 5])[0] == 0                  # existing pages keep working
+    assert eng.release(a) == 0
+    assert eng.step([c], [3])[0] == 0                        # page came back
+    eng.close()
+
+
+def test_seeded_context_matches_oracle(sb, oracle, workdir):
+    """Long contexts: seed 40..700-token histories, read them back, seed the
+    oracle sessions with the same K/V, then decode 3 tokens in one batch."""
+    path = os.path.join(str(workdir), "gqa_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=2,
+                      vocab=512, max_seq=512, q4k=True, seed=7)
+    eng = make_engine(sb, path, max_batch=8, max_seq=1024)
+    m = oracle.open(path)
+    ctxs = [40, 255, 256, 257, 511, 700]
+    slots = [eng.open() for _ in ctxs]
+    sess = []
+    for s, c in zip(slots, ctxs):
+        assert eng.seed_context(s, c, seed=1000 + c) == 0 and eng.position(s) == c
+        rc, K, V = eng.read_kv(s, c, 2, 128)
+        assert rc == 0 and np.abs(K).max() < 1 and np.abs(K).max() > 0.5
+        o = m.session(max_seq=1024)
+        assert o.seed_kv(K, V) == 0
+        sess.append(o)
+    toks = np.array([3, 1, 4, 1, 5, 9], np.int32)
+    for _ in range(3):
+        rc, out, lg = eng.step(slots, toks, want_logits=True)
+        assert rc == 0
+        for i, o in enumerate(sess):
+            rc, ref = o.decode(int(toks[i]))
+            assert rc == 0
+            assert scale_err(lg[i], ref) < 1e-4
+            assert greedy_agrees(int(out[i]), ref, 1e-4 * np.abs(ref).max())[0]
+        toks = out
+    m.close()
+    eng.close()
+
+
+def test_device_step_matches_host_step(sb, workdir):
+    import torch
+    path = os.path.join(str(workdir), "gqa_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=2,
+                      vocab=512, max_seq=512, q4k=True, seed=7)
+    res = []
+    for dev_api in (False, True):
+        eng = make_engine(sb, path, max_batch=16)
+        slots = np.array([eng.open() for _ in range(12)], np.int32)
+        toks = np.arange(12, dtype=np.int32) * 7
+        seq = []
+        if dev_api:
+            d_s = torch.tensor(slots, device="cuda")
+            d_t = torch.tensor(toks, device="cuda")
+            d_o = torch.zeros(12, dtype=torch.int32, device="cuda")
+            for _ in range(5):
+                assert eng.step_device(d_s.data_ptr(), 12, d_t.data_ptr(), d_o.data_ptr()) == 0
+                assert eng.sync() == 0
+                seq.append(d_o.cpu().numpy().copy())
+                d_t.copy_(d_o)
+            assert eng.position(int(slots[0])) == 5
+        else:
+            for _ in range(5):
+                rc, out, _ = eng.step(slots, toks)
+                assert rc == 0
+                seq.append(out.copy())
+                toks = out
+        res.append(np.stack(seq))
+        eng.close()
+    assert np.array_equal(res[0], res[1])
+
+
+def test_scheduler_batches_concurrent_callers(sb, oracle, workdir):
+    path = os.path.join(str(workdir), "gqa_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=2,
+                      vocab=512, max_seq=512, q4k=True, seed=7)
+    eng = make_engine(sb, path, max_batch=8)
+    sched = sb.Scheduler(eng, 8)
+    n_workers, n_tok = 6, 10
+    streams = {}
+
+    def worker(w):
+        slot = eng.open()
+        tok, out = 11 * w + 1, []
+        for _ in range(n_tok):
+            rc, nxt, _ = sched.decode(slot, tok)
+            assert rc == 0
+            out.append(nxt)
+            tok = nxt
+        streams[w] = out
+
+    th = [threading.Thread(target=worker, args=(w,)) for w in range(n_workers)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    _, batches, avg = sched.stats()
+    sched.close()
+    eng.close()
+    assert batches >= n_tok and avg >= 1.0
+    m = oracle.open(path)
+    for w, out in streams.items():
+        feed = np.array([11 * w + 1] + out[:-1], np.int32)
+        lg, ids = m.decode_many(feed[None, :])
+        for t in range(n_tok):
+            assert greedy_agrees(out[t], lg[0, t], 1e-4 * np.abs(lg[0, t]).max())[0]
+    m.close()
