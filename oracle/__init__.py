@@ -63,6 +63,7 @@ class Oracle:
             ("orc_rmsnorm_row", None, [Pf, Pf, Pf, C.c_int, C.c_float]),
             ("orc_silu_mul", None, [Pf, Pf, Pf, C.c_int]),
             ("orc_rope_row", None, [Pf, C.c_int, C.c_int, C.c_int, C.c_float]),
+            ("orc_rope_tables", None, [Pf, Pf, C.c_int, C.c_int, C.c_float]),
             ("orc_attention_gqa", None, [Pf, Pf, Pf, Pf, Pf, C.c_int, C.c_int, C.c_int, C.c_int]),
             ("orc_attention_step", None, [Pf, Pf, Pf, Pf, Pf, C.c_int, C.c_int]),
             ("orc_argmax", C.c_int, [Pf, C.c_int]),
@@ -121,6 +122,12 @@ class Oracle:
         r = _f(row).copy()
         self.lib.orc_rope_row(r.ctypes.data_as(Pf), n_heads, hd, pos, theta)
         return r
+
+    def rope_tables(self, max_seq, hd, theta):
+        c = np.zeros((max_seq, hd // 2), np.float32)
+        s = np.zeros_like(c)
+        self.lib.orc_rope_tables(c.ctypes.data_as(Pf), s.ctypes.data_as(Pf), max_seq, hd, theta)
+        return c, s
 
     def attention_gqa(self, q, K, V, nq, nkv, hd):
         q, K, V = _f(q), _f(K), _f(V)

@@ -171,6 +171,17 @@ void orc_rope_row(float* row, int n_heads, int hd, int pos, float theta) {
     }
 }
 
+void orc_rope_tables(float* cos_t, float* sin_t, int max_seq, int hd, float theta) {
+    int half = hd / 2;
+    for (int p = 0; p < max_seq; ++p)
+        for (int i = 0; i < half; ++i) {
+            float inv_freq = powf(theta, -2.0f * (float)i / (float)hd);
+            float ang = (float)p * inv_freq;
+            cos_t[(size_t)p * half + i] = cosf(ang);
+            sin_t[(size_t)p * half + i] = sinf(ang);
+        }
+}
+
 /* loader/llama_infer.c:97-129 -- per q-head softmax(q·Kᵀ/√hd)·V over L rows;
  * q-head hq reads kv-head hq / (nq/nkv).  Max-subtracted expf, Σ in double. */
 void orc_attention_gqa(float* out, const float* q, const float* K, const float* V,

@@ -6,7 +6,7 @@
  *
  * Every function names the reference file:line whose behaviour it restates.
  * Parity pin: the golden fixtures under tests/golden/ (produced by the
- * reference's own tools/*.py) and, where the reference builds here, the
+ * reference's own tools/make_*.py scripts) and, where the reference builds here, the
  * reference library compiled by oracle/Makefile into oracle/_ref/.
  */
 #ifndef SLATE_ORACLE_H
@@ -29,6 +29,8 @@ void  orc_linear_batch(float* C, const float* X, const float* W, int B, int K, i
 void  orc_rmsnorm_row(float* y, const float* x, const float* w, int D, float eps); /* backend_cpu.c:48-76 */
 void  orc_silu_mul(float* y, const float* g, const float* u, int H); /* backend_cpu.c:78-97 */
 void  orc_rope_row(float* row, int n_heads, int head_dim, int pos, float theta); /* llama_infer.c:77-92 */
+/* cos/sin[pos][hd/2] of the angles orc_rope_row uses (llama_infer.c:83-85). */
+void  orc_rope_tables(float* cos_t, float* sin_t, int max_seq, int head_dim, float theta);
 void  orc_attention_gqa(float* out, const float* q, const float* K, const float* V,
                         float* scores, int L, int nq, int nkv, int hd);   /* llama_infer.c:97-129 */
 void  orc_attention_step(float* out, const float* q, const float* K, const float* V,

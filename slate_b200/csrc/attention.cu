@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(128) attn_partial(
     const int32_t* __restrict__ page_table, int max_pages, const KT* __restrict__ pool,
     int64_t n_pages, int layer, int nchunk_max, float* __restrict__ part) {
     constexpr int DPL = HD >= 32 ? HD / 32 : 1;
-    constexpr int ACTIVE = HD / DPL;  // lanes holding dims (32, or 16 for hd 16)
+    constexpr int ACTIVE = HD / DPL;  // lanes holding dims (32; 16 or 8 for hd 16 / 8)
     const int lane = threadIdx.x & 31;
     const long w = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
     const int chunk = (int)(w % nchunk_max);
@@ -616,6 +616,7 @@ extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int 
     const int G = nq / nkv;
     const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
     switch (hd) {
+        case 8: return launch_attn_hd<8>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, pool, n_pages, layer, kv_dtype, nchunk, scratch, st);
         case 16: return launch_attn_hd<16>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, pool, n_pages, layer, kv_dtype, nchunk, scratch, st);
         case 32: return launch_attn_hd<32>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, pool, n_pages, layer, kv_dtype, nchunk, scratch, st);
         case 64: return launch_attn_hd<64>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, pool, n_pages, layer, kv_dtype, nchunk, scratch, st);

@@ -274,8 +274,8 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         sb_set_error("inconsistent model description");
         return NULL;
     }
-    if (hd != 16 && hd != 32 && hd != 64 && hd != 128) {
-        sb_set_error("head_dim %d unsupported (16, 32, 64, 128)", hd);
+    if (hd != 8 && hd != 16 && hd != 32 && hd != 64 && hd != 128) {
+        sb_set_error("head_dim %d unsupported (8, 16, 32, 64, 128)", hd);
         return NULL;
     }
     const int G = nq / nkv;

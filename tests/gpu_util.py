@@ -69,15 +69,6 @@ class Backend:
         self.live = []
 
 
-def rope_tables(max_seq, hd, theta):
-    """cos/sin[pos][hd/2] with the reference's f32 expressions (llama_infer.c:83-85)."""
-    half = hd // 2
-    i = np.arange(half, dtype=np.float32)
-    inv = np.power(np.float32(theta), np.float32(-2.0) * i / np.float32(hd)).astype(np.float32)
-    ang = (np.arange(max_seq, dtype=np.float32)[:, None] * inv[None, :]).astype(np.float32)
-    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
-
-
 def scale_err(got, want):
     """max |got - want| relative to the reference's largest magnitude."""
     return float(np.max(np.abs(np.asarray(got, np.float64) - want)) / max(np.abs(want).max(), 1e-30))

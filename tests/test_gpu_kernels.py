@@ -7,7 +7,7 @@ import pytest
 
 from conftest import golden
 from gguf_util import read_gguf
-from gpu_util import Backend, rope_tables, scale_err
+from gpu_util import Backend, scale_err
 
 pytestmark = pytest.mark.gpu
 
@@ -160,7 +160,7 @@ def build_paged(rng, ctxs, L_layers, nkv, hd, n_pages, kv_dtype, layer):
     return pool, table, dense, max_pages
 
 
-@pytest.mark.parametrize("nq,nkv,hd", [(8, 2, 64), (32, 8, 128), (4, 2, 16), (8, 8, 32), (64, 8, 128)])
+@pytest.mark.parametrize("nq,nkv,hd", [(8, 2, 64), (32, 8, 128), (4, 2, 16), (8, 8, 32), (64, 8, 128), (8, 2, 8)])
 @pytest.mark.parametrize("kv_dtype", [0, 1])
 def test_rope_append_and_paged_attention(be, oracle, nq, nkv, hd, kv_dtype):
     rng = np.random.default_rng(nq * 7 + hd + kv_dtype)
@@ -172,7 +172,7 @@ def test_rope_append_and_paged_attention(be, oracle, nq, nkv, hd, kv_dtype):
     q = rng.normal(0, 1, (B, nq * hd)).astype(np.float32)
     kk = rng.normal(0, 1, (B, nkv * hd)).astype(np.float32)
     vv = rng.normal(0, 1, (B, nkv * hd)).astype(np.float32)
-    cs, sn = rope_tables(1024, hd, theta)
+    cs, sn = oracle.rope_tables(1024, hd, theta)      # the engine builds the same tables
     d_pool, d_table = be.dev(pool), be.dev(table)
     d_q, d_k = be.dev(q), be.dev(kk)
     d_pos, d_slots = be.dev(pos), be.dev(slots)
@@ -194,7 +194,8 @@ def test_rope_append_and_paged_attention(be, oracle, nq, nkv, hd, kv_dtype):
         app_k = pool_after[layer, pg, 0, :, o, :].astype(np.float32).reshape(-1)
         app_v = pool_after[layer, pg, 1, :, o, :].astype(np.float32).reshape(-1)
         et = np.float16 if kv_dtype else np.float32
-        assert scale_err(app_k, want_k.astype(et).astype(np.float32)) < 1e-5
+        # f16 cache: one rounding of the rotated value (<= 2^-11 relative)
+        assert scale_err(app_k, want_k) < (6e-4 if kv_dtype else 1e-5)
         assert np.array_equal(app_v, vv[r].astype(et).astype(np.float32))
         Kd, Vd = dense[r]
         Kd[c - 1], Vd[c - 1] = app_k, app_v

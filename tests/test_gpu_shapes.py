@@ -68,7 +68,7 @@ def test_real_shapes(sb, oracle, workdir, name):
     toks = rng.integers(0, mc["vocab"], len(slots)).astype(np.int32)
     n_tie = 0
     pool = ThreadPoolExecutor(max_workers=os.cpu_count() or 8)
-    for rows in (list(range(len(slots))), [0, 3, 5, 7]):
+    for rows in (list(range(len(slots))), list(range(0, len(slots), 2))[:4]):
         rc, out, lg = eng.step([slots[r] for r in rows], toks[rows], want_logits=True)
         assert rc == 0
         refs = list(pool.map(lambda r: sess[r].decode(int(toks[r])), rows))
