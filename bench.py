@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--layers", type=int, default=CFG3["n_layers"],
                     help="reduce only for debugging; the benchmark workload is 32")
+    ap.add_argument("--gemm-path", type=int, default=0,
+                    help="0 auto (tcgen05, 3-pass hi/lo split), 1 CUDA cores, 2 tcgen05 single f16 pass")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     return ap.parse_args()
@@ -245,7 +247,7 @@ def main():
     total_steps = args.warmup + args.steps
     ctx = contexts(args, n, rank, 3 * total_steps + 4)
     eng = sb.LlamaBatch(path, device=local, max_batch=n, max_slots=n, kv_dtype=kv,
-                        max_seq=cfg["max_seq"])
+                        max_seq=cfg["max_seq"], gemm_path=args.gemm_path)
     slots = np.array([eng.open() for _ in range(n)], np.int32)
     assert (slots >= 0).all(), sb.last_error()
     for s, c in zip(slots, ctx):
@@ -353,6 +355,7 @@ def main():
                    "model": "llama3-8b-shape random N(0,0.02) Q4_K", "layers": cfg["n_layers"],
                    "global_batch": n * world, "seqs_per_gpu": n, "kv_dtype": args.kv,
                    "mean_ctx": float(ctx.mean()), "parallelism": f"replicas x{world}",
+                   "gemm_path": {0: "tcgen05 3-pass", 1: "cuda-core f32", 2: "tcgen05 1-pass f16"}[args.gemm_path],
                    "l2": "inputs larger than L2 (KV read per step >> 126 MB)"},
         "roofline": {"bound": "hbm", "kernel": "attn_partial+attn_combine (paged GQA attention)",
                      "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "GB/s",

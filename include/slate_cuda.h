@@ -97,6 +97,12 @@ typedef struct slate_backend_cuda {
                                const int32_t* row_slot, const int32_t* page_table,
                                int max_pages, const void* kv_pool, int64_t n_pages,
                                int layer, int B, int nq, int nkv, int hd, int kv_dtype);
+    /* matmul_q4k_batch on the tensor cores (tcgen05, f32 accumulate):
+     * passes 1 = f16 x f16 operands, 3 = f16 hi/lo split of both operands
+     * (f32-level products).  Needs M % 128 == 0, K % 256 == 0, 16 <= B.
+     * Synchronous: returns -5 if the device reported a pipeline timeout. */
+    int (*matmul_q4k_batch_tc)(float* Y, const void* A_q4k, const float* X, int B, int M, int K,
+                               int passes);
 } slate_backend_cuda_t;
 
 /* Reference-compatible accessor.  Returns NULL (exactly like the stub at

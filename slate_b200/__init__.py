@@ -71,7 +71,7 @@ class BackendBase(C.Structure):
 class BackendCuda(C.Structure):
     _fields_ = [("base", BackendBase), ("abi_version", c_int), ("device", c_int)] + [
         (n, P) for n in ("matmul_q4k_batch", "matmul_f32_batch", "rmsnorm_rows", "argmax_rows",
-                         "rope_kv_append_paged", "attention_paged_gqa")]
+                         "rope_kv_append_paged", "attention_paged_gqa", "matmul_q4k_batch_tc")]
 
 
 def _proto(name, res, *args):

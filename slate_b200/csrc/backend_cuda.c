@@ -12,6 +12,7 @@
 #define _GNU_SOURCE
 #include "sb_internal.h"
 #include "sb_kernels.h"
+#include "sb_tc.h"
 
 #include <pthread.h>
 #include <stdlib.h>
@@ -157,6 +158,40 @@ static int be_attention_paged(float* out, const float* q, const int32_t* pos,
     return rc;
 }
 
+static int be_matmul_q4k_tc(float* Y, const void* A, const float* X, int B, int M, int K,
+                            int passes) {
+    if (M % 128 || K % 256 || B < 16 || (passes != 1 && passes != 3)) {
+        sb_set_error("matmul_q4k_batch_tc: unsupported shape or passes");
+        return -1;
+    }
+    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0};
+    const int splits = sb_tc_splits_for(M, K);
+    void *hi = NULL, *lo = NULL, *ws = NULL, *err = NULL;
+    int rc = sb_cuda_check(cudaMallocAsync(&hi, (size_t)B * K * 2, g_stream), "alloc");
+    if (!rc && passes == 3) rc = sb_cuda_check(cudaMallocAsync(&lo, (size_t)B * K * 2, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&ws, (size_t)splits * B * M * 4, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&err, 16, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(err, 0, 16, g_stream), "memset");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "alloc sync");
+    sb_tc_operand op;
+    if (!rc && sb_tc_make_operand(&op, hi, lo, B, K, K)) rc = -1;
+    if (!rc) rc = fin(sb_tc_split(X, K, B, &op, g_stream), "tc split");
+    if (!rc) rc = fin(sb_tc_gemm(&W, &op, B, passes, splits, (float*)ws, Y, M, SB_EPI_STORE,
+                                 (int*)err, g_stream), "matmul_q4k_batch_tc");
+    int e = 0;
+    if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, g_stream), "err");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "matmul_q4k_batch_tc");
+    if (!rc && e) {
+        sb_set_error("tensor-core pipeline wait timed out (stage %d)", e);
+        rc = -5;
+    }
+    if (hi) cudaFreeAsync(hi, g_stream);
+    if (lo) cudaFreeAsync(lo, g_stream);
+    if (ws) cudaFreeAsync(ws, g_stream);
+    if (err) cudaFreeAsync(err, g_stream);
+    return rc;
+}
+
 const slate_backend_cuda_t* slate_backend_cuda_create(int device) {
     pthread_mutex_lock(&g_init);
     const slate_backend_cuda_t* r = NULL;
@@ -192,6 +227,8 @@ const slate_backend_cuda_t* slate_backend_cuda_create(int device) {
             g_be.argmax_rows = be_argmax_rows;
             g_be.rope_kv_append_paged = be_rope_kv;
             g_be.attention_paged_gqa = be_attention_paged;
+            g_be.matmul_q4k_batch_tc = be_matmul_q4k_tc;
+            sb_tc_prepare();
             g_device = device;
             r = &g_be;
         } else if (device < 0 || device >= n) {

@@ -22,6 +22,7 @@
 #define _GNU_SOURCE
 #include "sb_internal.h"
 #include "sb_kernels.h"
+#include "sb_tc.h"
 
 #include <math.h>
 #include <pthread.h>
@@ -67,7 +68,29 @@ struct slate_llama_batch {
     int64_t pages_used;
     /* graphs, one per batch size */
     cudaGraphExec_t* graphs;
+    /* tensor-core GEMM path: f16 operands (hi/lo) with TMA maps, K-split
+     * partials, device error word, split counts per weight */
+    int tc_passes;                 /* 0 = off, 1 or 3 */
+    sb_tc_operand op_d, op_f;      /* activations with K = d_model / ffn */
+    float* tc_ws;
+    int* tc_err;
+    int sp_qkv, sp_wo, sp_gu, sp_dn;
 };
+
+/* Rows from which a Q4_K GEMM runs on the tensor cores (below: CUDA cores). */
+#define SB_TC_MIN_ROWS 16
+
+/* One weight GEMM of the step on the path chosen for (weight, rows). */
+static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X, int ldx, int n,
+                     float* Y, int ldy, int epi, int splits, cudaStream_t s) {
+    if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
+        const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d : &b->op_f;
+        int rc = sb_tc_split(X, ldx, n, op, s);
+        return rc ? rc : sb_tc_gemm(W, op, n, b->tc_passes, splits, b->tc_ws, Y, ldy, epi,
+                                    b->tc_err, s);
+    }
+    return sb_gemm(W, X, ldx, n, Y, ldy, epi, b->gemm_path == 1 ? 1 : 0, s);
+}
 
 static int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
@@ -192,21 +215,20 @@ static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
     for (int l = 0; l < b->L && !rc; ++l) {
         const sb_layer* ly = &b->layers[l];
         rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, ly->attn_norm, n, b->D, b->eps, s);
-        rc |= sb_gemm(&ly->wqkv, b->xn, b->ld_x, n, b->qkv, b->ld_qkv, SB_EPI_STORE, b->gemm_path, s);
+        rc |= step_gemm(b, &ly->wqkv, b->xn, b->ld_x, n, b->qkv, b->ld_qkv, SB_EPI_STORE, b->sp_qkv, s);
         rc |= sb_rope_append(b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, b->row_pos, b->row_slot,
                              b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
                              b->rope_cos, b->rope_sin, s);
         rc |= sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
                                  b->row_pos, b->row_slot, b->page_table, b->max_pages, b->pool,
                                  b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch, s);
-        rc |= sb_gemm(&ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, SB_EPI_ADD, b->gemm_path, s);
+        rc |= step_gemm(b, &ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, SB_EPI_ADD, b->sp_wo, s);
         rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, ly->ffn_norm, n, b->D, b->eps, s);
-        rc |= sb_gemm(&ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->gemm_path, s);
-        rc |= sb_gemm(&ly->wdown, b->h, b->ld_h, n, b->x, b->ld_x, SB_EPI_ADD, b->gemm_path, s);
+        rc |= step_gemm(b, &ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
+        rc |= step_gemm(b, &ly->wdown, b->h, b->ld_h, n, b->x, b->ld_x, SB_EPI_ADD, b->sp_dn, s);
     }
     rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, b->out_norm, n, b->D, b->eps, s);
-    rc |= sb_gemm(&b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE,
-                  b->gemm_path, s);
+    rc |= step_gemm(b, &b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE, 1, s);
     rc |= sb_step_epilogue(b->logits, b->ld_logits, b->V, n, b->row_slot, b->row_pos, b->pos,
                            b->status, out, s);
     if (rc) {
@@ -312,6 +334,7 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         sb_cuda_check(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking), "stream"))
         goto fail;
     sb_gemm_prepare();
+    sb_tc_prepare();
 
     /* weights */
     if (upload_f32(b, &b->emb, m->token_embd, (size_t)V * D)) goto fail;
@@ -400,6 +423,42 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         if (sb_cuda_check(cudaHostAlloc((void**)&b->h_io, (size_t)(3 * B + 4) * 4,
                                         cudaHostAllocDefault), "cudaHostAlloc"))
             goto fail;
+    }
+
+    /* tensor-core path: gemm_path 0 (auto) and 3 use the 3-pass split, 2 the
+     * single f16 pass, 1 keeps every GEMM on the CUDA cores */
+    b->tc_passes = o->gemm_path == 1 ? 0 : o->gemm_path == 2 ? 1 : 3;
+    if (b->layers[0].wqkv.wtype != SB_WT_Q4K || D % 256 || F % 256) b->tc_passes = 0;
+    if (b->tc_passes) {
+        const int B = b->max_batch, lo = b->tc_passes == 3;
+        void* dh = dalloc(b, (size_t)B * D * 2);
+        void* dl = lo ? dalloc(b, (size_t)B * D * 2) : NULL;
+        void* fh = dalloc(b, (size_t)B * F * 2);
+        void* fl = lo ? dalloc(b, (size_t)B * F * 2) : NULL;
+        b->tc_err = (int*)dalloc(b, 16);
+        if (!dh || !fh || (lo && (!dl || !fl)) || !b->tc_err ||
+            sb_cuda_check(cudaMemset(dh, 0, (size_t)B * D * 2), "memset") ||
+            sb_cuda_check(cudaMemset(fh, 0, (size_t)B * F * 2), "memset") ||
+            (lo && (sb_cuda_check(cudaMemset(dl, 0, (size_t)B * D * 2), "memset") ||
+                    sb_cuda_check(cudaMemset(fl, 0, (size_t)B * F * 2), "memset"))) ||
+            sb_cuda_check(cudaMemset(b->tc_err, 0, 16), "memset"))
+            goto fail;
+        if (sb_tc_make_operand(&b->op_d, dh, dl, B, D, D) ||
+            sb_tc_make_operand(&b->op_f, fh, fl, B, F, F))
+            goto fail;
+        const sb_layer* l0 = &b->layers[0];
+        b->sp_qkv = sb_tc_splits_for(l0->wqkv.M_pad, D);
+        b->sp_wo = sb_tc_splits_for(l0->wo.M_pad, D);
+        b->sp_gu = sb_tc_splits_for(l0->wgu.M_pad, D);
+        b->sp_dn = sb_tc_splits_for(l0->wdown.M_pad, F);
+        size_t ws = 0, t;
+        if ((t = (size_t)b->sp_qkv * l0->wqkv.M_pad) > ws) ws = t;
+        if ((t = (size_t)b->sp_wo * l0->wo.M_pad) > ws) ws = t;
+        if ((t = (size_t)b->sp_gu * l0->wgu.M_pad) > ws) ws = t;
+        if ((t = (size_t)b->sp_dn * l0->wdown.M_pad) > ws) ws = t;
+        if (b->lm_head.wtype == SB_WT_Q4K && (t = (size_t)b->lm_head.M_pad) > ws) ws = t;
+        b->tc_ws = (float*)dalloc(b, ws * (size_t)B * 4);
+        if (!b->tc_ws) goto fail;
     }
 
     /* KV pool, page tables, free list */
@@ -523,6 +582,31 @@ int slate_llama_batch_position(const slate_llama_batch_t* cb, int slot) {
 
 /* ---- steps --------------------------------------------------------------- */
 
+/* Enqueues the copy of the device status words (step status, tensor-core
+ * wait status) into h_io[3B], h_io[3B+1] and their reset. */
+static int status_readback(slate_llama_batch_t* b) {
+    int32_t* h = b->h_io + 3 * b->max_batch;
+    h[1] = 0;
+    SB_CU(cudaMemcpyAsync(h, b->status, 4, cudaMemcpyDeviceToHost, b->stream));
+    SB_CU(cudaMemsetAsync(b->status, 0, 4, b->stream));
+    if (b->tc_err) {
+        SB_CU(cudaMemcpyAsync(h + 1, b->tc_err, 4, cudaMemcpyDeviceToHost, b->stream));
+        SB_CU(cudaMemsetAsync(b->tc_err, 0, 4, b->stream));
+    }
+    return 0;
+}
+/* After a synchronize: 0, the step's -1/-2/-3, or -5 when a tensor-core
+ * kernel gave up waiting (which makes that step's results invalid). */
+static int status_code(slate_llama_batch_t* b) {
+    const int32_t* h = b->h_io + 3 * b->max_batch;
+    if (h[1]) {
+        sb_set_error("tensor-core GEMM pipeline wait timed out (stage %d)", h[1]);
+        return -5;
+    }
+    if (h[0]) sb_set_error("device rejected the step (%d)", h[0]);
+    return h[0];
+}
+
 int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
                            const int32_t* tokens, int32_t* out_tokens, float* out_logits) {
     if (!b || !slots || !tokens || n < 1 || n > b->max_batch) return -1;
@@ -556,20 +640,16 @@ int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
         rc = sb_cuda_check(cudaMemcpyAsync(h + 2 * b->max_batch, b->d_io + 2 * b->max_batch,
                                            (size_t)n * 4, cudaMemcpyDeviceToHost, b->stream),
                            "D2H tokens");
-    if (!rc)
-        rc = sb_cuda_check(cudaMemcpyAsync(h + 3 * b->max_batch, b->status, 4,
-                                           cudaMemcpyDeviceToHost, b->stream), "D2H status");
+    if (!rc) rc = status_readback(b);
     if (!rc && out_logits)
         rc = sb_cuda_check(cudaMemcpy2DAsync(out_logits, (size_t)b->V * 4, b->logits,
                                              (size_t)b->ld_logits * 4, (size_t)b->V * 4, (size_t)n,
                                              cudaMemcpyDeviceToHost, b->stream), "D2H logits");
-    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(b->status, 0, 4, b->stream), "status reset");
     if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(b->stream), "step");
     if (!rc) {
-        const int st = h[3 * b->max_batch];
+        const int st = status_code(b);
         if (st) {
             rc = st;
-            sb_set_error("device rejected the step (%d)", st);
         } else {
             for (int r = 0; r < n; ++r) {
                 if (b->h_pos[slots[r]] % SB_PAGE_TOKENS == 0) ++b->pages_used;
@@ -623,11 +703,9 @@ int slate_llama_batch_sync(slate_llama_batch_t* b) {
     if (!b) return -1;
     pthread_mutex_lock(&b->lock);
     cudaSetDevice(b->device);
-    int rc = sb_cuda_check(cudaMemcpyAsync(b->h_io + 3 * b->max_batch, b->status, 4,
-                                           cudaMemcpyDeviceToHost, b->stream), "D2H status");
-    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(b->status, 0, 4, b->stream), "status reset");
+    int rc = status_readback(b);
     if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(b->stream), "sync");
-    if (!rc) rc = b->h_io[3 * b->max_batch];
+    if (!rc) rc = status_code(b);
     pthread_mutex_unlock(&b->lock);
     return rc;
 }
@@ -705,19 +783,19 @@ static int enqueue_kernel(slate_llama_batch_t* b, int kernel, int n, int layer, 
                                       b->pool, b->n_pages, layer, b->kv_dtype, b->max_seq,
                                       b->scratch, s);
         case SLATE_PROF_QKV:
-            return sb_gemm(&ly->wqkv, b->xn, b->ld_x, n, scratch_y, b->ld_logits, SB_EPI_STORE,
-                           b->gemm_path, s);
+            return step_gemm(b, &ly->wqkv, b->xn, b->ld_x, n, scratch_y, b->ld_logits, SB_EPI_STORE,
+                             b->sp_qkv, s);
         case SLATE_PROF_WO:
-            return sb_gemm(&ly->wo, b->att, b->ld_att, n, scratch_y, b->ld_logits, SB_EPI_STORE,
-                           b->gemm_path, s);
+            return step_gemm(b, &ly->wo, b->att, b->ld_att, n, scratch_y, b->ld_logits, SB_EPI_STORE,
+                             b->sp_wo, s);
         case SLATE_PROF_GATE_UP:
-            return sb_gemm(&ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->gemm_path, s);
+            return step_gemm(b, &ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
         case SLATE_PROF_DOWN:
-            return sb_gemm(&ly->wdown, b->h, b->ld_h, n, scratch_y, b->ld_logits, SB_EPI_STORE,
-                           b->gemm_path, s);
+            return step_gemm(b, &ly->wdown, b->h, b->ld_h, n, scratch_y, b->ld_logits, SB_EPI_STORE,
+                             b->sp_dn, s);
         case SLATE_PROF_LM_HEAD:
-            return sb_gemm(&b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE,
-                           b->gemm_path, s);
+            return step_gemm(b, &b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE,
+                             1, s);
         case SLATE_PROF_STEP:
             return run_step(b, n);
     }

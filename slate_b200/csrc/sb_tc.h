@@ -1,0 +1,45 @@
+/*
+ * sb_tc.h -- tensor-core (tcgen05) Q4_K GEMM launchers (internal).
+ */
+#ifndef SB_TC_H
+#define SB_TC_H
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+#include "sb_kernels.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* An f16 activation operand [rows][K] (row stride ld16 elements) with its
+ * TMA tensor maps (SWIZZLE_128B boxes of 64 x n_box).  `lo` (nullable) holds
+ * f16(x - hi) for the 3-pass split. */
+#ifdef __cplusplus
+#define SB_ALIGN64 alignas(64)
+#else
+#define SB_ALIGN64 _Alignas(64)
+#endif
+typedef struct sb_tc_operand {
+    SB_ALIGN64 unsigned char map_hi[128];   /* CUtensorMap */
+    SB_ALIGN64 unsigned char map_lo[128];
+    void* hi;
+    void* lo;
+    int rows, K, ld16, n_box;
+} sb_tc_operand;
+
+int sb_tc_make_operand(sb_tc_operand* op, void* hi, void* lo, int rows, int K, int ld16);
+/* X (f32, stride ldx) -> op->hi / op->lo for the first n_rows rows. */
+int sb_tc_split(const float* X, int ldx, int n_rows, const sb_tc_operand* op, cudaStream_t st);
+/* K-split count that fills the GPU for a weight of M_pad rows. */
+int sb_tc_splits_for(int M_pad, int K);
+/* ws: splits * n_rows * W->M_pad floats.  passes: 1 (f16 x f16) or 3 (hi/lo). */
+int sb_tc_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows, int passes, int splits,
+               float* ws, float* Y, int ldy, int epi, int* err, cudaStream_t st);
+/* Shared-memory attributes (outside stream capture). */
+void sb_tc_prepare(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -21,6 +21,7 @@ EXT = {
     "argmax_rows": (i32, p, p, i32, i32),
     "rope_kv_append_paged": (i32, p, p, p, p, p, p, i32, p, i64, i32, i32, i32, i32, i32, i32, p, p),
     "attention_paged_gqa": (i32, p, p, p, p, p, i32, p, i64, i32, i32, i32, i32, i32, i32),
+    "matmul_q4k_batch_tc": (i32, p, p, p, i32, i32, i32, i32),
 }
 
 

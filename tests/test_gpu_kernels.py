@@ -204,3 +204,22 @@ def test_rope_append_and_paged_attention(be, oracle, nq, nkv, hd, kv_dtype):
     # other layers untouched
     other = [l for l in range(layers) if l != layer]
     assert np.array_equal(pool_after[other], pool[other])
+
+
+@pytest.mark.parametrize("passes,tol", [(3, 1e-5), (1, 3e-3)])
+@pytest.mark.parametrize("B,M,K", [(16, 128, 256), (40, 384, 1024), (256, 1024, 4096),
+                                   (100, 256, 14336), (300, 256, 512)])
+def test_matmul_q4k_tensor_cores(be, oracle, sb, B, M, K, passes, tol):
+    """tcgen05 path: 3-pass hi/lo split reproduces f32 products; the single
+    f16 pass stays within f16 operand rounding.  Reference = the oracle's exact
+    Q4_K dequantisation, products in float64."""
+    rng = np.random.default_rng(B + M + K + passes)
+    q = sb.quantize_q4k(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    X = rng.normal(0, 1, (B, K)).astype(np.float32)
+    Y = be.empty(B * M * 4)
+    rc = be.matmul_q4k_batch_tc(Y, be.dev(q), be.dev(X), B, M, K, passes)
+    assert rc == 0, be.sb.last_error()
+    got = be.host(Y, (B, M))
+    Wd = oracle.dequant_q4k(q, M * K).reshape(M, K).astype(np.float64)
+    want = X.astype(np.float64) @ Wd.T
+    assert scale_err(got, want) < tol
