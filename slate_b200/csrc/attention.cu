@@ -7,15 +7,7 @@
 // A sequence slot owns pages through page_table[slot][pos / 16]; the same page
 // index serves every layer.  Pages come from a device-side free stack.
 //
-// Attention (src/loader/llama_infer.c:97-129): one warp per
-// (row, kv_head, 256-token chunk) streams the chunk's pages straight from HBM
-// into registers -- lane l holds head_dim/32 consecutive dims of each of the
-// page's 16 K (then V) rows, so one page row is one coalesced 512-byte (f32) or
-// 256-byte (f16) line and every K/V byte is read exactly once per step for all
-// G = n_heads / n_kv_heads query heads of the group.  Scores are reduced with a
-// 16-shuffle transpose-reduction (lanes 2t and 2t+1 end up holding token t),
-// then an online softmax (running max / sum, expf) updates per-head output
-// accumulators.  Chunk partials (m, l, o) are merged by a second kernel.
+// The attention kernels themselves live in attn_paged.cu.
 #include "sb_kernels.h"
 #include <cuda_fp16.h>
 #include <math.h>
@@ -60,186 +52,6 @@ __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 __device__ __forceinline__ void from_f(float& d, float v) { d = v; }
 __device__ __forceinline__ void from_f(__half& d, float v) { d = __float2half_rn(v); }
-
-// Reduce 16 per-lane partial values (one per token of a page) over the warp.
-// Afterwards lanes 2t and 2t+1 hold the full sum for token t.  16 shuffles.
-__device__ __forceinline__ float transpose_reduce16(float (&v)[16], int lane) {
-    float a8[8], a4[4], a2[2];
-    const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        float send = u16 ? v[i] : v[i + 8];
-        float keep = u16 ? v[i + 8] : v[i];
-        a8[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float send = u8 ? a8[i] : a8[i + 4];
-        float keep = u8 ? a8[i + 4] : a8[i];
-        a4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        float send = u4 ? a4[i] : a4[i + 2];
-        float keep = u4 ? a4[i + 2] : a4[i];
-        a2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-    float send = u2 ? a2[0] : a2[1];
-    float keep = u2 ? a2[1] : a2[0];
-    float a1 = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    return a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
-}
-
-template <int HD, int G, typename KT>
-__global__ void __launch_bounds__(128) attn_partial(
-    const float* __restrict__ qkv, int ld_qkv, int B, int nq, int nkv,
-    const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
-    const int32_t* __restrict__ page_table, int max_pages, const KT* __restrict__ pool,
-    int64_t n_pages, int layer, int nchunk_max, float* __restrict__ part) {
-    constexpr int DPL = HD >= 32 ? HD / 32 : 1;
-    constexpr int ACTIVE = HD / DPL;  // lanes holding dims (32; 16 or 8 for hd 16 / 8)
-    const int lane = threadIdx.x & 31;
-    const long w = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
-    const int chunk = (int)(w % nchunk_max);
-    const long rest = w / nchunk_max;
-    const int kvh = (int)(rest % nkv);
-    const int b = (int)(rest / nkv);
-    if (b >= B) return;
-    const int pos = row_pos[b];
-    if (pos < 0) return;
-    const int ctx = pos + 1;
-    const int t0 = chunk * SB_ATTN_CHUNK;
-    if (t0 >= ctx) return;
-    const int t1 = min(ctx, t0 + SB_ATTN_CHUNK);
-    const int slot = row_slot[b];
-    const bool dl = lane < ACTIVE;
-    const int d0 = dl ? lane * DPL : 0;
-
-    float q[G][DPL], o[G][DPL], m[G], l[G];
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-        const float* qp = qkv + (size_t)b * ld_qkv + (size_t)(kvh * G + h) * HD + d0;
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) {
-            q[h][i] = dl ? qp[i] : 0.f;
-            o[h][i] = 0.f;
-        }
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-    }
-    const float scale = 1.0f / sqrtf((float)HD);
-    const size_t head_stride = (size_t)SB_PAGE_TOKENS * HD;
-    const size_t page_stride = (size_t)2 * nkv * head_stride;
-
-    for (int tp = t0; tp < t1; tp += SB_PAGE_TOKENS) {
-        const int page = page_table[(size_t)slot * max_pages + tp / SB_PAGE_TOKENS];
-        if (page < 0 || page >= n_pages) continue;   // never allocated: skip, never fault
-        const KT* kp = pool + ((size_t)layer * n_pages + page) * page_stride +
-                       (size_t)kvh * head_stride + d0;
-        const KT* vp = kp + (size_t)nkv * head_stride;
-        const int nval = min(SB_PAGE_TOKENS, t1 - tp);  // valid tokens in this page
-
-        float kr[16][DPL];
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-            if (dl && t < nval) load_row<DPL>(kp + (size_t)t * HD, kr[t]);
-            else
-#pragma unroll
-                for (int i = 0; i < DPL; ++i) kr[t][i] = 0.f;
-        }
-        float p[G];
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-            float part_s[16];
-#pragma unroll
-            for (int t = 0; t < 16; ++t) {
-                float s = 0.f;
-#pragma unroll
-                for (int i = 0; i < DPL; ++i) s = fmaf(q[h][i], kr[t][i], s);
-                part_s[t] = s;
-            }
-            float s = transpose_reduce16(part_s, lane) * scale;
-            const bool valid = (lane >> 1) < nval;
-            s = valid ? s : -INFINITY;
-            float mx = s;
-#pragma unroll
-            for (int off = 2; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float mnew = fmaxf(m[h], mx);
-            const float pe = valid ? expf(s - mnew) : 0.f;
-            float ps = pe;
-#pragma unroll
-            for (int off = 2; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-            const float corr = expf(m[h] - mnew);
-            l[h] = l[h] * corr + ps;
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) o[h][i] *= corr;
-            m[h] = mnew;
-            p[h] = pe;
-        }
-        float vr[16][DPL];
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-            if (dl && t < nval) load_row<DPL>(vp + (size_t)t * HD, vr[t]);
-            else
-#pragma unroll
-                for (int i = 0; i < DPL; ++i) vr[t][i] = 0.f;
-        }
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-#pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float pt = __shfl_sync(0xffffffffu, p[h], 2 * t);
-#pragma unroll
-                for (int i = 0; i < DPL; ++i) o[h][i] = fmaf(pt, vr[t][i], o[h][i]);
-            }
-        }
-    }
-    // partial record: [m, l, o[HD]] per (b, q-head, chunk)
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-        float* rec = part + (((size_t)b * nq + kvh * G + h) * nchunk_max + chunk) * (HD + 2);
-        if (lane == 0) {
-            rec[0] = m[h];
-            rec[1] = l[h];
-        }
-        if (dl)
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) rec[2 + d0 + i] = o[h][i];
-    }
-}
-
-// Merge chunk partials: out = Σ_c o_c e^{m_c-M} / Σ_c l_c e^{m_c-M}.
-template <int HD>
-__global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ part, int B, int nq,
-                                                    const int32_t* __restrict__ row_pos,
-                                                    int nchunk_max, float* __restrict__ att,
-                                                    int ld_att) {
-    const int lane = threadIdx.x & 31;
-    const long w = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
-    const int hq = (int)(w % nq);
-    const int b = (int)(w / nq);
-    if (b >= B) return;
-    const int pos = row_pos[b];
-    if (pos < 0) return;
-    const int nch = (pos + SB_ATTN_CHUNK) / SB_ATTN_CHUNK;  // ceil((pos+1)/CHUNK)
-    const float* rec0 = part + ((size_t)b * nq + hq) * nchunk_max * (HD + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, rec0[(size_t)c * (HD + 2)]);
-    double L = 0.0;
-    for (int c = 0; c < nch; ++c) {
-        const float* r = rec0 + (size_t)c * (HD + 2);
-        L += (double)r[1] * (double)expf(r[0] - M);
-    }
-    const float invL = (float)(1.0 / L);
-    for (int d = lane; d < HD; d += 32) {
-        float acc = 0.f;
-        for (int c = 0; c < nch; ++c) {
-            const float* r = rec0 + (size_t)c * (HD + 2);
-            acc = fmaf(r[2 + d], expf(r[0] - M), acc);
-        }
-        att[(size_t)b * ld_att + (size_t)hq * HD + d] = acc * invL;
-    }
-}
 
 // ------------------------------------------------------------------------
 // RoPE + paged append.  One CTA per row.
@@ -562,68 +374,7 @@ __global__ void init_free_kernel(int32_t* free_stack, int32_t* free_top, int64_t
     if (blockIdx.x == 0 && threadIdx.x == 0) *free_top = (int32_t)n;
 }
 
-template <int HD, int G>
-int launch_attn_g(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq, int nkv,
-                  const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
-                  int max_pages, const void* pool, int64_t n_pages, int layer, int kv_dtype,
-                  int nchunk, float* scratch, cudaStream_t st) {
-    const long warps = (long)B * nkv * nchunk;
-    const unsigned grid = (unsigned)((warps + 3) / 4);
-    if (kv_dtype == SLATE_KV_F16)
-        attn_partial<HD, G, __half><<<grid, 128, 0, st>>>(qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
-                                                          page_table, max_pages, (const __half*)pool,
-                                                          n_pages, layer, nchunk, scratch);
-    else
-        attn_partial<HD, G, float><<<grid, 128, 0, st>>>(qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
-                                                         page_table, max_pages, (const float*)pool,
-                                                         n_pages, layer, nchunk, scratch);
-    const long cw = (long)B * nq;
-    attn_combine<HD><<<(unsigned)((cw + 3) / 4), 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att,
-                                                                ld_att);
-    return 0;
-}
-
-template <int HD>
-int launch_attn_hd(int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
-                   int nkv, const int32_t* row_pos, const int32_t* row_slot,
-                   const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
-                   int layer, int kv_dtype, int nchunk, float* scratch, cudaStream_t st) {
-    switch (G) {
-#define CASE(g)                                                                                  \
-    case g:                                                                                      \
-        return launch_attn_g<HD, g>(att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,     \
-                                    page_table, max_pages, pool, n_pages, layer, kv_dtype,       \
-                                    nchunk, scratch, st);
-        CASE(1) CASE(2) CASE(4) CASE(8)
-#undef CASE
-    }
-    return -1;
-}
-
 }  // namespace
-
-extern "C" size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int max_seq) {
-    const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
-    return (size_t)max_batch * nq * nchunk * (hd + 2);
-}
-
-extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B,
-                                  int nq, int nkv, int hd, const int32_t* row_pos,
-                                  const int32_t* row_slot, const int32_t* page_table,
-                                  int max_pages, const void* pool, int64_t n_pages, int layer,
-                                  int kv_dtype, int max_seq, float* scratch, cudaStream_t st) {
-    if (B < 1 || nkv < 1 || nq % nkv) return -1;
-    const int G = nq / nkv;
-    const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
-    switch (hd) {
-        case 8: return launch_attn_hd<8>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, pool, n_pages, layer, kv_dtype, nchunk, scratch, st);
-        case 16: return launch_attn_hd<16>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, pool, n_pages, layer, kv_dtype, nchunk, scratch, st);
-        case 32: return launch_attn_hd<32>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, pool, n_pages, layer, kv_dtype, nchunk, scratch, st);
-        case 64: return launch_attn_hd<64>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, pool, n_pages, layer, kv_dtype, nchunk, scratch, st);
-        case 128: return launch_attn_hd<128>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, pool, n_pages, layer, kv_dtype, nchunk, scratch, st);
-    }
-    return -1;
-}
 
 extern "C" int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd,
                               const int32_t* row_pos, const int32_t* row_slot,

@@ -1,0 +1,464 @@
+// attn_paged.cu -- paged-KV GQA decode attention (src/loader/llama_infer.c:97-129)
+// for a batch of sequences at their own positions (sm_100a).
+//
+// Pool layout: pool[layer][page][kv (0 = K, 1 = V)][kv_head][16 tokens][head_dim],
+// so one (page, kv, head) block -- 16 rows of head_dim -- is contiguous
+// (4 KB for f16 / 8 KB for f32 at head_dim 128).
+//
+// One CTA per (row, kv_head, 512-token chunk).  A producer warp streams the
+// chunk's pages with cp.async.bulk (TMA bulk copies, one for K and one for V,
+// completion on an mbarrier) into an 8-stage (f16) / 6-stage (f32) ring in
+// shared memory.  Four consumer warps take pages round-robin; each handles
+// all G = n_heads / n_kv_heads query heads of the group, lane l holding
+// head_dim/32 consecutive dims, so every K/V byte crosses HBM once and shared
+// memory once per step.  Per page a warp forms the 16 x G partial dots,
+// reduces them across lanes with a transpose-reduction (lane l ends up with
+// entries l*VPL .. of the [head][token] grid), applies an online softmax
+// (running max / sum, expf, as the reference's max-subtracted softmax) and
+// accumulates p*V with probabilities broadcast through shared memory.  The
+// warps' (m, l, o) states are merged in the CTA, then across chunks by
+// attn_combine.  Waits are bounded (2 s); a timeout sets *err and the CTA
+// drains its copies before exiting.
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "sb_kernels.h"
+
+namespace {
+
+constexpr int NW = 4;                     // consumer warps per CTA
+constexpr uint64_t WAIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint32_t su32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t c) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(c));
+}
+__device__ __forceinline__ void bar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ bool bar_wait(uint64_t* b, uint32_t parity, int* err, int code) {
+    if (bar_try(b, parity)) return true;
+    const uint64_t t0 = gtimer();
+    while (!bar_try(b, parity)) {
+        if (*(volatile int*)err) return false;
+        if (gtimer() - t0 > WAIT_NS) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            su32(dst)),
+        "l"(src), "r"(bytes), "r"(su32(bar))
+        : "memory");
+}
+
+template <int DPL>
+__device__ __forceinline__ void ld_row(const float* p, float (&v)[DPL]) {
+    if constexpr (DPL == 4) {
+        const float4 t = *(const float4*)p;
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else if constexpr (DPL == 2) {
+        const float2 t = *(const float2*)p;
+        v[0] = t.x; v[1] = t.y;
+    } else {
+        v[0] = p[0];
+    }
+}
+template <int DPL>
+__device__ __forceinline__ void ld_row(const __half* p, float (&v)[DPL]) {
+    if constexpr (DPL == 4) {
+        const uint2 t = *(const uint2*)p;
+        const float2 a = __half22float2(*(const __half2*)&t.x), b = __half22float2(*(const __half2*)&t.y);
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else if constexpr (DPL == 2) {
+        const uint32_t t = *(const uint32_t*)p;
+        const float2 a = __half22float2(*(const __half2*)&t);
+        v[0] = a.x; v[1] = a.y;
+    } else {
+        v[0] = __half2float(p[0]);
+    }
+}
+
+// Sum of v[NV] over the warp, spread so that lane l keeps entries
+// [l*NV/32, (l+1)*NV/32) (NV >= 32), or, for NV == 16, entry l/2.
+template <int NV>
+__device__ __forceinline__ void transpose_reduce(float (&v)[NV], float (&out)[NV >= 32 ? NV / 32 : 1],
+                                                 int lane) {
+    float cur[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) cur[i] = v[i];
+    int n = NV;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (n > 1) {
+            const bool up = lane & o;
+            const int h = n / 2;
+#pragma unroll
+            for (int i = 0; i < NV / 2; ++i) {
+                if (i < h) {
+                    const float send = up ? cur[i] : cur[i + h];
+                    const float keep = up ? cur[i + h] : cur[i];
+                    cur[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            n = h;
+        } else {
+            cur[0] += __shfl_xor_sync(0xffffffffu, cur[0], o);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < (NV >= 32 ? NV / 32 : 1); ++i) out[i] = cur[i];
+}
+
+template <int HD, int G, typename KT>
+struct AttnShape {
+    static constexpr int DPL = HD >= 32 ? HD / 32 : 1;
+    static constexpr int ACTIVE = HD / DPL;
+    static constexpr int STAGES = sizeof(KT) == 2 ? 8 : 6;
+    static constexpr int HEAD_ELEMS = 16 * HD;
+    static constexpr int HEAD_BYTES = HEAD_ELEMS * (int)sizeof(KT);
+    static constexpr int NV = 16 * G;
+    static constexpr int VPL = NV >= 32 ? NV / 32 : 1;
+    static constexpr int GL = NV >= 32 ? 16 / VPL : 32;        // lanes sharing one head
+    static constexpr size_t SMEM = (size_t)STAGES * 2 * HEAD_BYTES;
+};
+
+template <int HD, int G, typename KT>
+__global__ void __launch_bounds__(32 * (NW + 1)) attn_chunk(
+    const float* __restrict__ qkv, int ld_qkv, int B, int nq, int nkv,
+    const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
+    const int32_t* __restrict__ page_table, int max_pages, const KT* __restrict__ pool,
+    int64_t n_pages, int layer, int nchunk_max, float* __restrict__ part, int* err) {
+    using S = AttnShape<HD, G, KT>;
+    constexpr int DPL = S::DPL, STAGES = S::STAGES, NV = S::NV, VPL = S::VPL, GL = S::GL;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    KT* ring = (KT*)smem_raw;                        // [STAGES][2][16][HD]
+    __shared__ uint64_t full[STAGES], empty[STAGES];
+    __shared__ __align__(16) float p_s[NW][16 * G];  // probabilities [token][head]
+    __shared__ float red_m[NW][G], red_l[NW][G];
+    __shared__ float red_o[NW][G][HD];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int chunk = blockIdx.x % nchunk_max;
+    const int rest = blockIdx.x / nchunk_max;
+    const int kvh = rest % nkv, b = rest / nkv;
+    if (b >= B) return;
+    const int pos = row_pos[b];
+    if (pos < 0) return;
+    const int ctx = pos + 1, t0 = chunk * SB_ATTN_CHUNK;
+    if (t0 >= ctx) return;
+    const int t1 = min(ctx, t0 + SB_ATTN_CHUNK);
+    const int npg = (t1 - t0 + 15) / 16;
+    const int slot = row_slot[b];
+
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            bar_init(&full[s], 1);
+            bar_init(&empty[s], 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == NW) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const size_t hs = (size_t)S::HEAD_ELEMS;
+            int issued = 0;
+            for (int i = 0; i < npg; ++i) {
+                const int s = i % STAGES;
+                if (i >= STAGES && !bar_wait(&empty[s], ((i / STAGES) - 1) & 1, err, 4)) break;
+                int page = page_table[(size_t)slot * max_pages + t0 / 16 + i];
+                if (page < 0 || page >= n_pages) {      // never allocated: read page 0, flag it
+                    atomicCAS(err, 0, 6);
+                    page = 0;
+                }
+                const KT* src = pool + (((size_t)layer * n_pages + page) * 2 * nkv + kvh) * hs;
+                KT* dst = ring + (size_t)s * 2 * hs;
+                bar_expect(&full[s], 2 * S::HEAD_BYTES);
+                bulk_g2s(dst, src, S::HEAD_BYTES, &full[s]);
+                bulk_g2s(dst + hs, src + (size_t)nkv * hs, S::HEAD_BYTES, &full[s]);
+                issued = i + 1;
+            }
+            // no copy may still be landing when the CTA exits
+            for (int i = issued - STAGES > 0 ? issued - STAGES : 0; i < issued; ++i)
+                bar_wait(&full[i % STAGES], (i / STAGES) & 1, err, 5);
+        }
+    } else {
+        // ---------------- consumers ----------------
+        const bool dl = lane < S::ACTIVE;
+        const int d0 = dl ? lane * DPL : 0;
+        float q[G][DPL], o[G][DPL], m[G], l[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            const float* qp = qkv + (size_t)b * ld_qkv + (size_t)(kvh * G + h) * HD + d0;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) {
+                q[h][i] = dl ? qp[i] : 0.f;
+                o[h][i] = 0.f;
+            }
+            m[h] = -INFINITY;
+            l[h] = 0.f;
+        }
+        const float scale = 1.0f / sqrtf((float)HD);
+        for (int i = warp; i < npg; i += NW) {
+            const int s = i % STAGES;
+            if (!bar_wait(&full[s], (i / STAGES) & 1, err, 7)) break;
+            const KT* kp = ring + (size_t)s * 2 * S::HEAD_ELEMS + d0;
+            const KT* vp = kp + S::HEAD_ELEMS;
+            const int nval = min(16, t1 - (t0 + 16 * i));
+            float part_s[NV];
+            {
+                float kr[16][DPL];
+#pragma unroll
+                for (int t = 0; t < 16; ++t) {
+                    if (dl && t < nval) ld_row<DPL>(kp + t * HD, kr[t]);
+                    else
+#pragma unroll
+                        for (int c = 0; c < DPL; ++c) kr[t][c] = 0.f;
+                }
+#pragma unroll
+                for (int h = 0; h < G; ++h)
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) {
+                        float a = 0.f;
+#pragma unroll
+                        for (int c = 0; c < DPL; ++c) a = fmaf(q[h][c], kr[t][c], a);
+                        part_s[h * 16 + t] = a;
+                    }
+            }
+            float sv[VPL];
+            transpose_reduce<NV>(part_s, sv, lane);
+            // entries held by this lane: index idx = lane*VPL + j (or lane/2 when NV == 16)
+            float pmax = -INFINITY;
+            int hh = 0;
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) {
+                const int idx = NV >= 32 ? lane * VPL + j : lane >> 1;
+                hh = idx / 16;
+                const int t = idx % 16;
+                sv[j] = t < nval ? sv[j] * scale : -INFINITY;
+                pmax = fmaxf(pmax, sv[j]);
+            }
+#pragma unroll
+            for (int off = 1; off < GL; off <<= 1) pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, off));
+            float mloc = fmaxf(m[0], pmax);
+            // this lane's head is hh (all its entries share one head)
+#pragma unroll
+            for (int h = 0; h < G; ++h)
+                if (h == hh) mloc = fmaxf(m[h], pmax);
+            float psum = 0.f;
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) {
+                const int idx = NV >= 32 ? lane * VPL + j : lane >> 1;
+                const int t = idx % 16;
+                const float pe = t < nval ? expf(sv[j] - mloc) : 0.f;
+                psum += pe;
+                p_s[warp][t * G + idx / 16] = pe;
+            }
+            // the sum over a head's tokens (GL lanes; for NV == 16 lane pairs hold copies)
+#pragma unroll
+            for (int off = NV >= 32 ? 1 : 2; off < GL; off <<= 1)
+                psum += __shfl_xor_sync(0xffffffffu, psum, off);
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float mn = __shfl_sync(0xffffffffu, mloc, h * (NV >= 32 ? GL : 0));
+                const float sm = __shfl_sync(0xffffffffu, psum, h * (NV >= 32 ? GL : 0));
+                const float corr = expf(m[h] - mn);
+                l[h] = l[h] * corr + sm;
+#pragma unroll
+                for (int c = 0; c < DPL; ++c) o[h][c] *= corr;
+                m[h] = mn;
+            }
+            __syncwarp();
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+                float vr[DPL];
+                if (dl && t < nval) ld_row<DPL>(vp + t * HD, vr);
+                else
+#pragma unroll
+                    for (int c = 0; c < DPL; ++c) vr[c] = 0.f;
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float p = p_s[warp][t * G + h];
+#pragma unroll
+                    for (int c = 0; c < DPL; ++c) o[h][c] = fmaf(p, vr[c], o[h][c]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) bar_arrive(&empty[s]);
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            if (lane == 0) {
+                red_m[warp][h] = m[h];
+                red_l[warp][h] = l[h];
+            }
+            if (dl)
+#pragma unroll
+                for (int c = 0; c < DPL; ++c) red_o[warp][h][d0 + c] = o[h][c];
+        }
+    }
+    __syncthreads();
+    // merge the consumer warps: one thread per (head, dim)
+    for (int e = tid; e < G * HD; e += blockDim.x) {
+        const int h = e / HD, d = e % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, red_m[w][h]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float f = red_m[w][h] == -INFINITY ? 0.f : expf(red_m[w][h] - M);
+            L += red_l[w][h] * f;
+            O += red_o[w][h][d] * f;
+        }
+        float* rec = part + (((size_t)b * nq + kvh * G + h) * nchunk_max + chunk) * (HD + 2);
+        if (d == 0) {
+            rec[0] = M;
+            rec[1] = L;
+        }
+        rec[2 + d] = O;
+    }
+}
+
+// Merge chunk partials: out = Σ_c o_c e^{m_c-M} / Σ_c l_c e^{m_c-M}.
+template <int HD>
+__global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ part, int B, int nq,
+                                                    const int32_t* __restrict__ row_pos,
+                                                    int nchunk_max, float* __restrict__ att,
+                                                    int ld_att) {
+    const int lane = threadIdx.x & 31;
+    const long w = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int hq = (int)(w % nq);
+    const int b = (int)(w / nq);
+    if (b >= B) return;
+    const int pos = row_pos[b];
+    if (pos < 0) return;
+    const int nch = (pos + SB_ATTN_CHUNK) / SB_ATTN_CHUNK;  // ceil((pos+1)/CHUNK)
+    const float* rec0 = part + ((size_t)b * nq + hq) * nchunk_max * (HD + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, rec0[(size_t)c * (HD + 2)]);
+    double L = 0.0;
+    for (int c = 0; c < nch; ++c) {
+        const float* r = rec0 + (size_t)c * (HD + 2);
+        L += (double)r[1] * (double)expf(r[0] - M);
+    }
+    const float invL = (float)(1.0 / L);
+    for (int d = lane; d < HD; d += 32) {
+        float acc = 0.f;
+        for (int c = 0; c < nch; ++c) {
+            const float* r = rec0 + (size_t)c * (HD + 2);
+            acc = fmaf(r[2 + d], expf(r[0] - M), acc);
+        }
+        att[(size_t)b * ld_att + (size_t)hq * HD + d] = acc * invL;
+    }
+}
+
+template <int HD, int G, typename KT>
+int launch_g(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq, int nkv,
+             const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
+             int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk,
+             float* scratch, int* err, cudaStream_t st) {
+    using S = AttnShape<HD, G, KT>;
+    static unsigned long long attr_done = 0;   // per-device bit: > 48 KB dynamic smem
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (S::SMEM > 48 * 1024 && dev < 64 && !((attr_done >> dev) & 1ull)) {
+        cudaFuncSetAttribute(attn_chunk<HD, G, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)S::SMEM);
+        attr_done |= 1ull << dev;
+    }
+    const long ctas = (long)B * nkv * nchunk;
+    attn_chunk<HD, G, KT><<<(unsigned)ctas, 32 * (NW + 1), S::SMEM, st>>>(
+        qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, (const KT*)pool, n_pages,
+        layer, nchunk, scratch, err);
+    const long cw = (long)B * nq;
+    attn_combine<HD><<<(unsigned)((cw + 3) / 4), 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att,
+                                                                ld_att);
+    return 0;
+}
+
+template <int HD, typename KT>
+int launch_hd(int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq, int nkv,
+              const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
+              int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk,
+              float* scratch, int* err, cudaStream_t st) {
+    switch (G) {
+#define CASE(g)                                                                                  \
+    case g:                                                                                      \
+        return launch_g<HD, g, KT>(att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,      \
+                                   page_table, max_pages, pool, n_pages, layer, nchunk, scratch, \
+                                   err, st);
+        CASE(1) CASE(2) CASE(4) CASE(8)
+#undef CASE
+    }
+    return -1;
+}
+
+template <typename KT>
+int launch_kt(int hd, int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
+              int nkv, const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
+              int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk,
+              float* scratch, int* err, cudaStream_t st) {
+    switch (hd) {
+#define CASE(h)                                                                                  \
+    case h:                                                                                      \
+        return launch_hd<h, KT>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,      \
+                                page_table, max_pages, pool, n_pages, layer, nchunk, scratch,    \
+                                err, st);
+        CASE(8) CASE(16) CASE(32) CASE(64) CASE(128)
+#undef CASE
+    }
+    return -1;
+}
+
+}  // namespace
+
+extern "C" size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int max_seq) {
+    const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
+    return (size_t)max_batch * nq * nchunk * (hd + 2);
+}
+
+extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B,
+                                  int nq, int nkv, int hd, const int32_t* row_pos,
+                                  const int32_t* row_slot, const int32_t* page_table,
+                                  int max_pages, const void* pool, int64_t n_pages, int layer,
+                                  int kv_dtype, int max_seq, float* scratch, int* err,
+                                  cudaStream_t st) {
+    if (B < 1 || nkv < 1 || nq % nkv || !err) return -1;
+    const int G = nq / nkv;
+    const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
+    return kv_dtype == SLATE_KV_F16
+               ? launch_kt<__half>(hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
+                                   page_table, max_pages, pool, n_pages, layer, nchunk, scratch,
+                                   err, st)
+               : launch_kt<float>(hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
+                                  page_table, max_pages, pool, n_pages, layer, nchunk, scratch,
+                                  err, st);
+}

@@ -149,11 +149,23 @@ static int be_attention_paged(float* out, const float* q, const int32_t* pos,
     int max_seq = max_pages * SB_PAGE_TOKENS;
     size_t nf = sb_attention_scratch_floats(B, nq, hd, max_seq);
     float* scr = NULL;
-    int rc = sb_cuda_check(cudaMallocAsync((void**)&scr, nf * 4, g_stream), "scratch");
+    int* err = NULL;
+    int e = 0;
+    int rc = sb_cuda_check(cudaMallocAsync((void**)&scr, nf * 4 + 16, g_stream), "scratch");
     if (rc) return rc;
-    rc = fin(sb_attention_paged(out, nq * hd, q, nq * hd, B, nq, nkv, hd, pos, row_slot, page_table,
-                                max_pages, pool, n_pages, layer, kv_dtype, max_seq, scr, g_stream),
-             "attention_paged_gqa");
+    err = (int*)(scr + nf);
+    rc = sb_cuda_check(cudaMemsetAsync(err, 0, 4, g_stream), "memset");
+    if (!rc)
+        rc = fin(sb_attention_paged(out, nq * hd, q, nq * hd, B, nq, nkv, hd, pos, row_slot,
+                                    page_table, max_pages, pool, n_pages, layer, kv_dtype, max_seq,
+                                    scr, err, g_stream),
+                 "attention_paged_gqa");
+    if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, g_stream), "err");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "attention_paged_gqa");
+    if (!rc && e) {
+        sb_set_error("attention pipeline reported %d", e);
+        rc = -5;
+    }
     cudaFreeAsync(scr, g_stream);
     return rc;
 }

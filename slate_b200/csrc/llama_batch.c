@@ -221,7 +221,7 @@ static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
                              b->rope_cos, b->rope_sin, s);
         rc |= sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
                                  b->row_pos, b->row_slot, b->page_table, b->max_pages, b->pool,
-                                 b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch, s);
+                                 b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch, b->tc_err, s);
         rc |= step_gemm(b, &ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, SB_EPI_ADD, b->sp_wo, s);
         rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, ly->ffn_norm, n, b->D, b->eps, s);
         rc |= step_gemm(b, &ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
@@ -408,8 +408,10 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         b->row_slot = (int32_t*)dalloc(b, (size_t)B * 4);
         b->d_io = (int32_t*)dalloc(b, (size_t)3 * B * 4);
         b->status = (int32_t*)dalloc(b, 16);
+        b->tc_err = (int*)dalloc(b, 16);        /* pipeline-wait timeouts of any kernel */
         if (!b->x || !b->xn || !b->att || !b->qkv || !b->h || !b->logits || !b->scratch ||
-            !b->row_pos || !b->row_slot || !b->d_io || !b->status)
+            !b->row_pos || !b->row_slot || !b->d_io || !b->status || !b->tc_err ||
+            sb_cuda_check(cudaMemset(b->tc_err, 0, 16), "memset"))
             goto fail;
         /* zero padding columns are part of the GEMM contract */
         if (sb_cuda_check(cudaMemset(b->x, 0, (size_t)B * b->ld_x * 4), "memset") ||
@@ -435,13 +437,11 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         void* dl = lo ? dalloc(b, (size_t)B * D * 2) : NULL;
         void* fh = dalloc(b, (size_t)B * F * 2);
         void* fl = lo ? dalloc(b, (size_t)B * F * 2) : NULL;
-        b->tc_err = (int*)dalloc(b, 16);
-        if (!dh || !fh || (lo && (!dl || !fl)) || !b->tc_err ||
+        if (!dh || !fh || (lo && (!dl || !fl)) ||
             sb_cuda_check(cudaMemset(dh, 0, (size_t)B * D * 2), "memset") ||
             sb_cuda_check(cudaMemset(fh, 0, (size_t)B * F * 2), "memset") ||
             (lo && (sb_cuda_check(cudaMemset(dl, 0, (size_t)B * D * 2), "memset") ||
-                    sb_cuda_check(cudaMemset(fl, 0, (size_t)B * F * 2), "memset"))) ||
-            sb_cuda_check(cudaMemset(b->tc_err, 0, 16), "memset"))
+                    sb_cuda_check(cudaMemset(fl, 0, (size_t)B * F * 2), "memset"))))
             goto fail;
         if (sb_tc_make_operand(&b->op_d, dh, dl, B, D, D) ||
             sb_tc_make_operand(&b->op_f, fh, fl, B, F, F))
@@ -781,7 +781,7 @@ static int enqueue_kernel(slate_llama_batch_t* b, int kernel, int n, int layer, 
             return sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
                                       b->row_pos, b->row_slot, b->page_table, b->max_pages,
                                       b->pool, b->n_pages, layer, b->kv_dtype, b->max_seq,
-                                      b->scratch, s);
+                                      b->scratch, b->tc_err, s);
         case SLATE_PROF_QKV:
             return step_gemm(b, &ly->wqkv, b->xn, b->ld_x, n, scratch_y, b->ld_logits, SB_EPI_STORE,
                              b->sp_qkv, s);

@@ -89,13 +89,13 @@ int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd, const int
  * row_pos[b]+1.  Split over context chunks of SB_ATTN_CHUNK tokens into
  * scratch partials (m, l, o[hd]) of size sb_attention_scratch_floats(), then
  * combined. */
-#define SB_ATTN_CHUNK 256
+#define SB_ATTN_CHUNK 512
 size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int max_seq);
 int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
                        int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
                        const int32_t* page_table, int max_pages, const void* pool,
                        int64_t n_pages, int layer, int kv_dtype, int max_seq, float* scratch,
-                       cudaStream_t st);
+                       int* err, cudaStream_t st);
 
 /* Fills positions [0, n) of one slot with deterministic pseudo-random K/V
  * (benchmark stand-in for a prefilled prompt), allocating its pages. */
