@@ -380,19 +380,19 @@ __global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ pa
     }
 }
 
+// prepare != 0: only opt the instantiation into its shared-memory size (the
+// dynamic ring plus static state can exceed the 48 KB default); this happens
+// per device and outside any stream capture.
 template <int HD, int G, typename KT>
-int launch_g(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq, int nkv,
-             const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
+int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
+             int nkv, const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
              int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk,
              float* scratch, int* err, cudaStream_t st) {
     using S = AttnShape<HD, G, KT>;
-    static unsigned long long attr_done = 0;   // per-device bit: > 48 KB dynamic smem
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (S::SMEM > 48 * 1024 && dev < 64 && !((attr_done >> dev) & 1ull)) {
+    if (prepare) {
         cudaFuncSetAttribute(attn_chunk<HD, G, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)S::SMEM);
-        attr_done |= 1ull << dev;
+        return 0;
     }
     const long ctas = (long)B * nkv * nchunk;
     attn_chunk<HD, G, KT><<<(unsigned)ctas, 32 * (NW + 1), S::SMEM, st>>>(
@@ -405,16 +405,16 @@ int launch_g(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq
 }
 
 template <int HD, typename KT>
-int launch_hd(int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq, int nkv,
-              const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
-              int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk,
-              float* scratch, int* err, cudaStream_t st) {
+int launch_hd(int prepare, int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B,
+              int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
+              const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
+              int layer, int nchunk, float* scratch, int* err, cudaStream_t st) {
     switch (G) {
 #define CASE(g)                                                                                  \
     case g:                                                                                      \
-        return launch_g<HD, g, KT>(att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,      \
-                                   page_table, max_pages, pool, n_pages, layer, nchunk, scratch, \
-                                   err, st);
+        return launch_g<HD, g, KT>(prepare, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
+                                   row_slot, page_table, max_pages, pool, n_pages, layer,        \
+                                   nchunk, scratch, err, st);
         CASE(1) CASE(2) CASE(4) CASE(8)
 #undef CASE
     }
@@ -422,20 +422,36 @@ int launch_hd(int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B
 }
 
 template <typename KT>
-int launch_kt(int hd, int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
-              int nkv, const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
-              int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk,
-              float* scratch, int* err, cudaStream_t st) {
+int launch_kt(int prepare, int hd, int G, float* att, int ld_att, const float* qkv, int ld_qkv,
+              int B, int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
+              const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
+              int layer, int nchunk, float* scratch, int* err, cudaStream_t st) {
     switch (hd) {
 #define CASE(h)                                                                                  \
     case h:                                                                                      \
-        return launch_hd<h, KT>(G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,      \
-                                page_table, max_pages, pool, n_pages, layer, nchunk, scratch,    \
-                                err, st);
+        return launch_hd<h, KT>(prepare, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
+                                row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,   \
+                                scratch, err, st);
         CASE(8) CASE(16) CASE(32) CASE(64) CASE(128)
 #undef CASE
     }
     return -1;
+}
+
+int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
+             int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
+             const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
+             int layer, int kv_dtype, int max_seq, float* scratch, int* err, cudaStream_t st) {
+    if (nkv < 1 || nq % nkv) return -1;
+    const int G = nq / nkv;
+    const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
+    return kv_dtype == SLATE_KV_F16
+               ? launch_kt<__half>(prepare, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
+                                   row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,
+                                   scratch, err, st)
+               : launch_kt<float>(prepare, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
+                                  row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,
+                                  scratch, err, st);
 }
 
 }  // namespace
@@ -445,20 +461,18 @@ extern "C" size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int
     return (size_t)max_batch * nq * nchunk * (hd + 2);
 }
 
+extern "C" int sb_attention_prepare(int nq, int nkv, int hd, int kv_dtype) {
+    return dispatch(1, nullptr, 0, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr, 0,
+                    nullptr, 0, 0, kv_dtype, 0, nullptr, nullptr, 0);
+}
+
 extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B,
                                   int nq, int nkv, int hd, const int32_t* row_pos,
                                   const int32_t* row_slot, const int32_t* page_table,
                                   int max_pages, const void* pool, int64_t n_pages, int layer,
                                   int kv_dtype, int max_seq, float* scratch, int* err,
                                   cudaStream_t st) {
-    if (B < 1 || nkv < 1 || nq % nkv || !err) return -1;
-    const int G = nq / nkv;
-    const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
-    return kv_dtype == SLATE_KV_F16
-               ? launch_kt<__half>(hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
-                                   page_table, max_pages, pool, n_pages, layer, nchunk, scratch,
-                                   err, st)
-               : launch_kt<float>(hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
-                                  page_table, max_pages, pool, n_pages, layer, nchunk, scratch,
-                                  err, st);
+    if (B < 1 || !err) return -1;
+    return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
+                    max_pages, pool, n_pages, layer, kv_dtype, max_seq, scratch, err, st);
 }

@@ -155,6 +155,7 @@ static int be_attention_paged(float* out, const float* q, const int32_t* pos,
     if (rc) return rc;
     err = (int*)(scr + nf);
     rc = sb_cuda_check(cudaMemsetAsync(err, 0, 4, g_stream), "memset");
+    if (!rc && sb_attention_prepare(nq, nkv, hd, kv_dtype)) rc = -1;
     if (!rc)
         rc = fin(sb_attention_paged(out, nq * hd, q, nq * hd, B, nq, nkv, hd, pos, row_slot,
                                     page_table, max_pages, pool, n_pages, layer, kv_dtype, max_seq,

@@ -335,6 +335,10 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         goto fail;
     sb_gemm_prepare();
     sb_tc_prepare();
+    if (sb_attention_prepare(nq, nkv, hd, b->kv_dtype)) {
+        sb_set_error("no attention kernel for head_dim %d, group %d", hd, nq / nkv);
+        goto fail;
+    }
 
     /* weights */
     if (upload_f32(b, &b->emb, m->token_embd, (size_t)V * D)) goto fail;

@@ -91,6 +91,9 @@ int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd, const int
  * combined. */
 #define SB_ATTN_CHUNK 512
 size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int max_seq);
+/* Opts the (head_dim, group, dtype) kernel into its shared-memory size on the
+ * current device; call outside stream capture before the first launch. */
+int sb_attention_prepare(int nq, int nkv, int hd, int kv_dtype);
 int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
                        int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
                        const int32_t* page_table, int max_pages, const void* pool,
