@@ -188,17 +188,25 @@ __device__ __forceinline__ void dequant32(uint4 q, float sd, float sm, uint32_t 
     }
 }
 
-template <int PASSES, int STAGES>
+// AMODE 0: the A operand (weights) is Q4_K, dequantised by warps 0-3.
+// AMODE 1: the A operand is an f16 hi (+ lo) weight pair in global memory,
+//          loaded by TMA like the activations (f32 weights split once at load).
+// direct 0: write f32 partials ws[split][n][m]; 1: Y[n][m] = acc; 2: Y += acc
+// (direct modes need splits == 1).
+template <int PASSES, int STAGES, int AMODE>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    q4k_tc_kernel(const __grid_constant__ CUtensorMap xmap_hi, const __grid_constant__ CUtensorMap xmap_lo,
-                  const unsigned char* __restrict__ W, int M_pad, int K, int n_rows, int n_box,
-                  int splits, float* __restrict__ ws, int* err) {
+    tc_kernel(const __grid_constant__ CUtensorMap xmap_hi, const __grid_constant__ CUtensorMap xmap_lo,
+              const __grid_constant__ CUtensorMap amap_hi, const __grid_constant__ CUtensorMap amap_lo,
+              const unsigned char* __restrict__ W, int M, int M_pad, int K, int n_rows, int n_box,
+              int splits, float* __restrict__ ws, float* __restrict__ Y, int ldy, int direct,
+              int* err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-aligned carve-up: per stage [A_hi | A_lo | B_hi | B_lo]
     unsigned char* base = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    constexpr int PARTS = PASSES == 3 ? 2 : 1;
     const int a_bytes = BM * 128;            // 16 KB per operand part
     const int b_bytes = n_box * 128;
-    const int stage_bytes = (PASSES == 3 ? 2 : 1) * (a_bytes + b_bytes);
+    const int stage_bytes = PARTS * (a_bytes + b_bytes);
     __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], done_bar;
     __shared__ uint32_t tmem_slot;
 
@@ -213,7 +221,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full_bar[s], NPROD + 1);
+            mbar_init(&full_bar[s], AMODE == 0 ? NPROD + 1 : 1);
             mbar_init(&empty_bar[s], 1);
         }
         mbar_init(&done_bar, 1);
@@ -231,11 +239,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t tmem = tmem_slot;
     bool ok = true;
 
-    if (warp < 4) {
+    if (warp < 4 && (AMODE == 0 || tid == 0)) {
         // ---------------- producers ----------------
-        const int m = tid;                                   // tile row
+        const int m = tid;                                   // tile row (AMODE 0)
         const size_t row_bytes = (size_t)(K / 256) * 144;
-        const unsigned char* wrow = W + (size_t)(m_tile * BM + m) * row_bytes;
+        const unsigned char* wrow = AMODE == 0 ? W + (size_t)(m_tile * BM + m) * row_bytes : nullptr;
         const uint32_t row_off = (uint32_t)((m >> 3) * 1024 + (m & 7) * 128);
         uint4 hdr = make_uint4(0, 0, 0, 0);
         int hdr_blk = -1;
@@ -248,13 +256,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             unsigned char* st = base + (size_t)s * stage_bytes;
             unsigned char* a_hi = st;
             unsigned char* a_lo = st + a_bytes;
-            unsigned char* b_hi = st + (PASSES == 3 ? 2 : 1) * a_bytes;
+            unsigned char* b_hi = st + PARTS * a_bytes;
             unsigned char* b_lo = b_hi + b_bytes;
             if (tid == 0) {
-                mbar_expect_tx(&full_bar[s], (uint32_t)((PASSES == 3 ? 2 : 1) * b_bytes));
+                mbar_expect_tx(&full_bar[s],
+                               (uint32_t)(PARTS * b_bytes + (AMODE == 1 ? PARTS * a_bytes : 0)));
+                if (AMODE == 1) {
+                    tma_load_2d(a_hi, &amap_hi, &full_bar[s], ks * BK, m_tile * BM);
+                    if (PASSES == 3) tma_load_2d(a_lo, &amap_lo, &full_bar[s], ks * BK, m_tile * BM);
+                }
                 tma_load_2d(b_hi, &xmap_hi, &full_bar[s], ks * BK, n0);
                 if (PASSES == 3) tma_load_2d(b_lo, &xmap_lo, &full_bar[s], ks * BK, n0);
             }
+            if (AMODE == 1) continue;
             const int blk = ks >> 2, j0 = (ks & 3) * 2;     // 4 K-steps per super-block
             if (blk != hdr_blk) {
                 hdr = __ldg((const uint4*)(wrow + (size_t)blk * 144));
@@ -286,7 +300,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             fence_async_smem();
             mbar_arrive(&full_bar[s]);
         }
-    } else if (lane == 0) {
+    } else if (warp == 4 && lane == 0) {
         // ---------------- MMA issuer ----------------
         const uint32_t idesc = (1u << 4) | ((uint32_t)(n_mma >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
         for (int ks = ks0; ks < ks1; ++ks) {
@@ -298,7 +312,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tc_fence_after();
             unsigned char* st = base + (size_t)s * stage_bytes;
             const uint32_t a_hi = smem_u32(st), a_lo = a_hi + a_bytes;
-            const uint32_t b_hi = smem_u32(st + (PASSES == 3 ? 2 : 1) * a_bytes), b_lo = b_hi + b_bytes;
+            const uint32_t b_hi = smem_u32(st + PARTS * a_bytes), b_lo = b_hi + b_bytes;
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
                 const uint32_t koff = 32u * k;                // 16 f16 = 32 bytes along K
@@ -315,20 +329,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     __syncwarp();
 
-    // ---------------- epilogue: TMEM -> f32 partials ----------------
+    // ---------------- epilogue: TMEM -> f32 ----------------
     if (warp < 4) {
-        const bool have = ok && mbar_wait(&done_bar, 0, err, 3);
+        bool have = ok && mbar_wait(&done_bar, 0, err, 3);
+        have = __all_sync(0xffffffffu, have);   // tcgen05.ld is warp-collective
         tc_fence_after();
         if (have) {
             const int m = m_tile * BM + warp * 32 + lane;
-            float* out = ws + (size_t)split * n_rows * M_pad;
             for (int c0 = 0; c0 < n_mma; c0 += 16) {
                 float v[16];
                 tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int n = c0 + j;
-                    if (n < n_here) out[(size_t)(n0 + n) * M_pad + m] = v[j];
+                    if (n >= n_here) continue;
+                    if (direct == 0) {
+                        ws[((size_t)split * n_rows + n0 + n) * M_pad + m] = v[j];
+                    } else if (m < M) {
+                        float* y = Y + (size_t)(n0 + n) * ldy + m;
+                        *y = direct == 2 ? *y + v[j] : v[j];
+                    }
                 }
             }
         }
@@ -444,6 +464,65 @@ extern "C" int sb_tc_split(const float* X, int ldx, int n_rows, const sb_tc_oper
     return 0;
 }
 
+extern "C" int sb_tc_make_weight(sb_tc_weight* w, const float* W32, int ldw, int M, int K,
+                                 cudaStream_t st) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+    if (!enc || !w || K % BK) return -1;
+    const int M_pad = (M + BM - 1) / BM * BM;
+    void *hi = nullptr, *lo = nullptr;
+    if (cudaMalloc(&hi, (size_t)M_pad * K * 2) != cudaSuccess ||
+        cudaMalloc(&lo, (size_t)M_pad * K * 2) != cudaSuccess) {
+        if (hi) cudaFree(hi);
+        sb_set_error("cudaMalloc of %zu bytes for the f16 weight pair failed", (size_t)M_pad * K * 4);
+        return -5;
+    }
+    cudaMemsetAsync(hi, 0, (size_t)M_pad * K * 2, st);
+    cudaMemsetAsync(lo, 0, (size_t)M_pad * K * 2, st);
+    const long total = (long)M * K;
+    split_f16_kernel<<<(int)((total + 255) / 256 < 4736 ? (total + 255) / 256 : 4736), 256, 0, st>>>(
+        W32, ldw, M, K, (__half*)hi, (__half*)lo, K);
+    w->hi = hi;
+    w->lo = lo;
+    w->M = M;
+    w->M_pad = M_pad;
+    w->K = K;
+    for (int part = 0; part < 2; ++part) {
+        cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M_pad};
+        cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+        cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+        cuuint32_t estr[2] = {1, 1};
+        CUresult r = enc((CUtensorMap*)(part ? w->map_lo : w->map_hi), CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         2, part ? lo : hi, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            sb_set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+            return -1;
+        }
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+extern "C" void sb_tc_free_weight(sb_tc_weight* w) {
+    if (!w) return;
+    if (w->hi) cudaFree(w->hi);
+    if (w->lo) cudaFree(w->lo);
+    w->hi = w->lo = nullptr;
+}
+
+extern "C" int sb_tc_gemm_f16w(const sb_tc_weight* W, const sb_tc_operand* X, int n_rows,
+                               float* Y, int ldy, int epi, int* err, cudaStream_t st) {
+    if (!W || !W->hi || !X || !X->lo || W->K != X->K || n_rows < 1 || n_rows > X->rows ||
+        (epi != SB_EPI_STORE && epi != SB_EPI_ADD))
+        return -1;
+    dim3 grid((unsigned)(W->M_pad / BM), 1u, (unsigned)((n_rows + 255) / 256));
+    tc_kernel<3, stages_for<3>(), 1><<<grid, NTHREADS, smem_for<3>(X->n_box), st>>>(
+        *(const CUtensorMap*)X->map_hi, *(const CUtensorMap*)X->map_lo,
+        *(const CUtensorMap*)W->map_hi, *(const CUtensorMap*)W->map_lo, nullptr, W->M, W->M_pad,
+        W->K, n_rows, X->n_box, 1, nullptr, Y, ldy, epi == SB_EPI_ADD ? 2 : 1, err);
+    return 0;
+}
+
 extern "C" int sb_tc_splits_for(int M_pad, int K) {
     const int tiles = M_pad / BM, nk = K / BK;
     int s = 148 / (tiles > 0 ? tiles : 1);
@@ -453,9 +532,11 @@ extern "C" int sb_tc_splits_for(int M_pad, int K) {
 }
 
 extern "C" void sb_tc_prepare(void) {
-    cudaFuncSetAttribute(q4k_tc_kernel<1, stages_for<1>()>,
+    cudaFuncSetAttribute(tc_kernel<1, stages_for<1>(), 0>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for<1>(256));
-    cudaFuncSetAttribute(q4k_tc_kernel<3, stages_for<3>()>,
+    cudaFuncSetAttribute(tc_kernel<3, stages_for<3>(), 0>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for<3>(256));
+    cudaFuncSetAttribute(tc_kernel<3, stages_for<3>(), 1>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for<3>(256));
 }
 
@@ -468,14 +549,19 @@ extern "C" int sb_tc_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows
         return -1;
     dim3 grid((unsigned)(W->M_pad / BM), (unsigned)splits, (unsigned)((n_rows + 255) / 256));
     const unsigned char* w = (const unsigned char*)W->data;
+    const CUtensorMap* xh = (const CUtensorMap*)X->map_hi;
+    const CUtensorMap* xl = (const CUtensorMap*)(passes == 3 ? X->map_lo : X->map_hi);
+    // one split and a STORE / ADD epilogue: write Y straight from TMEM
+    const int direct = splits == 1 && epi != SB_EPI_SILU ? (epi == SB_EPI_ADD ? 2 : 1) : 0;
     if (passes == 1)
-        q4k_tc_kernel<1, stages_for<1>()><<<grid, NTHREADS, smem_for<1>(X->n_box), st>>>(
-            *(const CUtensorMap*)X->map_hi, *(const CUtensorMap*)X->map_hi, w, W->M_pad, W->K,
-            n_rows, X->n_box, splits, ws, err);
+        tc_kernel<1, stages_for<1>(), 0><<<grid, NTHREADS, smem_for<1>(X->n_box), st>>>(
+            *xh, *xl, *xh, *xh, w, W->M, W->M_pad, W->K, n_rows, X->n_box, splits, ws, Y, ldy,
+            direct, err);
     else
-        q4k_tc_kernel<3, stages_for<3>()><<<grid, NTHREADS, smem_for<3>(X->n_box), st>>>(
-            *(const CUtensorMap*)X->map_hi, *(const CUtensorMap*)X->map_lo, w, W->M_pad, W->K,
-            n_rows, X->n_box, splits, ws, err);
+        tc_kernel<3, stages_for<3>(), 0><<<grid, NTHREADS, smem_for<3>(X->n_box), st>>>(
+            *xh, *xl, *xh, *xh, w, W->M, W->M_pad, W->K, n_rows, X->n_box, splits, ws, Y, ldy,
+            direct, err);
+    if (direct) return 0;
     const int n_out = epi == SB_EPI_SILU ? W->M / 2 : W->M;
     const long total = (long)n_rows * n_out;
     const int fg = (int)((total + 255) / 256 < 4736 ? (total + 255) / 256 : 4736);

@@ -75,6 +75,7 @@ struct slate_llama_batch {
     float* tc_ws;
     int* tc_err;
     int sp_qkv, sp_wo, sp_gu, sp_dn;
+    sb_tc_weight head_tc;          /* f32 LM head as an f16 pair (hi set when used) */
 };
 
 /* Rows from which a Q4_K GEMM runs on the tensor cores (below: CUDA cores). */
@@ -83,6 +84,10 @@ struct slate_llama_batch {
 /* One weight GEMM of the step on the path chosen for (weight, rows). */
 static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X, int ldx, int n,
                      float* Y, int ldy, int epi, int splits, cudaStream_t s) {
+    if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) {
+        int rc = sb_tc_split(X, ldx, n, &b->op_d, s);
+        return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, &b->op_d, n, Y, ldy, epi, b->tc_err, s);
+    }
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
         const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d : &b->op_f;
         int rc = sb_tc_split(X, ldx, n, op, s);
@@ -275,6 +280,7 @@ void slate_llama_batch_free(slate_llama_batch_t* b) {
             if (b->graphs[i]) cudaGraphExecDestroy(b->graphs[i]);
         free(b->graphs);
     }
+    sb_tc_free_weight(&b->head_tc);
     for (int i = 0; i < b->n_allocs; ++i) cudaFree(b->allocs[i]);
     free(b->allocs);
     if (b->h_io) cudaFreeHost(b->h_io);
@@ -463,6 +469,12 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         if (b->lm_head.wtype == SB_WT_Q4K && (t = (size_t)b->lm_head.M_pad) > ws) ws = t;
         b->tc_ws = (float*)dalloc(b, ws * (size_t)B * 4);
         if (!b->tc_ws) goto fail;
+        /* an f32 LM head runs on the tensor cores as an exact f16 hi/lo pair */
+        if (b->tc_passes == 3 && b->lm_head.wtype == SB_WT_F32 &&
+            (sb_tc_make_weight(&b->head_tc, (const float*)b->lm_head.data, b->lm_head.ldw, V, D,
+                               b->stream) ||
+             sb_cuda_check(cudaStreamSynchronize(b->stream), "head split")))
+            goto fail;
     }
 
     /* KV pool, page tables, free list */

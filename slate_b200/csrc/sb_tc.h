@@ -39,6 +39,23 @@ int sb_tc_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows, int passe
 /* Shared-memory attributes (outside stream capture). */
 void sb_tc_prepare(void);
 
+/* An f32 weight [M][K] held as an f16 pair (hi = f16(w), lo = f16(w - hi),
+ * M padded to 128 with zeros) with TMA maps, for the 3-pass tensor-core GEMM
+ * without dequantisation (the f32 LM head). */
+typedef struct sb_tc_weight {
+    SB_ALIGN64 unsigned char map_hi[128];
+    SB_ALIGN64 unsigned char map_lo[128];
+    void* hi;
+    void* lo;
+    int M, M_pad, K;
+} sb_tc_weight;
+/* Splits the device f32 matrix W32 (row stride ldw) into a new pair. */
+int sb_tc_make_weight(sb_tc_weight* w, const float* W32, int ldw, int M, int K, cudaStream_t st);
+void sb_tc_free_weight(sb_tc_weight* w);
+/* Y[n][m] (=, +=) X[n] . W[m] for m < M with the 3-pass split (epi STORE / ADD). */
+int sb_tc_gemm_f16w(const sb_tc_weight* W, const sb_tc_operand* X, int n_rows, float* Y, int ldy,
+                    int epi, int* err, cudaStream_t st);
+
 #ifdef __cplusplus
 }
 #endif
