@@ -211,6 +211,10 @@ static int upload_f32(slate_llama_batch_t* b, float** dst, const void* src, size
 
 static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
     int rc = 0;
+    /* cudaGetLastError() below must only see this step's launches: a failure
+     * left by an earlier unchecked call on this thread is cleared here (a
+     * sticky device fault would still fail every call that follows). */
+    (void)cudaGetLastError();
     const int32_t* slots = b->d_io;
     const int32_t* toks = b->d_io + b->max_batch;
     int32_t* out = b->d_io + 2 * b->max_batch;

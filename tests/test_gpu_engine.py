@@ -63,7 +63,7 @@ def run_continuous(eng, requests, max_batch, rng):
             slots.append(a["slot"])
             toks.append(tok)
         rc, out, lg = eng.step(slots, toks, want_logits=True)
-        assert rc == 0
+        assert rc == 0, sb.last_error()
         for i, r in enumerate(reqs):
             a, (prompt, n_new) = active[r], requests[r]
             a["fed"] += 1
@@ -147,7 +147,7 @@ def test_graphs_and_eager_agree(sb, workdir):
         res = []
         for _ in range(6):
             rc, out, lg = eng.step(slots, toks, want_logits=True)
-            assert rc == 0
+            assert rc == 0, sb.last_error()
             res.append(lg)
             toks = out
         outs.append(np.stack(res))
@@ -213,10 +213,10 @@ def test_seeded_context_matches_oracle(sb, oracle, workdir):
     toks = np.array([3, 1, 4, 1, 5, 9], np.int32)
     for _ in range(3):
         rc, out, lg = eng.step(slots, toks, want_logits=True)
-        assert rc == 0
+        assert rc == 0, sb.last_error()
         for i, o in enumerate(sess):
             rc, ref = o.decode(int(toks[i]))
-            assert rc == 0
+            assert rc == 0, sb.last_error()
             assert scale_err(lg[i], ref) < 1e-4
             assert greedy_agrees(int(out[i]), ref, 1e-4 * np.abs(ref).max())[0]
         toks = out
@@ -249,7 +249,7 @@ def test_device_step_matches_host_step(sb, workdir):
         else:
             for _ in range(5):
                 rc, out, _ = eng.step(slots, toks)
-                assert rc == 0
+                assert rc == 0, sb.last_error()
                 seq.append(out.copy())
                 toks = out
         res.append(np.stack(seq))
@@ -272,7 +272,7 @@ def test_scheduler_batches_concurrent_callers(sb, oracle, workdir):
         tok, out = 11 * w + 1, []
         for _ in range(n_tok):
             rc, nxt, _ = sched.decode(slot, tok)
-            assert rc == 0
+            assert rc == 0, sb.last_error()
             out.append(nxt)
             tok = nxt
         streams[w] = out

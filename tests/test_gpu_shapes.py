@@ -58,7 +58,7 @@ def test_real_shapes(sb, oracle, workdir, name):
         s = eng.open()
         assert eng.seed_context(s, c, seed=77 + i) == 0
         rc, K, V = eng.read_kv(s, c, L, kvd)
-        assert rc == 0
+        assert rc == 0, sb.last_error()
         o = m.session(max_seq=mc["max_seq"])
         assert o.seed_kv(K, V) == 0
         slots.append(s)
@@ -70,7 +70,7 @@ def test_real_shapes(sb, oracle, workdir, name):
     pool = ThreadPoolExecutor(max_workers=os.cpu_count() or 8)
     for rows in (list(range(len(slots))), list(range(0, len(slots), 2))[:4]):
         rc, out, lg = eng.step([slots[r] for r in rows], toks[rows], want_logits=True)
-        assert rc == 0
+        assert rc == 0, sb.last_error()
         refs = list(pool.map(lambda r: sess[r].decode(int(toks[r])), rows))
         for i, r in enumerate(rows):
             rc_o, ref = refs[i]
