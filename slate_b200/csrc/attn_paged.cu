@@ -7,7 +7,7 @@
 //
 // One CTA per (row, kv_head, 512-token chunk).  A producer warp streams the
 // chunk's pages with cp.async.bulk (TMA bulk copies, one for K and one for V,
-// completion on an mbarrier) into an 8-stage (f16) / 6-stage (f32) ring in
+// completion on an mbarrier) into an 8-stage (f16) / 4-stage (f32) ring in
 // shared memory.  Four consumer warps take pages round-robin; each handles
 // all G = n_heads / n_kv_heads query heads of the group, lane l holding
 // head_dim/32 consecutive dims, so every K/V byte crosses HBM once and shared
@@ -139,7 +139,12 @@ template <int HD, int G, typename KT>
 struct AttnShape {
     static constexpr int DPL = HD >= 32 ? HD / 32 : 1;
     static constexpr int ACTIVE = HD / DPL;
-    static constexpr int STAGES = sizeof(KT) == 2 ? 8 : 6;
+    // Page i uses stage i % STAGES and is consumed by warp i % NW.  With
+    // STAGES a multiple of NW a stage always belongs to one warp, which waits
+    // for its phases in order; otherwise a warp could wait two phases ahead of
+    // another warp's pending use and the parity wait would alias.
+    static constexpr int STAGES = sizeof(KT) == 2 ? 8 : 4;
+    static_assert(STAGES % NW == 0, "each ring stage must belong to one consumer warp");
     static constexpr int HEAD_ELEMS = 16 * HD;
     static constexpr int HEAD_BYTES = HEAD_ELEMS * (int)sizeof(KT);
     static constexpr int NV = 16 * G;
