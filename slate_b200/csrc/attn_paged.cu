@@ -104,14 +104,13 @@ __device__ __forceinline__ void ld_row(const __half* p, float (&v)[DPL]) {
     }
 }
 
-// Sum of v[NV] over the warp, spread so that lane l keeps entries
-// [l*NV/32, (l+1)*NV/32) (NV >= 32), or, for NV == 16, entry l/2.
+// Sum of v[NV] over the warp's 32 lanes, spread so that lane l keeps the
+// entries [l*NV/32, (l+1)*NV/32) when NV >= 32, or entry l >> log2(32/NV)
+// (held by 32/NV lanes each) when NV < 32.  log2(32)=5 shuffle rounds; each
+// round halves what a lane holds until one entry is left, then adds copies.
 template <int NV>
 __device__ __forceinline__ void transpose_reduce(float (&v)[NV], float (&out)[NV >= 32 ? NV / 32 : 1],
                                                  int lane) {
-    float cur[NV];
-#pragma unroll
-    for (int i = 0; i < NV; ++i) cur[i] = v[i];
     int n = NV;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
@@ -121,19 +120,21 @@ __device__ __forceinline__ void transpose_reduce(float (&v)[NV], float (&out)[NV
 #pragma unroll
             for (int i = 0; i < NV / 2; ++i) {
                 if (i < h) {
-                    const float send = up ? cur[i] : cur[i + h];
-                    const float keep = up ? cur[i + h] : cur[i];
-                    cur[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                    const float send = up ? v[i] : v[i + h];
+                    const float keep = up ? v[i + h] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
                 }
             }
             n = h;
         } else {
-            cur[0] += __shfl_xor_sync(0xffffffffu, cur[0], o);
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
         }
     }
 #pragma unroll
-    for (int i = 0; i < (NV >= 32 ? NV / 32 : 1); ++i) out[i] = cur[i];
+    for (int i = 0; i < (NV >= 32 ? NV / 32 : 1); ++i) out[i] = v[i];
 }
+
+constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x / 2); }
 
 template <int HD, int G, typename KT>
 struct AttnShape {
@@ -147,26 +148,31 @@ struct AttnShape {
     static_assert(STAGES % NW == 0, "each ring stage must belong to one consumer warp");
     static constexpr int HEAD_ELEMS = 16 * HD;
     static constexpr int HEAD_BYTES = HEAD_ELEMS * (int)sizeof(KT);
-    static constexpr int NV = 16 * G;
-    static constexpr int VPL = NV >= 32 ? NV / 32 : 1;
-    static constexpr int GL = NV >= 32 ? 16 / VPL : 32;        // lanes sharing one head
-    static constexpr size_t SMEM = (size_t)STAGES * 2 * HEAD_BYTES;
+    // scores are formed 8 tokens (half a page) at a time
+    static constexpr int TOK = 8;
+    static constexpr int NV = TOK * G;
+    static constexpr int VPL = NV >= 32 ? NV / 32 : 1;       // entries per lane
+    static constexpr int SH = NV >= 32 ? 0 : ilog2(32 / NV); // lanes per entry = 1 << SH
+    static constexpr int GL = NV >= 32 ? TOK / VPL : (TOK << SH);  // lanes per head
+    static constexpr size_t RING = (size_t)STAGES * 2 * HEAD_BYTES;
+    static constexpr size_t MERGE = (size_t)NW * G * (HD + 2) * sizeof(float);
+    static constexpr size_t SMEM = RING > MERGE ? RING : MERGE;
 };
 
 template <int HD, int G, typename KT>
-__global__ void __launch_bounds__(32 * (NW + 1)) attn_chunk(
+__global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     const float* __restrict__ qkv, int ld_qkv, int B, int nq, int nkv,
     const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ page_table, int max_pages, const KT* __restrict__ pool,
     int64_t n_pages, int layer, int nchunk_max, float* __restrict__ part, int* err) {
     using S = AttnShape<HD, G, KT>;
-    constexpr int DPL = S::DPL, STAGES = S::STAGES, NV = S::NV, VPL = S::VPL, GL = S::GL;
+    constexpr int DPL = S::DPL, STAGES = S::STAGES, TOK = S::TOK, NV = S::NV, VPL = S::VPL,
+                  SH = S::SH, GL = S::GL;
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    KT* ring = (KT*)smem_raw;                        // [STAGES][2][16][HD]
+    KT* ring = (KT*)smem_raw;                        // [STAGES][2][16][HD]; reused for the merge
     __shared__ uint64_t full[STAGES], empty[STAGES];
-    __shared__ __align__(16) float p_s[NW][16 * G];  // probabilities [token][head]
-    __shared__ float red_m[NW][G], red_l[NW][G];
-    __shared__ float red_o[NW][G][HD];
+    __shared__ __align__(16) float p_s[NW][TOK * G]; // probabilities [token][head]
+    __shared__ int pages_s[SB_ATTN_CHUNK / 16];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int chunk = blockIdx.x % nchunk_max;
@@ -188,8 +194,23 @@ __global__ void __launch_bounds__(32 * (NW + 1)) attn_chunk(
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (warp == NW) {
+        // the chunk's page ids, fetched once so no copy waits on a table read
+        for (int i = lane; i < npg; i += 32) {
+            int page = page_table[(size_t)slot * max_pages + t0 / 16 + i];
+            if (page < 0 || page >= n_pages) {      // never allocated: read page 0, flag it
+                atomicCAS(err, 0, 6);
+                page = 0;
+            }
+            pages_s[i] = page;
+        }
+    }
     __syncthreads();
 
+    float* merge = (float*)smem_raw;                 // [NW][G][2 + HD] after the ring drains
+    const bool dl = lane < S::ACTIVE;
+    const int d0 = dl ? lane * DPL : 0;
+    float q[G][DPL], o[G][DPL], m[G], l[G];          // consumer state
     if (warp == NW) {
         // ---------------- producer ----------------
         if (lane == 0) {
@@ -198,27 +219,19 @@ __global__ void __launch_bounds__(32 * (NW + 1)) attn_chunk(
             for (int i = 0; i < npg; ++i) {
                 const int s = i % STAGES;
                 if (i >= STAGES && !bar_wait(&empty[s], ((i / STAGES) - 1) & 1, err, 4)) break;
-                int page = page_table[(size_t)slot * max_pages + t0 / 16 + i];
-                if (page < 0 || page >= n_pages) {      // never allocated: read page 0, flag it
-                    atomicCAS(err, 0, 6);
-                    page = 0;
-                }
-                const KT* src = pool + (((size_t)layer * n_pages + page) * 2 * nkv + kvh) * hs;
+                const KT* src = pool + (((size_t)layer * n_pages + pages_s[i]) * 2 * nkv + kvh) * hs;
                 KT* dst = ring + (size_t)s * 2 * hs;
                 bar_expect(&full[s], 2 * S::HEAD_BYTES);
                 bulk_g2s(dst, src, S::HEAD_BYTES, &full[s]);
                 bulk_g2s(dst + hs, src + (size_t)nkv * hs, S::HEAD_BYTES, &full[s]);
                 issued = i + 1;
             }
-            // no copy may still be landing when the CTA exits
+            // no copy may still be landing when the ring is reused or the CTA exits
             for (int i = issued - STAGES > 0 ? issued - STAGES : 0; i < issued; ++i)
                 bar_wait(&full[i % STAGES], (i / STAGES) & 1, err, 5);
         }
     } else {
         // ---------------- consumers ----------------
-        const bool dl = lane < S::ACTIVE;
-        const int d0 = dl ? lane * DPL : 0;
-        float q[G][DPL], o[G][DPL], m[G], l[G];
 #pragma unroll
         for (int h = 0; h < G; ++h) {
             const float* qp = qkv + (size_t)b * ld_qkv + (size_t)(kvh * G + h) * HD + d0;
@@ -234,99 +247,107 @@ __global__ void __launch_bounds__(32 * (NW + 1)) attn_chunk(
         for (int i = warp; i < npg; i += NW) {
             const int s = i % STAGES;
             if (!bar_wait(&full[s], (i / STAGES) & 1, err, 7)) break;
-            const KT* kp = ring + (size_t)s * 2 * S::HEAD_ELEMS + d0;
-            const KT* vp = kp + S::HEAD_ELEMS;
-            const int nval = min(16, t1 - (t0 + 16 * i));
-            float part_s[NV];
-            {
-                float kr[16][DPL];
+            const KT* kp0 = ring + (size_t)s * 2 * S::HEAD_ELEMS + d0;
+            const KT* vp0 = kp0 + S::HEAD_ELEMS;
+            const int nval_page = min(16, t1 - (t0 + 16 * i));
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {
+                const int nval = nval_page - TOK * half;   // valid tokens in this half (may be <= 0)
+                if (nval <= 0) break;
+                const KT* kp = kp0 + TOK * half * HD;
+                const KT* vp = vp0 + TOK * half * HD;
+                float part_s[NV];
+                {
+                    float kr[TOK][DPL];
 #pragma unroll
-                for (int t = 0; t < 16; ++t) {
-                    if (dl && t < nval) ld_row<DPL>(kp + t * HD, kr[t]);
-                    else
+                    for (int t = 0; t < TOK; ++t) {
+                        if (dl && t < nval) ld_row<DPL>(kp + t * HD, kr[t]);
+                        else
 #pragma unroll
-                        for (int c = 0; c < DPL; ++c) kr[t][c] = 0.f;
+                            for (int c = 0; c < DPL; ++c) kr[t][c] = 0.f;
+                    }
+#pragma unroll
+                    for (int h = 0; h < G; ++h)
+#pragma unroll
+                        for (int t = 0; t < TOK; ++t) {
+                            float a = 0.f;
+#pragma unroll
+                            for (int c = 0; c < DPL; ++c) a = fmaf(q[h][c], kr[t][c], a);
+                            part_s[h * TOK + t] = a;
+                        }
                 }
+                float sv[VPL];
+                transpose_reduce<NV>(part_s, sv, lane);
+                float pmax = -INFINITY;
+                int hh = 0;
+#pragma unroll
+                for (int j = 0; j < VPL; ++j) {
+                    const int idx = NV >= 32 ? lane * VPL + j : lane >> SH;
+                    hh = idx / TOK;
+                    sv[j] = (idx % TOK) < nval ? sv[j] * scale : -INFINITY;
+                    pmax = fmaxf(pmax, sv[j]);
+                }
+#pragma unroll
+                for (int off = 1; off < GL; off <<= 1)
+                    pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, off));
+                float mloc = -INFINITY;
 #pragma unroll
                 for (int h = 0; h < G; ++h)
+                    if (h == hh) mloc = fmaxf(m[h], pmax);
+                float psum = 0.f;
 #pragma unroll
-                    for (int t = 0; t < 16; ++t) {
-                        float a = 0.f;
+                for (int j = 0; j < VPL; ++j) {
+                    const int idx = NV >= 32 ? lane * VPL + j : lane >> SH;
+                    const int t = idx % TOK;
+                    const float pe = t < nval ? expf(sv[j] - mloc) : 0.f;
+                    psum += pe;
+                    p_s[warp][t * G + idx / TOK] = pe;     // copies write the same value
+                }
 #pragma unroll
-                        for (int c = 0; c < DPL; ++c) a = fmaf(q[h][c], kr[t][c], a);
-                        part_s[h * 16 + t] = a;
-                    }
-            }
-            float sv[VPL];
-            transpose_reduce<NV>(part_s, sv, lane);
-            // entries held by this lane: index idx = lane*VPL + j (or lane/2 when NV == 16)
-            float pmax = -INFINITY;
-            int hh = 0;
-#pragma unroll
-            for (int j = 0; j < VPL; ++j) {
-                const int idx = NV >= 32 ? lane * VPL + j : lane >> 1;
-                hh = idx / 16;
-                const int t = idx % 16;
-                sv[j] = t < nval ? sv[j] * scale : -INFINITY;
-                pmax = fmaxf(pmax, sv[j]);
-            }
-#pragma unroll
-            for (int off = 1; off < GL; off <<= 1) pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, off));
-            float mloc = fmaxf(m[0], pmax);
-            // this lane's head is hh (all its entries share one head)
-#pragma unroll
-            for (int h = 0; h < G; ++h)
-                if (h == hh) mloc = fmaxf(m[h], pmax);
-            float psum = 0.f;
-#pragma unroll
-            for (int j = 0; j < VPL; ++j) {
-                const int idx = NV >= 32 ? lane * VPL + j : lane >> 1;
-                const int t = idx % 16;
-                const float pe = t < nval ? expf(sv[j] - mloc) : 0.f;
-                psum += pe;
-                p_s[warp][t * G + idx / 16] = pe;
-            }
-            // the sum over a head's tokens (GL lanes; for NV == 16 lane pairs hold copies)
-#pragma unroll
-            for (int off = NV >= 32 ? 1 : 2; off < GL; off <<= 1)
-                psum += __shfl_xor_sync(0xffffffffu, psum, off);
-#pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float mn = __shfl_sync(0xffffffffu, mloc, h * (NV >= 32 ? GL : 0));
-                const float sm = __shfl_sync(0xffffffffu, psum, h * (NV >= 32 ? GL : 0));
-                const float corr = expf(m[h] - mn);
-                l[h] = l[h] * corr + sm;
-#pragma unroll
-                for (int c = 0; c < DPL; ++c) o[h][c] *= corr;
-                m[h] = mn;
-            }
-            __syncwarp();
-#pragma unroll
-            for (int t = 0; t < 16; ++t) {
-                float vr[DPL];
-                if (dl && t < nval) ld_row<DPL>(vp + t * HD, vr);
-                else
-#pragma unroll
-                    for (int c = 0; c < DPL; ++c) vr[c] = 0.f;
+                for (int off = 1 << SH; off < GL; off <<= 1)
+                    psum += __shfl_xor_sync(0xffffffffu, psum, off);
 #pragma unroll
                 for (int h = 0; h < G; ++h) {
-                    const float p = p_s[warp][t * G + h];
+                    const float mn = __shfl_sync(0xffffffffu, mloc, h * GL);
+                    const float sm = __shfl_sync(0xffffffffu, psum, h * GL);
+                    const float corr = expf(m[h] - mn);
+                    l[h] = l[h] * corr + sm;
 #pragma unroll
-                    for (int c = 0; c < DPL; ++c) o[h][c] = fmaf(p, vr[c], o[h][c]);
+                    for (int c = 0; c < DPL; ++c) o[h][c] *= corr;
+                    m[h] = mn;
                 }
+                __syncwarp();
+#pragma unroll
+                for (int t = 0; t < TOK; ++t) {
+                    float vr[DPL];
+                    if (dl && t < nval) ld_row<DPL>(vp + t * HD, vr);
+                    else
+#pragma unroll
+                        for (int c = 0; c < DPL; ++c) vr[c] = 0.f;
+#pragma unroll
+                    for (int h = 0; h < G; ++h) {
+                        const float p = p_s[warp][t * G + h];
+#pragma unroll
+                        for (int c = 0; c < DPL; ++c) o[h][c] = fmaf(p, vr[c], o[h][c]);
+                    }
+                }
+                __syncwarp();
             }
-            __syncwarp();
             if (lane == 0) bar_arrive(&empty[s]);
         }
+    }
+    __syncthreads();                                  // ring drained: reuse it for the merge
+    if (warp < NW) {
 #pragma unroll
         for (int h = 0; h < G; ++h) {
+            float* rec = merge + ((size_t)warp * G + h) * (HD + 2);
             if (lane == 0) {
-                red_m[warp][h] = m[h];
-                red_l[warp][h] = l[h];
+                rec[0] = m[h];
+                rec[1] = l[h];
             }
             if (dl)
 #pragma unroll
-                for (int c = 0; c < DPL; ++c) red_o[warp][h][d0 + c] = o[h][c];
+                for (int c = 0; c < DPL; ++c) rec[2 + d0 + c] = o[h][c];
         }
     }
     __syncthreads();
@@ -335,20 +356,21 @@ __global__ void __launch_bounds__(32 * (NW + 1)) attn_chunk(
         const int h = e / HD, d = e % HD;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, red_m[w][h]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, merge[((size_t)w * G + h) * (HD + 2)]);
         float L = 0.f, O = 0.f;
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
-            const float f = red_m[w][h] == -INFINITY ? 0.f : expf(red_m[w][h] - M);
-            L += red_l[w][h] * f;
-            O += red_o[w][h][d] * f;
+            const float* rec = merge + ((size_t)w * G + h) * (HD + 2);
+            const float f = rec[0] == -INFINITY ? 0.f : expf(rec[0] - M);
+            L += rec[1] * f;
+            O += rec[2 + d] * f;
         }
-        float* rec = part + (((size_t)b * nq + kvh * G + h) * nchunk_max + chunk) * (HD + 2);
+        float* out = part + (((size_t)b * nq + kvh * G + h) * nchunk_max + chunk) * (HD + 2);
         if (d == 0) {
-            rec[0] = M;
-            rec[1] = L;
+            out[0] = M;
+            out[1] = L;
         }
-        rec[2 + d] = O;
+        out[2 + d] = O;
     }
 }
 
@@ -397,6 +419,8 @@ int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
     if (prepare) {
         cudaFuncSetAttribute(attn_chunk<HD, G, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)S::SMEM);
+        cudaFuncSetAttribute(attn_chunk<HD, G, KT>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         return 0;
     }
     const long ctas = (long)B * nkv * nchunk;
