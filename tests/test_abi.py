@@ -99,3 +99,14 @@ def test_gguf_loader_fills_description(sb, oracle):
         assert L0.attn_q - d.token_embd == p - e and L0.attn_q_dtype == dt
         m.close()
         sb.F["slate_gguf_model_close"](h)
+
+
+def test_integration_shim_links_against_reference(sb):
+    """slate_b200/shim compiled against slate's headers resolves every symbol
+    from the reference library and libslate_cuda.so."""
+    shim = os.path.join(ROOT, "oracle", "_ref", "libslate_shim.so")
+    if not os.path.exists(shim):
+        pytest.skip("integration shim not built (reference headers unavailable)")
+    out = subprocess.run(["ldd", "-r", shim], capture_output=True, text=True).stdout
+    assert "undefined symbol" not in out and "not found" not in out, out
+    assert hasattr(C.CDLL(shim), "slate_llama_batch_new")
