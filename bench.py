@@ -59,6 +59,8 @@ def parse():
                     help="reduce only for debugging; the benchmark workload is 32")
     ap.add_argument("--gemm-path", type=int, default=0,
                     help="0 auto (tcgen05, 3-pass hi/lo split), 1 CUDA cores, 2 tcgen05 single f16 pass")
+    ap.add_argument("--attn-path", type=int, default=0,
+                    help="0: tensor-core attention for f16 KV (mma.sync), 1: CUDA-core kernel")
     ap.add_argument("--e2e-steps", type=int, default=-1,
                     help="host-API steps for the e2e figure (default max(3, steps/2))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -249,7 +251,8 @@ def main():
     total_steps = args.warmup + args.steps
     ctx = contexts(args, n, rank, 3 * total_steps + 4)
     eng = sb.LlamaBatch(path, device=local, max_batch=n, max_slots=n, kv_dtype=kv,
-                        max_seq=cfg["max_seq"], gemm_path=args.gemm_path)
+                        max_seq=cfg["max_seq"], gemm_path=args.gemm_path,
+                        attn_path=args.attn_path)
     slots = np.array([eng.open() for _ in range(n)], np.int32)
     assert (slots >= 0).all(), sb.last_error()
     for s, c in zip(slots, ctx):
@@ -358,6 +361,8 @@ def main():
                    "global_batch": n * world, "seqs_per_gpu": n, "kv_dtype": args.kv,
                    "mean_ctx": float(ctx.mean()), "parallelism": f"replicas x{world}",
                    "gemm_path": {0: "tcgen05 3-pass", 1: "cuda-core f32", 2: "tcgen05 1-pass f16"}[args.gemm_path],
+                   "attn_path": ("mma.sync f16 hi/lo" if args.attn_path == 0 and args.kv == "f16"
+                                 else "cuda-core"),
                    "l2": "inputs larger than L2 (KV read per step >> 126 MB)"},
         "roofline": {"bound": "hbm", "kernel": "attn_partial+attn_combine (paged GQA attention)",
                      "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "GB/s",

@@ -164,7 +164,9 @@ typedef struct slate_cuda_opts {
     int64_t kv_pages;    /* pool size in 16-token pages (0 = from kv_bytes) */
     size_t kv_bytes;     /* pool budget (0 = 90% of free HBM after weights) */
     int use_graphs;      /* capture one CUDA graph per batch size (1 = yes) */
-    int gemm_path;       /* 0 auto, 1 CUDA-core kernels only */
+    int gemm_path;       /* 0 auto, 1 CUDA-core kernels only, 2 tensor cores 1-pass f16 */
+    int attn_path;       /* 0 auto (tensor cores for f16 KV where the shape allows),
+                            1 CUDA-core attention only */
 } slate_cuda_opts_t;
 
 typedef struct slate_llama_batch slate_llama_batch_t;

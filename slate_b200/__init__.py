@@ -52,7 +52,8 @@ class LlamaDesc(C.Structure):
 class CudaOpts(C.Structure):
     _fields_ = [("device", c_int), ("max_batch", c_int), ("max_slots", c_int),
                 ("kv_dtype", c_int), ("max_seq", c_int), ("kv_pages", c_int64),
-                ("kv_bytes", c_size), ("use_graphs", c_int), ("gemm_path", c_int)]
+                ("kv_bytes", c_size), ("use_graphs", c_int), ("gemm_path", c_int),
+                ("attn_path", c_int)]
 
 
 class SynthConfig(C.Structure):
@@ -153,9 +154,9 @@ class LlamaBatch:
     """Device-resident batch engine (slate_llama_batch_*) over one GGUF."""
 
     def __init__(self, gguf_path: str, *, device=0, max_batch=16, max_slots=0, kv_dtype=KV_F32,
-                 max_seq=0, kv_pages=0, kv_bytes=0, use_graphs=True, gemm_path=0):
+                 max_seq=0, kv_pages=0, kv_bytes=0, use_graphs=True, gemm_path=0, attn_path=0):
         self.opts = CudaOpts(device, max_batch, max_slots, kv_dtype, max_seq, kv_pages, kv_bytes,
-                             int(use_graphs), gemm_path)
+                             int(use_graphs), gemm_path, attn_path)
         self.h = F["slate_llama_batch_new_gguf"](gguf_path.encode(), C.byref(self.opts))
         if not self.h:
             raise RuntimeError(f"slate_llama_batch_new_gguf failed: {last_error()}")

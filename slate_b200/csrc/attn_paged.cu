@@ -467,13 +467,40 @@ int launch_kt(int prepare, int hd, int G, float* att, int ld_att, const float* q
     return -1;
 }
 
+int combine(int hd, const float* scratch, int B, int nq, const int32_t* row_pos, int nchunk,
+            float* att, int ld_att, cudaStream_t st) {
+    const unsigned grid = (unsigned)(((long)B * nq + 3) / 4);
+    switch (hd) {
+        case 64:
+            attn_combine<64><<<grid, 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att, ld_att);
+            return 0;
+        case 128:
+            attn_combine<128><<<grid, 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att, ld_att);
+            return 0;
+    }
+    return -1;
+}
+
 int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
              int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
-             const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
-             int layer, int kv_dtype, int max_seq, float* scratch, int* err, cudaStream_t st) {
+             const int32_t* page_table, int max_pages, const void* pool, const void* kvmap,
+             int64_t n_pages, int layer, int kv_dtype, int max_seq, float* scratch, int* err,
+             cudaStream_t st) {
     if (nkv < 1 || nq % nkv) return -1;
     const int G = nq / nkv;
     const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
+    if (sb_attention_mma_supported(nq, nkv, hd, kv_dtype)) {
+        if (prepare) {
+            const int rc = sb_attention_mma(1, nullptr, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr,
+                                            nullptr, 0, 0, 0, 0, nullptr, nullptr, 0);
+            if (rc) return rc;          // the CUDA-core kernel is prepared too (calls without a map)
+        } else if (kvmap) {
+            const int rc = sb_attention_mma(0, kvmap, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot,
+                                            page_table, max_pages, n_pages, layer, nchunk, scratch,
+                                            err, st);
+            return rc ? rc : combine(hd, scratch, B, nq, row_pos, nchunk, att, ld_att, st);
+        }
+    }
     return kv_dtype == SLATE_KV_F16
                ? launch_kt<__half>(prepare, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
                                    row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,
@@ -492,16 +519,16 @@ extern "C" size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int
 
 extern "C" int sb_attention_prepare(int nq, int nkv, int hd, int kv_dtype) {
     return dispatch(1, nullptr, 0, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr, 0,
-                    nullptr, 0, 0, kv_dtype, 0, nullptr, nullptr, 0);
+                    nullptr, nullptr, 0, 0, kv_dtype, 0, nullptr, nullptr, 0);
 }
 
 extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B,
                                   int nq, int nkv, int hd, const int32_t* row_pos,
                                   const int32_t* row_slot, const int32_t* page_table,
-                                  int max_pages, const void* pool, int64_t n_pages, int layer,
-                                  int kv_dtype, int max_seq, float* scratch, int* err,
-                                  cudaStream_t st) {
+                                  int max_pages, const void* pool, const void* kvmap,
+                                  int64_t n_pages, int layer, int kv_dtype, int max_seq,
+                                  float* scratch, int* err, cudaStream_t st) {
     if (B < 1 || !err) return -1;
     return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
-                    max_pages, pool, n_pages, layer, kv_dtype, max_seq, scratch, err, st);
+                    max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, scratch, err, st);
 }

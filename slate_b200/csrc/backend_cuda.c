@@ -156,10 +156,19 @@ static int be_attention_paged(float* out, const float* q, const int32_t* pos,
     err = (int*)(scr + nf);
     rc = sb_cuda_check(cudaMemsetAsync(err, 0, 4, g_stream), "memset");
     if (!rc && sb_attention_prepare(nq, nkv, hd, kv_dtype)) rc = -1;
+    /* f16 pools of supported shapes run the tensor-core kernel; its map spans
+     * layers [0, layer] of the pool */
+    unsigned char map[SB_KVMAP_BYTES];
+    const void* mapp = NULL;
+    const char* path = getenv("SLATE_CUDA_ATTN_PATH");     /* "1": CUDA-core kernel only */
+    if (!rc && sb_attention_mma_supported(nq, nkv, hd, kv_dtype) && !(path && path[0] == '1')) {
+        if (sb_attention_make_map(map, (void*)pool, n_pages, layer + 1, nkv, hd)) rc = -1;
+        else mapp = map;
+    }
     if (!rc)
         rc = fin(sb_attention_paged(out, nq * hd, q, nq * hd, B, nq, nkv, hd, pos, row_slot,
-                                    page_table, max_pages, pool, n_pages, layer, kv_dtype, max_seq,
-                                    scr, err, g_stream),
+                                    page_table, max_pages, pool, mapp, n_pages, layer, kv_dtype,
+                                    max_seq, scr, err, g_stream),
                  "attention_paged_gqa");
     if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, g_stream), "err");
     if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "attention_paged_gqa");

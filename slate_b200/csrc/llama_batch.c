@@ -53,6 +53,8 @@ struct slate_llama_batch {
     int kv_dtype, max_pages, max_slots;
     int64_t n_pages;
     void* pool;
+    unsigned char kvmap[SB_KVMAP_BYTES];   /* tensor map of the pool */
+    const void* kvmap_p;                   /* kvmap when the tensor-core attention runs */
     int32_t *pos, *page_table, *free_stack, *free_top, *status;
     /* activations */
     int max_batch, gemm_path, use_graphs;
@@ -230,7 +232,8 @@ static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
                              b->rope_cos, b->rope_sin, s);
         rc |= sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
                                  b->row_pos, b->row_slot, b->page_table, b->max_pages, b->pool,
-                                 b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch, b->tc_err, s);
+                                 b->kvmap_p, b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch,
+                                 b->tc_err, s);
         rc |= step_gemm(b, &ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, SB_EPI_ADD, b->sp_wo, s);
         rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, ly->ffn_norm, n, b->D, b->eps, s);
         rc |= step_gemm(b, &ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
@@ -514,6 +517,10 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
                           "memset"))
             goto fail;
         if (sb_init_free_list(b->free_stack, b->free_top, pages, b->stream)) goto fail;
+        if (o->attn_path != 1 && sb_attention_mma_supported(nq, nkv, hd, b->kv_dtype)) {
+            if (sb_attention_make_map(b->kvmap, b->pool, pages, L, nkv, hd)) goto fail;
+            b->kvmap_p = b->kvmap;
+        }
     }
     b->h_pos = (int*)calloc((size_t)b->max_slots, sizeof(int));
     b->h_open = (unsigned char*)calloc((size_t)b->max_slots, 1);
@@ -800,8 +807,8 @@ static int enqueue_kernel(slate_llama_batch_t* b, int kernel, int n, int layer, 
         case SLATE_PROF_ATTENTION:
             return sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
                                       b->row_pos, b->row_slot, b->page_table, b->max_pages,
-                                      b->pool, b->n_pages, layer, b->kv_dtype, b->max_seq,
-                                      b->scratch, b->tc_err, s);
+                                      b->pool, b->kvmap_p, b->n_pages, layer, b->kv_dtype,
+                                      b->max_seq, b->scratch, b->tc_err, s);
         case SLATE_PROF_QKV:
             return step_gemm(b, &ly->wqkv, b->xn, b->ld_x, n, scratch_y, b->ld_logits, SB_EPI_STORE,
                              b->sp_qkv, s);

@@ -94,11 +94,26 @@ size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int max_seq);
 /* Opts the (head_dim, group, dtype) kernel into its shared-memory size on the
  * current device; call outside stream capture before the first launch. */
 int sb_attention_prepare(int nq, int nkv, int hd, int kv_dtype);
+/* kvmap: NULL, or a tensor map of the pool from sb_attention_make_map(); with
+ * one, f16 pools of supported shapes take the tensor-core kernel. */
 int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
                        int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
                        const int32_t* page_table, int max_pages, const void* pool,
-                       int64_t n_pages, int layer, int kv_dtype, int max_seq, float* scratch,
-                       int* err, cudaStream_t st);
+                       const void* kvmap, int64_t n_pages, int layer, int kv_dtype, int max_seq,
+                       float* scratch, int* err, cudaStream_t st);
+
+/* Tensor-core attention for f16 pools (head_dim 64 or 128, at most 8 query
+ * heads per kv head).  The map is an opaque 128-byte CUtensorMap over the
+ * pool viewed as [layers][n_pages*2*nkv*16][hd] f16. */
+#define SB_KVMAP_BYTES 128
+int sb_attention_mma_supported(int nq, int nkv, int hd, int kv_dtype);
+int sb_attention_make_map(void* map, void* pool, int64_t n_pages, int layers, int nkv, int hd);
+/* Chunk stage only (partials into `part`, same records as the CUDA-core
+ * kernel); prepare != 0 sets the shared-memory attributes instead. */
+int sb_attention_mma(int prepare, const void* map, const float* qkv, int ld_qkv, int B, int nq,
+                     int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
+                     const int32_t* page_table, int max_pages, int64_t n_pages, int layer,
+                     int nchunk, float* part, int* err, cudaStream_t st);
 
 /* Fills positions [0, n) of one slot with deterministic pseudo-random K/V
  * (benchmark stand-in for a prefilled prompt), allocating its pages. */

@@ -63,7 +63,7 @@ def run_continuous(eng, requests, max_batch, rng):
             slots.append(a["slot"])
             toks.append(tok)
         rc, out, lg = eng.step(slots, toks, want_logits=True)
-        assert rc == 0, sb.last_error()
+        assert rc == 0, rc
         for i, r in enumerate(reqs):
             a, (prompt, n_new) = active[r], requests[r]
             a["fed"] += 1

@@ -223,3 +223,61 @@ def test_matmul_q4k_tensor_cores(be, oracle, sb, B, M, K, passes, tol):
     Wd = oracle.dequant_q4k(q, M * K).reshape(M, K).astype(np.float64)
     want = X.astype(np.float64) @ Wd.T
     assert scale_err(got, want) < tol
+
+
+def run_attention(be, monkeypatch, path, q, pool, table, pos, nq, nkv, hd, kv_dtype, layer, n_pages):
+    """attention_paged_gqa with the kernel picked by SLATE_CUDA_ATTN_PATH
+    ("0": tensor cores where the f16 shape allows, "1": CUDA cores)."""
+    monkeypatch.setenv("SLATE_CUDA_ATTN_PATH", path)
+    B = q.shape[0]
+    out = be.empty(B * nq * hd * 4)
+    rc = be.attention_paged_gqa(out, be.dev(q), be.dev(pos), be.dev(np.arange(B, dtype=np.int32)),
+                                be.dev(table), table.shape[1], be.dev(pool), n_pages, layer, B, nq,
+                                nkv, hd, kv_dtype)
+    assert rc == 0, be.sb.last_error()
+    return be.host(out, (B, nq * hd))
+
+
+@pytest.mark.parametrize("nq,nkv,hd", [(32, 8, 128), (8, 2, 64), (8, 8, 64), (16, 2, 128), (64, 8, 128)])
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+@pytest.mark.parametrize("path", ["0", "1"])
+def test_paged_attention_ignores_rows_past_context(be, oracle, monkeypatch, nq, nkv, hd, kv_dtype, path):
+    """Rows of a sequence's last page beyond its position hold stale bits in a
+    live pool; here they are NaN and must not reach the output (0 * NaN)."""
+    rng = np.random.default_rng(hd + nq + kv_dtype)
+    ctxs = [1, 7, 16, 33, 513, 1030]
+    layers, layer, n_pages = 2, 1, 160
+    pool, table, dense, _ = build_paged(rng, ctxs, layers, nkv, hd, n_pages, kv_dtype, layer)
+    for r, c in enumerate(ctxs):
+        if c % 16:
+            pool[:, table[r, c // 16], :, :, c % 16:, :] = np.nan
+    pos = np.array([c - 1 for c in ctxs], np.int32)
+    q = rng.normal(0, 1, (len(ctxs), nq * hd)).astype(np.float32)
+    got = run_attention(be, monkeypatch, path, q, pool, table, pos, nq, nkv, hd, kv_dtype, layer, n_pages)
+    assert np.isfinite(got).all()
+    for r in range(len(ctxs)):
+        Kd, Vd = dense[r]
+        want = oracle.attention_gqa(q[r], Kd, Vd, nq, nkv, hd)
+        assert scale_err(got[r], want) < 1e-5, (r, ctxs[r])
+
+
+@pytest.mark.parametrize("nq,nkv,hd", [(32, 8, 128), (32, 4, 64)])
+def test_paged_attention_kernels_agree_long_context(be, oracle, monkeypatch, nq, nkv, hd):
+    """f16 pool, contexts across several 512-token chunks: the tensor-core and
+    CUDA-core kernels both match the oracle on large-magnitude q (peaked
+    softmax) and small-magnitude q (flat softmax)."""
+    rng = np.random.default_rng(nq + hd)
+    ctxs = [2047, 2048, 3001, 4097]
+    layers, layer = 1, 0
+    n_pages = sum((c + 15) // 16 for c in ctxs) + 3
+    pool, table, dense, _ = build_paged(rng, ctxs, layers, nkv, hd, n_pages, 1, layer)
+    pos = np.array([c - 1 for c in ctxs], np.int32)
+    for sigma in (4.0, 1e-3):
+        q = rng.normal(0, sigma, (len(ctxs), nq * hd)).astype(np.float32)
+        outs = [run_attention(be, monkeypatch, p, q, pool, table, pos, nq, nkv, hd, 1, layer, n_pages)
+                for p in ("0", "1")]
+        for r in range(len(ctxs)):
+            Kd, Vd = dense[r]
+            want = oracle.attention_gqa(q[r], Kd, Vd, nq, nkv, hd)
+            for got in outs:
+                assert scale_err(got[r], want) < 1e-5, (sigma, r)

@@ -35,6 +35,12 @@ SHAPES = {
                                         theta_base=500000.0, seed=22),
                              ctx=[5, 900, 2500, 4300, 64, 1500, 3800, 4000, 2222],
                              kv=1, tol=2e-3),
+    # the same f16 cache through the CUDA-core attention kernel (attn_path 1)
+    "8b_2layers_f16kv_cuda_cores": dict(model=dict(n_layers=2, d_model=4096, ffn_hidden=14336,
+                                                   n_heads=32, n_kv_heads=8, vocab=128256,
+                                                   max_seq=4352, theta_base=500000.0, seed=22),
+                                        ctx=[5, 900, 2500, 4300, 64, 1500, 3800, 4000, 2222],
+                                        kv=1, tol=2e-3, attn=1),
     "mistral_1layer_f16kv": dict(model=dict(n_layers=1, d_model=4096, ffn_hidden=14336, n_heads=32,
                                             n_kv_heads=8, vocab=32000, max_seq=32896,
                                             theta_base=1000000.0, seed=23),
@@ -51,7 +57,8 @@ def test_real_shapes(sb, oracle, workdir, name):
         sb.synth_gguf(path, q4k=True, **mc)
     L, kvd = mc["n_layers"], mc["n_kv_heads"] * mc["d_model"] // mc["n_heads"]
     eng = sb.LlamaBatch(path, max_batch=16, max_slots=16, kv_dtype=spec["kv"],
-                        kv_pages=sum((c + 2 + 15) // 16 + 1 for c in spec["ctx"]))
+                        kv_pages=sum((c + 2 + 15) // 16 + 1 for c in spec["ctx"]),
+                        attn_path=spec.get("attn", 0))
     m = oracle.open(path)
     slots, sess = [], []
     for i, c in enumerate(spec["ctx"]):
