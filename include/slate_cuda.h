@@ -120,6 +120,26 @@ const slate_backend_cuda_t* slate_backend_cuda_create(int device);
  * calling thread ("" if none). */
 const char* slate_cuda_last_error(void);
 
+/* attention_paged_gqa for callers that cannot allocate device memory during
+ * the call (an allocator that has already given all free HBM to its KV pool;
+ * a latency-critical loop that must not enter the driver's allocator).  This
+ * entry point has no counterpart in the reference.  Same arguments, kernels
+ * and results as the vtable entry, plus the stream to run on (NULL = the
+ * legacy default stream, which the call synchronises before returning).
+ * Its scratch is one fixed device array per device of
+ * SLATE_CUDA_NOALLOC_SCRATCH_FLOATS floats (8 MiB); a call needs
+ * B * nq * ceil(max_pages * 16 / 512) * (hd + 2) of them and is rejected with
+ * -1 beyond that.  All calls on a device share the array, so calls that
+ * overlap on the GPU race: serialise them.  The first call on a device
+ * resolves the array's address (cudaGetSymbolAddress) with that device
+ * current; make it before any stream capture.  No cudaMalloc/cudaFree. */
+#define SLATE_CUDA_NOALLOC_SCRATCH_FLOATS (1u << 21)
+int slate_cuda_attention_paged_gqa_noalloc(float* out, const float* q, const int32_t* pos,
+                                           const int32_t* row_slot, const int32_t* page_table,
+                                           int max_pages, const void* kv_pool, int64_t n_pages,
+                                           int layer, int B, int nq, int nkv, int hd,
+                                           int kv_dtype, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* 2. Device-resident LLaMA batch engine                                     */
 /* ------------------------------------------------------------------------ */

@@ -87,6 +87,8 @@ EXPORTS = {
     "slate_backend_cuda": (P,),
     "slate_backend_cuda_create": (C.POINTER(BackendCuda), c_int),
     "slate_cuda_last_error": (C.c_char_p,),
+    "slate_cuda_attention_paged_gqa_noalloc": (c_int, P, P, P, P, P, c_int, P, c_int64, c_int, c_int,
+                                               c_int, c_int, c_int, c_int, P),
     "slate_llama_batch_new_desc": (P, C.POINTER(LlamaDesc), C.POINTER(CudaOpts)),
     "slate_llama_batch_new_gguf": (P, C.c_char_p, C.POINTER(CudaOpts)),
     "slate_llama_batch_free": (None, P),
