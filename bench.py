@@ -43,7 +43,12 @@ sys.path.insert(0, ROOT)
 CFG3 = dict(n_layers=32, d_model=4096, ffn_hidden=14336, n_heads=32, n_kv_heads=8, vocab=128256,
             max_seq=4352, theta_base=500000.0, rms_eps=1e-5)
 METRIC = "decode tok/s (box), LLaMA-3-8B-shape Q4_K, 256 ragged seqs; p50 step latency"
-PROFILE_TRAFFIC = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+# DRAM bytes (read + write) per algorithmic byte of one attn_chunk_mma launch, from
+# an ncu capture of 32 rows at the 8B shape (profiles/attn_chunk_mma_8b_b32.md:
+# 300.40 MB read + 6.63 MB written for 300.74 MB of K/V, q and output).  Traffic
+# scales with the K/V tokens read, so the full launch's traffic is this ratio times
+# its algorithmic bytes.
+ATTN_MMA_TRAFFIC_RATIO = 1.0209
 
 
 def parse():
@@ -315,11 +320,8 @@ def main():
         peak, peak_src = 6650.0, "fallback"
     achieved = attn_bytes / (kt["attention"] / 1000.0) / 1e9
     traffic = None
-    try:
-        tr = json.load(open(PROFILE_TRAFFIC))
-        traffic = tr.get("attention_bytes_per_launch")
-    except Exception:
-        pass
+    if args.kv == "f16" and args.attn_path == 0:
+        traffic = ATTN_MMA_TRAFFIC_RATIO * attn_bytes
     step_s = tot_ms / 1000.0 / args.steps
 
     # end to end through the host-buffer API: H2D slots+tokens, D2H greedy tokens
@@ -364,7 +366,9 @@ def main():
                    "attn_path": ("mma.sync f16 hi/lo" if args.attn_path == 0 and args.kv == "f16"
                                  else "cuda-core"),
                    "l2": "inputs larger than L2 (KV read per step >> 126 MB)"},
-        "roofline": {"bound": "hbm", "kernel": "attn_partial+attn_combine (paged GQA attention)",
+        "roofline": {"bound": "hbm",
+                     "kernel": ("attn_chunk_mma+attn_combine" if args.kv == "f16" and args.attn_path == 0
+                                else "attn_chunk+attn_combine") + " (paged GQA attention, one layer)",
                      "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": kt["attention"]},
