@@ -43,6 +43,14 @@ sys.path.insert(0, ROOT)
 CFG3 = dict(n_layers=32, d_model=4096, ffn_hidden=14336, n_heads=32, n_kv_heads=8, vocab=128256,
             max_seq=4352, theta_base=500000.0, rms_eps=1e-5)
 METRIC = "decode tok/s (box), LLaMA-3-8B-shape Q4_K, 256 ragged seqs; p50 step latency"
+# 70B shape, tensor parallel; prompts U[256, 2048] + 256 tokens
+CFG5 = dict(n_layers=80, d_model=8192, ffn_hidden=28672, n_heads=64, n_kv_heads=8, vocab=128256,
+            max_seq=2368, theta_base=500000.0, rms_eps=1e-5)
+METRIC70 = "decode tok/s (box), LLaMA-3-70B-shape Q4_K tensor-parallel, 512 ragged seqs per TP group"
+MODELS = {"8b": dict(cfg=CFG3, metric=METRIC, batch=256, prompt=(128, 4096), period=0,
+                     workload="llama3-8b-shape q4k continuous-batching decode (BASELINE config 3)"),
+          "70b": dict(cfg=CFG5, metric=METRIC70, batch=512, prompt=(256, 2048), period=8,
+                      workload="llama3-70b-shape q4k tensor-parallel decode (BASELINE config 5)")}
 # DRAM bytes (read + write) per algorithmic byte of one attn_chunk_mma launch, from
 # an ncu capture of 32 rows at the 8B shape (profiles/attn_chunk_mma_8b_b32.md:
 # 300.40 MB read + 6.63 MB written for 300.74 MB of K/V, q and output).  Traffic
@@ -58,14 +66,21 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
-    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--model", default="8b", choices=list(MODELS),
+                    help="8b: the headline (config 3, replicas); 70b: config 5 with --tp")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel ranks per model replica (70b: 2, 4 or 8)")
+    ap.add_argument("--batch", type=int, default=0, help="sequences per replica (0: the config's)")
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--layers", type=int, default=CFG3["n_layers"],
-                    help="reduce only for debugging; the benchmark workload is 32")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="reduce only for debugging; 0 = the config's (32 for 8b, 80 for 70b)")
     ap.add_argument("--gemm-path", type=int, default=0,
                     help="0 auto (tcgen05, 3-pass hi/lo split), 1 CUDA cores, 2 tcgen05 single f16 pass")
     ap.add_argument("--attn-path", type=int, default=0,
                     help="0: tensor-core attention for f16 KV (mma.sync), 1: CUDA-core kernel")
+    ap.add_argument("--max-ctx", type=int, default=0,
+                    help="cap every context (profiling captures of the GEMMs on a small device "
+                         "footprint; 0 = the config's distribution)")
     ap.add_argument("--e2e-steps", type=int, default=-1,
                     help="host-API steps for the e2e figure (default max(3, steps/2))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -74,8 +89,8 @@ def parse():
 
 
 def model_path(args, cfg) -> str:
-    tag = f"slate_b200_cfg3_L{cfg['n_layers']}_s{args.seed}.gguf"
-    need = 9 << 30
+    tag = f"slate_b200_{args.model}_L{cfg['n_layers']}_s{args.seed}.gguf"
+    need = (9 << 30) if args.model == "8b" else (60 << 30)
     for d in (os.environ.get("SLATE_BENCH_DIR"), "/dev/shm", "/tmp"):
         if d and os.path.isdir(d) and shutil.disk_usage(d).free > need:
             return os.path.join(d, tag)
@@ -87,17 +102,34 @@ def ensure_model(args, cfg, rank, barrier) -> str:
     path = model_path(args, cfg)
     if int(os.environ.get("LOCAL_RANK", "0")) == 0 and not os.path.exists(path):
         tmp = path + f".{os.getpid()}.tmp"
-        sb.synth_gguf(tmp, q4k=True, seed=args.seed, **cfg)
+        # the 70B file repeats a period of 8 distinct random layers (written in
+        # about a minute instead of ten); the engine still holds every layer
+        sb.synth_gguf(tmp, q4k=True, seed=args.seed, layer_period=MODELS[args.model]["period"],
+                      **cfg)
         os.rename(tmp, path)
     barrier()
     return path
 
 
-def contexts(args, n, rank, steps):
-    rng = np.random.default_rng(args.seed * 1000 + rank)
-    prompt = rng.integers(128, 4097, n)
+def tp_group_id(dist, world, tp, rank, make_id):
+    """The NCCL id of this rank's tensor-parallel group (ranks [g*tp, g*tp+tp)):
+    made by the group's first rank, shared with an all-gather over all ranks."""
+    mine = make_id() if rank % tp == 0 else None
+    ids = [None] * world
+    dist.all_gather_object(ids, mine)
+    return ids[(rank // tp) * tp]
+
+
+def contexts(args, cfg, n, replica, steps):
+    """Prompt U[lo, hi] plus U[0, 256) already-decoded tokens per sequence."""
+    lo, hi = MODELS[args.model]["prompt"]
+    rng = np.random.default_rng(args.seed * 1000 + replica)
+    prompt = rng.integers(lo, hi + 1, n)
     done = rng.integers(0, 256, n)
-    return np.minimum(prompt + done, CFG3["max_seq"] - steps - 1).astype(np.int64)
+    cap = cfg["max_seq"] - steps - 1
+    if args.max_ctx:
+        cap = min(cap, args.max_ctx)
+    return np.minimum(prompt + done, cap).astype(np.int64)
 
 
 class ClockSampler:
@@ -206,11 +238,23 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    cfg = dict(CFG3)
-    cfg["n_layers"] = args.layers
+    spec = MODELS[args.model]
+    cfg = dict(spec["cfg"])
+    if args.layers:
+        cfg["n_layers"] = args.layers
+    if not args.batch:
+        args.batch = spec["batch"]
+    tp = max(1, args.tp)
+    if world % tp:
+        raise SystemExit(f"--tp {tp} must divide the {world} ranks")
+    replica, tp_rank = rank // tp, rank % tp
 
     if args.impl == "reference":
         if rank != 0:
+            return 0
+        if args.model != "8b":
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference CPU arm is timed on the 8b headline config only"}))
             return 0
         import oracle as O
         if not O.Reference.available():
@@ -254,10 +298,11 @@ def main():
     kv = sb.KV_F16 if args.kv == "f16" else sb.KV_F32
     n = args.batch
     total_steps = args.warmup + args.steps
-    ctx = contexts(args, n, rank, 3 * total_steps + 4)
+    ctx = contexts(args, cfg, n, replica, 3 * total_steps + 4)
+    tp_id = tp_group_id(dist, world, tp, rank, sb.tp_unique_id) if tp > 1 else b""
     eng = sb.LlamaBatch(path, device=local, max_batch=n, max_slots=n, kv_dtype=kv,
                         max_seq=cfg["max_seq"], gemm_path=args.gemm_path,
-                        attn_path=args.attn_path)
+                        attn_path=args.attn_path, tp_size=tp, tp_rank=tp_rank, tp_id=tp_id)
     slots = np.array([eng.open() for _ in range(n)], np.int32)
     assert (slots >= 0).all(), sb.last_error()
     for s, c in zip(slots, ctx):
@@ -265,7 +310,7 @@ def main():
         assert rc == 0, (rc, sb.last_error())
     stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
     d_slots = torch.tensor(slots, device="cuda")
-    rng = np.random.default_rng(args.seed + rank)
+    rng = np.random.default_rng(args.seed + replica)     # one token stream per TP group
     d_tok = [torch.tensor(rng.integers(0, cfg["vocab"], n).astype(np.int32), device="cuda"),
              torch.zeros(n, dtype=torch.int32, device="cuda")]
 
@@ -296,7 +341,8 @@ def main():
         t = torch.tensor([tot_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         tot_ms = float(t.item())
-    value = n * world * args.steps / (tot_ms / 1000.0)
+    replicas = world // tp
+    value = n * replicas * args.steps / (tot_ms / 1000.0)
 
     # per-kernel timing of the dominant kernels on the same state and stream
     layer = cfg["n_layers"] // 2
@@ -304,12 +350,15 @@ def main():
           [("attention", sb.PROF_ATTENTION), ("qkv", sb.PROF_QKV), ("wo", sb.PROF_WO),
            ("gate_up", sb.PROF_GATE_UP), ("down", sb.PROF_DOWN), ("lm_head", sb.PROF_LM_HEAD)]}
     esz = 2 if kv == sb.KV_F16 else 4
-    hd, nkv, L, D, F, V = 128, 8, cfg["n_layers"], 4096, 14336, cfg["vocab"]
+    # per-rank shares (tp = 1: the whole model)
+    D, L, V = cfg["d_model"], cfg["n_layers"], cfg["vocab"]
+    hd = D // cfg["n_heads"]
+    nq, nkv, F = cfg["n_heads"] // tp, cfg["n_kv_heads"] // tp, cfg["ffn_hidden"] // tp
     ctx_now = ctx + total_steps                        # contexts seen by the profiled launch
-    attn_bytes = float(ctx_now.sum()) * 2 * nkv * hd * esz + n * 32 * hd * 4 * 3
+    attn_bytes = float(ctx_now.sum()) * 2 * nkv * hd * esz + n * nq * hd * 4 * 3
     q4k = 144 / 256
-    w_layer = (D * (D + 2 * nkv * hd) + D * D + 3 * D * F) * q4k
-    head = V * D * 4
+    w_layer = (D * (nq + 2 * nkv) * hd + nq * hd * D + 3 * D * F) * q4k
+    head = V // tp * D * 4
     kv_read_step = float((ctx + total_steps - args.steps // 2).sum()) * 2 * nkv * hd * esz * L
     step_bytes = w_layer * L + head + kv_read_step + n * 2 * nkv * hd * esz * L
     peaks = {}
@@ -338,10 +387,10 @@ def main():
         t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = n * world * e2e_steps / e2e_s if e2e_steps else None
+    e2e = n * replicas * e2e_steps / e2e_s if e2e_steps else None
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and args.model == "8b" and not args.no_cpu_baseline:
         import oracle as O
         if O.Reference.available():
             cpu = reference_cpu(path, cfg, args.cpu_seconds)
@@ -354,14 +403,15 @@ def main():
     if rank != 0:
         return 0
     line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "metric": spec["metric"], "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
         "p50_step_ms": float(np.median(step_ms)), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "llama3-8b-shape q4k continuous-batching decode (BASELINE config 3)",
-                   "model": "llama3-8b-shape random N(0,0.02) Q4_K", "layers": cfg["n_layers"],
-                   "global_batch": n * world, "seqs_per_gpu": n, "kv_dtype": args.kv,
-                   "mean_ctx": float(ctx.mean()), "parallelism": f"replicas x{world}",
+        "config": {"workload": spec["workload"],
+                   "model": f"llama3-{args.model}-shape random N(0,0.02) Q4_K", "layers": cfg["n_layers"],
+                   "global_batch": n * replicas, "seqs_per_replica": n, "kv_dtype": args.kv,
+                   "mean_ctx": float(ctx.mean()),
+                   "parallelism": f"replicas x{replicas}" + (f", tensor parallel {tp}" if tp > 1 else ""),
                    "gemm_path": {0: "tcgen05 3-pass", 1: "cuda-core f32", 2: "tcgen05 1-pass f16"}[args.gemm_path],
                    "attn_path": ("mma.sync f16 hi/lo" if args.attn_path == 0 and args.kv == "f16"
                                  else "cuda-core"),

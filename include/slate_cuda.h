@@ -187,7 +187,24 @@ typedef struct slate_cuda_opts {
     int gemm_path;       /* 0 auto, 1 CUDA-core kernels only, 2 tensor cores 1-pass f16 */
     int attn_path;       /* 0 auto (tensor cores for f16 KV where the shape allows),
                             1 CUDA-core attention only */
+    /* Tensor parallelism (the 70B plan): tp_size ranks, one process or thread
+     * per GPU, each creating its engine with its tp_rank and the same tp_id
+     * (from slate_cuda_tp_unique_id on one rank).  Wq/Wk/Wv and gate/up are
+     * split by rows (heads / FFN units), Wo and down by columns with an
+     * all-reduce(sum) of the [n, d_model] activations after each, the LM head
+     * by vocabulary rows with a gathered (max, index) per row for the greedy
+     * token.  Needs n_kv_heads, vocab and ffn_hidden / 256 divisible by
+     * tp_size.  All ranks must make the same calls in the same order (steps,
+     * opens, closes); logits are gathered when any is requested.  tp_size 0
+     * or 1 = one GPU. */
+    int tp_size;
+    int tp_rank;
+    unsigned char tp_id[128];
 } slate_cuda_opts_t;
+
+/* A fresh NCCL unique id (128 bytes) for a tensor-parallel group: create it on
+ * one rank and hand it to every rank's slate_cuda_opts_t.tp_id. */
+int slate_cuda_tp_unique_id(void* out, size_t n);
 
 typedef struct slate_llama_batch slate_llama_batch_t;
 
@@ -310,6 +327,10 @@ typedef struct slate_synth_config {
     int tied_output;      /* 1: omit output.weight */
     uint64_t seed;
     int n_threads;        /* 0 = all online CPUs */
+    int layer_period;     /* 0: every layer drawn independently; p > 0: layer l
+                             repeats the weights of layer l % p (a file of a
+                             large model written in a fraction of the time;
+                             the engine still holds one copy per layer) */
 } slate_synth_config_t;
 /* Writes a LLaMA GGUF with N(0, 0.02) weights (counter-based, deterministic
  * in seed), unit norm gains, f32 embedding/head.  Returns 0 or <0. */

@@ -53,14 +53,15 @@ class CudaOpts(C.Structure):
     _fields_ = [("device", c_int), ("max_batch", c_int), ("max_slots", c_int),
                 ("kv_dtype", c_int), ("max_seq", c_int), ("kv_pages", c_int64),
                 ("kv_bytes", c_size), ("use_graphs", c_int), ("gemm_path", c_int),
-                ("attn_path", c_int)]
+                ("attn_path", c_int), ("tp_size", c_int), ("tp_rank", c_int),
+                ("tp_id", C.c_ubyte * 128)]
 
 
 class SynthConfig(C.Structure):
     _fields_ = [(n, c_int) for n in ("n_layers", "d_model", "ffn_hidden", "n_heads", "n_kv_heads",
                                      "vocab", "max_seq")] + [
         ("theta_base", c_float), ("rms_eps", c_float), ("q4k", c_int), ("tied_output", c_int),
-        ("seed", c_u64), ("n_threads", c_int)]
+        ("seed", c_u64), ("n_threads", c_int), ("layer_period", c_int)]
 
 
 class BackendBase(C.Structure):
@@ -87,6 +88,7 @@ EXPORTS = {
     "slate_backend_cuda": (P,),
     "slate_backend_cuda_create": (C.POINTER(BackendCuda), c_int),
     "slate_cuda_last_error": (C.c_char_p,),
+    "slate_cuda_tp_unique_id": (c_int, P, c_size),
     "slate_cuda_attention_paged_gqa_noalloc": (c_int, P, P, P, P, P, c_int, P, c_int64, c_int, c_int,
                                                c_int, c_int, c_int, c_int, P),
     "slate_llama_batch_new_desc": (P, C.POINTER(LlamaDesc), C.POINTER(CudaOpts)),
@@ -143,22 +145,35 @@ def quantize_q4k(w: np.ndarray) -> np.ndarray:
 
 def synth_gguf(path: str, *, n_layers, d_model, ffn_hidden, n_heads, n_kv_heads, vocab, max_seq,
                theta_base=10000.0, rms_eps=1e-5, q4k=True, tied_output=False, seed=0,
-               n_threads=0) -> None:
+               n_threads=0, layer_period=0) -> None:
     """Writes a synthetic LLaMA GGUF (N(0,0.02) weights, Slate Q4_K layout)."""
     cfg = SynthConfig(n_layers, d_model, ffn_hidden, n_heads, n_kv_heads, vocab, max_seq,
-                      theta_base, rms_eps, int(q4k), int(tied_output), seed, n_threads)
+                      theta_base, rms_eps, int(q4k), int(tied_output), seed, n_threads,
+                      layer_period)
     rc = F["slate_synth_llama_gguf"](path.encode(), C.byref(cfg))
     if rc:
         raise OSError(f"slate_synth_llama_gguf({path}) rc={rc}")
+
+
+def tp_unique_id() -> bytes:
+    """128-byte id for a tensor-parallel group (slate_cuda_tp_unique_id)."""
+    buf = C.create_string_buffer(128)
+    rc = F["slate_cuda_tp_unique_id"](buf, 128)
+    if rc:
+        raise RuntimeError(f"slate_cuda_tp_unique_id rc={rc}: {last_error()}")
+    return buf.raw
 
 
 class LlamaBatch:
     """Device-resident batch engine (slate_llama_batch_*) over one GGUF."""
 
     def __init__(self, gguf_path: str, *, device=0, max_batch=16, max_slots=0, kv_dtype=KV_F32,
-                 max_seq=0, kv_pages=0, kv_bytes=0, use_graphs=True, gemm_path=0, attn_path=0):
+                 max_seq=0, kv_pages=0, kv_bytes=0, use_graphs=True, gemm_path=0, attn_path=0,
+                 tp_size=0, tp_rank=0, tp_id=b""):
         self.opts = CudaOpts(device, max_batch, max_slots, kv_dtype, max_seq, kv_pages, kv_bytes,
-                             int(use_graphs), gemm_path, attn_path)
+                             int(use_graphs), gemm_path, attn_path, tp_size, tp_rank)
+        if tp_id:
+            C.memmove(self.opts.tp_id, bytes(tp_id), min(len(tp_id), 128))
         self.h = F["slate_llama_batch_new_gguf"](gguf_path.encode(), C.byref(self.opts))
         if not self.h:
             raise RuntimeError(f"slate_llama_batch_new_gguf failed: {last_error()}")

@@ -281,6 +281,30 @@ __global__ void epilogue_kernel(const float* logits, int ldl, int V, const int32
     }
 }
 
+// Tensor parallelism: each rank holds a vocabulary slice [v0, v0 + V) of the LM
+// head; it reduces its logits to one (max, global index) pair per row, the pairs
+// of all ranks are gathered, and every rank picks the same winner: the larger
+// value, ties to the lower global index -- the first maximum over the whole
+// vocabulary, as sampling.c:14-18 takes it.
+struct sb_vi { float v; int i; };
+__global__ void argmax_pairs_kernel(const float* logits, int ldl, int V, int v0, sb_vi* pairs) {
+    float v;
+    int i;
+    block_argmax(logits + (size_t)blockIdx.x * ldl, V, v, i);
+    if (threadIdx.x == 0) pairs[blockIdx.x] = sb_vi{v, v0 + i};
+}
+__global__ void tp_epilogue_kernel(const sb_vi* all, int T, int B, const int32_t* row_slot,
+                                   const int32_t* row_pos, int32_t* pos, const int32_t* status,
+                                   int32_t* out_tokens) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= B) return;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int t = 0; t < T; ++t) am_merge(bv, bi, all[(size_t)t * B + r].v, all[(size_t)t * B + r].i);
+    if (out_tokens) out_tokens[r] = bi == 0x7fffffff ? 0 : bi;
+    if (*status == 0 && row_pos[r] >= 0) pos[row_slot[r]] = row_pos[r] + 1;
+}
+
 __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z += 0x9e3779b97f4a7c15ull;
     z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
@@ -442,6 +466,22 @@ extern "C" int sb_step_prologue(const int32_t* slots, const int32_t* tokens, int
                                        row_pos, row_slot, status);
     return 0;
 }
+extern "C" int sb_argmax_pairs(const float* logits, int ldl, int V, int B, int v0, void* pairs,
+                               cudaStream_t st) {
+    if (B < 1 || V < 1) return -1;
+    argmax_pairs_kernel<<<B, 512, 0, st>>>(logits, ldl, V, v0, (sb_vi*)pairs);
+    return 0;
+}
+
+extern "C" int sb_tp_epilogue(const void* all_pairs, int T, int B, const int32_t* row_slot,
+                              const int32_t* row_pos, int32_t* pos, const int32_t* status,
+                              int32_t* out_tokens, cudaStream_t st) {
+    if (B < 1 || T < 1) return -1;
+    tp_epilogue_kernel<<<(B + 127) / 128, 128, 0, st>>>((const sb_vi*)all_pairs, T, B, row_slot,
+                                                          row_pos, pos, status, out_tokens);
+    return 0;
+}
+
 extern "C" int sb_step_epilogue(const float* logits, int ldl, int V, int B,
                                      const int32_t* row_slot, const int32_t* row_pos, int32_t* pos,
                                      const int32_t* status, int32_t* out_tokens, cudaStream_t st) {

@@ -78,6 +78,13 @@ struct slate_llama_batch {
     int* tc_err;
     int sp_qkv, sp_wo, sp_gu, sp_dn;
     sb_tc_weight head_tc;          /* f32 LM head as an f16 pair (hi set when used) */
+    sb_tc_operand op_a;            /* attention output, K = nq*hd (tensor parallel: local heads) */
+    /* tensor parallelism: nq, nkv, F above are this rank's shares, V the full
+     * vocabulary of which the LM head holds rows [v0, v0 + V_l) */
+    int tp, rank, V_l, v0, Dq;     /* Dq = nq * hd (local) */
+    void* comm;                    /* NCCL communicator (tp > 1) */
+    void *pairs, *pairs_all;       /* per-row (max, index) of this rank / of all ranks */
+    float* logits_all;             /* [tp][max_batch][ld_logits], gathered on request */
 };
 
 /* Rows from which a Q4_K GEMM runs on the tensor cores (below: CUDA cores). */
@@ -91,7 +98,8 @@ static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X,
         return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, &b->op_d, n, Y, ldy, epi, b->tc_err, s);
     }
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
-        const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d : &b->op_f;
+        const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
+                                  : W->K == b->op_f.K ? &b->op_f : &b->op_a;
         int rc = sb_tc_split(X, ldx, n, op, s);
         return rc ? rc : sb_tc_gemm(W, op, n, b->tc_passes, splits, b->tc_ws, Y, ldy, epi,
                                     b->tc_err, s);
@@ -114,8 +122,10 @@ static void* dalloc(slate_llama_batch_t* b, size_t bytes) {
 
 /* ---- weight packing ------------------------------------------------------ */
 
-/* Source rows of one logical matrix: `rows` rows of length K, dtype 0|18. */
-typedef struct { const void* p; int dtype; int rows; } src_part;
+/* Source rows of one logical matrix: rows [row0, row0 + rows) of a source
+ * matrix with src_k columns, dtype 0|18, of which columns [k0, k0 + K) are
+ * taken (a Q4_K column slice starts and ends on 256-column super-blocks). */
+typedef struct { const void* p; int dtype; int rows; int row0; int src_k; int k0; } src_part;
 
 static size_t q4k_row_bytes(int K) { return (size_t)(K / 256) * 144; }
 
@@ -164,11 +174,13 @@ static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, cons
     out->ldw = all_q4k ? 0 : round_up(K, 128);
     const size_t row_bytes = all_q4k ? q4k_row_bytes(K) : (size_t)out->ldw * 4;
     const size_t bytes = row_bytes * (size_t)M_pad;
-    if (nparts == 1 && !interleave64 && (all_q4k || (parts[0].dtype == 0 && out->ldw == K))) {
+    if (nparts == 1 && !interleave64 && parts[0].src_k == K &&
+        (all_q4k || (parts[0].dtype == 0 && out->ldw == K))) {
         /* already in the device layout: copy rows straight from the source */
         unsigned char* dptr = (unsigned char*)dalloc(b, bytes);
         if (!dptr) return -5;
-        SB_CU(cudaMemcpy(dptr, parts[0].p, row_bytes * (size_t)M, cudaMemcpyHostToDevice));
+        SB_CU(cudaMemcpy(dptr, (const unsigned char*)parts[0].p + (size_t)parts[0].row0 * row_bytes,
+                         row_bytes * (size_t)M, cudaMemcpyHostToDevice));
         if (M_pad > M) SB_CU(cudaMemset(dptr + row_bytes * (size_t)M, 0, row_bytes * (size_t)(M_pad - M)));
         out->data = dptr;
         return 0;
@@ -182,14 +194,16 @@ static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, cons
     /* destination row of source row r of part i */
     for (int i = 0, base = 0; i < nparts; ++i) {
         const src_part* sp = &parts[i];
-        const size_t src_row = sp->dtype == 18 ? q4k_row_bytes(K) : (size_t)K * 4;
+        const size_t src_row = sp->dtype == 18 ? q4k_row_bytes(sp->src_k) : (size_t)sp->src_k * 4;
+        const size_t col0 = sp->dtype == 18 ? q4k_row_bytes(sp->k0) : (size_t)sp->k0 * 4;
         for (int r = 0; r < sp->rows; ++r) {
             int dr;
             if (interleave64) dr = (r / 64) * 128 + (i ? 64 : 0) + r % 64;
             else dr = base + r;
-            const unsigned char* s = (const unsigned char*)sp->p + (size_t)r * src_row;
+            const unsigned char* s =
+                (const unsigned char*)sp->p + (size_t)(sp->row0 + r) * src_row + col0;
             unsigned char* d = h + (size_t)dr * row_bytes;
-            if (all_q4k) memcpy(d, s, src_row);
+            if (all_q4k) memcpy(d, s, q4k_row_bytes(K));
             else if (sp->dtype == 0) memcpy(d, s, (size_t)K * 4);
             else sb_q4k_dequant_rows((float*)d, s, 1, K);
         }
@@ -220,6 +234,10 @@ static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
     const int32_t* slots = b->d_io;
     const int32_t* toks = b->d_io + b->max_batch;
     int32_t* out = b->d_io + 2 * b->max_batch;
+    /* Wo and down add into the residual stream; tensor parallel ranks hold
+     * partial sums that are all-reduced into it, with rank 0 alone adding the
+     * residual itself */
+    const int res_epi = b->tp > 1 && b->rank != 0 ? SB_EPI_STORE : SB_EPI_ADD;
     rc |= sb_step_prologue(slots, toks, n, b->pos, b->page_table, b->max_pages, b->free_stack,
                            b->free_top, b->max_slots, b->max_seq, b->V, b->emb, b->D, b->x,
                            b->ld_x, b->row_pos, b->row_slot, b->status, s);
@@ -234,15 +252,24 @@ static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
                                  b->row_pos, b->row_slot, b->page_table, b->max_pages, b->pool,
                                  b->kvmap_p, b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch,
                                  b->tc_err, s);
-        rc |= step_gemm(b, &ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, SB_EPI_ADD, b->sp_wo, s);
+        rc |= step_gemm(b, &ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, res_epi, b->sp_wo, s);
+        if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, b->x, (size_t)n * b->ld_x, s);
         rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, ly->ffn_norm, n, b->D, b->eps, s);
         rc |= step_gemm(b, &ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
-        rc |= step_gemm(b, &ly->wdown, b->h, b->ld_h, n, b->x, b->ld_x, SB_EPI_ADD, b->sp_dn, s);
+        rc |= step_gemm(b, &ly->wdown, b->h, b->ld_h, n, b->x, b->ld_x, res_epi, b->sp_dn, s);
+        if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, b->x, (size_t)n * b->ld_x, s);
     }
     rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, b->out_norm, n, b->D, b->eps, s);
     rc |= step_gemm(b, &b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE, 1, s);
-    rc |= sb_step_epilogue(b->logits, b->ld_logits, b->V, n, b->row_slot, b->row_pos, b->pos,
-                           b->status, out, s);
+    if (b->tp > 1) {
+        rc |= sb_argmax_pairs(b->logits, b->ld_logits, b->V_l, n, b->v0, b->pairs, s);
+        rc |= sb_tp_allgather(b->comm, b->pairs, b->pairs_all, (size_t)n * 8, s);
+        rc |= sb_tp_epilogue(b->pairs_all, b->tp, n, b->row_slot, b->row_pos, b->pos, b->status,
+                             out, s);
+    } else {
+        rc |= sb_step_epilogue(b->logits, b->ld_logits, b->V, n, b->row_slot, b->row_pos, b->pos,
+                               b->status, out, s);
+    }
     if (rc) {
         sb_set_error("kernel launch rejected its arguments");
         return -1;
@@ -250,9 +277,26 @@ static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
     return sb_cuda_check(cudaGetLastError(), "step launch");
 }
 
+/* Kernel launches step_gemm makes for (W, n rows, epilogue, splits). */
+static int gemm_launches(const slate_llama_batch_t* b, const sb_matrix* W, int n, int epi,
+                         int splits) {
+    if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return 2;   /* split + GEMM */
+    if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
+        return 2 + (splits == 1 && epi != SB_EPI_SILU ? 0 : 1);               /* + finish */
+    return 1;
+}
+
 int slate_llama_batch_launches_per_step(const slate_llama_batch_t* b, int n) {
-    (void)n;
-    return b ? 4 + 9 * b->L : 0;
+    if (!b || n < 1) return 0;
+    const sb_layer* l0 = &b->layers[0];
+    const int res_epi = b->tp > 1 && b->rank != 0 ? SB_EPI_STORE : SB_EPI_ADD;
+    const int per_layer = 2 /* rmsnorm x2 */ + 1 /* rope + append */ + 2 /* attention */ +
+                          gemm_launches(b, &l0->wqkv, n, SB_EPI_STORE, b->sp_qkv) +
+                          gemm_launches(b, &l0->wo, n, res_epi, b->sp_wo) +
+                          gemm_launches(b, &l0->wgu, n, SB_EPI_SILU, b->sp_gu) +
+                          gemm_launches(b, &l0->wdown, n, res_epi, b->sp_dn);
+    return 1 /* prologue */ + b->L * per_layer + 1 /* final rmsnorm */ +
+           gemm_launches(b, &b->lm_head, n, SB_EPI_STORE, 1) + (b->tp > 1 ? 2 : 1);
 }
 
 /* Runs the step for n rows whose metadata is already in d_io. */
@@ -288,6 +332,7 @@ void slate_llama_batch_free(slate_llama_batch_t* b) {
         free(b->graphs);
     }
     sb_tc_free_weight(&b->head_tc);
+    if (b->comm) sb_tp_destroy(b->comm);      /* after the graphs that hold its collectives */
     for (int i = 0; i < b->n_allocs; ++i) cudaFree(b->allocs[i]);
     free(b->allocs);
     if (b->h_io) cudaFreeHost(b->h_io);
@@ -326,12 +371,29 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         sb_set_error("max_batch %d out of range", o->max_batch);
         return NULL;
     }
+    const int tp = o->tp_size > 1 ? o->tp_size : 1, rank = tp > 1 ? o->tp_rank : 0;
+    if (tp > 1) {
+        /* column slices of Wo (K = nq*hd) and down (K = F) must stay whole
+         * Q4_K super-blocks; heads, kv heads and vocabulary split evenly */
+        if (rank < 0 || rank >= tp || nkv % tp || V % tp || F % (256 * tp) ||
+            ((nq / tp) * hd) % 256) {
+            sb_set_error("tensor parallel %d (rank %d) needs n_kv_heads, vocab, ffn/256 and "
+                         "(n_heads/tp)*head_dim/256 divisible", tp, rank);
+            return NULL;
+        }
+    }
     slate_llama_batch_t* b = (slate_llama_batch_t*)calloc(1, sizeof(*b));
     pthread_mutex_init(&b->lock, NULL);
     b->device = o->device;
-    b->L = L; b->D = D; b->F = F; b->nq = nq; b->nkv = nkv; b->hd = hd; b->V = V;
-    b->kvd = nkv * hd;
-    b->qkv_dim = D + 2 * b->kvd;
+    b->tp = tp;
+    b->rank = rank;
+    /* this rank's share: heads, kv heads, FFN units, vocabulary rows */
+    b->L = L; b->D = D; b->F = F / tp; b->nq = nq / tp; b->nkv = nkv / tp; b->hd = hd; b->V = V;
+    b->V_l = V / tp;
+    b->v0 = rank * b->V_l;
+    b->Dq = b->nq * hd;
+    b->kvd = b->nkv * hd;
+    b->qkv_dim = b->Dq + 2 * b->kvd;
     b->theta = m->theta_base;
     b->eps = m->rms_eps;
     b->max_seq = o->max_seq > 0 ? o->max_seq : m->max_seq;
@@ -339,16 +401,19 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
     b->max_slots = o->max_slots > 0 ? o->max_slots : o->max_batch;
     b->kv_dtype = o->kv_dtype == SLATE_KV_F16 ? SLATE_KV_F16 : SLATE_KV_F32;
     b->gemm_path = o->gemm_path;
-    b->use_graphs = o->use_graphs;
+    /* tensor-parallel steps are launched eagerly: their NCCL collectives set
+     * up connections lazily, which stream capture does not allow */
+    b->use_graphs = tp > 1 ? 0 : o->use_graphs;
     b->max_pages = (b->max_seq + SB_PAGE_TOKENS - 1) / SB_PAGE_TOKENS;
     stage_t stg = {NULL, 0};
 
     if (sb_cuda_check(cudaSetDevice(b->device), "cudaSetDevice") ||
         sb_cuda_check(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking), "stream"))
         goto fail;
+    if (tp > 1 && sb_tp_init(&b->comm, tp, rank, o->tp_id)) goto fail;
     sb_gemm_prepare();
     sb_tc_prepare();
-    if (sb_attention_prepare(nq, nkv, hd, b->kv_dtype)) {
+    if (sb_attention_prepare(b->nq, b->nkv, hd, b->kv_dtype)) {
         sb_set_error("no attention kernel for head_dim %d, group %d", hd, nq / nkv);
         goto fail;
     }
@@ -356,10 +421,11 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
     /* weights */
     if (upload_f32(b, &b->emb, m->token_embd, (size_t)V * D)) goto fail;
     if (upload_f32(b, &b->out_norm, m->output_norm, (size_t)D)) goto fail;
-    if (m->output == m->token_embd && m->output_dtype == 0 && D % 128 == 0 && V % 128 == 0) {
-        b->lm_head = (sb_matrix){SB_WT_F32, b->emb, V, V, D, D};   /* tied: share the table */
+    if (m->output == m->token_embd && m->output_dtype == 0 && D % 128 == 0 && b->V_l % 128 == 0) {
+        /* tied: share the table (this rank's vocabulary rows) */
+        b->lm_head = (sb_matrix){SB_WT_F32, b->emb + (size_t)b->v0 * D, b->V_l, b->V_l, D, D};
     } else {
-        src_part p = {m->output, m->output_dtype, V};
+        src_part p = {m->output, m->output_dtype, b->V_l, b->v0, D, 0};
         if (pack_matrix(b, &stg, &b->lm_head, &p, 1, D, 0)) goto fail;
     }
     b->layers = (sb_layer*)calloc((size_t)L, sizeof(sb_layer));
@@ -370,16 +436,20 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         if (upload_f32(b, &ly->attn_norm, s->attn_norm, (size_t)D) ||
             upload_f32(b, &ly->ffn_norm, s->ffn_norm, (size_t)D))
             goto fail;
-        src_part qkv[3] = {{s->attn_q, s->attn_q_dtype, D},
-                           {s->attn_k, s->attn_k_dtype, b->kvd},
-                           {s->attn_v, s->attn_v_dtype, b->kvd}};
-        src_part wo = {s->attn_output, s->attn_output_dtype, D};
-        src_part gu[2] = {{s->ffn_gate, s->ffn_gate_dtype, F}, {s->ffn_up, s->ffn_up_dtype, F}};
-        src_part dn = {s->ffn_down, s->ffn_down_dtype, D};
+        /* rows of this rank's heads / FFN units; Wo and down take the matching
+         * column slice (with tp == 1 every part is the whole matrix) */
+        const int Fl = b->F;
+        src_part qkv[3] = {{s->attn_q, s->attn_q_dtype, b->Dq, rank * b->Dq, D, 0},
+                           {s->attn_k, s->attn_k_dtype, b->kvd, rank * b->kvd, D, 0},
+                           {s->attn_v, s->attn_v_dtype, b->kvd, rank * b->kvd, D, 0}};
+        src_part wo = {s->attn_output, s->attn_output_dtype, D, 0, D, rank * b->Dq};
+        src_part gu[2] = {{s->ffn_gate, s->ffn_gate_dtype, Fl, rank * Fl, D, 0},
+                          {s->ffn_up, s->ffn_up_dtype, Fl, rank * Fl, D, 0}};
+        src_part dn = {s->ffn_down, s->ffn_down_dtype, D, 0, F, rank * Fl};
         if (pack_matrix(b, &stg, &ly->wqkv, qkv, 3, D, 0) ||
-            pack_matrix(b, &stg, &ly->wo, &wo, 1, D, 0) ||
+            pack_matrix(b, &stg, &ly->wo, &wo, 1, b->Dq, 0) ||
             pack_matrix(b, &stg, &ly->wgu, gu, 2, D, 1) ||
-            pack_matrix(b, &stg, &ly->wdown, &dn, 1, F, 0))
+            pack_matrix(b, &stg, &ly->wdown, &dn, 1, Fl, 0))
             goto fail;
     }
     if (stg.p) cudaFreeHost(stg.p);
@@ -409,11 +479,11 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         const int Dp = round_up(D, 128);
         const int B = b->max_batch;
         b->ld_x = Dp;
-        b->ld_att = Dp;
+        b->ld_att = round_up(b->Dq, 128);
         b->ld_qkv = round_up(b->layers[0].wqkv.M_pad, 4);
         b->ld_h = round_up(b->layers[0].wgu.M_pad / 2, 128);
         b->ld_logits = round_up(b->lm_head.M_pad, 4);
-        size_t scr = sb_attention_scratch_floats(B, nq, hd, b->max_seq);
+        size_t scr = sb_attention_scratch_floats(B, b->nq, hd, b->max_seq);
         b->x = (float*)dalloc(b, (size_t)B * b->ld_x * 4);
         b->xn = (float*)dalloc(b, (size_t)B * b->ld_x * 4);
         b->att = (float*)dalloc(b, (size_t)B * b->ld_att * 4);
@@ -442,32 +512,42 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         if (sb_cuda_check(cudaHostAlloc((void**)&b->h_io, (size_t)(3 * B + 4) * 4,
                                         cudaHostAllocDefault), "cudaHostAlloc"))
             goto fail;
+        if (tp > 1) {
+            b->pairs = dalloc(b, (size_t)B * 8);
+            b->pairs_all = dalloc(b, (size_t)tp * B * 8);
+            if (!b->pairs || !b->pairs_all) goto fail;
+        }
     }
 
     /* tensor-core path: gemm_path 0 (auto) and 3 use the 3-pass split, 2 the
      * single f16 pass, 1 keeps every GEMM on the CUDA cores */
     b->tc_passes = o->gemm_path == 1 ? 0 : o->gemm_path == 2 ? 1 : 3;
-    if (b->layers[0].wqkv.wtype != SB_WT_Q4K || D % 256 || F % 256) b->tc_passes = 0;
+    if (b->layers[0].wqkv.wtype != SB_WT_Q4K || D % 256 || b->F % 256 || b->Dq % 256)
+        b->tc_passes = 0;
     if (b->tc_passes) {
         const int B = b->max_batch, lo = b->tc_passes == 3;
-        void* dh = dalloc(b, (size_t)B * D * 2);
-        void* dl = lo ? dalloc(b, (size_t)B * D * 2) : NULL;
-        void* fh = dalloc(b, (size_t)B * F * 2);
-        void* fl = lo ? dalloc(b, (size_t)B * F * 2) : NULL;
-        if (!dh || !fh || (lo && (!dl || !fl)) ||
-            sb_cuda_check(cudaMemset(dh, 0, (size_t)B * D * 2), "memset") ||
-            sb_cuda_check(cudaMemset(fh, 0, (size_t)B * F * 2), "memset") ||
-            (lo && (sb_cuda_check(cudaMemset(dl, 0, (size_t)B * D * 2), "memset") ||
-                    sb_cuda_check(cudaMemset(fl, 0, (size_t)B * F * 2), "memset"))))
-            goto fail;
-        if (sb_tc_make_operand(&b->op_d, dh, dl, B, D, D) ||
-            sb_tc_make_operand(&b->op_f, fh, fl, B, F, F))
-            goto fail;
+        /* f16 (hi, lo) staging of the GEMM inputs: K = d_model, the local FFN
+         * width, and (tensor parallel) the local attention width */
+        const int Ks[3] = {D, b->F, b->Dq};
+        sb_tc_operand* ops[3] = {&b->op_d, &b->op_f, &b->op_a};
+        for (int i = 0; i < 3; ++i) {
+            if (i == 2 && b->Dq == D) {
+                b->op_a = b->op_d;
+                break;
+            }
+            const size_t nb = (size_t)B * Ks[i] * 2;
+            void* hi = dalloc(b, nb);
+            void* lw = lo ? dalloc(b, nb) : NULL;
+            if (!hi || (lo && !lw) || sb_cuda_check(cudaMemset(hi, 0, nb), "memset") ||
+                (lo && sb_cuda_check(cudaMemset(lw, 0, nb), "memset")) ||
+                sb_tc_make_operand(ops[i], hi, lw, B, Ks[i], Ks[i]))
+                goto fail;
+        }
         const sb_layer* l0 = &b->layers[0];
         b->sp_qkv = sb_tc_splits_for(l0->wqkv.M_pad, D);
-        b->sp_wo = sb_tc_splits_for(l0->wo.M_pad, D);
+        b->sp_wo = sb_tc_splits_for(l0->wo.M_pad, b->Dq);
         b->sp_gu = sb_tc_splits_for(l0->wgu.M_pad, D);
-        b->sp_dn = sb_tc_splits_for(l0->wdown.M_pad, F);
+        b->sp_dn = sb_tc_splits_for(l0->wdown.M_pad, b->F);
         size_t ws = 0, t;
         if ((t = (size_t)b->sp_qkv * l0->wqkv.M_pad) > ws) ws = t;
         if ((t = (size_t)b->sp_wo * l0->wo.M_pad) > ws) ws = t;
@@ -478,8 +558,8 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         if (!b->tc_ws) goto fail;
         /* an f32 LM head runs on the tensor cores as an exact f16 hi/lo pair */
         if (b->tc_passes == 3 && b->lm_head.wtype == SB_WT_F32 &&
-            (sb_tc_make_weight(&b->head_tc, (const float*)b->lm_head.data, b->lm_head.ldw, V, D,
-                               b->stream) ||
+            (sb_tc_make_weight(&b->head_tc, (const float*)b->lm_head.data, b->lm_head.ldw, b->V_l,
+                               D, b->stream) ||
              sb_cuda_check(cudaStreamSynchronize(b->stream), "head split")))
             goto fail;
     }
@@ -487,7 +567,7 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
     /* KV pool, page tables, free list */
     {
         const size_t esz = b->kv_dtype == SLATE_KV_F16 ? 2 : 4;
-        const size_t page_bytes_all = (size_t)L * 2 * nkv * SB_PAGE_TOKENS * hd * esz;
+        const size_t page_bytes_all = (size_t)L * 2 * b->nkv * SB_PAGE_TOKENS * hd * esz;
         int64_t pages = o->kv_pages;
         if (pages <= 0) {
             size_t budget = o->kv_bytes;
@@ -517,8 +597,8 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
                           "memset"))
             goto fail;
         if (sb_init_free_list(b->free_stack, b->free_top, pages, b->stream)) goto fail;
-        if (o->attn_path != 1 && sb_attention_mma_supported(nq, nkv, hd, b->kv_dtype)) {
-            if (sb_attention_make_map(b->kvmap, b->pool, pages, L, nkv, hd)) goto fail;
+        if (o->attn_path != 1 && sb_attention_mma_supported(b->nq, b->nkv, hd, b->kv_dtype)) {
+            if (sb_attention_make_map(b->kvmap, b->pool, pages, L, b->nkv, hd)) goto fail;
             b->kvmap_p = b->kvmap;
         }
     }
@@ -634,6 +714,28 @@ static int status_code(slate_llama_batch_t* b) {
     return h[0];
 }
 
+/* Copies the step's logits [n][V] to dst (host or device).  A tensor-parallel
+ * rank holds only its vocabulary slice: the slices of all ranks are gathered
+ * first (a collective, so every rank asks for logits in the same steps). */
+static int copy_logits(slate_llama_batch_t* b, int n, float* dst, enum cudaMemcpyKind kind) {
+    const size_t ldl = (size_t)b->ld_logits;
+    if (b->tp == 1)
+        return sb_cuda_check(cudaMemcpy2DAsync(dst, (size_t)b->V * 4, b->logits, ldl * 4,
+                                               (size_t)b->V * 4, (size_t)n, kind, b->stream),
+                             "logits copy");
+    if (!b->logits_all) {
+        b->logits_all = (float*)dalloc(b, (size_t)b->tp * b->max_batch * ldl * 4);
+        if (!b->logits_all) return -5;
+    }
+    int rc = sb_tp_allgather(b->comm, b->logits, b->logits_all, (size_t)n * ldl * 4, b->stream);
+    for (int r = 0; r < b->tp && !rc; ++r)
+        rc = sb_cuda_check(cudaMemcpy2DAsync(dst + (size_t)r * b->V_l, (size_t)b->V * 4,
+                                             b->logits_all + (size_t)r * n * ldl, ldl * 4,
+                                             (size_t)b->V_l * 4, (size_t)n, kind, b->stream),
+                           "logits copy");
+    return rc;
+}
+
 int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
                            const int32_t* tokens, int32_t* out_tokens, float* out_logits) {
     if (!b || !slots || !tokens || n < 1 || n > b->max_batch) return -1;
@@ -668,10 +770,7 @@ int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
                                            (size_t)n * 4, cudaMemcpyDeviceToHost, b->stream),
                            "D2H tokens");
     if (!rc) rc = status_readback(b);
-    if (!rc && out_logits)
-        rc = sb_cuda_check(cudaMemcpy2DAsync(out_logits, (size_t)b->V * 4, b->logits,
-                                             (size_t)b->ld_logits * 4, (size_t)b->V * 4, (size_t)n,
-                                             cudaMemcpyDeviceToHost, b->stream), "D2H logits");
+    if (!rc && out_logits) rc = copy_logits(b, n, out_logits, cudaMemcpyDeviceToHost);
     if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(b->stream), "step");
     if (!rc) {
         const int st = status_code(b);
@@ -712,10 +811,7 @@ int slate_llama_batch_step_device(slate_llama_batch_t* b, const int32_t* d_slots
     if (!rc && d_out_tokens)
         rc = sb_cuda_check(cudaMemcpyAsync(d_out_tokens, b->d_io + 2 * b->max_batch, (size_t)n * 4,
                                            cudaMemcpyDeviceToDevice, b->stream), "out tokens");
-    if (!rc && d_out_logits)
-        rc = sb_cuda_check(cudaMemcpy2DAsync(d_out_logits, (size_t)b->V * 4, b->logits,
-                                             (size_t)b->ld_logits * 4, (size_t)b->V * 4, (size_t)n,
-                                             cudaMemcpyDeviceToDevice, b->stream), "out logits");
+    if (!rc && d_out_logits) rc = copy_logits(b, n, d_out_logits, cudaMemcpyDeviceToDevice);
     if (!rc && ev) {
         rc = sb_cuda_check(cudaEventRecord(ev, b->stream), "event record");
         if (!rc) rc = sb_cuda_check(cudaStreamWaitEvent(us, ev, 0), "event wait");

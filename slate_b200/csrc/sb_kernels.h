@@ -115,6 +115,21 @@ int sb_attention_mma(int prepare, const void* map, const float* qkv, int ld_qkv,
                      const int32_t* page_table, int max_pages, int64_t n_pages, int layer,
                      int nchunk, float* part, int* err, cudaStream_t st);
 
+/* Tensor parallelism.  Per row, the (max logit, global index) pair of this
+ * rank's vocabulary slice [v0, v0 + V) -> pairs[B] (8 bytes each); after an
+ * all-gather of the pairs into all[T][B], every rank picks the first maximum
+ * over the whole vocabulary and advances the positions. */
+int sb_argmax_pairs(const float* logits, int ldl, int V, int B, int v0, void* pairs,
+                    cudaStream_t st);
+int sb_tp_epilogue(const void* all_pairs, int T, int B, const int32_t* row_slot,
+                   const int32_t* row_pos, int32_t* pos, const int32_t* status,
+                   int32_t* out_tokens, cudaStream_t st);
+/* NCCL communicator of a tensor-parallel group (tp_nccl.c). */
+int sb_tp_init(void** comm, int nranks, int rank, const void* unique_id);
+void sb_tp_destroy(void* comm);
+int sb_tp_allreduce_sum(void* comm, float* buf, size_t n, cudaStream_t st);
+int sb_tp_allgather(void* comm, const void* send, void* recv, size_t bytes, cudaStream_t st);
+
 /* Fills positions [0, n) of one slot with deterministic pseudo-random K/V
  * (benchmark stand-in for a prefilled prompt), allocating its pages. */
 int sb_seed_context(int slot, int n, uint64_t seed, int n_layers, int nkv, int hd, int32_t* pos,

@@ -147,6 +147,7 @@ typedef struct {
     char name[64];
     int64_t rows, cols;   /* logical [rows, cols]; cols == 1 for vectors */
     int n_dims, ggml_type, kind, id;   /* kind 0 = normal, 1 = ones */
+    int src;              /* >= 0: a copy of tensor src (layer_period) */
     uint64_t off;
     size_t bytes;
 } tdesc;
@@ -180,6 +181,7 @@ static void* writer(void* arg) {
     fesetround(FE_TONEAREST);
     for (int ti = 0; ti < j->nt && !j->rc; ++ti) {
         const tdesc* t = &j->t[ti];
+        if (t->src >= 0) continue;
         int64_t per = (t->rows + j->nthreads - 1) / j->nthreads;
         int64_t r0 = (int64_t)j->tid * per, r1 = r0 + per;
         if (r1 > t->rows) r1 = t->rows;
@@ -210,6 +212,28 @@ static void* writer(void* arg) {
     return NULL;
 }
 
+/* Copies repeated-layer tensors from their source tensor, one tensor per
+ * thread in turn. */
+static void* copier(void* arg) {
+    job_t* j = (job_t*)arg;
+    const size_t chunk = (size_t)64 << 20;
+    unsigned char* buf = (unsigned char*)malloc(chunk);
+    if (!buf) { j->rc = -6; return NULL; }
+    for (int ti = j->tid; ti < j->nt && !j->rc; ti += j->nthreads) {
+        const tdesc* t = &j->t[ti];
+        if (t->src < 0) continue;
+        const tdesc* s = &j->t[t->src];
+        for (size_t done = 0; done < t->bytes && !j->rc; done += chunk) {
+            size_t n = t->bytes - done < chunk ? t->bytes - done : chunk;
+            if (pread(j->fd, buf, n, (off_t)(j->data_off + s->off + done)) != (ssize_t)n ||
+                pwrite(j->fd, buf, n, (off_t)(j->data_off + t->off + done)) != (ssize_t)n)
+                j->rc = -6;
+        }
+    }
+    free(buf);
+    return NULL;
+}
+
 int slate_synth_llama_gguf(const char* path, const slate_synth_config_t* c) {
     if (!path || !c || c->n_layers < 1 || c->d_model < 1 || c->n_heads < 1 ||
         c->d_model % c->n_heads || c->vocab < 1 || c->ffn_hidden < 1)
@@ -225,6 +249,7 @@ int slate_synth_llama_gguf(const char* path, const slate_synth_config_t* c) {
         snprintf(t[k].name, sizeof t[k].name, "%s", nm);                                       \
         t[k].rows = (R); t[k].cols = (C); t[k].n_dims = (nd); t[k].kind = (kd); t[k].id = k;   \
         t[k].ggml_type = ((q) && c->q4k && (C) % 256 == 0) ? 12 : 0;                           \
+        t[k].src = -1;                                                                         \
         ++k;                                                                                   \
     } while (0)
     ADD("token_embd.weight", V, D, 2, 0, 0);
@@ -244,6 +269,8 @@ int slate_synth_llama_gguf(const char* path, const slate_synth_config_t* c) {
         L_ADD("ffn_up.weight", F, D, 2, 1, 0);
         L_ADD("ffn_down.weight", D, F, 2, 1, 0);
 #undef L_ADD
+        if (c->layer_period > 0 && l >= c->layer_period)
+            for (int j = 0; j < 9; ++j) t[k - 9 + j].src = k - 9 + j - 9 * (l - l % c->layer_period);
     }
 #undef ADD
     uint64_t cur = 0;
@@ -284,7 +311,7 @@ int slate_synth_llama_gguf(const char* path, const slate_synth_config_t* c) {
     }
     while (h.n % 32) put(&h, "", 1);
     const uint64_t data_off = h.n;
-    int fd = open(path, O_CREAT | O_TRUNC | O_WRONLY, 0644);
+    int fd = open(path, O_CREAT | O_TRUNC | O_RDWR, 0644);
     int rc = 0;
     if (fd < 0) rc = -6;
     if (!rc && (ftruncate(fd, (off_t)(data_off + cur)) != 0 ||
@@ -303,6 +330,16 @@ int slate_synth_llama_gguf(const char* path, const slate_synth_config_t* c) {
         for (int i = 0; i < nth; ++i) {
             pthread_join(th[i], NULL);
             if (!rc) rc = jobs[i].rc;
+        }
+        if (!rc && c->layer_period > 0 && c->layer_period < c->n_layers) {
+            for (int i = 0; i < nth; ++i) {
+                jobs[i] = (job_t){fd, t, nt, data_off, c->seed, i, nth, 0};
+                pthread_create(&th[i], NULL, copier, &jobs[i]);
+            }
+            for (int i = 0; i < nth; ++i) {
+                pthread_join(th[i], NULL);
+                if (!rc) rc = jobs[i].rc;
+            }
         }
     }
     if (fd >= 0) close(fd);

@@ -58,6 +58,27 @@ def test_synth_writer_deterministic_across_threads(sb, workdir):
     assert open(a, "rb").read() == open(b, "rb").read()
 
 
+def test_synth_layer_period_repeats_layers(sb, workdir):
+    """layer_period p: layer l's tensors are byte copies of layer l % p; the
+    first p layers and the non-layer tensors are what p = 0 writes."""
+    from gguf_util import read_gguf
+    cfg = dict(SYNTH["gqa_q4k"], n_layers=5)
+    a, b = os.path.join(str(workdir), "p0.gguf"), os.path.join(str(workdir), "p2.gguf")
+    sb.synth_gguf(a, **cfg)
+    sb.synth_gguf(b, layer_period=2, n_threads=3, **cfg)
+    _, ta = read_gguf(a)
+    _, tb = read_gguf(b)
+    assert ta.keys() == tb.keys()
+    for name, (ty, dims, data) in tb.items():
+        if name.startswith("blk."):
+            l = int(name.split(".")[1])
+            src = name.replace(f"blk.{l}.", f"blk.{l % 2}.", 1)
+            assert np.array_equal(data, ta[src][2]), name
+        else:
+            assert np.array_equal(data, ta[name][2]), name
+    assert not np.array_equal(ta["blk.2.attn_q.weight"][2], ta["blk.0.attn_q.weight"][2])
+
+
 def test_synth_weights_statistics(sb, synth_models):
     from gguf_util import read_gguf
     kv, t = read_gguf(synth_models["tiny_f32"])
