@@ -99,7 +99,10 @@ typedef struct slate_backend_cuda {
                                int layer, int B, int nq, int nkv, int hd, int kv_dtype);
     /* matmul_q4k_batch on the tensor cores (tcgen05, f32 accumulate):
      * passes 1 = f16 x f16 operands, 3 = f16 hi/lo split of both operands
-     * (f32-level products).  Needs M % 128 == 0, K % 256 == 0, 16 <= B.
+     * (f32-level products), both for 16 <= B; 2 = exact f16 weights (sc*q)
+     * against x as f16 hi/lo with the Q4_K block scales applied per
+     * super-block (f32-level products), any B >= 1.  M % 128 == 0,
+     * K % 256 == 0.
      * Synchronous: returns -5 if the device reported a pipeline timeout. */
     int (*matmul_q4k_batch_tc)(float* Y, const void* A_q4k, const float* X, int B, int M, int K,
                                int passes);
@@ -184,7 +187,9 @@ typedef struct slate_cuda_opts {
     int64_t kv_pages;    /* pool size in 16-token pages (0 = from kv_bytes) */
     size_t kv_bytes;     /* pool budget (0 = 90% of free HBM after weights) */
     int use_graphs;      /* capture one CUDA graph per batch size (1 = yes) */
-    int gemm_path;       /* 0 auto, 1 CUDA-core kernels only, 2 tensor cores 1-pass f16 */
+    int gemm_path;       /* 0 auto (tcgen05 3-pass hi/lo split), 1 CUDA-core kernels
+                            only, 2 tcgen05 1-pass f16, 3 = 0, 4 Q4_K on the
+                            exact-weight stream-K tcgen05 kernel (2 f16 passes) */
     int attn_path;       /* 0 auto (tensor cores for f16 KV where the shape allows),
                             1 CUDA-core attention only */
     /* Tensor parallelism (the 70B plan): tp_size ranks, one process or thread

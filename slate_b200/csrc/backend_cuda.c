@@ -180,8 +180,47 @@ static int be_attention_paged(float* out, const float* q, const int32_t* pos,
     return rc;
 }
 
+/* passes 2: the exact-weight kernel (gemm_q4k.cu), any B >= 1 */
+static int be_matmul_q4k_exact(float* Y, const void* A, const float* X, int B, int M, int K) {
+    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0};
+    sb_q4_prepare();
+    const int r_pad = (B + 127) / 128 * 128;
+    const size_t xs_bytes = (size_t)((K / 256 + 1) & ~1) * r_pad * 8 * 2;
+    const int tiles = sb_q4_tiles(M, B);
+    void *hi = NULL, *lo = NULL, *xh = NULL, *xl = NULL, *ws = NULL, *cnt = NULL;
+    int rc = sb_cuda_check(cudaMallocAsync(&hi, (size_t)B * K * 2, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&lo, (size_t)B * K * 2, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&xh, xs_bytes, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&xl, xs_bytes, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&ws, sb_q4_ws_floats() * 4, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&cnt, (size_t)tiles * 4 + 16, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(cnt, 0, (size_t)tiles * 4 + 16, g_stream), "memset");
+    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(xh, 0, xs_bytes, g_stream), "memset");
+    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(xl, 0, xs_bytes, g_stream), "memset");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "alloc sync");
+    int* err = (int*)cnt + tiles;
+    sb_q4_operand op;
+    if (!rc && sb_q4_make_operand(&op, hi, lo, xh, xl, B, r_pad, K, K)) rc = -1;
+    if (!rc) rc = fin(sb_q4_split(X, K, B, &op, g_stream), "q4 split");
+    if (!rc) rc = fin(sb_q4_gemm(&W, &op, B, Y, M, SB_EPI_STORE, (float*)ws, (int*)cnt, err, g_stream),
+                      "matmul_q4k_batch_tc");
+    int e = 0;
+    if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, g_stream), "err");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "matmul_q4k_batch_tc");
+    if (!rc && e) {
+        sb_set_error("tensor-core pipeline wait timed out (stage %d)", e);
+        rc = -5;
+    }
+    void* bufs[6] = {hi, lo, xh, xl, ws, cnt};
+    for (int i = 0; i < 6; ++i)
+        if (bufs[i]) cudaFreeAsync(bufs[i], g_stream);
+    return rc;
+}
+
 static int be_matmul_q4k_tc(float* Y, const void* A, const float* X, int B, int M, int K,
                             int passes) {
+    if (passes == 2 && M % 128 == 0 && K % 256 == 0 && B >= 1 && K % 4 == 0)
+        return be_matmul_q4k_exact(Y, A, X, B, M, K);
     if (M % 128 || K % 256 || B < 16 || (passes != 1 && passes != 3)) {
         sb_set_error("matmul_q4k_batch_tc: unsupported shape or passes");
         return -1;

@@ -79,6 +79,13 @@ struct slate_llama_batch {
     int sp_qkv, sp_wo, sp_gu, sp_dn;
     sb_tc_weight head_tc;          /* f32 LM head as an f16 pair (hi set when used) */
     sb_tc_operand op_a;            /* attention output, K = nq*hd (tensor parallel: local heads) */
+    /* exact-weight Q4_K GEMM (gemm_path 0): operands over the same f16 hi/lo
+     * buffers plus sub-block sums, stream-K partials and tile counters */
+    int q4_on;
+    sb_q4_operand q4_d, q4_f, q4_a;
+    float* q4_ws;
+    int* q4_cnt;
+    size_t q4_cnt_n;
     /* tensor parallelism: nq, nkv, F above are this rank's shares, V the full
      * vocabulary of which the LM head holds rows [v0, v0 + V_l) */
     int tp, rank, V_l, v0, Dq;     /* Dq = nq * hd (local) */
@@ -96,6 +103,12 @@ static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X,
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) {
         int rc = sb_tc_split(X, ldx, n, &b->op_d, s);
         return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, &b->op_d, n, Y, ldy, epi, b->tc_err, s);
+    }
+    if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
+        const sb_q4_operand* op = W->K == b->q4_d.K ? &b->q4_d
+                                  : W->K == b->q4_f.K ? &b->q4_f : &b->q4_a;
+        int rc = sb_q4_split(X, ldx, n, op, s);
+        return rc ? rc : sb_q4_gemm(W, op, n, Y, ldy, epi, b->q4_ws, b->q4_cnt, b->tc_err, s);
     }
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
         const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
@@ -281,6 +294,8 @@ static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
 static int gemm_launches(const slate_llama_batch_t* b, const sb_matrix* W, int n, int epi,
                          int splits) {
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return 2;   /* split + GEMM */
+    if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
+        return 2;                                                               /* split + GEMM */
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2 + (splits == 1 && epi != SB_EPI_SILU ? 0 : 1);               /* + finish */
     return 1;
@@ -519,7 +534,8 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         }
     }
 
-    /* tensor-core path: gemm_path 0 (auto) and 3 use the 3-pass split, 2 the
+    /* tensor-core path: gemm_path 0 (auto), 3 and 4 use the 3-pass split (4
+     * only for the f32 LM head), 2 the
      * single f16 pass, 1 keeps every GEMM on the CUDA cores */
     b->tc_passes = o->gemm_path == 1 ? 0 : o->gemm_path == 2 ? 1 : 3;
     if (b->layers[0].wqkv.wtype != SB_WT_Q4K || D % 256 || b->F % 256 || b->Dq % 256)
@@ -562,6 +578,36 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
                                D, b->stream) ||
              sb_cuda_check(cudaStreamSynchronize(b->stream), "head split")))
             goto fail;
+        /* gemm_path 4: Q4_K weights on the exact-weight stream-K kernel (two f16
+         * passes, block scales per super-block) */
+        if (o->gemm_path == 4) {
+            sb_q4_prepare();
+            const int r_pad = (B + 127) / 128 * 128;
+            const sb_tc_operand* src[3] = {&b->op_d, &b->op_f, &b->op_a};
+            sb_q4_operand* dst[3] = {&b->q4_d, &b->q4_f, &b->q4_a};
+            for (int i = 0; i < 3; ++i) {
+                const size_t xs = (size_t)((src[i]->K / 256 + 1) & ~1) * r_pad * 8 * 2;
+                void* xh = dalloc(b, xs);
+                void* xl = dalloc(b, xs);
+                if (!xh || !xl || sb_cuda_check(cudaMemset(xh, 0, xs), "memset") ||
+                    sb_cuda_check(cudaMemset(xl, 0, xs), "memset") ||
+                    sb_q4_make_operand(dst[i], src[i]->hi, src[i]->lo, xh, xl, B, r_pad, src[i]->K,
+                                       src[i]->K))
+                    goto fail;
+            }
+            int mp = l0->wqkv.M_pad;
+            if (l0->wo.M_pad > mp) mp = l0->wo.M_pad;
+            if (l0->wgu.M_pad > mp) mp = l0->wgu.M_pad;
+            if (l0->wdown.M_pad > mp) mp = l0->wdown.M_pad;
+            if (b->lm_head.wtype == SB_WT_Q4K && b->lm_head.M_pad > mp) mp = b->lm_head.M_pad;
+            const size_t tiles = (size_t)sb_q4_tiles(mp, B);
+            b->q4_ws = (float*)dalloc(b, sb_q4_ws_floats() * 4);
+            b->q4_cnt = (int*)dalloc(b, tiles * 4);
+            b->q4_cnt_n = tiles;
+            if (!b->q4_ws || !b->q4_cnt || sb_cuda_check(cudaMemset(b->q4_cnt, 0, tiles * 4), "memset"))
+                goto fail;
+            b->q4_on = 1;
+        }
     }
 
     /* KV pool, page tables, free list */
@@ -707,6 +753,8 @@ static int status_readback(slate_llama_batch_t* b) {
 static int status_code(slate_llama_batch_t* b) {
     const int32_t* h = b->h_io + 3 * b->max_batch;
     if (h[1]) {
+        /* a step that gave up may leave stream-K tile counters raised */
+        if (b->q4_cnt) cudaMemset(b->q4_cnt, 0, b->q4_cnt_n * 4);
         sb_set_error("tensor-core GEMM pipeline wait timed out (stage %d)", h[1]);
         return -5;
     }

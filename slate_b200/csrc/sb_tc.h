@@ -56,6 +56,31 @@ void sb_tc_free_weight(sb_tc_weight* w);
 int sb_tc_gemm_f16w(const sb_tc_weight* W, const sb_tc_operand* X, int n_rows, float* Y, int ldy,
                     int epi, int* err, cudaStream_t st);
 
+/* Operand of the exact-weight Q4_K GEMM (gemm_q4k.cu): f16 hi / lo rows
+ * [rows][ld16] with TMA maps of 64 x 128 boxes, plus the per-sub-block sums
+ * of x as f16 hi / lo in [K/256 rounded up to even][r_pad][8] (r_pad: rows
+ * rounded up to 128; zero-filled once, the padding block stays zero). */
+typedef struct sb_q4_operand {
+    SB_ALIGN64 unsigned char map_hi[128];
+    SB_ALIGN64 unsigned char map_lo[128];
+    void *hi, *lo, *xs_hi, *xs_lo;
+    int rows, r_pad, K, ld16;
+} sb_q4_operand;
+int sb_q4_make_operand(sb_q4_operand* op, void* hi, void* lo, void* xs_hi, void* xs_lo, int rows,
+                       int r_pad, int K, int ld16);
+/* X (f32, stride ldx, ldx % 4 == 0) -> hi / lo / sub-block sums, n_rows rows. */
+int sb_q4_split(const float* X, int ldx, int n_rows, const sb_q4_operand* op, cudaStream_t st);
+/* Y[n][m] (=, +=, SiLU(gate)*up) over Q4_K W for n < n_rows, two f16 passes with
+ * exact weights.  ws: sb_q4_ws_floats() floats; cnt: sb_q4_tiles(M_pad, n_rows)
+ * ints, zero before the first call (the kernel leaves them zero). */
+int sb_q4_gemm(const sb_matrix* W, const sb_q4_operand* X, int n_rows, float* Y, int ldy, int epi,
+               float* ws, int* cnt, int* err, cudaStream_t st);
+size_t sb_q4_ws_floats(void);
+int sb_q4_tiles(int M_pad, int n_rows);
+/* SM count and shared-memory attribute on the current device (outside capture;
+ * before sb_q4_ws_floats). */
+void sb_q4_prepare(void);
+
 #ifdef __cplusplus
 }
 #endif

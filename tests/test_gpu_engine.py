@@ -293,3 +293,31 @@ def test_scheduler_batches_concurrent_callers(sb, oracle, workdir):
         for t in range(n_tok):
             assert greedy_agrees(out[t], lg[0, t], 1e-4 * np.abs(lg[0, t]).max())[0]
     m.close()
+
+
+@pytest.mark.parametrize("n_rows", [40, 150])
+def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
+    """The GEMM paths of the engine -- the 3-pass split (gemm_path 0), the
+    exact-weight stream-K kernel (4, with its STORE / residual ADD / fused
+    SiLU*up epilogues) and CUDA cores (1) -- each match the oracle on a 2-layer
+    Q4_K model at batch sizes with a partial second row tile."""
+    path = os.path.join(str(workdir), "paths_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=1024, ffn_hidden=2816, n_heads=16, n_kv_heads=4,
+                      vocab=2000, max_seq=64, q4k=True, seed=11)
+    rng = np.random.default_rng(n_rows)
+    T = 3
+    feed = rng.integers(0, 2000, (n_rows, T)).astype(np.int32)
+    m = oracle.open(path)
+    ref, _ = m.decode_many(feed)
+    m.close()
+    scale = np.abs(ref).max()
+    for gp in (0, 4, 1):
+        eng = make_engine(sb, path, max_batch=n_rows, gemm_path=gp)
+        slots = [eng.open() for _ in range(n_rows)]
+        for t in range(T):
+            rc, out, lg = eng.step(slots, feed[:, t], want_logits=True)
+            assert rc == 0, (gp, rc, sb.last_error())
+            err = np.max(np.abs(lg - ref[:, t])) / scale
+            assert err < 1e-4, (gp, t, err)
+        eng.close()

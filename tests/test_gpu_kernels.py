@@ -225,6 +225,28 @@ def test_matmul_q4k_tensor_cores(be, oracle, sb, B, M, K, passes, tol):
     assert scale_err(got, want) < tol
 
 
+@pytest.mark.parametrize("B,M,K", [(1, 128, 256), (5, 256, 1024), (16, 128, 256), (130, 384, 4096),
+                                   (256, 1024, 4096), (256, 6144, 4096), (100, 256, 14336),
+                                   (300, 256, 512), (513, 512, 2048)])
+def test_matmul_q4k_exact_weights(be, oracle, sb, B, M, K):
+    """passes=2: f16(sc*q) weights are exact, x enters as f16 hi + lo, the
+    d / dmin block scales are applied per super-block in f32 -- f32-level
+    products like the 3-pass split, over a stream-K schedule whose shared tiles
+    are summed by the last CTA to finish (shapes with 1..5 tiles per SM and
+    partial row tiles)."""
+    rng = np.random.default_rng(B * 7 + M + K)
+    q = sb.quantize_q4k(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    X = rng.normal(0, 1, (B, K)).astype(np.float32)
+    Y = be.empty(B * M * 4)
+    for rep in range(2):                      # counters must be left at zero
+        rc = be.matmul_q4k_batch_tc(Y, be.dev(q), be.dev(X), B, M, K, 2)
+        assert rc == 0, be.sb.last_error()
+        got = be.host(Y, (B, M))
+        Wd = oracle.dequant_q4k(q, M * K).reshape(M, K).astype(np.float64)
+        want = X.astype(np.float64) @ Wd.T
+        assert scale_err(got, want) < 1e-5, rep
+
+
 def run_attention(be, monkeypatch, path, q, pool, table, pos, nq, nkv, hd, kv_dtype, layer, n_pages):
     """attention_paged_gqa with the kernel picked by SLATE_CUDA_ATTN_PATH
     ("0": tensor cores where the f16 shape allows, "1": CUDA cores)."""
