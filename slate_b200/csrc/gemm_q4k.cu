@@ -41,6 +41,8 @@
 // timeout records an error code, the roles stop, in-flight copies are waited
 // for and TMEM is freed.
 #include <cuda.h>
+#include <stdlib.h>
+#include <string.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
@@ -220,8 +222,9 @@ __device__ __forceinline__ void scale_min(uint4 h, int j, uint32_t& sc, uint32_t
 // the single rounding of the fused multiply-add.
 __device__ __forceinline__ void nib4(uint32_t nibs, __half2 sc2, __half2 off2, uint32_t& w0,
                                      uint32_t& w1) {
-    const uint32_t p0 = __byte_perm(nibs, 0u, 0x4140) | 0x64006400u;
-    const uint32_t p1 = __byte_perm(nibs, 0u, 0x4342) | 0x64006400u;
+    // bytes [n0, 0x64, n1, 0x64]: the f16 pair (1024 + n0, 1024 + n1)
+    const uint32_t p0 = __byte_perm(nibs, 0x64646464u, 0x4140);
+    const uint32_t p1 = __byte_perm(nibs, 0x64646464u, 0x4342);
     const __half2 h0 = __hfma2(*(const __half2*)&p0, sc2, off2);
     const __half2 h1 = __hfma2(*(const __half2*)&p1, sc2, off2);
     w0 = *(const uint32_t*)&h0;
@@ -364,17 +367,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const size_t row_bytes = (size_t)(a.K / 256) * 144;
 
     if (tid == 0) {
+        // producer warps arrive once per warp (elected lane)
         for (int s = 0; s < STAGES; ++s) {
-            bar_init(&full[s], NPROD + 1);
+            bar_init(&full[s], NPROD / 32 + 1);
             bar_init(&empty[s], 1);
         }
         for (int p = 0; p < 2; ++p) {
             bar_init(&acc_full[p], 1);
             bar_init(&acc_empty[p], 4);
-            bar_init(&qa_full[p], NPROD + 1);
+            bar_init(&qa_full[p], NPROD / 32 + 1);
             bar_init(&qa_empty[p], 1);
             bar_init(&raw_full[p], 1);
-            bar_init(&raw_empty[p], NPROD);
+            bar_init(&raw_empty[p], NPROD / 32);
         }
         bar_init(&q_full, 1);
         bar_init(&q_empty, 4);
@@ -409,14 +413,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint4 raw[9];
             {
                 const int r = (int)(si & 1);
-                if (!bar_wait(&raw_full[r], (uint32_t)((si >> 1) & 1), a.err, 22)) {
+                if (!__all_sync(0xffffffffu, bar_wait(&raw_full[r], (uint32_t)((si >> 1) & 1), a.err, 22))) {
                     ok = false;
                     break;
                 }
                 const uint4* src = (const uint4*)(rawbuf + r * RAW_BYTES + m * 144);
 #pragma unroll
                 for (int i = 0; i < 9; ++i) raw[i] = src[i];
-                bar_arrive(&raw_empty[r]);
+                __syncwarp();
+                if (lane == 0) bar_arrive(&raw_empty[r]);
                 ++si;
             }
             const int sb = cur.sb;
@@ -427,7 +432,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             unsigned char* qg = qbuf + g * QGRP_BYTES;
             const uint4 hdr = raw[0];
             if (opens) {
-                if (gi >= 2 && !bar_wait(&qa_empty[g], (uint32_t)(((gi >> 1) - 1) & 1), a.err, 11)) {
+                if (gi >= 2 &&
+                    !__all_sync(0xffffffffu, bar_wait(&qa_empty[g], (uint32_t)(((gi >> 1) - 1) & 1), a.err, 11))) {
                     ok = false;
                     break;
                 }
@@ -465,7 +471,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     *(uint4*)(qg + QOP_BYTES + 2048 + m * 16) = zero4;
                 }
                 fence_async_smem();
-                bar_arrive(&qa_full[g]);
+                __syncwarp();
+                if (lane == 0) bar_arrive(&qa_full[g]);
                 ++gi;
             }
 #pragma unroll
@@ -474,7 +481,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (k < ks || k >= ke || !ok) continue;
                 const int s = (int)(it % STAGES);
                 if (it >= STAGES &&
-                    !bar_wait(&empty[s], (uint32_t)(((it / STAGES) - 1) & 1), a.err, 12)) {
+                    !__all_sync(0xffffffffu, bar_wait(&empty[s], (uint32_t)(((it / STAGES) - 1) & 1), a.err, 12))) {
                     ok = false;
                     continue;
                 }
@@ -503,7 +510,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 tmem_st32(lane_a + (uint32_t)(32 * s), w);
                 tc_fence_before();
-                bar_arrive(&full[s]);
+                __syncwarp();
+                if (lane == 0) bar_arrive(&full[s]);
                 ++it;
             }
             cur.next();
@@ -750,6 +758,530 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
+// ============================================================================
+// Two-SM version (cta_group::2): a cluster of 2 CTAs computes a tile of 256
+// weight rows x 128 activation rows.  CTA r holds weight rows [128 r, 128 r +
+// 128) of the tile in its TMEM lanes (A, P1, Q) and activation rows [64 r, 64 r
+// + 64) of the tile in its shared memory; the leader CTA (r = 0) issues MMAs of
+// M = 256 that read both CTAs' operands, so each SM brings in half of the
+// activation bytes per multiply-add of the one-SM kernel.  Completions are
+// committed to both CTAs' barriers (tcgen05.commit multicast); producers of
+// both CTAs arrive on the leader's barriers; the x tiles of both CTAs land on
+// the leader's barrier (2-SM TMA form, no multicast).
+constexpr int BN2 = 64;                    // activation rows per CTA (of 128 per pair)
+constexpr int STAGES2 = 8;                 // x stages in shared memory
+constexpr int B2_BYTES = BN2 * 128;        // 8 KB per part
+constexpr int STAGE2_BYTES = 2 * B2_BYTES;
+constexpr int QA2_BYTES = 128 * 32;        // c hi or lo: [128 rows][16]
+constexpr int QB2_BYTES = BN2 * 32;        // X hi or lo: [64 rows][16]
+constexpr int QGRP2_BYTES = 2 * QA2_BYTES + 2 * QB2_BYTES;
+// (+ 8 KB of slack after the last stage: every operand read stays inside the
+// allocation even if a descriptor spanned a whole 128-row tile)
+constexpr size_t SMEM2 = 2 * QGRP2_BYTES + XCH_FLOATS * 4 + 2 * RAW_BYTES +
+                         (size_t)STAGES2 * STAGE2_BYTES + 1024 + 8192;
+static_assert((2 * QGRP2_BYTES + XCH_FLOATS * 4 + 2 * RAW_BYTES) % 1024 == 0, "stage alignment");
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// arrive on the barrier at the same offset in CTA 0 of the cluster
+__device__ __forceinline__ void bar_arrive_leader(uint64_t* b) {
+    asm volatile(
+        "{\n\t.reg .b32 ra;\n\tmapa.shared::cluster.u32 ra, %0, 0;\n\t"
+        "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(su32(b))
+        : "memory");
+}
+__device__ __forceinline__ bool bar_try_cl(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait with cluster-scope acquire (barriers that receive remote arrivals)
+__device__ bool bar_wait_cl(uint64_t* b, uint32_t parity, int* err, int code) {
+    if (bar_try_cl(b, parity)) return true;
+    const uint64_t t0 = gtimer();
+    for (uint32_t n = 1;; ++n) {
+        if (bar_try_cl(b, parity)) return true;
+        if ((n & 31) == 0) {
+            if (*(volatile int*)err) return false;
+            if (gtimer() - t0 > WAIT_NS) {
+                atomicCAS(err, 0, code);
+                return false;
+            }
+        }
+    }
+}
+// TMA tile load into this CTA's shared memory, completion counted on the
+// leader CTA's barrier (2-SM form; no multicast)
+__device__ __forceinline__ void tma_2d_2sm(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    const uint32_t b = su32(bar) & 0xFEFFFFFFu;
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%3, %4}], [%2];" ::"r"(su32(dst)),
+        "l"(map), "r"(b), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void mma2_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma2_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// commit to the barrier at this offset in both CTAs of the pair
+__device__ __forceinline__ void commit2(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+            su32(bar))
+        : "memory");
+}
+// K-major, no swizzle, two 8-column K groups `lbo` bytes apart, 8-row groups 128 B apart
+__device__ __forceinline__ uint64_t desc_plain_lbo(uint32_t saddr, uint32_t lbo) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) |
+           ((uint64_t)(128 >> 4) << 32) | (1ull << 46);
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    q4k_gemm2_kernel(const __grid_constant__ CUtensorMap xmap_hi,
+                     const __grid_constant__ CUtensorMap xmap_lo,
+                     const __grid_constant__ CUtensorMap xsmap_hi,
+                     const __grid_constant__ CUtensorMap xsmap_lo,
+                     const __grid_constant__ CUtensorMap wmap, const Args a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // [Q groups x2 (c hi, c lo, X hi, X lo) | SiLU exchange | raw x2 | x stages]
+    unsigned char* qbuf = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    float* xch = (float*)(qbuf + 2 * QGRP2_BYTES);
+    unsigned char* rawbuf = (unsigned char*)(xch + XCH_FLOATS);
+    unsigned char* bst = rawbuf + 2 * RAW_BYTES;
+    // full / qa_full / acc_empty / q_empty are used in the leader only (both
+    // CTAs arrive there); the others are per CTA (multicast commits, local TMA)
+    __shared__ uint64_t full[STAGES2], empty[STAGES2], acc_full[2], acc_empty[2], qa_full[2],
+        qa_empty[2], q_full, q_empty, raw_full[2], raw_empty[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ int last_flag;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int C = gridDim.x >> 1, c = blockIdx.x >> 1;      // clusters, this cluster
+    const int nk = a.K / BK;
+    const int MT = a.M_pad / (2 * BM);
+    const long long U = (long long)MT * a.NT * nk;
+    const long long u0 = u_begin(c, C, U), u1 = u_begin(c + 1, C, U);
+    const size_t row_bytes = (size_t)(a.K / 256) * 144;
+
+    if (tid == 0) {
+        // producer warps of both CTAs arrive once per warp (elected lane)
+        for (int s = 0; s < STAGES2; ++s) {
+            bar_init(&full[s], 2 * (NPROD / 32) + 1);
+            bar_init(&empty[s], 1);
+        }
+        for (int p = 0; p < 2; ++p) {
+            bar_init(&acc_full[p], 1);
+            bar_init(&acc_empty[p], 8);
+            bar_init(&qa_full[p], 2 * (NPROD / 32) + 1);
+            bar_init(&qa_empty[p], 1);
+            bar_init(&raw_full[p], 1);
+            bar_init(&raw_empty[p], NPROD / 32);
+        }
+        bar_init(&q_full, 1);
+        bar_init(&q_empty, 8);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == MMA_WARP) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         su32(&tmem_slot)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    cluster_sync();                 // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    bool ok = true;
+
+    if (warp < 4) {
+        // ---------------- producers (both CTAs): own 128 weight rows ----------------
+        const int m = tid;
+        const uint32_t lane_a = tmem + ((uint32_t)(warp * 32) << 16) + COL_A;
+        long long it = 0, gi = 0, si = 0;
+        SbsIt cur;
+        cur.start(u0, u1, nk);
+        const uint4 zero4 = make_uint4(0, 0, 0, 0);
+        while (cur.valid() && ok) {
+            uint4 raw[9];
+            {
+                const int r = (int)(si & 1);
+                if (!__all_sync(0xffffffffu, bar_wait(&raw_full[r], (uint32_t)((si >> 1) & 1), a.err, 22))) {
+                    ok = false;
+                    break;
+                }
+                const uint4* src = (const uint4*)(rawbuf + r * RAW_BYTES + m * 144);
+#pragma unroll
+                for (int i = 0; i < 9; ++i) raw[i] = src[i];
+                __syncwarp();
+                if (lane == 0) bar_arrive(&raw_empty[r]);
+                ++si;
+            }
+            const int sb = cur.sb;
+            const int ks = max(cur.ka, 4 * sb), ke = min(cur.kb, 4 * sb + 4);
+            const bool first = sb == cur.ka / 4, last = sb == (cur.kb - 1) / 4;
+            const bool opens = first || !(sb & 1), closes = last || (sb & 1);
+            const int g = (int)(gi & 1);
+            unsigned char* qg = qbuf + g * QGRP2_BYTES;
+            const uint4 hdr = raw[0];
+            if (opens) {
+                if (gi >= 2 &&
+                    !__all_sync(0xffffffffu, bar_wait_cl(&qa_empty[g], (uint32_t)(((gi >> 1) - 1) & 1), a.err, 11))) {
+                    ok = false;
+                    break;
+                }
+                if (sb & 1) {
+                    *(uint4*)(qg + m * 16) = zero4;
+                    *(uint4*)(qg + QA2_BYTES + m * 16) = zero4;
+                }
+            }
+            {
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+                uint32_t hw[4], lw[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t sc0, mn0, sc1, mn1;
+                    scale_min(hdr, 2 * q, sc0, mn0);
+                    scale_min(hdr, 2 * q + 1, sc1, mn1);
+                    const int kstep = 4 * sb + q;
+                    const bool in = kstep >= ks && kstep < ke;
+                    const float c0 = in ? dmin * (float)mn0 : 0.f, c1 = in ? dmin * (float)mn1 : 0.f;
+                    const __half2 h = __floats2half2_rn(c0, c1);
+                    const float2 back = __half22float2(h);
+                    const __half2 l = __floats2half2_rn(c0 - back.x, c1 - back.y);
+                    hw[q] = *(const uint32_t*)&h;
+                    lw[q] = *(const uint32_t*)&l;
+                }
+                const uint32_t kg = (uint32_t)(sb & 1) * 2048u;
+                *(uint4*)(qg + kg + m * 16) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *(uint4*)(qg + QA2_BYTES + kg + m * 16) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            }
+            if (closes) {
+                if (!(sb & 1)) {
+                    *(uint4*)(qg + 2048 + m * 16) = zero4;
+                    *(uint4*)(qg + QA2_BYTES + 2048 + m * 16) = zero4;
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) bar_arrive_leader(&qa_full[g]);
+                ++gi;
+            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const int k = 4 * sb + kk;
+                if (k < ks || k >= ke || !ok) continue;
+                const int s = (int)(it % STAGES2);
+                // The A ring has STAGES (4) TMEM slots, the x ring STAGES2 (8)
+                // stages: slot it % 4 is free once the MMAs of K step it - 4
+                // have completed, which empty[(it - 4) % 8] reports.
+                const int sa = (int)(it % STAGES);
+                if (it >= STAGES) {
+                    const long long j = it - STAGES;
+                    if (!__all_sync(0xffffffffu, bar_wait_cl(&empty[j % STAGES2], (uint32_t)((j / STAGES2) & 1), a.err, 12))) {
+                        ok = false;
+                        continue;
+                    }
+                }
+                uint32_t sc0, mn0, sc1, mn1;
+                scale_min(hdr, 2 * kk, sc0, mn0);
+                scale_min(hdr, 2 * kk + 1, sc1, mn1);
+                uint32_t w[32];
+                {
+                    uint4 c4[4];
+                    subblock_sc_q(raw[1 + 2 * kk], sc0, c4);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        w[4 * i] = c4[i].x;
+                        w[4 * i + 1] = c4[i].y;
+                        w[4 * i + 2] = c4[i].z;
+                        w[4 * i + 3] = c4[i].w;
+                    }
+                    subblock_sc_q(raw[2 + 2 * kk], sc1, c4);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        w[16 + 4 * i] = c4[i].x;
+                        w[16 + 4 * i + 1] = c4[i].y;
+                        w[16 + 4 * i + 2] = c4[i].z;
+                        w[16 + 4 * i + 3] = c4[i].w;
+                    }
+                }
+                tmem_st32(lane_a + (uint32_t)(32 * sa), w);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) bar_arrive_leader(&full[s]);
+                ++it;
+            }
+            cur.next();
+        }
+    } else if (warp == TMA_WARP) {
+        // ---------------- x halves, sub-block sums (both CTAs), raw weights ----------------
+        if (lane == 0) {
+            long long it = 0, gi = 0, go = 0, ri = 0;
+            SbsIt cur;
+            cur.start(u0, u1, nk);
+            SbsIt rw = cur;
+            const int wrow0 = (int)rank * BM;
+            auto raw_issue = [&]() {
+                const int r = (int)(ri & 1);
+                if (ri >= 2 && !bar_wait(&raw_empty[r], (uint32_t)(((ri >> 1) - 1) & 1), a.err, 23))
+                    return false;
+                bar_expect(&raw_full[r], (uint32_t)RAW_BYTES);
+                tma_2d(rawbuf + r * RAW_BYTES, &wmap, &raw_full[r], rw.sb * 144,
+                       (rw.t / a.NT) * 2 * BM + wrow0);
+                ++ri;
+                rw.next();
+                return true;
+            };
+            if (rw.valid() && !raw_issue()) ok = false;
+            while (cur.valid() && ok) {
+                if (rw.valid() && !raw_issue()) {
+                    ok = false;
+                    break;
+                }
+                const int sb = cur.sb;
+                const int ks = max(cur.ka, 4 * sb), ke = min(cur.kb, 4 * sb + 4);
+                const bool first = sb == cur.ka / 4, last = sb == (cur.kb - 1) / 4;
+                const bool opens = first || !(sb & 1), closes = last || (sb & 1);
+                const int g = (int)(gi & 1);
+                const int n0 = (cur.t % a.NT) * (2 * BN2) + (int)rank * BN2;   // this CTA's x rows
+                if (opens) {
+                    if (gi >= 2 &&
+                        !bar_wait_cl(&qa_empty[g], (uint32_t)(((gi >> 1) - 1) & 1), a.err, 13)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* qg = qbuf + g * QGRP2_BYTES + 2 * QA2_BYTES;
+                    if (leader) bar_expect(&qa_full[g], (uint32_t)(2 * 2 * QB2_BYTES));
+                    const int sb0 = sb & ~1;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int y = (sb0 + h) * a.r_pad + n0;
+                        tma_2d_2sm(qg + h * (QB2_BYTES / 2), &xsmap_hi, &qa_full[g], 0, y);
+                        tma_2d_2sm(qg + QB2_BYTES + h * (QB2_BYTES / 2), &xsmap_lo, &qa_full[g], 0, y);
+                    }
+                    ++go;
+                }
+                if (closes) ++gi;
+                for (int k = ks; k < ke; ++k, ++it) {
+                    const int s = (int)(it % STAGES2);
+                    if (it >= STAGES2 &&
+                        !bar_wait_cl(&empty[s], (uint32_t)(((it / STAGES2) - 1) & 1), a.err, 14)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* st = bst + (size_t)s * STAGE2_BYTES;
+                    if (leader) bar_expect(&full[s], (uint32_t)(2 * STAGE2_BYTES));
+                    tma_2d_2sm(st, &xmap_hi, &full[s], k * BK, n0);
+                    tma_2d_2sm(st + B2_BYTES, &xmap_lo, &full[s], k * BK, n0);
+                }
+                cur.next();
+            }
+            // local copies must land before the CTA exits (the x halves and sums
+            // complete on the leader's barriers, which the leader's MMA waits for)
+            for (long long i = ri - 2 > 0 ? ri - 2 : 0; i < ri; ++i)
+                bar_wait(&raw_full[i & 1], (uint32_t)((i >> 1) & 1), a.err, 15);
+            (void)go;
+        }
+    } else if (warp == MMA_WARP) {
+        // ---------------- MMA issue (leader only) ----------------
+        if (lane == 0 && leader) {
+            const uint32_t idesc = (1u << 4) | ((uint32_t)((2 * BN2) >> 3) << 17) |
+                                   ((uint32_t)((2 * BM) >> 4) << 24);
+            long long it = 0, si = 0, gi = 0, seg = 0;
+            bool q_fresh = true;
+            SbsIt cur;
+            cur.start(u0, u1, nk);
+            while (cur.valid() && ok) {
+                const int sb = cur.sb;
+                const int ks = max(cur.ka, 4 * sb), ke = min(cur.kb, 4 * sb + 4);
+                const bool first = sb == cur.ka / 4, last = sb == (cur.kb - 1) / 4;
+                const bool closes = last || (sb & 1);
+                const int p = (int)(si & 1), g = (int)(gi & 1);
+                if (first) q_fresh = true;
+                if (si >= 2 &&
+                    !bar_wait_cl(&acc_empty[p], (uint32_t)(((si >> 1) - 1) & 1), a.err, 16)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t p1 = tmem + (uint32_t)(p * 128);
+                for (int k = ks; k < ke; ++k, ++it) {
+                    const int s = (int)(it % STAGES2), sa = (int)(it % STAGES);
+                    if (!bar_wait_cl(&full[s], (uint32_t)((it / STAGES2) & 1), a.err, 17)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t bh = su32(bst + (size_t)s * STAGE2_BYTES), bl = bh + B2_BYTES;
+                    const uint32_t at = tmem + COL_A + (uint32_t)(32 * sa);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        mma2_ta(p1, at + 8u * kk, desc_sw128(bh + 32u * kk), idesc,
+                                (k > ks || kk > 0) ? 1u : 0u);
+                        mma2_ta(p1, at + 8u * kk, desc_sw128(bl + 32u * kk), idesc, 1u);
+                    }
+                    commit2(&empty[s]);
+                }
+                if (!ok) break;
+                if (closes) {
+                    if (!bar_wait_cl(&qa_full[g], (uint32_t)((gi >> 1) & 1), a.err, 18) ||
+                        (q_fresh && seg > 0 &&
+                         !bar_wait_cl(&q_empty, (uint32_t)((seg - 1) & 1), a.err, 20))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t qa = su32(qbuf + g * QGRP2_BYTES);
+                    const uint32_t qb = qa + 2 * QA2_BYTES;
+                    const uint32_t cq = tmem + COL_Q;
+                    mma2_ss(cq, desc_plain_lbo(qa, 2048), desc_plain_lbo(qb, QB2_BYTES / 2), idesc,
+                            q_fresh ? 0u : 1u);
+                    mma2_ss(cq, desc_plain_lbo(qa, 2048), desc_plain_lbo(qb + QB2_BYTES, QB2_BYTES / 2),
+                            idesc, 1u);
+                    mma2_ss(cq, desc_plain_lbo(qa + QA2_BYTES, 2048), desc_plain_lbo(qb, QB2_BYTES / 2),
+                            idesc, 1u);
+                    q_fresh = false;
+                    commit2(&qa_empty[g]);
+                    ++gi;
+                    if (last) {
+                        commit2(&q_full);
+                        ++seg;
+                    }
+                }
+                commit2(&acc_full[p]);
+                ++si;
+                cur.next();
+            }
+        }
+    } else {
+        // ---------------- drain (both CTAs): own 128 rows x 128 columns ----------------
+        const int q = warp & 3, m = q * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        const int mrow0 = (int)rank * BM;                 // this CTA's rows within the pair tile
+        float acc[BN];
+#pragma unroll
+        for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+        long long si = 0, seg = 0;
+        SbsIt cur;
+        cur.start(u0, u1, nk);
+        while (cur.valid()) {
+            const int t = cur.t, ka = cur.ka, kb = cur.kb, sb = cur.sb;
+            const bool last = sb == (kb - 1) / 4;
+            const int mt = t / a.NT, n0 = (t % a.NT) * BN;
+            const int p = (int)(si & 1);
+            const int grow = mt * 2 * BM + mrow0 + m;     // global weight row
+            const uint32_t dd = __ldg((const uint32_t*)(a.W + (size_t)grow * row_bytes + (size_t)sb * 144));
+            const float d = __half2float(__ushort_as_half((unsigned short)(dd & 0xffffu)));
+            bool have = ok && bar_wait_cl(&acc_full[p], (uint32_t)((si >> 1) & 1), a.err, 19);
+            have = __all_sync(0xffffffffu, have);
+            if (have) {
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(lane_base + (uint32_t)(p * 128 + c0), v);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) acc[c0 + i] = fmaf(d, v[i], acc[c0 + i]);
+                }
+            } else {
+                ok = false;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) bar_arrive_leader(&acc_empty[p]);
+            ++si;
+            if (last) {
+                have = ok && bar_wait_cl(&q_full, (uint32_t)(seg & 1), a.err, 21);
+                have = __all_sync(0xffffffffu, have);
+                if (have) {
+                    tc_fence_after();
+#pragma unroll
+                    for (int c0 = 0; c0 < BN; c0 += 16) {
+                        float v[16];
+                        tmem_ld16(lane_base + COL_Q + (uint32_t)c0, v);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) acc[c0 + i] -= v[i];
+                    }
+                } else {
+                    ok = false;
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) bar_arrive_leader(&q_empty);
+                ++seg;
+                // this CTA's 128-row slab of pair tile t behaves as one-SM tile mt*2 + rank
+                const int mt1 = mt * 2 + (int)rank;
+                if (ka == 0 && kb == nk) {
+                    tile_out(a, acc, mt1, n0, m, xch);
+                } else {
+                    const long long tu0 = (long long)t * nk;
+                    const int slot = u0 >= tu0 ? 0 : 1;
+                    float* wsp = a.ws + (((size_t)c * 2 + slot) * 2 + rank) * (BN * BM);
+#pragma unroll
+                    for (int j = 0; j < BN; ++j) wsp[(size_t)j * BM + m] = acc[j];
+                    __threadfence();
+                    drain_sync();
+                    const int cf = owner_of(tu0, C, U), cl = owner_of(tu0 + nk - 1, C, U);
+                    if (warp == DRAIN_WARP0 && lane == 0) {
+                        const int prev = atomicAdd(&a.cnt[t * 2 + (int)rank], 1);
+                        last_flag = prev == cl - cf;
+                    }
+                    drain_sync();
+                    if (last_flag) {
+                        __threadfence();
+#pragma unroll
+                        for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+                        for (int cc = cf; cc <= cl; ++cc) {
+                            const int sl = u_begin(cc, C, U) >= tu0 ? 0 : 1;
+                            const float* src = a.ws + (((size_t)cc * 2 + sl) * 2 + rank) * (BN * BM);
+#pragma unroll
+                            for (int j = 0; j < BN; ++j) acc[j] += __ldcg(src + (size_t)j * BM + m);
+                        }
+                        tile_out(a, acc, mt1, n0, m, xch);
+                        if (warp == DRAIN_WARP0 && lane == 0) a.cnt[t * 2 + (int)rank] = 0;
+                    }
+                    drain_sync();
+                }
+#pragma unroll
+                for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+            }
+            cur.next();
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                 // no CTA leaves while its peer may still address it
+    if (warp == MMA_WARP) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+}
+
 // f32 activations -> f16 hi / lo rows plus the per-sub-block sums X_j as f16
 // hi / lo in [K/256][r_pad][8] (one thread per (row, sub-block)).
 __global__ void q4_split_kernel(const float* __restrict__ X, int ldx, int n_rows, int K,
@@ -816,15 +1348,22 @@ extern "C" int sb_q4_make_operand(sb_q4_operand* op, void* hi, void* lo, void* x
     op->r_pad = r_pad;
     op->K = K;
     op->ld16 = ld16;
-    for (int part = 0; part < 2; ++part) {
-        cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-        cuuint64_t strides[1] = {(cuuint64_t)ld16 * 2};
-        cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BN};
+    const cuuint64_t nsb = (cuuint64_t)((K / 256 + 1) & ~1);
+    for (int part = 0; part < 6; ++part) {
+        // parts 0-1: x hi / lo, 64 x 128 boxes; 2-3: x hi / lo, 64 x 64 boxes;
+        // 4-5: sub-block sums hi / lo as [nsb * r_pad][8] with 8 x 64 boxes
+        unsigned char* maps[6] = {op->map_hi, op->map_lo, op->map2_hi, op->map2_lo, op->xsmap_hi,
+                                  op->xsmap_lo};
+        void* base[6] = {hi, lo, hi, lo, xs_hi, xs_lo};
+        const bool xs = part >= 4;
+        cuuint64_t dims[2] = {xs ? 8 : (cuuint64_t)K, xs ? nsb * (cuuint64_t)r_pad : (cuuint64_t)rows};
+        cuuint64_t strides[1] = {xs ? 16 : (cuuint64_t)ld16 * 2};
+        cuuint32_t box[2] = {xs ? 8u : (cuuint32_t)BK, part < 2 ? (cuuint32_t)BN : (cuuint32_t)BN2};
         cuuint32_t estr[2] = {1, 1};
-        CUresult r = enc((CUtensorMap*)(part ? op->map_lo : op->map_hi), CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                         2, part ? lo : hi, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        CUresult r = enc((CUtensorMap*)maps[part], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base[part], dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         xs ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) {
             sb_set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
             return -1;
@@ -857,6 +1396,7 @@ extern "C" void sb_q4_prepare(void) {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
     cudaFuncSetAttribute(q4k_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+    cudaFuncSetAttribute(q4k_gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2);
 }
 
 extern "C" int sb_q4_gemm(const sb_matrix* W, const sb_q4_operand* X, int n_rows, float* Y, int ldy,
@@ -903,6 +1443,32 @@ extern "C" int sb_q4_gemm(const sb_matrix* W, const sb_q4_operand* X, int n_rows
             sb_set_error("Q4_K tensor map: cuTensorMapEncodeTiled failed (%d)", (int)r);
             return -1;
         }
+    }
+    const char* one = getenv("SLATE_Q4_ONE_SM");
+    if (W->M_pad % (2 * BM) == 0 && !(one && one[0] == '1') && g_sms >= 2) {
+        // pairs of CTAs over tiles of 256 weight rows x 128 activation rows
+        const long long U = (long long)(W->M_pad / (2 * BM)) * a.NT * (W->K / BK);
+        const int C = (int)(U < g_sms / 2 ? U : g_sms / 2);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(2 * C));
+        cfg.blockDim = dim3(NTHREADS);
+        cfg.dynamicSmemBytes = SMEM2;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        CUtensorMap m2h, m2l, xsh, xsl;
+        memcpy(&m2h, X->map2_hi, sizeof m2h);
+        memcpy(&m2l, X->map2_lo, sizeof m2l);
+        memcpy(&xsh, X->xsmap_hi, sizeof xsh);
+        memcpy(&xsl, X->xsmap_lo, sizeof xsl);
+        return cudaLaunchKernelEx(&cfg, q4k_gemm2_kernel, m2h, m2l, xsh, xsl, wmap, a) == cudaSuccess
+                   ? 0
+                   : -5;
     }
     const long long U = (long long)(W->M_pad / BM) * a.NT * (W->K / BK);
     const int C = (int)(U < g_sms ? U : g_sms);

@@ -61,8 +61,12 @@ int sb_tc_gemm_f16w(const sb_tc_weight* W, const sb_tc_operand* X, int n_rows, f
  * of x as f16 hi / lo in [K/256 rounded up to even][r_pad][8] (r_pad: rows
  * rounded up to 128; zero-filled once, the padding block stays zero). */
 typedef struct sb_q4_operand {
-    SB_ALIGN64 unsigned char map_hi[128];
+    SB_ALIGN64 unsigned char map_hi[128];    /* x boxes 64 x 128 (one-SM kernel) */
     SB_ALIGN64 unsigned char map_lo[128];
+    SB_ALIGN64 unsigned char map2_hi[128];   /* x boxes 64 x 64 (two-SM kernel) */
+    SB_ALIGN64 unsigned char map2_lo[128];
+    SB_ALIGN64 unsigned char xsmap_hi[128];  /* sub-block sums, boxes 8 x 64 */
+    SB_ALIGN64 unsigned char xsmap_lo[128];
     void *hi, *lo, *xs_hi, *xs_lo;
     int rows, r_pad, K, ld16;
 } sb_q4_operand;
@@ -71,7 +75,8 @@ int sb_q4_make_operand(sb_q4_operand* op, void* hi, void* lo, void* xs_hi, void*
 /* X (f32, stride ldx, ldx % 4 == 0) -> hi / lo / sub-block sums, n_rows rows. */
 int sb_q4_split(const float* X, int ldx, int n_rows, const sb_q4_operand* op, cudaStream_t st);
 /* Y[n][m] (=, +=, SiLU(gate)*up) over Q4_K W for n < n_rows, two f16 passes with
- * exact weights.  ws: sb_q4_ws_floats() floats; cnt: sb_q4_tiles(M_pad, n_rows)
+ * exact weights; weights with M_pad % 256 == 0 run on CTA pairs (cta_group::2)
+ * unless SLATE_Q4_ONE_SM=1.  ws: sb_q4_ws_floats() floats; cnt: sb_q4_tiles(M_pad, n_rows)
  * ints, zero before the first call (the kernel leaves them zero). */
 int sb_q4_gemm(const sb_matrix* W, const sb_q4_operand* X, int n_rows, float* Y, int ldy, int epi,
                float* ws, int* cnt, int* err, cudaStream_t st);

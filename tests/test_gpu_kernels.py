@@ -228,12 +228,15 @@ def test_matmul_q4k_tensor_cores(be, oracle, sb, B, M, K, passes, tol):
 @pytest.mark.parametrize("B,M,K", [(1, 128, 256), (5, 256, 1024), (16, 128, 256), (130, 384, 4096),
                                    (256, 1024, 4096), (256, 6144, 4096), (100, 256, 14336),
                                    (300, 256, 512), (513, 512, 2048)])
-def test_matmul_q4k_exact_weights(be, oracle, sb, B, M, K):
+@pytest.mark.parametrize("one_sm", ["0", "1"])
+def test_matmul_q4k_exact_weights(be, oracle, sb, monkeypatch, B, M, K, one_sm):
     """passes=2: f16(sc*q) weights are exact, x enters as f16 hi + lo, the
     d / dmin block scales are applied per super-block in f32 -- f32-level
     products like the 3-pass split, over a stream-K schedule whose shared tiles
     are summed by the last CTA to finish (shapes with 1..5 tiles per SM and
-    partial row tiles)."""
+    partial row tiles).  Weights with M % 256 == 0 run on CTA pairs unless
+    SLATE_Q4_ONE_SM=1 keeps them on single CTAs."""
+    monkeypatch.setenv("SLATE_Q4_ONE_SM", one_sm)
     rng = np.random.default_rng(B * 7 + M + K)
     q = sb.quantize_q4k(rng.normal(0, 0.02, (M, K)).astype(np.float32))
     X = rng.normal(0, 1, (B, K)).astype(np.float32)
