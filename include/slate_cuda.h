@@ -123,6 +123,14 @@ const slate_backend_cuda_t* slate_backend_cuda_create(int device);
  * calling thread ("" if none). */
 const char* slate_cuda_last_error(void);
 
+struct slate_sampler_config;
+/* Draws one token per row of DEVICE logits (B rows of V, row stride ld) with
+ * the reference sampler's rules (slate_sample_token, util/sampling.c:9-83)
+ * from HOST configurations and RNG states; out_tokens (host) and rng_state
+ * (advanced as the reference advances it) are written back.  Synchronous. */
+int slate_cuda_sample_rows(int32_t* out_tokens, const float* logits, int ld, int B, int V,
+                           const struct slate_sampler_config* cfg, uint64_t* rng_state);
+
 /* attention_paged_gqa for callers that cannot allocate device memory during
  * the call (an allocator that has already given all free HBM to its KV pool;
  * a latency-critical loop that must not enter the driver's allocator).  This
@@ -213,6 +221,17 @@ int slate_cuda_tp_unique_id(void* out, size_t n);
 
 typedef struct slate_llama_batch slate_llama_batch_t;
 
+#ifndef SLATE_SAMPLING_H
+#define SLATE_SAMPLING_H
+/* Identical to include/slate/sampling.h:15-20. */
+typedef struct slate_sampler_config {
+    float temperature;   /* 0 = greedy / argmax; > 0 = sample */
+    int   top_k;         /* 0 = disabled; > 0 = restrict to top-k tokens */
+    float top_p;         /* 0 = disabled; (0, 1] = nucleus sampling */
+    uint64_t seed;
+} slate_sampler_config_t;
+#endif
+
 /* Uploads the weights once and creates the KV page pool.
  * KV pool layout in HBM (one pool, layer-major):
  *   pool[layer][page][kv = 0 (K) | 1 (V)][kv_head][16 tokens][head_dim]
@@ -244,6 +263,17 @@ int slate_llama_batch_position(const slate_llama_batch_t* b, int slot);
  * -5; on error no sequence advances. */
 int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
                            const int32_t* tokens, int32_t* out_tokens, float* out_logits);
+
+/* One step whose next tokens are drawn by the reference sampler's rules
+ * (slate_sample_token, util/sampling.c:9-83) on the device: per row a
+ * sampler configuration and an RNG state, advanced exactly as the reference
+ * advances it (rows with temperature <= 0 take the greedy token and keep their
+ * state).  Same slots / positions / return codes as slate_llama_batch_step;
+ * top_k up to 2048 (or >= vocab, i.e. off).  Not available with tensor
+ * parallelism. */
+int slate_llama_batch_step_sample(slate_llama_batch_t* b, const int32_t* slots, int n,
+                                  const int32_t* tokens, const slate_sampler_config_t* cfg,
+                                  uint64_t* rng_state, int32_t* out_tokens, float* out_logits);
 
 /* The same step on DEVICE buffers, enqueued on `stream` (a cudaStream_t, or
  * NULL for the engine's stream) without host synchronisation; token / slot

@@ -219,6 +219,12 @@ class RefLlamaConfig(C.Structure):
         ("theta_base", C.c_float), ("rms_eps", C.c_float), ("tied_output", C.c_int)]
 
 
+class RefSamplerConfig(C.Structure):
+    """slate_sampler_config_t as include/slate/sampling.h:15-20 declares it."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float),
+                ("seed", C.c_uint64)]
+
+
 class Reference:
     """The reference library itself (unmodified sources, oracle/_ref)."""
 
@@ -247,10 +253,20 @@ class Reference:
             ("slate_backend_cpu", C.c_void_p, []),
             ("slate_backend_cuda", C.c_void_p, []),
             ("slate_backend_default", C.c_void_p, []),
+            ("slate_sample_token", C.c_int,
+             [Pf, C.c_int, C.POINTER(RefSamplerConfig), C.POINTER(C.c_uint64)]),
         ]:
             fn = getattr(L, name)
             fn.restype = res
             fn.argtypes = args
+
+    def sample_token(self, logits, temperature, top_k, top_p, rng):
+        """slate_sample_token (util/sampling.c:43-83) -> (token, next rng state)."""
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        cfg = RefSamplerConfig(float(temperature), int(top_k), float(top_p), 0)
+        st = C.c_uint64(int(rng))
+        tok = self.lib.slate_sample_token(lg.ctypes.data_as(Pf), len(lg), C.byref(cfg), C.byref(st))
+        return int(tok), int(st.value)
 
     def open(self, path: str):
         g = self.lib.slate_gguf_open(path.encode())

@@ -57,6 +57,20 @@ class CudaOpts(C.Structure):
                 ("tp_id", C.c_ubyte * 128)]
 
 
+class SamplerConfig(C.Structure):
+    """slate_sampler_config_t (include/slate/sampling.h:15-20)."""
+    _fields_ = [("temperature", c_float), ("top_k", c_int), ("top_p", c_float), ("seed", c_u64)]
+
+
+def sampler_configs(n, temperature=1.0, top_k=0, top_p=0.0):
+    """An array of n SamplerConfig; each argument a scalar or a length-n sequence."""
+    arr = (SamplerConfig * n)()
+    t, k, p = (np.broadcast_to(np.asarray(v), (n,)) for v in (temperature, top_k, top_p))
+    for i in range(n):
+        arr[i] = SamplerConfig(float(t[i]), int(k[i]), float(p[i]), 0)
+    return arr
+
+
 class SynthConfig(C.Structure):
     _fields_ = [(n, c_int) for n in ("n_layers", "d_model", "ffn_hidden", "n_heads", "n_kv_heads",
                                      "vocab", "max_seq")] + [
@@ -89,6 +103,7 @@ EXPORTS = {
     "slate_backend_cuda_create": (C.POINTER(BackendCuda), c_int),
     "slate_cuda_last_error": (C.c_char_p,),
     "slate_cuda_tp_unique_id": (c_int, P, c_size),
+    "slate_cuda_sample_rows": (c_int, Pi32, P, c_int, c_int, c_int, P, C.POINTER(c_u64)),
     "slate_cuda_attention_paged_gqa_noalloc": (c_int, P, P, P, P, P, c_int, P, c_int64, c_int, c_int,
                                                c_int, c_int, c_int, c_int, P),
     "slate_llama_batch_new_desc": (P, C.POINTER(LlamaDesc), C.POINTER(CudaOpts)),
@@ -102,6 +117,7 @@ EXPORTS = {
     "slate_llama_batch_close": (c_int, P, c_int),
     "slate_llama_batch_position": (c_int, P, c_int),
     "slate_llama_batch_step": (c_int, P, Pi32, c_int, Pi32, Pi32, Pf32),
+    "slate_llama_batch_step_sample": (c_int, P, Pi32, c_int, Pi32, P, C.POINTER(c_u64), Pi32, Pf32),
     "slate_llama_batch_step_device": (c_int, P, P, c_int, P, P, P, P),
     "slate_llama_batch_sync": (c_int, P),
     "slate_llama_batch_prefill": (c_int, P, c_int, Pi32, c_int, Pf32),
@@ -153,6 +169,16 @@ def synth_gguf(path: str, *, n_layers, d_model, ffn_hidden, n_heads, n_kv_heads,
     rc = F["slate_synth_llama_gguf"](path.encode(), C.byref(cfg))
     if rc:
         raise OSError(f"slate_synth_llama_gguf({path}) rc={rc}")
+
+
+def sample_rows(d_logits, ld, B, V, cfg, rng):
+    """slate_cuda_sample_rows: device logits pointer, host configs and uint64
+    RNG states (updated in place).  Returns (rc, tokens[B])."""
+    assert rng.dtype == np.uint64 and rng.flags.c_contiguous and len(rng) == B
+    out = np.zeros(B, dtype=np.int32)
+    rc = F["slate_cuda_sample_rows"](_ptr(out, C.c_int32), d_logits, ld, B, V, C.byref(cfg),
+                                     rng.ctypes.data_as(C.POINTER(c_u64)))
+    return rc, out
 
 
 def tp_unique_id() -> bytes:
@@ -214,6 +240,22 @@ class LlamaBatch:
         rc = F["slate_llama_batch_step"](self.h, _ptr(slots, C.c_int32), n, _ptr(tokens, C.c_int32),
                                          _ptr(out, C.c_int32),
                                          _ptr(lg) if lg is not None else None)
+        return rc, out, lg
+
+    def step_sample(self, slots, tokens, cfg, rng, want_logits=False):
+        """Sampling step: cfg from sampler_configs(n, ...), rng uint64[n] (updated
+        in place).  Returns (rc, out_tokens[n], logits[n, V] or None)."""
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        n = len(slots)
+        assert rng.dtype == np.uint64 and rng.flags.c_contiguous and len(rng) == n
+        out = np.zeros(n, dtype=np.int32)
+        lg = np.zeros((n, self.vocab), dtype=np.float32) if want_logits else None
+        rc = F["slate_llama_batch_step_sample"](self.h, _ptr(slots, C.c_int32), n,
+                                                _ptr(tokens, C.c_int32), C.byref(cfg),
+                                                rng.ctypes.data_as(C.POINTER(c_u64)),
+                                                _ptr(out, C.c_int32),
+                                                _ptr(lg) if lg is not None else None)
         return rc, out, lg
 
     def step_device(self, d_slots, n, d_tokens, d_out_tokens, d_out_logits=None, stream=None):

@@ -253,6 +253,49 @@ static int be_matmul_q4k_tc(float* Y, const void* A, const float* X, int B, int 
     return rc;
 }
 
+int slate_cuda_sample_rows(int32_t* out_tokens, const float* logits, int ld, int B, int V,
+                           const slate_sampler_config_t* cfg, uint64_t* rng_state) {
+    if (!out_tokens || !logits || !cfg || !rng_state || B < 1 || V < 1 || ld < V) {
+        sb_set_error("sample_rows: bad arguments");
+        return -1;
+    }
+    for (int r = 0; r < B; ++r)
+        if (cfg[r].temperature > 0.0f && cfg[r].top_k > SB_SAMPLE_TOPK_MAX && cfg[r].top_k < V) {
+            sb_set_error("top_k %d above the device sampler's %d", cfg[r].top_k, SB_SAMPLE_TOPK_MAX);
+            return -1;
+        }
+    sb_sampler* hc = (sb_sampler*)malloc((size_t)B * sizeof(sb_sampler));
+    if (!hc) return -5;
+    for (int r = 0; r < B; ++r) hc[r] = (sb_sampler){cfg[r].temperature, cfg[r].top_k, cfg[r].top_p, 0};
+    void *dc = NULL, *dr = NULL, *dout = NULL, *scr = NULL;
+    int rc = sb_cuda_check(cudaDeviceSynchronize(), "sample_rows: pending work");
+    if (!rc) rc = sb_cuda_check(cudaMalloc(&dc, (size_t)B * sizeof(sb_sampler)), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMalloc(&dr, (size_t)B * 8), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMalloc(&dout, (size_t)B * 4 + 16), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMalloc(&scr, (size_t)B * V * 4), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMemset(dout, 0, (size_t)B * 4 + 16), "memset");
+    if (!rc) rc = sb_cuda_check(cudaMemcpy(dc, hc, (size_t)B * sizeof(sb_sampler), cudaMemcpyHostToDevice), "H2D");
+    if (!rc) rc = sb_cuda_check(cudaMemcpy(dr, rng_state, (size_t)B * 8, cudaMemcpyHostToDevice), "H2D");
+    int* err = dout ? (int*)((int32_t*)dout + B) : NULL;
+    if (!rc && sb_sample_rows(logits, ld, V, B, (const sb_sampler*)dc, (uint64_t*)dr, (float*)scr,
+                              (int32_t*)dout, NULL, NULL, NULL, NULL, err, 0))
+        rc = -1;
+    int e = 0;
+    if (!rc) rc = sb_cuda_check(cudaMemcpy(out_tokens, dout, (size_t)B * 4, cudaMemcpyDeviceToHost), "D2H");
+    if (!rc) rc = sb_cuda_check(cudaMemcpy(rng_state, dr, (size_t)B * 8, cudaMemcpyDeviceToHost), "D2H");
+    if (!rc) rc = sb_cuda_check(cudaMemcpy(&e, err, 4, cudaMemcpyDeviceToHost), "D2H");
+    if (!rc && e) {
+        sb_set_error("sampler reported %d", e);
+        rc = -1;
+    }
+    cudaFree(dc);
+    cudaFree(dr);
+    cudaFree(dout);
+    cudaFree(scr);
+    free(hc);
+    return rc;
+}
+
 const slate_backend_cuda_t* slate_backend_cuda_create(int device) {
     pthread_mutex_lock(&g_init);
     const slate_backend_cuda_t* r = NULL;

@@ -92,6 +92,14 @@ struct slate_llama_batch {
     void* comm;                    /* NCCL communicator (tp > 1) */
     void *pairs, *pairs_all;       /* per-row (max, index) of this rank / of all ranks */
     float* logits_all;             /* [tp][max_batch][ld_logits], gathered on request */
+    /* stochastic sampling (allocated on first use): per-row configs and RNG
+     * states (device + pinned host mirrors), softmax scratch, graphs per n */
+    sb_sampler* d_samp;
+    uint64_t* d_rng;
+    float* samp_scratch;
+    sb_sampler* h_samp;
+    uint64_t* h_rng;
+    cudaGraphExec_t* graphs_s;
 };
 
 /* Rows from which a Q4_K GEMM runs on the tensor cores (below: CUDA cores). */
@@ -238,7 +246,7 @@ static int upload_f32(slate_llama_batch_t* b, float** dst, const void* src, size
 
 /* ---- step enqueue ------------------------------------------------------- */
 
-static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
+static int enqueue_step(slate_llama_batch_t* b, int n, int sample, cudaStream_t s) {
     int rc = 0;
     /* cudaGetLastError() below must only see this step's launches: a failure
      * left by an earlier unchecked call on this thread is cleared here (a
@@ -274,7 +282,10 @@ static int enqueue_step(slate_llama_batch_t* b, int n, cudaStream_t s) {
     }
     rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, b->out_norm, n, b->D, b->eps, s);
     rc |= step_gemm(b, &b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE, 1, s);
-    if (b->tp > 1) {
+    if (sample) {
+        rc |= sb_sample_rows(b->logits, b->ld_logits, b->V, n, b->d_samp, b->d_rng, b->samp_scratch,
+                             out, b->row_slot, b->row_pos, b->pos, b->status, b->tc_err, s);
+    } else if (b->tp > 1) {
         rc |= sb_argmax_pairs(b->logits, b->ld_logits, b->V_l, n, b->v0, b->pairs, s);
         rc |= sb_tp_allgather(b->comm, b->pairs, b->pairs_all, (size_t)n * 8, s);
         rc |= sb_tp_epilogue(b->pairs_all, b->tp, n, b->row_slot, b->row_pos, b->pos, b->status,
@@ -315,25 +326,29 @@ int slate_llama_batch_launches_per_step(const slate_llama_batch_t* b, int n) {
 }
 
 /* Runs the step for n rows whose metadata is already in d_io. */
-static int run_step(slate_llama_batch_t* b, int n) {
-    if (!b->use_graphs) return enqueue_step(b, n, b->stream);
-    if (!b->graphs[n]) {
+/* Runs the step for n rows whose metadata is already in d_io; sample != 0
+ * ends it with the stochastic sampler instead of the greedy argmax. */
+static int run_step_mode(slate_llama_batch_t* b, int n, int sample) {
+    if (!b->use_graphs) return enqueue_step(b, n, sample, b->stream);
+    cudaGraphExec_t* slot = sample ? &b->graphs_s[n] : &b->graphs[n];
+    if (!*slot) {
         cudaGraph_t g = NULL;
         SB_CU(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
-        int rc = enqueue_step(b, n, b->stream);
+        int rc = enqueue_step(b, n, sample, b->stream);
         cudaError_t e = cudaStreamEndCapture(b->stream, &g);
         if (rc) {
             if (g) cudaGraphDestroy(g);
             return rc;
         }
         SB_CU(e);
-        e = cudaGraphInstantiate(&b->graphs[n], g, 0);
+        e = cudaGraphInstantiate(slot, g, 0);
         cudaGraphDestroy(g);
         SB_CU(e);
     }
-    SB_CU(cudaGraphLaunch(b->graphs[n], b->stream));
+    SB_CU(cudaGraphLaunch(*slot, b->stream));
     return 0;
 }
+static int run_step(slate_llama_batch_t* b, int n) { return run_step_mode(b, n, 0); }
 
 /* ---- construction ------------------------------------------------------- */
 
@@ -346,6 +361,13 @@ void slate_llama_batch_free(slate_llama_batch_t* b) {
             if (b->graphs[i]) cudaGraphExecDestroy(b->graphs[i]);
         free(b->graphs);
     }
+    if (b->graphs_s) {
+        for (int i = 0; i <= b->max_batch; ++i)
+            if (b->graphs_s[i]) cudaGraphExecDestroy(b->graphs_s[i]);
+        free(b->graphs_s);
+    }
+    if (b->h_samp) cudaFreeHost(b->h_samp);
+    if (b->h_rng) cudaFreeHost(b->h_rng);
     sb_tc_free_weight(&b->head_tc);
     if (b->comm) sb_tp_destroy(b->comm);      /* after the graphs that hold its collectives */
     for (int i = 0; i < b->n_allocs; ++i) cudaFree(b->allocs[i]);
@@ -828,6 +850,95 @@ int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
             for (int r = 0; r < n; ++r) {
                 if (b->h_pos[slots[r]] % SB_PAGE_TOKENS == 0) ++b->pages_used;
                 b->h_pos[slots[r]]++;
+            }
+            if (out_tokens) memcpy(out_tokens, h + 2 * b->max_batch, (size_t)n * 4);
+        }
+    }
+    pthread_mutex_unlock(&b->lock);
+    return rc;
+}
+
+/* Lazily creates the sampling buffers (outside any capture). */
+static int sampling_ready(slate_llama_batch_t* b) {
+    if (b->d_samp) return 0;
+    const int B = b->max_batch;
+    b->graphs_s = (cudaGraphExec_t*)calloc((size_t)B + 1, sizeof(cudaGraphExec_t));
+    b->d_samp = (sb_sampler*)dalloc(b, (size_t)B * sizeof(sb_sampler));
+    b->d_rng = (uint64_t*)dalloc(b, (size_t)B * 8);
+    b->samp_scratch = (float*)dalloc(b, (size_t)B * b->V * 4);
+    if (!b->graphs_s || !b->d_samp || !b->d_rng || !b->samp_scratch) return -5;
+    SB_CU(cudaHostAlloc((void**)&b->h_samp, (size_t)B * sizeof(sb_sampler), cudaHostAllocDefault));
+    SB_CU(cudaHostAlloc((void**)&b->h_rng, (size_t)B * 8, cudaHostAllocDefault));
+    return 0;
+}
+
+int slate_llama_batch_step_sample(slate_llama_batch_t* b, const int32_t* slots, int n,
+                                  const int32_t* tokens, const slate_sampler_config_t* cfg,
+                                  uint64_t* rng_state, int32_t* out_tokens, float* out_logits) {
+    if (!b || !slots || !tokens || !cfg || !rng_state || n < 1 || n > b->max_batch) return -1;
+    if (b->tp > 1) {
+        sb_set_error("sampling steps are not available with tensor parallelism");
+        return -1;
+    }
+    for (int r = 0; r < n; ++r)
+        if (cfg[r].temperature > 0.0f && cfg[r].top_k > SB_SAMPLE_TOPK_MAX && cfg[r].top_k < b->V) {
+            sb_set_error("top_k %d above the device sampler's %d", cfg[r].top_k, SB_SAMPLE_TOPK_MAX);
+            return -1;
+        }
+    pthread_mutex_lock(&b->lock);
+    int rc = refresh_positions(b);
+    int64_t new_pages = 0;
+    for (int r = 0; r < n && !rc; ++r) {
+        const int s = slots[r];
+        if (s < 0 || s >= b->max_slots || !b->h_open[s]) { rc = -1; break; }
+        for (int q = 0; q < r; ++q)
+            if (slots[q] == s) { rc = -1; break; }
+        if (rc) break;
+        if (b->h_pos[s] >= b->max_seq) { rc = -2; break; }
+        if (tokens[r] < 0 || tokens[r] >= b->V) { rc = -3; break; }
+        if (b->h_pos[s] % SB_PAGE_TOKENS == 0) ++new_pages;
+    }
+    if (!rc && b->pages_used + new_pages > b->n_pages) rc = -2;
+    if (!rc) {
+        cudaSetDevice(b->device);
+        rc = sampling_ready(b);
+    }
+    if (rc) {
+        pthread_mutex_unlock(&b->lock);
+        return rc;
+    }
+    int32_t* h = b->h_io;
+    memcpy(h, slots, (size_t)n * 4);
+    memcpy(h + b->max_batch, tokens, (size_t)n * 4);
+    for (int r = 0; r < n; ++r) {
+        b->h_samp[r] = (sb_sampler){cfg[r].temperature, cfg[r].top_k, cfg[r].top_p, 0};
+        b->h_rng[r] = rng_state[r];
+    }
+    rc = sb_cuda_check(cudaMemcpyAsync(b->d_io, h, (size_t)2 * b->max_batch * 4,
+                                       cudaMemcpyHostToDevice, b->stream), "H2D metadata");
+    if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(b->d_samp, b->h_samp, (size_t)n * sizeof(sb_sampler),
+                                                cudaMemcpyHostToDevice, b->stream), "H2D sampler");
+    if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(b->d_rng, b->h_rng, (size_t)n * 8,
+                                                cudaMemcpyHostToDevice, b->stream), "H2D rng");
+    if (!rc) rc = run_step_mode(b, n, 1);
+    if (!rc)
+        rc = sb_cuda_check(cudaMemcpyAsync(h + 2 * b->max_batch, b->d_io + 2 * b->max_batch,
+                                           (size_t)n * 4, cudaMemcpyDeviceToHost, b->stream),
+                           "D2H tokens");
+    if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(b->h_rng, b->d_rng, (size_t)n * 8,
+                                                cudaMemcpyDeviceToHost, b->stream), "D2H rng");
+    if (!rc) rc = status_readback(b);
+    if (!rc && out_logits) rc = copy_logits(b, n, out_logits, cudaMemcpyDeviceToHost);
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(b->stream), "step");
+    if (!rc) {
+        const int st = status_code(b);
+        if (st) {
+            rc = st;
+        } else {
+            for (int r = 0; r < n; ++r) {
+                if (b->h_pos[slots[r]] % SB_PAGE_TOKENS == 0) ++b->pages_used;
+                b->h_pos[slots[r]]++;
+                rng_state[r] = b->h_rng[r];
             }
             if (out_tokens) memcpy(out_tokens, h + 2 * b->max_batch, (size_t)n * 4);
         }

@@ -130,6 +130,17 @@ void sb_tp_destroy(void* comm);
 int sb_tp_allreduce_sum(void* comm, float* buf, size_t n, cudaStream_t st);
 int sb_tp_allgather(void* comm, const void* send, void* recv, size_t bytes, cudaStream_t st);
 
+/* Stochastic sampling with the reference sampler's semantics
+ * (util/sampling.c:9-83), one row of logits per CTA; rng[b] is advanced as
+ * the reference advances its state.  scratch: B * V floats.  With pos != NULL
+ * the positions advance like the greedy epilogue.  *err = 1 for a top_k above
+ * SB_SAMPLE_TOPK_MAX. */
+#define SB_SAMPLE_TOPK_MAX 2048
+typedef struct sb_sampler { float temperature; int top_k; float top_p; int pad; } sb_sampler;
+int sb_sample_rows(const float* logits, int ldl, int V, int B, const sb_sampler* cfg, uint64_t* rng,
+                   float* scratch, int32_t* out, const int32_t* row_slot, const int32_t* row_pos,
+                   int32_t* pos, const int32_t* status, int* err, cudaStream_t st);
+
 /* Fills positions [0, n) of one slot with deterministic pseudo-random K/V
  * (benchmark stand-in for a prefilled prompt), allocating its pages. */
 int sb_seed_context(int slot, int n, uint64_t seed, int n_layers, int nkv, int hd, int32_t* pos,
