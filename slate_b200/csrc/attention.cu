@@ -241,13 +241,21 @@ __global__ void prologue_kernel(const int32_t* __restrict__ slots, const int32_t
         int p = -1;
         if (slot < 0 || slot >= max_slots) { set_status(status, -1); ok = 0; }
         if (ok && (tok < 0 || tok >= vocab)) { set_status(status, -3); ok = 0; }
+        // a slot may occur several times in one step (a prompt chunk): its
+        // k-th occurrence takes position pos[slot] + k
+        int rank = 0;
+        if (ok)
+            for (int r = 0; r < b; ++r) rank += slots[r] == slot;
         if (ok) {
-            p = pos[slot];
+            p = pos[slot] + rank;
             if (p >= max_seq) { set_status(status, -2); ok = 0; }
         }
         if (ok) {
+            // the row at a page's first position allocates it (so rows of one
+            // chunk never race for a page); a first occurrence also repairs a
+            // missing entry
             int32_t* e = page_table + (size_t)slot * max_pages + p / SB_PAGE_TOKENS;
-            if (*e < 0) {
+            if (*e < 0 && (p % SB_PAGE_TOKENS == 0 || rank == 0)) {
                 int pg = alloc_page(free_stack, free_top);
                 if (pg < 0) { set_status(status, -2); ok = 0; }
                 else *e = pg;
@@ -277,7 +285,7 @@ __global__ void epilogue_kernel(const float* logits, int ldl, int V, const int32
     if (threadIdx.x == 0) {
         if (out_tokens) out_tokens[blockIdx.x] = i;
         if (*status == 0 && row_pos[blockIdx.x] >= 0)
-            pos[row_slot[blockIdx.x]] = row_pos[blockIdx.x] + 1;
+            atomicMax(&pos[row_slot[blockIdx.x]], row_pos[blockIdx.x] + 1);
     }
 }
 
@@ -302,7 +310,7 @@ __global__ void tp_epilogue_kernel(const sb_vi* all, int T, int B, const int32_t
     int bi = 0x7fffffff;
     for (int t = 0; t < T; ++t) am_merge(bv, bi, all[(size_t)t * B + r].v, all[(size_t)t * B + r].i);
     if (out_tokens) out_tokens[r] = bi == 0x7fffffff ? 0 : bi;
-    if (*status == 0 && row_pos[r] >= 0) pos[row_slot[r]] = row_pos[r] + 1;
+    if (*status == 0 && row_pos[r] >= 0) atomicMax(&pos[row_slot[r]], row_pos[r] + 1);
 }
 
 __device__ __forceinline__ uint64_t mix64(uint64_t z) {

@@ -798,7 +798,7 @@ static int copy_logits(slate_llama_batch_t* b, int n, float* dst, enum cudaMemcp
         if (!b->logits_all) return -5;
     }
     int rc = sb_tp_allgather(b->comm, b->logits, b->logits_all, (size_t)n * ldl * 4, b->stream);
-    for (int r = 0; r < b->tp && !rc; ++r)
+    for (int r = 0; r < b->tp && !rc && dst; ++r)
         rc = sb_cuda_check(cudaMemcpy2DAsync(dst + (size_t)r * b->V_l, (size_t)b->V * 4,
                                              b->logits_all + (size_t)r * n * ldl, ldl * 4,
                                              (size_t)b->V_l * 4, (size_t)n, kind, b->stream),
@@ -806,8 +806,27 @@ static int copy_logits(slate_llama_batch_t* b, int n, float* dst, enum cudaMemcp
     return rc;
 }
 
-int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
-                           const int32_t* tokens, int32_t* out_tokens, float* out_logits) {
+/* Row n - 1 of the step's logits to host dst[V] (after copy_logits(.., NULL,
+ * ..) has gathered them on a tensor-parallel rank). */
+static int copy_last_logits(slate_llama_batch_t* b, int n, float* dst) {
+    const size_t ldl = (size_t)b->ld_logits;
+    if (b->tp == 1)
+        return sb_cuda_check(cudaMemcpyAsync(dst, b->logits + (size_t)(n - 1) * ldl, (size_t)b->V * 4,
+                                             cudaMemcpyDeviceToHost, b->stream), "logits copy");
+    int rc = 0;
+    for (int r = 0; r < b->tp && !rc; ++r)
+        rc = sb_cuda_check(cudaMemcpyAsync(dst + (size_t)r * b->V_l,
+                                           b->logits_all + ((size_t)r * n + (n - 1)) * ldl,
+                                           (size_t)b->V_l * 4, cudaMemcpyDeviceToHost, b->stream),
+                           "logits copy");
+    return rc;
+}
+
+/* One step over host buffers.  allow_dup: a slot may occur several times (a
+ * prompt chunk), its k-th occurrence at position pos + k.  out_logits gets all
+ * n rows, last_logits (nullable) only row n - 1. */
+static int step_host(slate_llama_batch_t* b, const int32_t* slots, int n, const int32_t* tokens,
+                     int32_t* out_tokens, float* out_logits, float* last_logits, int allow_dup) {
     if (!b || !slots || !tokens || n < 1 || n > b->max_batch) return -1;
     pthread_mutex_lock(&b->lock);
     int rc = refresh_positions(b);
@@ -816,12 +835,12 @@ int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
     for (int r = 0; r < n && !rc; ++r) {
         const int s = slots[r];
         if (s < 0 || s >= b->max_slots || !b->h_open[s]) { rc = -1; break; }
-        for (int q = 0; q < r; ++q)
-            if (slots[q] == s) { rc = -1; break; }
-        if (rc) break;
-        if (b->h_pos[s] >= b->max_seq) { rc = -2; break; }
+        int rank = 0;
+        for (int q = 0; q < r; ++q) rank += slots[q] == s;
+        if (rank && !allow_dup) { rc = -1; break; }
+        if (b->h_pos[s] + rank >= b->max_seq) { rc = -2; break; }
         if (tokens[r] < 0 || tokens[r] >= b->V) { rc = -3; break; }
-        if (b->h_pos[s] % SB_PAGE_TOKENS == 0) ++new_pages;
+        if ((b->h_pos[s] + rank) % SB_PAGE_TOKENS == 0) ++new_pages;
     }
     if (!rc && b->pages_used + new_pages > b->n_pages) rc = -2;
     if (rc) {
@@ -841,6 +860,12 @@ int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
                            "D2H tokens");
     if (!rc) rc = status_readback(b);
     if (!rc && out_logits) rc = copy_logits(b, n, out_logits, cudaMemcpyDeviceToHost);
+    if (!rc && last_logits) {
+        if (b->tp > 1) {
+            rc = copy_logits(b, n, NULL, cudaMemcpyDeviceToHost);   /* gathers only */
+        }
+        if (!rc) rc = copy_last_logits(b, n, last_logits);
+    }
     if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(b->stream), "step");
     if (!rc) {
         const int st = status_code(b);
@@ -856,6 +881,11 @@ int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
     }
     pthread_mutex_unlock(&b->lock);
     return rc;
+}
+
+int slate_llama_batch_step(slate_llama_batch_t* b, const int32_t* slots, int n,
+                           const int32_t* tokens, int32_t* out_tokens, float* out_logits) {
+    return step_host(b, slots, n, tokens, out_tokens, out_logits, NULL, 0);
 }
 
 /* Lazily creates the sampling buffers (outside any capture). */
@@ -995,13 +1025,21 @@ int slate_llama_batch_sync(slate_llama_batch_t* b) {
 int slate_llama_batch_prefill(slate_llama_batch_t* b, int slot, const int32_t* tokens,
                               int n_tokens, float* out_logits) {
     if (!b || !tokens || n_tokens <= 0) return -1;
-    int32_t s = slot;
-    for (int i = 0; i < n_tokens; ++i) {
-        int rc = slate_llama_batch_step(b, &s, 1, &tokens[i], NULL,
-                                        i == n_tokens - 1 ? out_logits : NULL);
-        if (rc) return rc;
+    /* chunks of up to max_batch prompt tokens, each one step whose rows are
+     * consecutive positions of this slot: the GEMMs see a chunk of rows, each
+     * row attends to everything before it (earlier chunks and earlier rows of
+     * its own chunk, appended first in the step) */
+    int32_t* slots = (int32_t*)malloc((size_t)b->max_batch * 4);
+    if (!slots) return -5;
+    for (int i = 0; i < b->max_batch; ++i) slots[i] = slot;
+    int rc = 0;
+    for (int i = 0; i < n_tokens && !rc; i += b->max_batch) {
+        const int n = n_tokens - i < b->max_batch ? n_tokens - i : b->max_batch;
+        const int last = i + n == n_tokens;
+        rc = step_host(b, slots, n, tokens + i, NULL, NULL, last ? out_logits : NULL, 1);
     }
-    return 0;
+    free(slots);
+    return rc;
 }
 
 int slate_llama_batch_seed_context(slate_llama_batch_t* b, int slot, int n_tokens, uint64_t seed) {

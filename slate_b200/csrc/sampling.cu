@@ -218,7 +218,8 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(
     __syncthreads();
     if (tid == 0) {
         out[b] = s_tok;
-        if (pos && (!status || *status == 0) && row_pos[b] >= 0) pos[row_slot[b]] = row_pos[b] + 1;
+        if (pos && (!status || *status == 0) && row_pos[b] >= 0)
+            atomicMax(&pos[row_slot[b]], row_pos[b] + 1);
     }
 }
 

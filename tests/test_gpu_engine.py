@@ -321,3 +321,50 @@ def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
             err = np.max(np.abs(lg - ref[:, t])) / scale
             assert err < 1e-4, (gp, t, err)
         eng.close()
+
+
+@pytest.mark.parametrize("kv_dtype,tol", [(0, 1e-4), (1, 2e-3)])
+@pytest.mark.parametrize("max_batch", [16, 64])
+def test_batched_prefill_matches_oracle(sb, oracle, workdir, kv_dtype, tol, max_batch):
+    """Prefill in chunks of max_batch prompt tokens (rows of one slot at
+    consecutive positions, crossing 16-token pages inside a chunk), then greedy
+    decode of all sequences together; every logit against the oracle's
+    token-by-token sessions (llama_infer.c:262-272 semantics)."""
+    path = os.path.join(str(workdir), "prefill_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=2,
+                      vocab=800, max_seq=512, q4k=True, seed=17)
+    rng = np.random.default_rng(max_batch + kv_dtype)
+    lens = [1, 15, 17, 100, 333]
+    prompts = [rng.integers(0, 800, L).astype(np.int32) for L in lens]
+    eng = make_engine(sb, path, max_batch=max_batch, max_slots=len(lens), kv_dtype=kv_dtype)
+    slots = [eng.open() for _ in lens]
+    last = []
+    for s, p in zip(slots, prompts):
+        rc, lg = eng.prefill(s, p)
+        assert rc == 0, sb.last_error()
+        assert eng.position(s) == len(p)
+        last.append(lg)
+    m = oracle.open(path)
+    n_new = 6
+    toks = np.array([int(np.argmax(l)) for l in last], np.int32)
+    streams = [[t] for t in toks]
+    dec = []
+    for _ in range(n_new - 1):
+        rc, out, lg = eng.step(slots, toks, want_logits=True)
+        assert rc == 0, sb.last_error()
+        dec.append(lg)
+        toks = out
+        for i, t in enumerate(out):
+            streams[i].append(int(t))
+    for i, p in enumerate(prompts):
+        feed = np.array(list(p) + streams[i][:-1], np.int32)
+        ref, _ = m.decode_many(feed[None, :])
+        ref = ref[0]
+        scale = np.abs(ref).max()
+        assert np.max(np.abs(last[i] - ref[len(p) - 1])) / scale <= tol, (i, "prefill")
+        for t in range(n_new - 1):
+            err = np.max(np.abs(dec[t][i] - ref[len(p) + t])) / scale
+            assert err <= tol, (i, t, err)
+    m.close()
+    eng.close()
