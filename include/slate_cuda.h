@@ -213,6 +213,12 @@ typedef struct slate_cuda_opts {
     int tp_size;
     int tp_rank;
     unsigned char tp_id[128];
+    /* Nibble packing of the model's Q4_K tensors: 0 = Slate's (sub-block j in
+     * qs[16j..16j+15], low nibble element i, high nibble i + 16;
+     * util/quant.c:182-199), 1 = llama.cpp / ggml's (64-element pairs: byte
+     * 32g + e holds element e of sub-block 2g low and of 2g + 1 high), repacked
+     * to Slate's at upload, so real llama.cpp Q4_K files decode as intended. */
+    int q4k_order;
 } slate_cuda_opts_t;
 
 /* A fresh NCCL unique id (128 bytes) for a tensor-parallel group: create it on
@@ -366,6 +372,9 @@ typedef struct slate_synth_config {
                              repeats the weights of layer l % p (a file of a
                              large model written in a fraction of the time;
                              the engine still holds one copy per layer) */
+    int q4k_order;        /* 0: Slate's nibble packing; 1: llama.cpp / ggml's */
+    int embd_f16;         /* 0: f32 token_embd / output; 1: stored as f16;
+                             2: f32 holding the f16-rounded values */
 } slate_synth_config_t;
 /* Writes a LLaMA GGUF with N(0, 0.02) weights (counter-based, deterministic
  * in seed), unit norm gains, f32 embedding/head.  Returns 0 or <0. */

@@ -54,7 +54,7 @@ class CudaOpts(C.Structure):
                 ("kv_dtype", c_int), ("max_seq", c_int), ("kv_pages", c_int64),
                 ("kv_bytes", c_size), ("use_graphs", c_int), ("gemm_path", c_int),
                 ("attn_path", c_int), ("tp_size", c_int), ("tp_rank", c_int),
-                ("tp_id", C.c_ubyte * 128)]
+                ("tp_id", C.c_ubyte * 128), ("q4k_order", c_int)]
 
 
 class SamplerConfig(C.Structure):
@@ -75,7 +75,8 @@ class SynthConfig(C.Structure):
     _fields_ = [(n, c_int) for n in ("n_layers", "d_model", "ffn_hidden", "n_heads", "n_kv_heads",
                                      "vocab", "max_seq")] + [
         ("theta_base", c_float), ("rms_eps", c_float), ("q4k", c_int), ("tied_output", c_int),
-        ("seed", c_u64), ("n_threads", c_int), ("layer_period", c_int)]
+        ("seed", c_u64), ("n_threads", c_int), ("layer_period", c_int), ("q4k_order", c_int),
+        ("embd_f16", c_int)]
 
 
 class BackendBase(C.Structure):
@@ -161,11 +162,13 @@ def quantize_q4k(w: np.ndarray) -> np.ndarray:
 
 def synth_gguf(path: str, *, n_layers, d_model, ffn_hidden, n_heads, n_kv_heads, vocab, max_seq,
                theta_base=10000.0, rms_eps=1e-5, q4k=True, tied_output=False, seed=0,
-               n_threads=0, layer_period=0) -> None:
-    """Writes a synthetic LLaMA GGUF (N(0,0.02) weights, Slate Q4_K layout)."""
+               n_threads=0, layer_period=0, q4k_order=0, embd_f16=0) -> None:
+    """Writes a synthetic LLaMA GGUF (N(0,0.02) weights; Q4_K in Slate's nibble
+    order, or llama.cpp's with q4k_order=1; embd_f16: 1 f16 embedding/output
+    tables, 2 f32 tables holding f16-rounded values)."""
     cfg = SynthConfig(n_layers, d_model, ffn_hidden, n_heads, n_kv_heads, vocab, max_seq,
                       theta_base, rms_eps, int(q4k), int(tied_output), seed, n_threads,
-                      layer_period)
+                      layer_period, q4k_order, embd_f16)
     rc = F["slate_synth_llama_gguf"](path.encode(), C.byref(cfg))
     if rc:
         raise OSError(f"slate_synth_llama_gguf({path}) rc={rc}")
@@ -195,9 +198,10 @@ class LlamaBatch:
 
     def __init__(self, gguf_path: str, *, device=0, max_batch=16, max_slots=0, kv_dtype=KV_F32,
                  max_seq=0, kv_pages=0, kv_bytes=0, use_graphs=True, gemm_path=0, attn_path=0,
-                 tp_size=0, tp_rank=0, tp_id=b""):
+                 tp_size=0, tp_rank=0, tp_id=b"", q4k_order=0):
         self.opts = CudaOpts(device, max_batch, max_slots, kv_dtype, max_seq, kv_pages, kv_bytes,
                              int(use_graphs), gemm_path, attn_path, tp_size, tp_rank)
+        self.opts.q4k_order = q4k_order
         if tp_id:
             C.memmove(self.opts.tp_id, bytes(tp_id), min(len(tp_id), 128))
         self.h = F["slate_llama_batch_new_gguf"](gguf_path.encode(), C.byref(self.opts))

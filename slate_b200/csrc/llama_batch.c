@@ -81,6 +81,7 @@ struct slate_llama_batch {
     sb_tc_operand op_a;            /* attention output, K = nq*hd (tensor parallel: local heads) */
     /* exact-weight Q4_K GEMM (gemm_path 0): operands over the same f16 hi/lo
      * buffers plus sub-block sums, stream-K partials and tile counters */
+    int q4k_order;                 /* source Q4_K packing: 0 Slate, 1 ggml (repacked) */
     int q4_on;
     sb_q4_operand q4_d, q4_f, q4_a;
     float* q4_ws;
@@ -170,11 +171,27 @@ static void* stage_get(stage_t* s, size_t bytes) {
  * part 0 (gate) and part 1 (up) in alternating 64-row groups for the fused
  * SwiGLU epilogue.  All-Q4_K groups stay Q4_K; any f32 part makes the whole
  * matrix f32 (Q4_K parts dequantised exactly). */
+/* llama.cpp / ggml nibble packing of one Q4_K block -> Slate's
+ * (util/quant.c:182-199): ggml byte 32g + e holds element e of sub-block 2g in
+ * its low nibble and of 2g + 1 in its high nibble; Slate's byte 16s + i holds
+ * elements i (low) and i + 16 (high) of sub-block s. */
+static void q4k_from_ggml(uint8_t* dst, const uint8_t* src) {
+    memcpy(dst, src, 16);                        /* d, dmin, packed scales: same */
+    uint8_t e[8][32];
+    for (int g = 0; g < 4; ++g)
+        for (int i = 0; i < 32; ++i) {
+            e[2 * g][i] = src[16 + 32 * g + i] & 15;
+            e[2 * g + 1][i] = src[16 + 32 * g + i] >> 4;
+        }
+    for (int sb = 0; sb < 8; ++sb)
+        for (int i = 0; i < 16; ++i) dst[16 + 16 * sb + i] = (uint8_t)(e[sb][i] | (e[sb][i + 16] << 4));
+}
+
 static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, const src_part* parts,
                        int nparts, int K, int interleave64) {
     int all_q4k = 1, M = 0;
     for (int i = 0; i < nparts; ++i) {
-        if (parts[i].dtype != 0 && parts[i].dtype != 18) {
+        if (parts[i].dtype != 0 && parts[i].dtype != 1 && parts[i].dtype != 18) {
             sb_set_error("unsupported weight dtype %d", parts[i].dtype);
             return -1;
         }
@@ -195,7 +212,7 @@ static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, cons
     out->ldw = all_q4k ? 0 : round_up(K, 128);
     const size_t row_bytes = all_q4k ? q4k_row_bytes(K) : (size_t)out->ldw * 4;
     const size_t bytes = row_bytes * (size_t)M_pad;
-    if (nparts == 1 && !interleave64 && parts[0].src_k == K &&
+    if (nparts == 1 && !interleave64 && parts[0].src_k == K && !(all_q4k && b->q4k_order) &&
         (all_q4k || (parts[0].dtype == 0 && out->ldw == K))) {
         /* already in the device layout: copy rows straight from the source */
         unsigned char* dptr = (unsigned char*)dalloc(b, bytes);
@@ -215,8 +232,9 @@ static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, cons
     /* destination row of source row r of part i */
     for (int i = 0, base = 0; i < nparts; ++i) {
         const src_part* sp = &parts[i];
-        const size_t src_row = sp->dtype == 18 ? q4k_row_bytes(sp->src_k) : (size_t)sp->src_k * 4;
-        const size_t col0 = sp->dtype == 18 ? q4k_row_bytes(sp->k0) : (size_t)sp->k0 * 4;
+        const size_t esz = sp->dtype == 1 ? 2 : 4;
+        const size_t src_row = sp->dtype == 18 ? q4k_row_bytes(sp->src_k) : (size_t)sp->src_k * esz;
+        const size_t col0 = sp->dtype == 18 ? q4k_row_bytes(sp->k0) : (size_t)sp->k0 * esz;
         for (int r = 0; r < sp->rows; ++r) {
             int dr;
             if (interleave64) dr = (r / 64) * 128 + (i ? 64 : 0) + r % 64;
@@ -224,9 +242,26 @@ static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, cons
             const unsigned char* s =
                 (const unsigned char*)sp->p + (size_t)(sp->row0 + r) * src_row + col0;
             unsigned char* d = h + (size_t)dr * row_bytes;
-            if (all_q4k) memcpy(d, s, q4k_row_bytes(K));
-            else if (sp->dtype == 0) memcpy(d, s, (size_t)K * 4);
-            else sb_q4k_dequant_rows((float*)d, s, 1, K);
+            if (sp->dtype == 18 && b->q4k_order) {
+                /* repack each block to Slate's order (into d, or a temp row
+                 * that is then dequantised) */
+                uint8_t* q = all_q4k ? (uint8_t*)d : (uint8_t*)malloc(q4k_row_bytes(K));
+                if (!q) return -5;
+                for (int blk = 0; blk < K / 256; ++blk) q4k_from_ggml(q + 144 * blk, s + 144 * blk);
+                if (!all_q4k) {
+                    sb_q4k_dequant_rows((float*)d, q, 1, K);
+                    free(q);
+                }
+            } else if (all_q4k) {
+                memcpy(d, s, q4k_row_bytes(K));
+            } else if (sp->dtype == 0) {
+                memcpy(d, s, (size_t)K * 4);
+            } else if (sp->dtype == 1) {
+                const uint16_t* h16 = (const uint16_t*)s;
+                for (int k = 0; k < K; ++k) ((float*)d)[k] = sb_f16_to_f32(h16[k]);
+            } else {
+                sb_q4k_dequant_rows((float*)d, s, 1, K);
+            }
         }
         base += sp->rows;
     }
@@ -400,8 +435,8 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         sb_set_error("GQA group %d unsupported (1, 2, 4, 8)", G);
         return NULL;
     }
-    if (m->token_embd_dtype != 0) {
-        sb_set_error("token_embd must be f32 (llama_infer.c:149-150 reads it as f32)");
+    if (m->token_embd_dtype != 0 && m->token_embd_dtype != 1) {
+        sb_set_error("token_embd must be f32 or f16");
         return NULL;
     }
     if (o->max_batch < 1 || o->max_batch > 1024) {
@@ -438,6 +473,7 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
     b->max_slots = o->max_slots > 0 ? o->max_slots : o->max_batch;
     b->kv_dtype = o->kv_dtype == SLATE_KV_F16 ? SLATE_KV_F16 : SLATE_KV_F32;
     b->gemm_path = o->gemm_path;
+    b->q4k_order = o->q4k_order == 1;
     /* tensor-parallel steps are launched eagerly: their NCCL collectives set
      * up connections lazily, which stream capture does not allow */
     b->use_graphs = tp > 1 ? 0 : o->use_graphs;
@@ -455,10 +491,21 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         goto fail;
     }
 
-    /* weights */
-    if (upload_f32(b, &b->emb, m->token_embd, (size_t)V * D)) goto fail;
+    /* weights (an f16 embedding table is widened to f32 once, exactly) */
+    if (m->token_embd_dtype == 1) {
+        float* e32 = (float*)malloc((size_t)V * D * 4);
+        if (!e32) { sb_set_error("host memory for the f16 embedding"); goto fail; }
+        const uint16_t* e16 = (const uint16_t*)m->token_embd;
+        for (size_t i = 0; i < (size_t)V * D; ++i) e32[i] = sb_f16_to_f32(e16[i]);
+        const int rc_e = upload_f32(b, &b->emb, e32, (size_t)V * D);
+        free(e32);
+        if (rc_e) goto fail;
+    } else if (upload_f32(b, &b->emb, m->token_embd, (size_t)V * D)) {
+        goto fail;
+    }
     if (upload_f32(b, &b->out_norm, m->output_norm, (size_t)D)) goto fail;
-    if (m->output == m->token_embd && m->output_dtype == 0 && D % 128 == 0 && b->V_l % 128 == 0) {
+    if (m->output == m->token_embd && m->output_dtype == m->token_embd_dtype && D % 128 == 0 &&
+        b->V_l % 128 == 0) {
         /* tied: share the table (this rank's vocabulary rows) */
         b->lm_head = (sb_matrix){SB_WT_F32, b->emb + (size_t)b->v0 * D, b->V_l, b->V_l, D, D};
     } else {

@@ -22,6 +22,7 @@
  */
 #define _GNU_SOURCE
 #include "slate_cuda.h"
+#include "sb_internal.h"
 
 #include <fcntl.h>
 #include <fenv.h>
@@ -146,7 +147,7 @@ static void gen_normal(float* out, int64_t first, int64_t n, uint64_t seed, int 
 typedef struct {
     char name[64];
     int64_t rows, cols;   /* logical [rows, cols]; cols == 1 for vectors */
-    int n_dims, ggml_type, kind, id;   /* kind 0 = normal, 1 = ones */
+    int n_dims, ggml_type, kind, id;   /* kind 0 = normal, 1 = ones, 2 = embedding */
     int src;              /* >= 0: a copy of tensor src (layer_period) */
     uint64_t off;
     size_t bytes;
@@ -173,7 +174,23 @@ typedef struct {
     int nt;
     uint64_t data_off, seed;
     int tid, nthreads, rc;
+    int q4k_order, embd_f16;
 } job_t;
+
+/* Slate's nibble packing of one block -> llama.cpp / ggml's: byte 32g + e
+ * holds element e of sub-block 2g (low nibble) and of 2g + 1 (high). */
+static void to_ggml_order(uint8_t* blk) {
+    uint8_t* qs = blk + 16;
+    uint8_t e[8][32], out[128];
+    for (int s = 0; s < 8; ++s)
+        for (int i = 0; i < 16; ++i) {
+            e[s][i] = qs[16 * s + i] & 15;
+            e[s][i + 16] = qs[16 * s + i] >> 4;
+        }
+    for (int g = 0; g < 4; ++g)
+        for (int i = 0; i < 32; ++i) out[32 * g + i] = (uint8_t)(e[2 * g][i] | (e[2 * g + 1][i] << 4));
+    memcpy(qs, out, 128);
+}
 
 static void* writer(void* arg) {
     job_t* j = (job_t*)arg;
@@ -188,7 +205,8 @@ static void* writer(void* arg) {
         if (r0 >= r1) continue;
         const int64_t chunk = 64;
         float* f = (float*)malloc((size_t)chunk * t->cols * 4);
-        uint8_t* qb = (uint8_t*)malloc((size_t)chunk * (t->cols / 256 + 1) * 144);
+        uint8_t* qb = (uint8_t*)malloc((size_t)chunk * (t->cols / 256 + 1) * 144 +
+                                       (size_t)chunk * t->cols * 2);
         for (int64_t r = r0; r < r1 && !j->rc; r += chunk) {
             int64_t nr = r1 - r < chunk ? r1 - r : chunk;
             const int64_t n = nr * t->cols;
@@ -197,10 +215,21 @@ static void* writer(void* arg) {
             const void* src = f;
             size_t bytes = (size_t)n * 4, row_bytes = (size_t)t->cols * 4;
             if (t->ggml_type == 12) {
-                for (int64_t b = 0; b < n / 256; ++b) quant_block(qb + b * 144, f + b * 256);
+                for (int64_t b = 0; b < n / 256; ++b) {
+                    quant_block(qb + b * 144, f + b * 256);
+                    if (j->q4k_order == 1) to_ggml_order(qb + b * 144);
+                }
                 src = qb;
                 row_bytes = (size_t)(t->cols / 256) * 144;
                 bytes = row_bytes * (size_t)nr;
+            } else if (t->ggml_type == 1) {              /* f16 storage */
+                uint16_t* h16 = (uint16_t*)qb;
+                for (int64_t i = 0; i < n; ++i) h16[i] = f64_to_f16((double)f[i]);
+                src = qb;
+                row_bytes = (size_t)t->cols * 2;
+                bytes = row_bytes * (size_t)nr;
+            } else if (t->kind == 2 && j->embd_f16 == 2) {   /* f32 of f16-rounded values */
+                for (int64_t i = 0; i < n; ++i) f[i] = sb_f16_to_f32(f64_to_f16((double)f[i]));
             }
             off_t at = (off_t)(j->data_off + t->off + (uint64_t)r * row_bytes);
             if (pwrite(j->fd, src, bytes, at) != (ssize_t)bytes) j->rc = -6;
@@ -252,9 +281,13 @@ int slate_synth_llama_gguf(const char* path, const slate_synth_config_t* c) {
         t[k].src = -1;                                                                         \
         ++k;                                                                                   \
     } while (0)
-    ADD("token_embd.weight", V, D, 2, 0, 0);
+    ADD("token_embd.weight", V, D, 2, 0, 2);
     ADD("output_norm.weight", 1, D, 1, 0, 1);
-    if (!c->tied_output) ADD("output.weight", V, D, 2, 0, 0);
+    if (!c->tied_output) ADD("output.weight", V, D, 2, 0, 2);
+    if (c->embd_f16 == 1) {
+        t[0].ggml_type = 1;
+        if (!c->tied_output) t[2].ggml_type = 1;
+    }
     for (int l = 0; l < c->n_layers; ++l) {
         char nm[64];
 #define L_ADD(suffix, R, C, nd, q, kd) \
@@ -278,7 +311,7 @@ int slate_synth_llama_gguf(const char* path, const slate_synth_config_t* c) {
         cur = (cur + 31) / 32 * 32;
         t[i].off = cur;
         t[i].bytes = t[i].ggml_type == 12 ? (size_t)t[i].rows * (t[i].cols / 256) * 144
-                                          : (size_t)t[i].rows * t[i].cols * 4;
+                     : (size_t)t[i].rows * t[i].cols * (t[i].ggml_type == 1 ? 2 : 4);
         cur += t[i].bytes;
     }
     buf_t h = {0};
@@ -324,7 +357,7 @@ int slate_synth_llama_gguf(const char* path, const slate_synth_config_t* c) {
         pthread_t th[256];
         job_t jobs[256];
         for (int i = 0; i < nth; ++i) {
-            jobs[i] = (job_t){fd, t, nt, data_off, c->seed, i, nth, 0};
+            jobs[i] = (job_t){fd, t, nt, data_off, c->seed, i, nth, 0, c->q4k_order, c->embd_f16};
             pthread_create(&th[i], NULL, writer, &jobs[i]);
         }
         for (int i = 0; i < nth; ++i) {
@@ -333,7 +366,7 @@ int slate_synth_llama_gguf(const char* path, const slate_synth_config_t* c) {
         }
         if (!rc && c->layer_period > 0 && c->layer_period < c->n_layers) {
             for (int i = 0; i < nth; ++i) {
-                jobs[i] = (job_t){fd, t, nt, data_off, c->seed, i, nth, 0};
+                jobs[i] = (job_t){fd, t, nt, data_off, c->seed, i, nth, 0, c->q4k_order, c->embd_f16};
                 pthread_create(&th[i], NULL, copier, &jobs[i]);
             }
             for (int i = 0; i < nth; ++i) {

@@ -51,6 +51,6 @@ def read_gguf(path):
     out = {}
     for name, dims, ty, toff in infos:
         n = int(np.prod(dims))
-        nbytes = n * 4 if ty == 0 else n // 256 * 144 if ty == 12 else 0
+        nbytes = n * 4 if ty == 0 else n * 2 if ty == 1 else n // 256 * 144 if ty == 12 else 0
         out[name] = (ty, dims, np.frombuffer(buf, np.uint8, nbytes, data + toff))
     return kv, out

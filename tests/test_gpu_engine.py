@@ -368,3 +368,39 @@ def test_batched_prefill_matches_oracle(sb, oracle, workdir, kv_dtype, tol, max_
             assert err <= tol, (i, t, err)
     m.close()
     eng.close()
+
+
+@pytest.mark.parametrize("n_rows", [5, 40])
+def test_llama_cpp_order_and_f16_embeddings(sb, oracle, workdir, n_rows):
+    """A file in llama.cpp's Q4_K nibble order loaded with q4k_order=1, and a file
+    with an f16 embedding table, give logits bitwise equal to the Slate-order /
+    f32-table engine (GEMV rows and tensor-core rows); that engine matches the
+    oracle."""
+    cfg = dict(n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=2, vocab=700,
+               max_seq=64, q4k=True, seed=23)
+    paths = {}
+    for name, kw in (("slate", {"embd_f16": 2}), ("ggml", {"embd_f16": 2, "q4k_order": 1}),
+                     ("f16", {"embd_f16": 1})):
+        paths[name] = os.path.join(str(workdir), f"fmt_{name}.gguf")
+        if not os.path.exists(paths[name]):
+            sb.synth_gguf(paths[name], **cfg, **kw)
+    rng = np.random.default_rng(n_rows)
+    T = 3
+    feed = rng.integers(0, 700, (n_rows, T)).astype(np.int32)
+    outs = {}
+    for name, q4k_order in (("slate", 0), ("ggml", 1), ("f16", 0)):
+        eng = make_engine(sb, paths[name], max_batch=n_rows, q4k_order=q4k_order)
+        slots = [eng.open() for _ in range(n_rows)]
+        lgs = []
+        for t in range(T):
+            rc, _, lg = eng.step(slots, feed[:, t], want_logits=True)
+            assert rc == 0, (name, sb.last_error())
+            lgs.append(lg)
+        outs[name] = np.stack(lgs, 1)
+        eng.close()
+    assert np.array_equal(outs["ggml"], outs["slate"])
+    assert np.array_equal(outs["f16"], outs["slate"])
+    m = oracle.open(paths["slate"])
+    ref, _ = m.decode_many(feed)
+    m.close()
+    assert np.max(np.abs(outs["slate"] - ref)) / np.abs(ref).max() <= 1e-4

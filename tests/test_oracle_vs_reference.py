@@ -130,3 +130,64 @@ def test_reference_cuda_stub_is_null(reference):
     path (the oracle) never reaches a GPU."""
     assert not reference.lib.slate_backend_cuda()
     assert reference.lib.slate_backend_default() == reference.lib.slate_backend_cpu()
+
+
+def _q4k_dequant_ggml(raw, n_blocks):
+    """llama.cpp / ggml's Q4_K element order (restated from ggml's
+    dequantize_row_q4_k): for the 64-element pair g, element e of sub-block 2g
+    is the low nibble of qs[32g + e] and of 2g + 1 the high nibble; the header
+    (d, dmin, packed 6-bit scales / mins) is as in util/quant.c:139-166."""
+    b = raw.reshape(n_blocks, 144)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+    dm = b[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
+    sc_b = b[:, 4:16].astype(np.int32)
+    sc = np.zeros((n_blocks, 8), np.int32)
+    mn = np.zeros((n_blocks, 8), np.int32)
+    for j in range(8):
+        if j < 4:
+            sc[:, j] = sc_b[:, j] & 63
+            mn[:, j] = sc_b[:, j + 4] & 63
+        else:
+            sc[:, j] = (sc_b[:, j + 4] & 15) | ((sc_b[:, j - 4] >> 6) << 4)
+            mn[:, j] = (sc_b[:, j + 4] >> 4) | ((sc_b[:, j] >> 6) << 4)
+    qs = b[:, 16:].astype(np.int32)
+    out = np.zeros((n_blocks, 256), np.float32)
+    for g in range(4):
+        q = qs[:, 32 * g:32 * g + 32]
+        for half, s in ((0, 2 * g), (1, 2 * g + 1)):
+            nib = (q >> 4) if half else (q & 15)
+            out[:, 32 * s:32 * s + 32] = (d * sc[:, s])[:, None] * nib - (dm * mn[:, s])[:, None]
+    return out.reshape(-1)
+
+
+def test_synth_llama_cpp_order_and_f16_tables(sb, oracle, workdir):
+    """q4k_order=1 writes the same weights in llama.cpp's nibble order (each
+    Q4_K tensor decodes under ggml's rules to what the Slate-order file decodes
+    to under Slate's); embd_f16=1 stores the embedding table as f16 with the
+    values that embd_f16=2 stores as f32."""
+    from gguf_util import read_gguf
+    cfg = dict(SYNTH["gqa_q4k"])
+    paths = {}
+    for name, kw in (("s", {}), ("g", {"q4k_order": 1}), ("h", {"embd_f16": 1}),
+                     ("r", {"embd_f16": 2})):
+        paths[name] = os.path.join(str(workdir), f"order_{name}.gguf")
+        sb.synth_gguf(paths[name], **cfg, **kw)
+    _, ts = read_gguf(paths["s"])
+    _, tg = read_gguf(paths["g"])
+    n_q4k = 0
+    for name, (ty, dims, data) in ts.items():
+        if ty != 12:
+            assert np.array_equal(data, tg[name][2]), name
+            continue
+        n_q4k += 1
+        nb = len(data) // 144
+        want = oracle.dequant_q4k(data, nb * 256)
+        got = _q4k_dequant_ggml(tg[name][2], nb)
+        assert np.array_equal(got, want), name
+        assert not np.array_equal(data, tg[name][2])
+    assert n_q4k > 0
+    _, th = read_gguf(paths["h"])
+    _, tr = read_gguf(paths["r"])
+    assert th["token_embd.weight"][0] == 1 and tr["token_embd.weight"][0] == 0
+    assert np.array_equal(th["token_embd.weight"][2].view(np.float16).astype(np.float32),
+                          tr["token_embd.weight"][2].view(np.float32))
