@@ -76,7 +76,7 @@ def parse():
                     help="reduce only for debugging; 0 = the config's (32 for 8b, 80 for 70b)")
     ap.add_argument("--gemm-path", type=int, default=0,
                     help="0 auto (tcgen05 3-pass hi/lo split), 1 CUDA cores, 2 tcgen05 single f16 "
-                         "pass, 3 = 0, 4 exact-weight stream-K kernel")
+                         "pass, 3 = 0, 4 exact-weight stream-K kernel, 5 3-pass stream-K kernel")
     ap.add_argument("--attn-path", type=int, default=0,
                     help="0: tensor-core attention for f16 KV (mma.sync), 1: CUDA-core kernel")
     ap.add_argument("--max-ctx", type=int, default=0,
@@ -415,7 +415,8 @@ def main():
                    "parallelism": f"replicas x{replicas}" + (f", tensor parallel {tp}" if tp > 1 else ""),
                    "gemm_path": {0: "tcgen05 3-pass hi/lo", 1: "cuda-core f32", 2: "tcgen05 1-pass f16",
                                  3: "tcgen05 3-pass hi/lo",
-                                 4: "tcgen05 exact f16 weights, 2-pass x, stream-K"}[args.gemm_path],
+                                 4: "tcgen05 exact f16 weights, 2-pass x, stream-K",
+                                 5: "tcgen05 3-pass hi/lo, weights in TMEM, stream-K"}[args.gemm_path],
                    "attn_path": ("mma.sync f16 hi/lo" if args.attn_path == 0 and args.kv == "f16"
                                  else "cuda-core"),
                    "l2": "inputs larger than L2 (KV read per step >> 126 MB)"},

@@ -217,10 +217,45 @@ static int be_matmul_q4k_exact(float* Y, const void* A, const float* X, int B, i
     return rc;
 }
 
+/* passes 3 on the stream-K kernel (gemm_sk.cu) */
+static int be_matmul_q4k_sk(float* Y, const void* A, const float* X, int B, int M, int K) {
+    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0};
+    sb_sk_prepare();
+    void *hi = NULL, *lo = NULL, *ws = NULL, *err = NULL;
+    int rc = sb_cuda_check(cudaMallocAsync(&hi, (size_t)B * K * 2, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&lo, (size_t)B * K * 2, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&ws, sb_sk_ws_floats() * 4, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&err, 16, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(err, 0, 16, g_stream), "memset");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "alloc sync");
+    sb_tc_operand op;
+    if (!rc && sb_tc_make_operand(&op, hi, lo, B, K, K)) rc = -1;
+    if (!rc) rc = fin(sb_tc_split(X, K, B, &op, g_stream), "tc split");
+    if (!rc) rc = fin(sb_sk_gemm(&W, &op, B, (float*)ws, Y, M, SB_EPI_STORE, (int*)err, g_stream),
+                      "matmul_q4k_batch_tc");
+    int e = 0;
+    if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, g_stream), "err");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "matmul_q4k_batch_tc");
+    if (!rc && e) {
+        sb_set_error("tensor-core pipeline wait timed out (stage %d)", e);
+        rc = -5;
+    }
+    void* bufs[4] = {hi, lo, ws, err};
+    for (int i = 0; i < 4; ++i)
+        if (bufs[i]) cudaFreeAsync(bufs[i], g_stream);
+    return rc;
+}
+
 static int be_matmul_q4k_tc(float* Y, const void* A, const float* X, int B, int M, int K,
                             int passes) {
     if (passes == 2 && M % 128 == 0 && K % 256 == 0 && B >= 1 && K % 4 == 0)
         return be_matmul_q4k_exact(Y, A, X, B, M, K);
+    {
+        /* SLATE_TC_SK=1: three passes on the stream-K kernel */
+        const char* e = getenv("SLATE_TC_SK");
+        if (passes == 3 && e && e[0] == '1' && M % 128 == 0 && K % 256 == 0 && B >= 16)
+            return be_matmul_q4k_sk(Y, A, X, B, M, K);
+    }
     if (M % 128 || K % 256 || B < 16 || (passes != 1 && passes != 3)) {
         sb_set_error("matmul_q4k_batch_tc: unsupported shape or passes");
         return -1;

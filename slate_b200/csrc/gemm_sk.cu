@@ -1,0 +1,693 @@
+// gemm_sk.cu -- Q4_K weight GEMM on the tcgen05 tensor cores: three f16
+// passes, dequantised weights in tensor memory, persistent stream-K schedule.
+//
+//   Y[n][m] (op)= sum_k X[n][k] * W[m][k]       (op: store, residual add, or
+//                                                SiLU(gate) * up for the fused FFN)
+//
+// W is Q4_K (src/util/quant.c:187-199: w = d * sc_j * q - dmin * m_j in f32,
+// the reference's own reconstruction); X is f32, staged as an f16 hi + lo pair
+// (x = hi + lo to ~22 bits) by sb_tc_split().  Each weight is also split into
+// f16 hi + lo, and the tensor cores accumulate hi*hi + hi*lo + lo*hi in f32,
+// which reproduces f32 products to ~1e-6 relative (the same numerics as
+// gemm_tc.cu's three-pass kernel).
+//
+// Work decomposition: a tile is 128 weight rows (TMEM lanes) x up to 256
+// activation rows (MMA N); the (tile, 64-wide K step) space is cut into one
+// contiguous range per CTA, one CTA per SM.  A tile covered by one CTA is
+// written directly; a tile shared by several CTAs is written as f32 partials,
+// and the last CTA to arrive (per-tile counter) sums them in CTA order and
+// applies the epilogue, so results do not depend on timing.  This keeps every
+// SM busy whatever the tile count (the 224 tiles of the 8B gate/up projection
+// are 1.5 waves of 148 SMs as a plain grid) and needs no separate K-split
+// reduction kernel.
+//
+// Operand placement: the dequantised weights go register -> TMEM
+// (tcgen05.st; MMA with A in tensor memory), so shared memory holds only the
+// activation ring, deep enough (3 x 64 KB) to keep the TMA stream ahead of the
+// MMAs, and the tensor core reads only B from shared memory.
+//
+// Roles (512 threads): warps 0-7 dequantise (warp w, lane l: weight row
+// 32 (w % 4) + l, sub-block w / 4 of the K step's two; each thread copies the
+// Q4_K bytes of the next two K steps into its own shared-memory ring slots
+// with cp.async while the current step converts; two producer warps per
+// scheduler hide each other's latency); warp 8 issues the MMAs; warp 9
+// issues the TMA loads of x; warps 12-15 drain the accumulator (warp 12 + q
+// reads TMEM lanes 32q..32q+31).  TMEM: the
+// accumulator in columns [0, 256), the A ring (4 stages x (32 hi + 32 lo)
+// columns) in [256, 512).  Every wait is bounded (2 s of %globaltimer): a
+// timeout records an error code in *err and the roles stop; copies and MMAs
+// in flight are waited for and TMEM is freed before the CTA exits.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include "sb_internal.h"
+#include "sb_kernels.h"
+#include "sb_tc.h"
+
+namespace {
+
+constexpr int BM = 128;                 // weight rows per tile
+constexpr int BN = 256;                 // activation rows per tile (max MMA N)
+constexpr int BK = 64;                  // K per step (one 128-byte swizzle row of f16)
+constexpr int ASTAGES = 4;              // A stages in TMEM
+constexpr int BSTAGES = 3;              // x stages in shared memory
+constexpr int NPROD = 256;             // 8 producer warps: two per weight row, one sub-block each
+constexpr int MMA_WARP = 8, TMA_WARP = 9, DRAIN_WARP0 = 12;
+constexpr int NTHREADS = 512;
+constexpr uint32_t COL_A = 256;
+constexpr int B_PART = BN * 128;        // 32 KB: 256 rows x 64 f16
+constexpr int B_STAGE = 2 * B_PART;     // hi | lo
+constexpr int XCH_FLOATS = 16 * 64;     // SiLU exchange: 16 columns x 64 rows
+constexpr int WSTAGES = 3;              // per-thread ring of Q4_K bytes (cp.async)
+constexpr int W_STAGE = 2 * NPROD * 16; // [header | nibbles][producer thread] x 16 B
+constexpr size_t SMEM = (size_t)BSTAGES * B_STAGE + XCH_FLOATS * 4 + (size_t)WSTAGES * W_STAGE + 1024;
+constexpr uint64_t WAIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint32_t su32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t c) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(c));
+}
+__device__ __forceinline__ void bar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false (and *err set) after WAIT_NS, or soon after another
+// thread of the grid has failed (the error word is polled every 32 tries).
+__device__ bool bar_wait(uint64_t* b, uint32_t parity, int* err, int code) {
+    if (bar_try(b, parity)) return true;
+    const uint64_t t0 = gtimer();
+    for (uint32_t n = 1;; ++n) {
+        if (bar_try(b, parity)) return true;
+        if ((n & 31) == 0) {
+            if (*(volatile int*)err) return false;
+            if (gtimer() - t0 > WAIT_NS) {
+                atomicCAS(err, 0, code);
+                return false;
+            }
+        }
+    }
+}
+// Wait used before the CTA exits for its own copies / MMAs in flight: bounded
+// by time only (not cut short by another CTA's error), so that nothing still
+// writes into this CTA's shared or tensor memory once it has gone.
+__device__ void bar_wait_exit(uint64_t* b, uint32_t parity, int* err) {
+    const uint64_t t0 = gtimer();
+    while (!bar_try(b, parity)) {
+        if (gtimer() - t0 > WAIT_NS) {
+            atomicCAS(err, 0, 9);
+            return;
+        }
+    }
+}
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%3, %4}], [%2];" ::"r"(su32(dst)),
+        "l"(map), "r"(su32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// K-major, SWIZZLE_128B: 8-row atoms of 128-byte rows, 1024 B apart.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+// D (+)= A * B, A in tensor memory (lane = weight row, column c = K pair 2c, 2c+1).
+__device__ __forceinline__ void mma_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     su32(bar))
+                 : "memory");
+}
+// 16 columns of this warp's 32 lanes (no wait: the caller waits once).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void drain_sync() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// 16 bytes global -> shared without a register (L2 only); completion by group.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Pulls one 144-byte Q4_K super-block into L2 ahead of use (the lines holding
+// its first, middle and last byte).
+__device__ __forceinline__ void l2_prefetch_block(const unsigned char* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + 72));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + 143));
+}
+
+// ---- Q4_K dequantisation (util/quant.c:157-166 scale packing, :187-199 values)
+__device__ __forceinline__ float f16_lo(uint32_t w) {
+    return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+}
+__device__ __forceinline__ float f16_hi(uint32_t w) {
+    return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+__device__ __forceinline__ uint32_t hbyte(uint4 h, int i) {
+    const uint32_t w = i < 4 ? h.y : (i < 8 ? h.z : h.w);
+    return (w >> ((i & 3) * 8)) & 0xffu;
+}
+// d * sc_j and dmin * m_j of sub-block j, in f32 as the reference forms them.
+__device__ __forceinline__ void sub_scale(uint4 h, int j, float& sd, float& sm) {
+    uint32_t sc, mn;
+    if (j < 4) {
+        sc = hbyte(h, j) & 63u;
+        mn = hbyte(h, j + 4) & 63u;
+    } else {
+        sc = (hbyte(h, j + 4) & 15u) | ((hbyte(h, j - 4) >> 6) << 4);
+        mn = (hbyte(h, j + 4) >> 4) | ((hbyte(h, j) >> 6) << 4);
+    }
+    sd = f16_lo(h.x) * (float)sc;
+    sm = f16_hi(h.x) * (float)mn;
+}
+// One sub-block (16 nibble bytes, Slate order: byte i holds element i in its
+// low nibble and element i + 16 in its high nibble) -> 16 columns of f16 pairs
+// (column c = elements 2c, 2c+1) as hi = f16(w) and lo = f16(w - hi), with
+// w = sd * q - sm formed in f32 by one fused multiply-add per element.
+// A nibble q becomes the float 2^23 + q by a byte permute (q in the low
+// mantissa byte under the exponent byte 0x4B), and subtracting 2^23 leaves q
+// exactly; the element pairs go through the paired f32 pipes (FADD2 / FFMA2,
+// round-to-nearest like their scalar forms).
+__device__ __forceinline__ void dequant_sub(uint4 q, float sd, float sm, uint32_t* hi, uint32_t* lo) {
+    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+    const float2 sd2 = make_float2(sd, sd), nsm2 = make_float2(-sm, -sm);
+    const float2 off2 = make_float2(-8388608.0f, -8388608.0f);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {                        // low nibbles, then high
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t nb = (h ? qw[wi] >> 4 : qw[wi]) & 0x0f0f0f0fu;
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr) {             // bytes 2pr, 2pr+1 of the word
+                const float2 mg = make_float2(
+                    __uint_as_float(__byte_perm(nb, 0x4B000000u, 0x7440u + 2 * pr)),
+                    __uint_as_float(__byte_perm(nb, 0x4B000000u, 0x7441u + 2 * pr)));
+                const float2 w = __ffma2_rn(sd2, __fadd2_rn(mg, off2), nsm2);
+                const __half2 hh = __floats2half2_rn(w.x, w.y);
+                const float2 back = __half22float2(hh);
+                const __half2 ll = __floats2half2_rn(w.x - back.x, w.y - back.y);
+                const int c = h * 8 + wi * 2 + pr;       // elements 2c, 2c+1
+                hi[c] = *(const uint32_t*)&hh;
+                lo[c] = *(const uint32_t*)&ll;
+            }
+        }
+    }
+}
+
+// ---- stream-K schedule ----------------------------------------------------
+// CTA c of C owns units [U*c/C, U*(c+1)/C) of the U = tiles * nk (tile, K step)
+// units, tile-major; a segment is one tile's part of that range.
+__device__ __forceinline__ long long u_begin(int c, int C, long long U) {
+    return U * c / C;
+}
+__device__ int owner_of(long long u, int C, long long U) {
+    int c = (int)((u * C) / U);
+    while (c > 0 && u_begin(c, C, U) > u) --c;
+    while (c + 1 < C && u_begin(c + 1, C, U) <= u) ++c;
+    return c;
+}
+struct Seg {
+    long long u, u1;
+    int nk, t, ka, kb;
+    __device__ __forceinline__ void set() {
+        t = (int)(u / nk);
+        ka = (int)(u - (long long)t * nk);
+        kb = (int)min((long long)nk, u1 - (long long)t * nk);
+    }
+    __device__ __forceinline__ void start(long long a, long long b, int nk_) {
+        u = a;
+        u1 = b;
+        nk = nk_;
+        t = ka = kb = 0;
+        if (u < u1) set();
+    }
+    __device__ __forceinline__ bool valid() const { return u < u1; }
+    __device__ __forceinline__ void next() {
+        u = (long long)t * nk + kb;
+        if (u < u1) set();
+    }
+};
+
+struct SkArgs {
+    const unsigned char* W;   // Q4_K rows [M_pad][K/256 * 144]
+    float* Y;
+    float* ws;                // [C][2] partial tile slots (ws_slot)
+    int* err;
+    int M, M_pad, K, n_rows, NT, n_box, ldy, epi;
+};
+
+// Partial-tile slot of CTA cc: a 128 x 256 tile as [BN/4][BM] float4 (column
+// group c/4, row m), so that a warp's 32 rows of one column group are 512
+// contiguous bytes.  Slot 0: the CTA's first segment, slot 1: its last.
+__device__ __forceinline__ float4* ws_slot(float* ws, int cc, int slot) {
+    return (float4*)(ws + ((size_t)cc * 2 + slot) * (BN * BM));
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    return g / (1.0f + expf(-g)) * u;
+}
+
+// Epilogue of a tile this CTA computed alone, straight from TMEM, by the four
+// drain warps (thread m = weight row m, 16 columns per round).  STORE writes
+// the accumulator; ADD adds it to Y, whose next 16 values are loaded while the
+// current ones are written; SILU pairs gate row m < 64 with up row m + 64
+// through shared memory, each of the two threads producing 8 of the 16 outputs.
+__device__ __forceinline__ void alone_out(const SkArgs& a, uint32_t lane_base, int mt, int n0,
+                                          int n_mma, int m, float* xch) {
+    if (a.epi == SB_EPI_SILU) {
+        const int unit = mt * 64 + (m & 63);
+        const bool up = m >= 64;
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+            float v[16];
+            tmem_ld16(lane_base + (uint32_t)c0, v);
+            // up rows publish columns 0-7, gate rows columns 8-15
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xch[(up ? i : 8 + i) * 64 + (m & 63)] = v[up ? i : 8 + i];
+            drain_sync();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int col = up ? 8 + i : i;
+                const float g = up ? xch[col * 64 + (m & 63)] : v[i];
+                const float u = up ? v[8 + i] : xch[col * 64 + (m & 63)];
+                const int n = n0 + c0 + col;
+                if (n < a.n_rows && unit < a.M / 2) a.Y[(size_t)n * a.ldy + unit] = silu_mul(g, u);
+            }
+            drain_sync();
+        }
+        return;
+    }
+    const int row = mt * BM + m;
+    const bool live = row < a.M;
+    float y[16];
+    auto load_y = [&](int c0) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int n = n0 + c0 + i;
+            y[i] = (live && n < a.n_rows) ? a.Y[(size_t)n * a.ldy + row] : 0.f;
+        }
+    };
+    if (a.epi == SB_EPI_ADD) load_y(0);
+    for (int c0 = 0; c0 < n_mma; c0 += 16) {
+        float v[16];
+        tmem_ld16(lane_base + (uint32_t)c0, v);
+        float o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = a.epi == SB_EPI_ADD ? y[i] + v[i] : v[i];
+        if (a.epi == SB_EPI_ADD && c0 + 16 < n_mma) load_y(c0 + 16);
+        if (live) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int n = n0 + c0 + i;
+                if (n < a.n_rows) a.Y[(size_t)n * a.ldy + row] = o[i];
+            }
+        }
+    }
+}
+
+// ---- reduction of the shared tiles (second launch) ----------------------
+// CTA (t, g): tile t, column group g (4 columns); thread m: weight row m (up
+// rows are read by the gate row's thread for SiLU).  Tiles that one CTA of the
+// GEMM covered alone were written by it and are skipped.  The partials of CTAs
+// cf..cl are summed in that order (the result does not depend on timing), then
+// the epilogue is applied.
+__global__ void __launch_bounds__(BM) sk_finish_kernel(const float* __restrict__ ws, float* Y, int C,
+                                                       int NT, int nk, long long U, int M, int n_rows,
+                                                       int ldy, int epi) {
+    const int t = blockIdx.x, g4 = blockIdx.y, m = threadIdx.x;
+    const long long tu0 = (long long)t * nk;
+    const int cf = owner_of(tu0, C, U), cl = owner_of(tu0 + nk - 1, C, U);
+    const int mt = t / NT, n0 = (t % NT) * BN;
+    const bool silu = epi == SB_EPI_SILU;
+    if (cf == cl || n0 + 4 * g4 >= n_rows || (silu && m >= 64)) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f), acc2 = acc;
+#pragma unroll 4
+    for (int cc = cf; cc <= cl; ++cc) {
+        const int sl = u_begin(cc, C, U) >= tu0 ? 0 : 1;
+        const float4* src = (const float4*)(ws + ((size_t)cc * 2 + sl) * (BN * BM)) + (size_t)g4 * BM;
+        const float4 p = __ldcg(src + m);
+        acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+        if (silu) {
+            const float4 q = __ldcg(src + m + 64);
+            acc2.x += q.x; acc2.y += q.y; acc2.z += q.z; acc2.w += q.w;
+        }
+    }
+    const float v[4] = {acc.x, acc.y, acc.z, acc.w}, u[4] = {acc2.x, acc2.y, acc2.z, acc2.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int n = n0 + 4 * g4 + j;
+        if (n >= n_rows) continue;
+        if (silu) {
+            const int unit = mt * 64 + m;
+            if (unit < M / 2) Y[(size_t)n * ldy + unit] = silu_mul(v[j], u[j]);
+        } else {
+            const int row = mt * BM + m;
+            if (row < M) {
+                float* y = Y + (size_t)n * ldy + row;
+                *y = epi == SB_EPI_ADD ? *y + v[j] : v[j];
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    sk_kernel(const __grid_constant__ CUtensorMap xmap_hi, const __grid_constant__ CUtensorMap xmap_lo,
+              const SkArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* bst = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    float* xch = (float*)(bst + (size_t)BSTAGES * B_STAGE);
+    uint4* wring = (uint4*)(xch + XCH_FLOATS);     // [WSTAGES][2][NPROD]
+    __shared__ uint64_t a_full[ASTAGES], a_empty[ASTAGES], b_full[BSTAGES], b_empty[BSTAGES];
+    __shared__ uint64_t acc_full, acc_empty, done_bar;
+    __shared__ uint32_t tmem_slot;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int C = gridDim.x, c = blockIdx.x;
+    const int nk = a.K / BK;
+    const long long U = (long long)(a.M_pad / BM) * a.NT * nk;
+    const long long u0 = u_begin(c, C, U), u1 = u_begin(c + 1, C, U);
+
+    if (tid == 0) {
+        for (int s = 0; s < ASTAGES; ++s) {
+            bar_init(&a_full[s], NPROD / 32);      // one arrival per producer warp
+            bar_init(&a_empty[s], 1);
+        }
+        for (int s = 0; s < BSTAGES; ++s) {
+            bar_init(&b_full[s], 1);
+            bar_init(&b_empty[s], 1);
+        }
+        bar_init(&acc_full, 1);
+        bar_init(&acc_empty, 4);                  // one arrival per drain warp
+        bar_init(&done_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == MMA_WARP) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         su32(&tmem_slot)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    bool ok = true;
+
+    if (warp < 8) {
+        // ---------------- producers: Q4_K -> f16 hi | lo in TMEM ----------------
+        const int m = (warp & 3) * 32 + lane, half = warp >> 2;
+        const uint32_t lane_a = tmem + ((uint32_t)((warp & 3) * 32) << 16) + COL_A + 16u * half;
+        const size_t row_bytes = (size_t)(a.K / 256) * 144;
+        long long it = 0;
+        Seg sg;
+        sg.start(u0, u1, nk);
+        while (sg.valid() && ok) {
+            const int mt = sg.t / a.NT;
+            const unsigned char* wrow = a.W + (size_t)(mt * BM + m) * row_bytes;
+            const int nsb = a.K / 256;
+            // The Q4_K bytes (header, this thread's 16 nibble bytes) of K steps
+            // k+1 and k+2 are in flight into this thread's ring slots while
+            // step k converts (cp.async: no register waits on the copies).
+            auto issue = [&](int kk, long long slot) {
+                const unsigned char* p = wrow + (size_t)(kk >> 2) * 144;
+                uint4* d = wring + (size_t)(slot % WSTAGES) * 2 * NPROD + tid;
+                cp_async16(d, p);
+                cp_async16(d + NPROD, p + 16 + 32 * (kk & 3) + 16 * half);
+            };
+            long long wi = 0;                      // ring position of step sg.ka
+            for (int j = 0; j < WSTAGES - 1; ++j) {
+                if (sg.ka + j < sg.kb) issue(sg.ka + j, wi + j);
+                cp_async_commit();
+            }
+            for (int k = sg.ka; k < sg.kb; ++k, ++it, ++wi) {
+                const int s = (int)(it % ASTAGES);
+                if (it >= ASTAGES &&
+                    !__all_sync(0xffffffffu,
+                                bar_wait(&a_empty[s], (uint32_t)(((it / ASTAGES) - 1) & 1), a.err, 31))) {
+                    ok = false;
+                    break;
+                }
+                if (half == 0 && (k & 3) == 0 && (k >> 2) + 2 < nsb)
+                    l2_prefetch_block(wrow + (size_t)((k >> 2) + 2) * 144);
+                if (k + WSTAGES - 1 < sg.kb) issue(k + WSTAGES - 1, wi + WSTAGES - 1);
+                cp_async_commit();
+                cp_async_wait<WSTAGES - 1>();     // step k's copies have landed
+                const uint4* src = wring + (size_t)(wi % WSTAGES) * 2 * NPROD + tid;
+                const uint4 h0 = src[0], q0 = src[NPROD];
+                uint32_t hi[16], lo[16];
+                float sd, sm;
+                sub_scale(h0, (k & 3) * 2 + half, sd, sm);
+                dequant_sub(q0, sd, sm, hi, lo);
+                tmem_st16(lane_a + (uint32_t)(64 * s), hi);
+                tmem_st16(lane_a + (uint32_t)(64 * s + 32), lo);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) bar_arrive(&a_full[s]);
+            }
+            cp_async_wait<0>();                    // nothing in flight past the segment
+            sg.next();
+        }
+    } else if (warp == TMA_WARP) {
+        // ---------------- x hi / lo tiles by TMA ----------------
+        if (lane == 0) {
+            long long it = 0;
+            Seg sg;
+            sg.start(u0, u1, nk);
+            const uint32_t bytes = 2u * (uint32_t)a.n_box * 128u;
+            while (sg.valid() && ok) {
+                const int n0 = (sg.t % a.NT) * BN;
+                for (int k = sg.ka; k < sg.kb; ++k, ++it) {
+                    const int s = (int)(it % BSTAGES);
+                    if (it >= BSTAGES &&
+                        !bar_wait(&b_empty[s], (uint32_t)(((it / BSTAGES) - 1) & 1), a.err, 32)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* st = bst + (size_t)s * B_STAGE;
+                    bar_expect(&b_full[s], bytes);
+                    tma_2d(st, &xmap_hi, &b_full[s], k * BK, n0);
+                    tma_2d(st + B_PART, &xmap_lo, &b_full[s], k * BK, n0);
+                }
+                sg.next();
+            }
+            // no copy may still be in flight when the CTA exits
+            for (long long i = it - BSTAGES > 0 ? it - BSTAGES : 0; i < it; ++i)
+                bar_wait_exit(&b_full[i % BSTAGES], (uint32_t)((i / BSTAGES) & 1), a.err);
+        }
+    } else if (warp == MMA_WARP) {
+        // ---------------- MMA issue ----------------
+        if (lane == 0) {
+            long long it = 0, seg = 0;
+            Seg sg;
+            sg.start(u0, u1, nk);
+            while (sg.valid() && ok) {
+                const int n0 = (sg.t % a.NT) * BN;
+                const int n_here = min(a.n_rows - n0, BN);
+                const int n_mma = (n_here + 15) & ~15;
+                const uint32_t idesc =
+                    (1u << 4) | ((uint32_t)(n_mma >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+                if (seg > 0 && !bar_wait(&acc_empty, (uint32_t)((seg - 1) & 1), a.err, 33)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int k = sg.ka; k < sg.kb; ++k, ++it) {
+                    const int sa = (int)(it % ASTAGES), sb = (int)(it % BSTAGES);
+                    if (!bar_wait(&a_full[sa], (uint32_t)((it / ASTAGES) & 1), a.err, 34) ||
+                        !bar_wait(&b_full[sb], (uint32_t)((it / BSTAGES) & 1), a.err, 35)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t bh = su32(bst + (size_t)sb * B_STAGE), bl = bh + B_PART;
+                    const uint32_t ah = tmem + COL_A + (uint32_t)(64 * sa), al = ah + 32;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        mma_ta(tmem, ah + 8u * kk, desc_sw128(bh + 32u * kk), idesc,
+                               (k > sg.ka || kk > 0) ? 1u : 0u);
+                        mma_ta(tmem, ah + 8u * kk, desc_sw128(bl + 32u * kk), idesc, 1u);
+                        mma_ta(tmem, al + 8u * kk, desc_sw128(bh + 32u * kk), idesc, 1u);
+                    }
+                    mma_commit(&a_empty[sa]);
+                    mma_commit(&b_empty[sb]);
+                }
+                if (!ok) break;
+                mma_commit(&acc_full);
+                ++seg;
+                sg.next();
+            }
+            // every MMA issued above has completed before TMEM is freed
+            mma_commit(&done_bar);
+            bar_wait_exit(&done_bar, 0, a.err);
+        }
+    } else if (warp >= DRAIN_WARP0) {
+        // ---------------- drain: TMEM -> output or partials ----------------
+        // A tile computed alone is written from TMEM with its epilogue; the
+        // part of a shared tile goes to this CTA's workspace slot for
+        // sk_finish_kernel.  The four drain warps meet at named barriers (SiLU
+        // exchange), so they take every segment even after a failed wait;
+        // they then skip the TMEM reads and the writes.
+        const int q = warp & 3, m = q * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        long long seg = 0;
+        Seg sg;
+        sg.start(u0, u1, nk);
+        while (sg.valid()) {
+            const int t = sg.t, mt = t / a.NT, n0 = (t % a.NT) * BN;
+            const int n_mma = (min(a.n_rows - n0, BN) + 15) & ~15;
+            bool have = ok && bar_wait(&acc_full, (uint32_t)(seg & 1), a.err, 36);
+            have = __all_sync(0xffffffffu, have);
+            if (!have) ok = false;
+            tc_fence_after();
+            const bool alone = sg.ka == 0 && sg.kb == nk;
+            if (alone) {
+                if (have) {
+                    alone_out(a, lane_base, mt, n0, n_mma, m, xch);
+                } else if (a.epi == SB_EPI_SILU) {
+                    for (int c0 = 0; c0 < n_mma; c0 += 16) {   // keep the barrier schedule
+                        drain_sync();
+                        drain_sync();
+                    }
+                }
+            } else if (have) {
+                const int slot = u0 >= (long long)t * nk ? 0 : 1;   // first or last segment
+                float4* wsp = ws_slot(a.ws, c, slot) + m;
+                for (int c0 = 0; c0 < n_mma; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(lane_base + (uint32_t)c0, v);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        wsp[(size_t)((c0 >> 2) + j) * BM] =
+                            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) bar_arrive(&acc_empty);
+            ++seg;
+            sg.next();
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == MMA_WARP) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+}
+
+int g_sms = 0;
+
+}  // namespace
+
+extern "C" size_t sb_sk_ws_floats(void) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return (size_t)sms * 2 * BN * BM;
+}
+
+extern "C" void sb_sk_prepare(void) {
+    cudaFuncSetAttribute(sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+}
+
+extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows, float* ws,
+                          float* Y, int ldy, int epi, int* err, cudaStream_t st) {
+    if (!W || !X || !X->lo || W->wtype != SB_WT_Q4K || W->M_pad % BM || W->K % 256 ||
+        W->K != X->K || n_rows < 1 || n_rows > X->rows || !ws || !Y || !err ||
+        (epi != SB_EPI_STORE && epi != SB_EPI_ADD && epi != SB_EPI_SILU) ||
+        (epi == SB_EPI_SILU && W->M % 128))
+        return -1;
+    if (!g_sms) sb_sk_prepare();
+    SkArgs a;
+    a.W = (const unsigned char*)W->data;
+    a.Y = Y;
+    a.ws = ws;
+    a.err = err;
+    a.M = W->M;
+    a.M_pad = W->M_pad;
+    a.K = W->K;
+    a.n_rows = n_rows;
+    a.NT = (n_rows + BN - 1) / BN;
+    a.n_box = X->n_box;
+    a.ldy = ldy;
+    a.epi = epi;
+    const int MT = W->M_pad / BM, nk = W->K / BK;
+    const long long U = (long long)MT * a.NT * nk;
+    const int C = (int)(U < g_sms ? U : g_sms);
+    sk_kernel<<<C, NTHREADS, SMEM, st>>>(*(const CUtensorMap*)X->map_hi,
+                                         *(const CUtensorMap*)X->map_lo, a);
+    // shared tiles exist only when some CTA boundary falls inside a tile
+    bool shared = false;
+    for (int c = 1; c < C && !shared; ++c) shared = (U * c / C) % nk != 0;
+    if (shared) {
+        const int groups = (n_rows < BN ? (n_rows + 15) & ~15 : BN) / 4;
+        sk_finish_kernel<<<dim3((unsigned)(MT * a.NT), (unsigned)groups), BM, 0, st>>>(
+            ws, Y, C, a.NT, nk, U, W->M, n_rows, ldy, epi);
+    }
+    return 0;
+}

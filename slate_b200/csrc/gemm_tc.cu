@@ -164,6 +164,21 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *(uint32_t*)&h;
 }
 
+// Pulls one 144-byte Q4_K super-block into L2 ahead of use (the lines holding
+// its first, middle and last byte).
+__device__ __forceinline__ void l2_prefetch_block(const unsigned char* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + 72));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + 143));
+}
+
+// The low nibble of v as a float, exactly: 2^23 + q has q in its low mantissa
+// bits, so subtracting 2^23 leaves q (an OR and an FADD on the full-rate
+// pipes instead of an integer-to-float conversion).
+__device__ __forceinline__ float nib_f32(uint32_t v) {
+    return __uint_as_float(0x4B000000u | (v & 15u)) - 8388608.0f;
+}
+
 // Dequantises 32 weights (one Q4_K sub-block, 16 nibble bytes) into f16 hi
 // (and lo) words: out[c] holds elements 2c, 2c+1.
 template <int PASSES>
@@ -173,9 +188,9 @@ __device__ __forceinline__ void dequant32(uint4 q, float sd, float sm, uint32_t 
     float w[32];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        const uint32_t b = (qw[i >> 2] >> ((i & 3) * 8)) & 0xffu;
-        w[i] = sd * (float)(b & 15u) - sm;
-        w[i + 16] = sd * (float)(b >> 4) - sm;
+        const uint32_t b = qw[i >> 2] >> ((i & 3) * 8);
+        w[i] = sd * nib_f32(b) - sm;
+        w[i + 16] = sd * nib_f32(b >> 4) - sm;
     }
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
@@ -245,8 +260,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const size_t row_bytes = (size_t)(K / 256) * 144;
         const unsigned char* wrow = AMODE == 0 ? W + (size_t)(m_tile * BM + m) * row_bytes : nullptr;
         const uint32_t row_off = (uint32_t)((m >> 3) * 1024 + (m & 7) * 128);
-        uint4 hdr = make_uint4(0, 0, 0, 0);
-        int hdr_blk = -1;
+        // Weight bytes are loaded one K step ahead (registers), so the DRAM
+        // latency of step ks+1 overlaps the dequantisation of step ks.
+        uint4 hdr = make_uint4(0, 0, 0, 0), q0 = hdr, q1 = hdr, nhdr = hdr, nq0 = hdr, nq1 = hdr;
+        const int nsb = K / 256;
+        if (AMODE == 0 && ks0 < ks1) {
+            const unsigned char* p = wrow + (size_t)(ks0 >> 2) * 144;
+            hdr = __ldg((const uint4*)p);
+            q0 = __ldg((const uint4*)(p + 16 + 32 * (ks0 & 3)));
+            q1 = __ldg((const uint4*)(p + 32 + 32 * (ks0 & 3)));
+            // the next super-block goes to L2 now, the one after it on
+            // entering each block (below): two blocks ahead
+            if ((ks0 >> 2) + 1 < nsb) l2_prefetch_block(p + 144);
+        }
         for (int ks = ks0; ks < ks1 && ok; ++ks) {
             const int it = ks - ks0, s = it % STAGES;
             if (it >= STAGES && !mbar_wait(&empty_bar[s], ((it / STAGES) - 1) & 1, err, 1)) {
@@ -269,13 +295,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (PASSES == 3) tma_load_2d(b_lo, &xmap_lo, &full_bar[s], ks * BK, n0);
             }
             if (AMODE == 1) continue;
-            const int blk = ks >> 2, j0 = (ks & 3) * 2;     // 4 K-steps per super-block
-            if (blk != hdr_blk) {
-                hdr = __ldg((const uint4*)(wrow + (size_t)blk * 144));
-                hdr_blk = blk;
+            const int j0 = (ks & 3) * 2;                     // 4 K-steps per super-block
+            if ((ks & 3) == 0 && (ks >> 2) + 2 < nsb)
+                l2_prefetch_block(wrow + (size_t)((ks >> 2) + 2) * 144);
+            if (ks + 1 < ks1) {
+                const unsigned char* p = wrow + (size_t)((ks + 1) >> 2) * 144;
+                nhdr = ((ks + 1) & 3) == 0 ? __ldg((const uint4*)p) : hdr;
+                nq0 = __ldg((const uint4*)(p + 16 + 32 * ((ks + 1) & 3)));
+                nq1 = __ldg((const uint4*)(p + 32 + 32 * ((ks + 1) & 3)));
             }
-            const uint4 q0 = __ldg((const uint4*)(wrow + (size_t)blk * 144 + 16 + 16 * j0));
-            const uint4 q1 = __ldg((const uint4*)(wrow + (size_t)blk * 144 + 32 + 16 * j0));
             uint32_t hi[32], lo[32];
             {
                 float sd, sm;
@@ -299,6 +327,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             fence_async_smem();
             mbar_arrive(&full_bar[s]);
+            hdr = nhdr;
+            q0 = nq0;
+            q1 = nq1;
         }
     } else if (warp == 4 && lane == 0) {
         // ---------------- MMA issuer ----------------
@@ -389,7 +420,30 @@ __global__ void tc_finish_kernel(const float* __restrict__ ws, int splits, int n
     }
 }
 
-// f32 activations -> f16 hi (and lo = f16(x - hi)) rows for the TMA operand.
+// f32 activations -> f16 hi (and lo = f16(x - hi)) rows for the TMA operand:
+// one row per blockIdx.y, four elements (one float4, one 8-byte hi word and one
+// lo word) per thread.  Needs K % 4 == 0, ldx % 4 == 0, ld16 % 4 == 0 and a
+// 16-byte aligned X.
+__global__ void split_f16_rows_kernel(const float* __restrict__ X, int ldx, int K,
+                                     __half* __restrict__ hi, __half* __restrict__ lo, int ld16) {
+    const int n = blockIdx.y;
+    const float4* x4 = (const float4*)(X + (size_t)n * ldx);
+    uint2* h2 = (uint2*)(hi + (size_t)n * ld16);
+    uint2* l2 = lo ? (uint2*)(lo + (size_t)n * ld16) : nullptr;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < K / 4; j += gridDim.x * blockDim.x) {
+        const float4 v = __ldg(x4 + j);
+        const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+        h2[j] = make_uint2(*(const uint32_t*)&a, *(const uint32_t*)&b);
+        if (l2) {
+            const float2 ab = __half22float2(a), bb = __half22float2(b);
+            const __half2 la = __floats2half2_rn(v.x - ab.x, v.y - ab.y);
+            const __half2 lb = __floats2half2_rn(v.z - bb.x, v.w - bb.y);
+            l2[j] = make_uint2(*(const uint32_t*)&la, *(const uint32_t*)&lb);
+        }
+    }
+}
+
+// Scalar form of the same split, for any strides and alignment.
 __global__ void split_f16_kernel(const float* __restrict__ X, int ldx, int n_rows, int K,
                                  __half* __restrict__ hi, __half* __restrict__ lo, int ld16) {
     const long total = (long)n_rows * K;
@@ -457,6 +511,14 @@ extern "C" int sb_tc_make_operand(sb_tc_operand* op, void* hi, void* lo, int row
 extern "C" int sb_tc_split(const float* X, int ldx, int n_rows, const sb_tc_operand* op,
                            cudaStream_t st) {
     if (n_rows < 1 || n_rows > op->rows) return -1;
+    if (op->K % 4 == 0 && ldx % 4 == 0 && op->ld16 % 4 == 0 && ((uintptr_t)X & 15) == 0 &&
+        n_rows <= 65535) {
+        const int q = op->K / 4;
+        dim3 grid((unsigned)((q + 255) / 256), (unsigned)n_rows);
+        split_f16_rows_kernel<<<grid, 256, 0, st>>>(X, ldx, op->K, (__half*)op->hi,
+                                                    (__half*)op->lo, op->ld16);
+        return 0;
+    }
     const long total = (long)n_rows * op->K;
     const int grid = (int)((total + 255) / 256 < 2368 ? (total + 255) / 256 : 2368);
     split_f16_kernel<<<grid, 256, 0, st>>>(X, ldx, n_rows, op->K, (__half*)op->hi,

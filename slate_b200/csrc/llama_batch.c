@@ -87,6 +87,9 @@ struct slate_llama_batch {
     float* q4_ws;
     int* q4_cnt;
     size_t q4_cnt_n;
+    /* three-pass stream-K GEMM (gemm_sk.cu): partials of shared tiles */
+    int sk_on;
+    float* sk_ws;
     /* tensor parallelism: nq, nkv, F above are this rank's shares, V the full
      * vocabulary of which the LM head holds rows [v0, v0 + V_l) */
     int tp, rank, V_l, v0, Dq;     /* Dq = nq * hd (local) */
@@ -118,6 +121,13 @@ static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X,
                                   : W->K == b->q4_f.K ? &b->q4_f : &b->q4_a;
         int rc = sb_q4_split(X, ldx, n, op, s);
         return rc ? rc : sb_q4_gemm(W, op, n, Y, ldy, epi, b->q4_ws, b->q4_cnt, b->tc_err, s);
+    }
+    if (b->sk_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0 &&
+        (epi != SB_EPI_SILU || W->M % 128 == 0)) {
+        const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
+                                  : W->K == b->op_f.K ? &b->op_f : &b->op_a;
+        int rc = sb_tc_split(X, ldx, n, op, s);
+        return rc ? rc : sb_sk_gemm(W, op, n, b->sk_ws, Y, ldy, epi, b->tc_err, s);
     }
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
         const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
@@ -342,6 +352,9 @@ static int gemm_launches(const slate_llama_batch_t* b, const sb_matrix* W, int n
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return 2;   /* split + GEMM */
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2;                                                               /* split + GEMM */
+    if (b->sk_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0 &&
+        (epi != SB_EPI_SILU || W->M % 128 == 0))
+        return 3;                                         /* split + GEMM + shared-tile sums */
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2 + (splits == 1 && epi != SB_EPI_SILU ? 0 : 1);               /* + finish */
     return 1;
@@ -676,6 +689,13 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
             if (!b->q4_ws || !b->q4_cnt || sb_cuda_check(cudaMemset(b->q4_cnt, 0, tiles * 4), "memset"))
                 goto fail;
             b->q4_on = 1;
+        }
+        /* gemm_path 5: Q4_K weights on the three-pass stream-K kernel */
+        if (o->gemm_path == 5) {
+            sb_sk_prepare();
+            b->sk_ws = (float*)dalloc(b, sb_sk_ws_floats() * 4);
+            if (!b->sk_ws) goto fail;
+            b->sk_on = 1;
         }
     }
 

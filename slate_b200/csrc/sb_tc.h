@@ -86,6 +86,17 @@ int sb_q4_tiles(int M_pad, int n_rows);
  * before sb_q4_ws_floats). */
 void sb_q4_prepare(void);
 
+/* Three-pass Q4_K GEMM on a persistent stream-K grid (gemm_sk.cu): Y[n][m]
+ * (=, +=, SiLU(gate)*up) over Q4_K W for n < n_rows with X's f16 hi / lo pair.
+ * Tiles split between CTAs are summed by a second, small launch.  ws:
+ * sb_sk_ws_floats() floats.  SiLU needs W->M % 128 == 0 (gate rows 0-63 and up
+ * rows 64-127 of every 128-row tile). */
+int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows, float* ws, float* Y,
+               int ldy, int epi, int* err, cudaStream_t st);
+size_t sb_sk_ws_floats(void);
+/* SM count and shared-memory attribute on the current device (outside capture). */
+void sb_sk_prepare(void);
+
 #ifdef __cplusplus
 }
 #endif

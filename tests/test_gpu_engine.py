@@ -298,9 +298,10 @@ def test_scheduler_batches_concurrent_callers(sb, oracle, workdir):
 @pytest.mark.parametrize("n_rows", [40, 150])
 def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
     """The GEMM paths of the engine -- the 3-pass split (gemm_path 0), the
-    exact-weight stream-K kernel (4, with its STORE / residual ADD / fused
-    SiLU*up epilogues) and CUDA cores (1) -- each match the oracle on a 2-layer
-    Q4_K model at batch sizes with a partial second row tile."""
+    exact-weight stream-K kernel (4), the 3-pass stream-K kernel (5; both
+    stream-K kernels with their STORE / residual ADD / fused SiLU*up epilogues)
+    and CUDA cores (1) -- each match the oracle on a 2-layer Q4_K model at batch
+    sizes with a partial second row tile."""
     path = os.path.join(str(workdir), "paths_q4k.gguf")
     if not os.path.exists(path):
         sb.synth_gguf(path, n_layers=2, d_model=1024, ffn_hidden=2816, n_heads=16, n_kv_heads=4,
@@ -312,7 +313,7 @@ def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
     ref, _ = m.decode_many(feed)
     m.close()
     scale = np.abs(ref).max()
-    for gp in (0, 4, 1):
+    for gp in (0, 4, 5, 1):
         eng = make_engine(sb, path, max_batch=n_rows, gemm_path=gp)
         slots = [eng.open() for _ in range(n_rows)]
         for t in range(T):

@@ -250,6 +250,30 @@ def test_matmul_q4k_exact_weights(be, oracle, sb, monkeypatch, B, M, K, one_sm):
         assert scale_err(got, want) < 1e-5, rep
 
 
+@pytest.mark.parametrize("B,M,K", [(16, 128, 256), (40, 384, 1024), (130, 384, 4096),
+                                   (256, 1024, 4096), (256, 6144, 4096), (100, 256, 14336),
+                                   (300, 256, 512), (513, 512, 2048)])
+def test_matmul_q4k_streamk(be, oracle, sb, monkeypatch, B, M, K):
+    """passes=3 on the stream-K kernel (SLATE_TC_SK=1): Q4_K dequantised into
+    tensor memory as f16 hi + lo, x as f16 hi + lo, three MMA passes; the
+    (tile, K step) space split evenly over one CTA per SM, shared tiles summed
+    by the last CTA to finish (shapes with fewer units than SMs, 1..5 tiles per
+    SM, and partial row tiles).  Two calls: the tile counters must be left at
+    zero."""
+    monkeypatch.setenv("SLATE_TC_SK", "1")
+    rng = np.random.default_rng(B * 11 + M + K)
+    q = sb.quantize_q4k(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    X = rng.normal(0, 1, (B, K)).astype(np.float32)
+    Y = be.empty(B * M * 4)
+    Wd = oracle.dequant_q4k(q, M * K).reshape(M, K).astype(np.float64)
+    want = X.astype(np.float64) @ Wd.T
+    for rep in range(2):
+        rc = be.matmul_q4k_batch_tc(Y, be.dev(q), be.dev(X), B, M, K, 3)
+        assert rc == 0, be.sb.last_error()
+        got = be.host(Y, (B, M))
+        assert scale_err(got, want) < 1e-5, rep
+
+
 def run_attention(be, monkeypatch, path, q, pool, table, pos, nq, nkv, hd, kv_dtype, layer, n_pages):
     """attention_paged_gqa with the kernel picked by SLATE_CUDA_ATTN_PATH
     ("0": tensor cores where the f16 shape allows, "1": CUDA cores)."""
