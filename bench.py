@@ -75,8 +75,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=0,
                     help="reduce only for debugging; 0 = the config's (32 for 8b, 80 for 70b)")
     ap.add_argument("--gemm-path", type=int, default=0,
-                    help="0 auto (tcgen05 3-pass hi/lo split), 1 CUDA cores, 2 tcgen05 single f16 "
-                         "pass, 3 = 0, 4 exact-weight stream-K kernel, 5 3-pass stream-K kernel")
+                    help="0 auto (tcgen05 3-pass hi/lo split; stream-K kernel from 128 rows), 1 CUDA "
+                         "cores, 2 tcgen05 single f16 pass, 3 3-pass tile-per-CTA kernel only, 4 "
+                         "exact-weight stream-K kernel, 5 3-pass stream-K kernel from 16 rows")
     ap.add_argument("--attn-path", type=int, default=0,
                     help="0: tensor-core attention for f16 KV (mma.sync), 1: CUDA-core kernel")
     ap.add_argument("--max-ctx", type=int, default=0,
@@ -413,8 +414,9 @@ def main():
                    "global_batch": n * replicas, "seqs_per_replica": n, "kv_dtype": args.kv,
                    "mean_ctx": float(ctx.mean()),
                    "parallelism": f"replicas x{replicas}" + (f", tensor parallel {tp}" if tp > 1 else ""),
-                   "gemm_path": {0: "tcgen05 3-pass hi/lo", 1: "cuda-core f32", 2: "tcgen05 1-pass f16",
-                                 3: "tcgen05 3-pass hi/lo",
+                   "gemm_path": {0: "tcgen05 3-pass hi/lo, stream-K (weights in TMEM) from 128 rows",
+                                 1: "cuda-core f32", 2: "tcgen05 1-pass f16",
+                                 3: "tcgen05 3-pass hi/lo, tile per CTA",
                                  4: "tcgen05 exact f16 weights, 2-pass x, stream-K",
                                  5: "tcgen05 3-pass hi/lo, weights in TMEM, stream-K"}[args.gemm_path],
                    "attn_path": ("mma.sync f16 hi/lo" if args.attn_path == 0 and args.kv == "f16"

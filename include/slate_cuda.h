@@ -195,10 +195,12 @@ typedef struct slate_cuda_opts {
     int64_t kv_pages;    /* pool size in 16-token pages (0 = from kv_bytes) */
     size_t kv_bytes;     /* pool budget (0 = 90% of free HBM after weights) */
     int use_graphs;      /* capture one CUDA graph per batch size (1 = yes) */
-    int gemm_path;       /* 0 auto (tcgen05 3-pass hi/lo split), 1 CUDA-core kernels
-                            only, 2 tcgen05 1-pass f16, 3 = 0, 4 Q4_K on the
+    int gemm_path;       /* 0 auto (tcgen05 3-pass hi/lo split: the stream-K
+                            kernel from 128 rows, the tile-per-CTA kernel below),
+                            1 CUDA-core kernels only, 2 tcgen05 1-pass f16, 3 the
+                            3-pass tile-per-CTA kernel only, 4 Q4_K on the
                             exact-weight stream-K tcgen05 kernel (2 f16 passes),
-                            5 Q4_K on the 3-pass stream-K kernel (weights in TMEM) */
+                            5 Q4_K on the 3-pass stream-K kernel from 16 rows */
     int attn_path;       /* 0 auto (tensor cores for f16 KV where the shape allows),
                             1 CUDA-core attention only */
     /* Tensor parallelism (the 70B plan): tp_size ranks, one process or thread

@@ -224,14 +224,15 @@ static int be_matmul_q4k_sk(float* Y, const void* A, const float* X, int B, int 
     void *hi = NULL, *lo = NULL, *ws = NULL, *err = NULL;
     int rc = sb_cuda_check(cudaMallocAsync(&hi, (size_t)B * K * 2, g_stream), "alloc");
     if (!rc) rc = sb_cuda_check(cudaMallocAsync(&lo, (size_t)B * K * 2, g_stream), "alloc");
-    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&ws, sb_sk_ws_floats() * 4, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&ws, sb_sk_ws_floats(0) * 4, g_stream), "alloc");
     if (!rc) rc = sb_cuda_check(cudaMallocAsync(&err, 16, g_stream), "alloc");
     if (!rc) rc = sb_cuda_check(cudaMemsetAsync(err, 0, 16, g_stream), "memset");
     if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "alloc sync");
     sb_tc_operand op;
     if (!rc && sb_tc_make_operand(&op, hi, lo, B, K, K)) rc = -1;
     if (!rc) rc = fin(sb_tc_split(X, K, B, &op, g_stream), "tc split");
-    if (!rc) rc = fin(sb_sk_gemm(&W, &op, B, (float*)ws, Y, M, SB_EPI_STORE, (int*)err, g_stream),
+    if (!rc) rc = fin(sb_sk_gemm(&W, &op, B, (float*)ws, Y, M, SB_EPI_STORE, NULL, NULL, 0, (int*)err,
+                                 g_stream),
                       "matmul_q4k_batch_tc");
     int e = 0;
     if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, g_stream), "err");

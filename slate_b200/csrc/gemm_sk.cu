@@ -13,13 +13,14 @@
 //
 // Work decomposition: a tile is 128 weight rows (TMEM lanes) x up to 256
 // activation rows (MMA N); the (tile, 64-wide K step) space is cut into one
-// contiguous range per CTA, one CTA per SM.  A tile covered by one CTA is
-// written directly; a tile shared by several CTAs is written as f32 partials,
-// and the last CTA to arrive (per-tile counter) sums them in CTA order and
-// applies the epilogue, so results do not depend on timing.  This keeps every
-// SM busy whatever the tile count (the 224 tiles of the 8B gate/up projection
-// are 1.5 waves of 148 SMs as a plain grid) and needs no separate K-split
-// reduction kernel.
+// contiguous range per CTA, one CTA per SM.  A STORE / ADD tile covered by
+// one CTA is written from TMEM with its epilogue; the parts of a tile shared
+// by several CTAs, and every tile of the fused SiLU(gate) * up projection, go
+// to a workspace as f32, and a second launch spread over the whole GPU sums
+// the parts in CTA order -- results do not depend on timing -- and applies the
+// epilogue.  This keeps every SM busy whatever the tile count
+// (the 224 tiles of the 8B gate/up projection are 1.5 waves of 148 SMs as a
+// plain grid), and the accumulator is released as soon as it is copied out.
 //
 // Operand placement: the dequantised weights go register -> TMEM
 // (tcgen05.st; MMA with A in tensor memory), so shared memory holds only the
@@ -58,10 +59,9 @@ constexpr int NTHREADS = 512;
 constexpr uint32_t COL_A = 256;
 constexpr int B_PART = BN * 128;        // 32 KB: 256 rows x 64 f16
 constexpr int B_STAGE = 2 * B_PART;     // hi | lo
-constexpr int XCH_FLOATS = 16 * 64;     // SiLU exchange: 16 columns x 64 rows
 constexpr int WSTAGES = 3;              // per-thread ring of Q4_K bytes (cp.async)
 constexpr int W_STAGE = 2 * NPROD * 16; // [header | nibbles][producer thread] x 16 B
-constexpr size_t SMEM = (size_t)BSTAGES * B_STAGE + XCH_FLOATS * 4 + (size_t)WSTAGES * W_STAGE + 1024;
+constexpr size_t SMEM = (size_t)BSTAGES * B_STAGE + (size_t)WSTAGES * W_STAGE + 1024;
 constexpr uint64_t WAIT_NS = 2000000000ull;
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -172,9 +172,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void drain_sync() {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
 // 16 bytes global -> shared without a register (L2 only); completion by group.
@@ -291,51 +288,44 @@ struct Seg {
 struct SkArgs {
     const unsigned char* W;   // Q4_K rows [M_pad][K/256 * 144]
     float* Y;
-    float* ws;                // [C][2] partial tile slots (ws_slot)
+    float* ws;                // partial tile slots (ws_slot), SiLU tile areas (ws_tile)
+    __half* h_hi;             // SiLU: optional f16 hi / lo copy of the output
+    __half* h_lo;
     int* err;
-    int M, M_pad, K, n_rows, NT, n_box, ldy, epi;
+    int M, M_pad, K, n_rows, NT, n_box, ldy, epi, ld16;
 };
 
-// Partial-tile slot of CTA cc: a 128 x 256 tile as [BN/4][BM] float4 (column
-// group c/4, row m), so that a warp's 32 rows of one column group are 512
-// contiguous bytes.  Slot 0: the CTA's first segment, slot 1: its last.
-__device__ __forceinline__ float4* ws_slot(float* ws, int cc, int slot) {
+// Workspace: a 128 x 256 tile is stored as [BN/4][BM] float4 (column group
+// c/4, row m), so that a warp's 32 rows of one column group are 512
+// contiguous bytes.  CTA cc has two slots for the parts of shared tiles
+// (slot 0: its first segment, slot 1: its last); after the C * 2 slots, each
+// tile of a fused SiLU GEMM has an area for the accumulator of a CTA that
+// computed it alone.
+__device__ __forceinline__ float4* ws_slot(const float* ws, int cc, int slot) {
     return (float4*)(ws + ((size_t)cc * 2 + slot) * (BN * BM));
 }
+__device__ __forceinline__ float4* ws_tile(const float* ws, int C, int t) {
+    return (float4*)(ws + ((size_t)C * 2 + t) * (BN * BM));
+}
 
+// SiLU(g) * u as the reference forms it (expf, IEEE division).
 __device__ __forceinline__ float silu_mul(float g, float u) {
     return g / (1.0f + expf(-g)) * u;
 }
-
-// Epilogue of a tile this CTA computed alone, straight from TMEM, by the four
-// drain warps (thread m = weight row m, 16 columns per round).  STORE writes
-// the accumulator; ADD adds it to Y, whose next 16 values are loaded while the
-// current ones are written; SILU pairs gate row m < 64 with up row m + 64
-// through shared memory, each of the two threads producing 8 of the 16 outputs.
-__device__ __forceinline__ void alone_out(const SkArgs& a, uint32_t lane_base, int mt, int n0,
-                                          int n_mma, int m, float* xch) {
-    if (a.epi == SB_EPI_SILU) {
-        const int unit = mt * 64 + (m & 63);
-        const bool up = m >= 64;
-        for (int c0 = 0; c0 < n_mma; c0 += 16) {
-            float v[16];
-            tmem_ld16(lane_base + (uint32_t)c0, v);
-            // up rows publish columns 0-7, gate rows columns 8-15
-#pragma unroll
-            for (int i = 0; i < 8; ++i) xch[(up ? i : 8 + i) * 64 + (m & 63)] = v[up ? i : 8 + i];
-            drain_sync();
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int col = up ? 8 + i : i;
-                const float g = up ? xch[col * 64 + (m & 63)] : v[i];
-                const float u = up ? v[8 + i] : xch[col * 64 + (m & 63)];
-                const int n = n0 + c0 + col;
-                if (n < a.n_rows && unit < a.M / 2) a.Y[(size_t)n * a.ldy + unit] = silu_mul(g, u);
-            }
-            drain_sync();
-        }
-        return;
+__device__ __forceinline__ void store_h(const SkArgs& a, int n, int unit, float h) {
+    a.Y[(size_t)n * a.ldy + unit] = h;
+    if (a.h_hi) {
+        const __half hh = __float2half_rn(h);
+        a.h_hi[(size_t)n * a.ld16 + unit] = hh;
+        a.h_lo[(size_t)n * a.ld16 + unit] = __float2half_rn(h - __half2float(hh));
     }
+}
+
+// STORE / ADD epilogue of a tile this CTA computed alone, straight from TMEM,
+// by the four drain warps (thread m = weight row m, 16 columns per round; ADD
+// loads the next 16 values of Y while the current ones are written).
+__device__ __forceinline__ void alone_out(const SkArgs& a, uint32_t lane_base, int mt, int n0,
+                                          int n_mma, int m) {
     const int row = mt * BM + m;
     const bool live = row < a.M;
     float y[16];
@@ -364,46 +354,93 @@ __device__ __forceinline__ void alone_out(const SkArgs& a, uint32_t lane_base, i
     }
 }
 
-// ---- reduction of the shared tiles (second launch) ----------------------
-// CTA (t, g): tile t, column group g (4 columns); thread m: weight row m (up
-// rows are read by the gate row's thread for SiLU).  Tiles that one CTA of the
-// GEMM covered alone were written by it and are skipped.  The partials of CTAs
-// cf..cl are summed in that order (the result does not depend on timing), then
-// the epilogue is applied.
-__global__ void __launch_bounds__(BM) sk_finish_kernel(const float* __restrict__ ws, float* Y, int C,
-                                                       int NT, int nk, long long U, int M, int n_rows,
-                                                       int ldy, int epi) {
+// ---- output passes (second launch) -----------------------------------------
+// STORE / ADD: CTA (t, g) finishes column group g (4 columns) of shared tile t,
+// thread m weight row m; tiles that one CTA of the GEMM computed alone were
+// written by it and are skipped.  The parts of CTAs cf..cl are summed in that
+// order (the result does not depend on timing), then the epilogue is applied.
+__global__ void __launch_bounds__(BM) sk_out_kernel(const SkArgs a, int C, long long U) {
+    const int nk = a.K / BK;
     const int t = blockIdx.x, g4 = blockIdx.y, m = threadIdx.x;
     const long long tu0 = (long long)t * nk;
     const int cf = owner_of(tu0, C, U), cl = owner_of(tu0 + nk - 1, C, U);
-    const int mt = t / NT, n0 = (t % NT) * BN;
-    const bool silu = epi == SB_EPI_SILU;
-    if (cf == cl || n0 + 4 * g4 >= n_rows || (silu && m >= 64)) return;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f), acc2 = acc;
+    const int mt = t / a.NT, n0 = (t % a.NT) * BN;
+    const int row = mt * BM + m;
+    if (cf == cl || n0 + 4 * g4 >= a.n_rows || row >= a.M) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
     for (int cc = cf; cc <= cl; ++cc) {
-        const int sl = u_begin(cc, C, U) >= tu0 ? 0 : 1;
-        const float4* src = (const float4*)(ws + ((size_t)cc * 2 + sl) * (BN * BM)) + (size_t)g4 * BM;
+        const float4* src = ws_slot(a.ws, cc, u_begin(cc, C, U) >= tu0 ? 0 : 1) + (size_t)g4 * BM;
         const float4 p = __ldcg(src + m);
         acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
-        if (silu) {
-            const float4 q = __ldcg(src + m + 64);
-            acc2.x += q.x; acc2.y += q.y; acc2.z += q.z; acc2.w += q.w;
-        }
     }
-    const float v[4] = {acc.x, acc.y, acc.z, acc.w}, u[4] = {acc2.x, acc2.y, acc2.z, acc2.w};
+    const float v[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int n = n0 + 4 * g4 + j;
-        if (n >= n_rows) continue;
-        if (silu) {
-            const int unit = mt * 64 + m;
-            if (unit < M / 2) Y[(size_t)n * ldy + unit] = silu_mul(v[j], u[j]);
-        } else {
-            const int row = mt * BM + m;
-            if (row < M) {
-                float* y = Y + (size_t)n * ldy + row;
-                *y = epi == SB_EPI_ADD ? *y + v[j] : v[j];
+        if (n >= a.n_rows) continue;
+        float* y = a.Y + (size_t)n * a.ldy + row;
+        *y = a.epi == SB_EPI_ADD ? *y + v[j] : v[j];
+    }
+}
+
+// SiLU: CTA (t, q) finishes columns [64 q, 64 q + 64) of every tile t (the
+// GEMM leaves all its SiLU tiles in the workspace: a tile computed alone in
+// its own area, the parts of a shared tile in the CTAs' slots); item (column
+// group, gate row m < 64) reads gate row m and up row m + 64, four items per
+// thread with their loads issued together.
+constexpr int ST = 256;
+__global__ void __launch_bounds__(ST) sk_silu_out_kernel(const SkArgs a, int C, long long U) {
+    const int nk = a.K / BK;
+    const int t = blockIdx.x, q = blockIdx.y;
+    const long long tu0 = (long long)t * nk;
+    const int cf = owner_of(tu0, C, U), cl = owner_of(tu0 + nk - 1, C, U);
+    const int mt = t / a.NT, n0 = (t % a.NT) * BN;
+    const int groups = (min(a.n_rows - n0, BN) + 3) / 4;
+    const int g_lo = q * 16, g_hi = min(groups, g_lo + 16);
+    if (g_lo >= g_hi) return;
+    const int items = (g_hi - g_lo) * 64;
+    for (int base = threadIdx.x; base < items; base += 4 * ST) {
+        float4 acc[4], acc2[4];
+        int g4[4], mm[4];
+        bool live[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int it = base + j * ST;
+            live[j] = it < items;
+            g4[j] = g_lo + (live[j] ? it / 64 : 0);
+            mm[j] = live[j] ? it % 64 : 0;
+            acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            acc2[j] = acc[j];
+        }
+        for (int cc = cf; cc <= cl; ++cc) {
+            const float4* src = cf == cl ? ws_tile(a.ws, C, t)
+                                         : ws_slot(a.ws, cc, u_begin(cc, C, U) >= tu0 ? 0 : 1);
+            float4 p[4], p2[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (!live[j]) continue;
+                p[j] = __ldcg(src + (size_t)g4[j] * BM + mm[j]);
+                p2[j] = __ldcg(src + (size_t)g4[j] * BM + mm[j] + 64);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (!live[j]) continue;
+                acc[j].x += p[j].x; acc[j].y += p[j].y; acc[j].z += p[j].z; acc[j].w += p[j].w;
+                acc2[j].x += p2[j].x; acc2[j].y += p2[j].y; acc2[j].z += p2[j].z; acc2[j].w += p2[j].w;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (!live[j]) continue;
+            const float v[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
+            const float u[4] = {acc2[j].x, acc2[j].y, acc2[j].z, acc2[j].w};
+            const int unit = mt * 64 + mm[j];
+            if (unit >= a.M / 2) continue;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int n = n0 + 4 * g4[j] + e;
+                if (n < a.n_rows) store_h(a, n, unit, silu_mul(v[e], u[e]));
             }
         }
     }
@@ -414,8 +451,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const SkArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* bst = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    float* xch = (float*)(bst + (size_t)BSTAGES * B_STAGE);
-    uint4* wring = (uint4*)(xch + XCH_FLOATS);     // [WSTAGES][2][NPROD]
+    uint4* wring = (uint4*)(bst + (size_t)BSTAGES * B_STAGE);     // [WSTAGES][2][NPROD]
     __shared__ uint64_t a_full[ASTAGES], a_empty[ASTAGES], b_full[BSTAGES], b_empty[BSTAGES];
     __shared__ uint64_t acc_full, acc_empty, done_bar;
     __shared__ uint32_t tmem_slot;
@@ -581,12 +617,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             bar_wait_exit(&done_bar, 0, a.err);
         }
     } else if (warp >= DRAIN_WARP0) {
-        // ---------------- drain: TMEM -> output or partials ----------------
-        // A tile computed alone is written from TMEM with its epilogue; the
-        // part of a shared tile goes to this CTA's workspace slot for
-        // sk_finish_kernel.  The four drain warps meet at named barriers (SiLU
-        // exchange), so they take every segment even after a failed wait;
-        // they then skip the TMEM reads and the writes.
+        // ---------------- drain: TMEM -> output or workspace ----------------
+        // A STORE / ADD tile computed alone is written from TMEM with its
+        // epilogue; the part of a shared tile, and every SiLU tile, goes to the
+        // workspace for the output pass.  The accumulator is released right
+        // after.
         const int q = warp & 3, m = q * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
         long long seg = 0;
@@ -600,18 +635,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (!have) ok = false;
             tc_fence_after();
             const bool alone = sg.ka == 0 && sg.kb == nk;
-            if (alone) {
-                if (have) {
-                    alone_out(a, lane_base, mt, n0, n_mma, m, xch);
-                } else if (a.epi == SB_EPI_SILU) {
-                    for (int c0 = 0; c0 < n_mma; c0 += 16) {   // keep the barrier schedule
-                        drain_sync();
-                        drain_sync();
-                    }
-                }
+            if (have && alone && a.epi != SB_EPI_SILU) {
+                alone_out(a, lane_base, mt, n0, n_mma, m);
             } else if (have) {
-                const int slot = u0 >= (long long)t * nk ? 0 : 1;   // first or last segment
-                float4* wsp = ws_slot(a.ws, c, slot) + m;
+                float4* wsp = (alone ? ws_tile(a.ws, C, t)
+                                     : ws_slot(a.ws, c, u0 >= (long long)t * nk ? 0 : 1)) + m;
                 for (int c0 = 0; c0 < n_mma; c0 += 16) {
                     float v[16];
                     tmem_ld16(lane_base + (uint32_t)c0, v);
@@ -641,11 +669,32 @@ int g_sms = 0;
 
 }  // namespace
 
-extern "C" size_t sb_sk_ws_floats(void) {
+extern "C" size_t sb_sk_ws_floats(int max_silu_tiles) {
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess)
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    return (size_t)sms * 2 * BN * BM;
+    return ((size_t)sms * 2 + (size_t)(max_silu_tiles > 0 ? max_silu_tiles : 0)) * BN * BM;
+}
+
+extern "C" int sb_sk_tiles(int M_pad, int n_rows) {
+    return (M_pad / BM) * ((n_rows + BN - 1) / BN);
+}
+
+// Grid size and whether the output pass runs, as sb_sk_gemm decides them.
+static bool sk_plan(int M_pad, int K, int n_rows, int epi, int* C_out, long long* U_out) {
+    const int NT = (n_rows + BN - 1) / BN, nk = K / BK;
+    const long long U = (long long)(M_pad / BM) * NT * nk;
+    const int C = (int)(U < g_sms ? U : g_sms);
+    bool pass = epi == SB_EPI_SILU;
+    for (int c = 1; c < C && !pass; ++c) pass = (U * c / C) % nk != 0;
+    if (C_out) *C_out = C;
+    if (U_out) *U_out = U;
+    return pass;
+}
+
+extern "C" int sb_sk_kernels(int M_pad, int K, int n_rows, int epi) {
+    if (!g_sms) sb_sk_prepare();
+    return 1 + (sk_plan(M_pad, K, n_rows, epi, NULL, NULL) ? 1 : 0);
 }
 
 extern "C" void sb_sk_prepare(void) {
@@ -656,11 +705,12 @@ extern "C" void sb_sk_prepare(void) {
 }
 
 extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows, float* ws,
-                          float* Y, int ldy, int epi, int* err, cudaStream_t st) {
+                          float* Y, int ldy, int epi, void* h_hi, void* h_lo, int ld16, int* err,
+                          cudaStream_t st) {
     if (!W || !X || !X->lo || W->wtype != SB_WT_Q4K || W->M_pad % BM || W->K % 256 ||
         W->K != X->K || n_rows < 1 || n_rows > X->rows || !ws || !Y || !err ||
         (epi != SB_EPI_STORE && epi != SB_EPI_ADD && epi != SB_EPI_SILU) ||
-        (epi == SB_EPI_SILU && W->M % 128))
+        (epi == SB_EPI_SILU && W->M % 128) || (h_hi && (!h_lo || epi != SB_EPI_SILU || ld16 < W->M / 2)))
         return -1;
     if (!g_sms) sb_sk_prepare();
     SkArgs a;
@@ -676,18 +726,21 @@ extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows
     a.n_box = X->n_box;
     a.ldy = ldy;
     a.epi = epi;
-    const int MT = W->M_pad / BM, nk = W->K / BK;
-    const long long U = (long long)MT * a.NT * nk;
-    const int C = (int)(U < g_sms ? U : g_sms);
+    a.h_hi = (__half*)h_hi;
+    a.h_lo = (__half*)h_lo;
+    a.ld16 = ld16;
+    const int MT = W->M_pad / BM;
+    int C = 0;
+    long long U = 0;
+    // the output pass: every SiLU tile; shared tiles exist only when some CTA
+    // boundary falls inside a tile
+    const bool pass = sk_plan(W->M_pad, W->K, n_rows, epi, &C, &U);
     sk_kernel<<<C, NTHREADS, SMEM, st>>>(*(const CUtensorMap*)X->map_hi,
                                          *(const CUtensorMap*)X->map_lo, a);
-    // shared tiles exist only when some CTA boundary falls inside a tile
-    bool shared = false;
-    for (int c = 1; c < C && !shared; ++c) shared = (U * c / C) % nk != 0;
-    if (shared) {
-        const int groups = (n_rows < BN ? (n_rows + 15) & ~15 : BN) / 4;
-        sk_finish_kernel<<<dim3((unsigned)(MT * a.NT), (unsigned)groups), BM, 0, st>>>(
-            ws, Y, C, a.NT, nk, U, W->M, n_rows, ldy, epi);
-    }
+    if (pass && epi == SB_EPI_SILU)
+        sk_silu_out_kernel<<<dim3((unsigned)(MT * a.NT), 4u), ST, 0, st>>>(a, C, U);
+    else if (pass)
+        sk_out_kernel<<<dim3((unsigned)(MT * a.NT), (unsigned)((min(n_rows, BN) + 3) / 4)), BM, 0, st>>>(
+            a, C, U);
     return 0;
 }

@@ -87,8 +87,9 @@ struct slate_llama_batch {
     float* q4_ws;
     int* q4_cnt;
     size_t q4_cnt_n;
-    /* three-pass stream-K GEMM (gemm_sk.cu): partials of shared tiles */
-    int sk_on;
+    /* three-pass stream-K GEMM (gemm_sk.cu): workspace; sk_h: the gate/up
+     * GEMM writes its SiLU output also as the down GEMM's f16 hi / lo operand */
+    int sk_on, sk_h, sk_min;       /* sk_min: rows from which a GEMM uses it */
     float* sk_ws;
     /* tensor parallelism: nq, nkv, F above are this rank's shares, V the full
      * vocabulary of which the LM head holds rows [v0, v0 + V_l) */
@@ -108,6 +109,9 @@ struct slate_llama_batch {
 
 /* Rows from which a Q4_K GEMM runs on the tensor cores (below: CUDA cores). */
 #define SB_TC_MIN_ROWS 16
+/* Rows from which the default path uses the stream-K kernel (gemm_sk.cu)
+ * rather than gemm_tc.cu's tile-per-CTA kernel. */
+#define SB_SK_MIN_ROWS 128
 
 /* One weight GEMM of the step on the path chosen for (weight, rows). */
 static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X, int ldx, int n,
@@ -122,12 +126,15 @@ static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X,
         int rc = sb_q4_split(X, ldx, n, op, s);
         return rc ? rc : sb_q4_gemm(W, op, n, Y, ldy, epi, b->q4_ws, b->q4_cnt, b->tc_err, s);
     }
-    if (b->sk_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0 &&
+    if (b->sk_on && W->wtype == SB_WT_Q4K && n >= b->sk_min && W->M_pad % 128 == 0 &&
         (epi != SB_EPI_SILU || W->M % 128 == 0)) {
         const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
                                   : W->K == b->op_f.K ? &b->op_f : &b->op_a;
-        int rc = sb_tc_split(X, ldx, n, op, s);
-        return rc ? rc : sb_sk_gemm(W, op, n, b->sk_ws, Y, ldy, epi, b->tc_err, s);
+        /* the down GEMM's operand was written by the gate/up GEMM */
+        int rc = X == b->h && b->sk_h ? 0 : sb_tc_split(X, ldx, n, op, s);
+        const int fuse = epi == SB_EPI_SILU && b->sk_h && Y == b->h;
+        return rc ? rc : sb_sk_gemm(W, op, n, b->sk_ws, Y, ldy, epi, fuse ? b->op_f.hi : NULL,
+                                    fuse ? b->op_f.lo : NULL, b->op_f.ld16, b->tc_err, s);
     }
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
         const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
@@ -352,9 +359,10 @@ static int gemm_launches(const slate_llama_batch_t* b, const sb_matrix* W, int n
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return 2;   /* split + GEMM */
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2;                                                               /* split + GEMM */
-    if (b->sk_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0 &&
+    if (b->sk_on && W->wtype == SB_WT_Q4K && n >= b->sk_min && W->M_pad % 128 == 0 &&
         (epi != SB_EPI_SILU || W->M % 128 == 0))
-        return 3;                                         /* split + GEMM + shared-tile sums */
+        return (W == &b->layers[0].wdown && b->sk_h ? 0 : 1) +   /* split (down: fused) */
+               sb_sk_kernels(W->M_pad, W->K, n, epi);          /* GEMM (+ output pass) */
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2 + (splits == 1 && epi != SB_EPI_SILU ? 0 : 1);               /* + finish */
     return 1;
@@ -616,9 +624,11 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         }
     }
 
-    /* tensor-core path: gemm_path 0 (auto), 3 and 4 use the 3-pass split (4
-     * only for the f32 LM head), 2 the
-     * single f16 pass, 1 keeps every GEMM on the CUDA cores */
+    /* tensor-core path: gemm_path 0 (auto: the stream-K kernel from 128 rows,
+     * gemm_tc.cu's kernel below), 3 (gemm_tc.cu's kernel only), 4 (exact-
+     * weight kernel; 3-pass split for the f32 LM head) and 5 (stream-K kernel
+     * from 16 rows) use the 3-pass split, 2 the single f16 pass, 1 keeps every
+     * GEMM on the CUDA cores */
     b->tc_passes = o->gemm_path == 1 ? 0 : o->gemm_path == 2 ? 1 : 3;
     if (b->layers[0].wqkv.wtype != SB_WT_Q4K || D % 256 || b->F % 256 || b->Dq % 256)
         b->tc_passes = 0;
@@ -690,12 +700,17 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
                 goto fail;
             b->q4_on = 1;
         }
-        /* gemm_path 5: Q4_K weights on the three-pass stream-K kernel */
-        if (o->gemm_path == 5) {
+        /* gemm_path 5: Q4_K weights on the three-pass stream-K kernel; the
+         * default (0) uses it from 128 rows, where it is the faster kernel */
+        if (o->gemm_path == 5 || o->gemm_path == 0) {
+            b->sk_min = o->gemm_path == 5 ? SB_TC_MIN_ROWS : SB_SK_MIN_ROWS;
             sb_sk_prepare();
-            b->sk_ws = (float*)dalloc(b, sb_sk_ws_floats() * 4);
+            b->sk_ws = (float*)dalloc(b, sb_sk_ws_floats(sb_sk_tiles(l0->wgu.M_pad, B)) * 4);
             if (!b->sk_ws) goto fail;
             b->sk_on = 1;
+            /* gate/up on this kernel whenever down is: its output pass can
+             * write down's f16 operand */
+            b->sk_h = l0->wgu.M % 128 == 0 && l0->wdown.K == b->op_f.K && l0->wgu.M / 2 == b->op_f.K;
         }
     }
 

@@ -88,12 +88,18 @@ void sb_q4_prepare(void);
 
 /* Three-pass Q4_K GEMM on a persistent stream-K grid (gemm_sk.cu): Y[n][m]
  * (=, +=, SiLU(gate)*up) over Q4_K W for n < n_rows with X's f16 hi / lo pair.
- * Tiles split between CTAs are summed by a second, small launch.  ws:
- * sb_sk_ws_floats() floats.  SiLU needs W->M % 128 == 0 (gate rows 0-63 and up
- * rows 64-127 of every 128-row tile). */
+ * Tiles split between CTAs, and SiLU tiles, are finished by a second launch.
+ * ws: sb_sk_ws_floats(t) floats, t >= sb_sk_tiles(M_pad, n_rows) of every
+ * SiLU weight it is used with (0 if none).  SiLU needs W->M % 128 == 0 (gate rows 0-63 and up
+ * rows 64-127 of every 128-row tile) and may also write the result as an f16
+ * hi / lo pair (h_hi / h_lo, row stride ld16; NULL: not written), the operand
+ * of the GEMM that follows. */
 int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows, float* ws, float* Y,
-               int ldy, int epi, int* err, cudaStream_t st);
-size_t sb_sk_ws_floats(void);
+               int ldy, int epi, void* h_hi, void* h_lo, int ld16, int* err, cudaStream_t st);
+size_t sb_sk_ws_floats(int max_silu_tiles);
+/* Kernel launches of one sb_sk_gemm call (1, or 2 with the output pass). */
+int sb_sk_kernels(int M_pad, int K, int n_rows, int epi);
+int sb_sk_tiles(int M_pad, int n_rows);
 /* SM count and shared-memory attribute on the current device (outside capture). */
 void sb_sk_prepare(void);
 

@@ -297,8 +297,9 @@ def test_scheduler_batches_concurrent_callers(sb, oracle, workdir):
 
 @pytest.mark.parametrize("n_rows", [40, 150])
 def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
-    """The GEMM paths of the engine -- the 3-pass split (gemm_path 0), the
-    exact-weight stream-K kernel (4), the 3-pass stream-K kernel (5; both
+    """The GEMM paths of the engine -- the default (0: the 3-pass split, on the
+    stream-K kernel from 128 rows), the tile-per-CTA 3-pass kernel (3), the
+    exact-weight stream-K kernel (4), the 3-pass stream-K kernel (5; the
     stream-K kernels with their STORE / residual ADD / fused SiLU*up epilogues)
     and CUDA cores (1) -- each match the oracle on a 2-layer Q4_K model at batch
     sizes with a partial second row tile."""
@@ -313,7 +314,7 @@ def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
     ref, _ = m.decode_many(feed)
     m.close()
     scale = np.abs(ref).max()
-    for gp in (0, 4, 5, 1):
+    for gp in (0, 3, 4, 5, 1):
         eng = make_engine(sb, path, max_batch=n_rows, gemm_path=gp)
         slots = [eng.open() for _ in range(n_rows)]
         for t in range(T):
