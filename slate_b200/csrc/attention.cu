@@ -124,6 +124,64 @@ __global__ void rmsnorm_kernel(float* __restrict__ Y, int ldy, const float* __re
     for (int i = threadIdx.x; i < D; i += blockDim.x) y[i] = x[i] * w[i] * inv;
 }
 
+// The same normalisation with the row held in registers (float4, up to
+// RN_MAX * 4 * RN_T elements) and, besides the f32 row, the row as the f16
+// hi / lo pair (hi = f16(y), lo = f16(y - hi)) that the tensor-core GEMMs take
+// as their operand (lo may be null).  Sum of squares: f32 per thread, double
+// across the block, as above.
+constexpr int RN_T = 256, RN_MAX = 8;
+__global__ void __launch_bounds__(RN_T) rmsnorm_split_kernel(
+    float* __restrict__ Y, int ldy, const float* __restrict__ X, int ldx,
+    const float* __restrict__ w, int D, float eps, __half* __restrict__ hi, __half* __restrict__ lo,
+    int ld16) {
+    const int n = blockIdx.x, q4 = D / 4;
+    const float4* x4 = (const float4*)(X + (size_t)n * ldx);
+    float4 v[RN_MAX];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < RN_MAX; ++j) {
+        const int i = threadIdx.x + j * RN_T;
+        v[j] = i < q4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        s = fmaf(v[j].x, v[j].x, s);
+        s = fmaf(v[j].y, v[j].y, s);
+        s = fmaf(v[j].z, v[j].z, s);
+        s = fmaf(v[j].w, v[j].w, s);
+    }
+    __shared__ double red[32];
+    double sd = s;
+    for (int o = 16; o > 0; o >>= 1) sd += __shfl_xor_sync(0xffffffffu, sd, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sd;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double t = threadIdx.x < RN_T / 32 ? red[threadIdx.x] : 0.0;
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = 1.0f / sqrtf((float)(red[0] / (double)D) + eps);
+    const float4* w4 = (const float4*)w;
+    float4* y4 = (float4*)(Y + (size_t)n * ldy);
+    uint2* h2 = (uint2*)(hi + (size_t)n * ld16);
+    uint2* l2 = lo ? (uint2*)(lo + (size_t)n * ld16) : nullptr;
+#pragma unroll
+    for (int j = 0; j < RN_MAX; ++j) {
+        const int i = threadIdx.x + j * RN_T;
+        if (i >= q4) break;
+        const float4 g = __ldg(w4 + i);
+        const float4 y = make_float4(v[j].x * g.x * inv, v[j].y * g.y * inv, v[j].z * g.z * inv,
+                                     v[j].w * g.w * inv);
+        y4[i] = y;
+        const __half2 a = __floats2half2_rn(y.x, y.y), b = __floats2half2_rn(y.z, y.w);
+        h2[i] = make_uint2(*(const uint32_t*)&a, *(const uint32_t*)&b);
+        if (l2) {
+            const float2 ab = __half22float2(a), bb = __half22float2(b);
+            const __half2 la = __floats2half2_rn(y.x - ab.x, y.y - ab.y);
+            const __half2 lb = __floats2half2_rn(y.z - bb.x, y.w - bb.y);
+            l2[i] = make_uint2(*(const uint32_t*)&la, *(const uint32_t*)&lb);
+        }
+    }
+}
+
 __global__ void silu_mul_kernel(float* y, const float* g, const float* u, int n) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) {
@@ -429,6 +487,18 @@ extern "C" int sb_rmsnorm_rows(float* Y, int ldy, const float* X, int ldx, const
                                int D, float eps, cudaStream_t st) {
     if (B < 1 || D < 1) return -1;
     rmsnorm_kernel<<<B, 256, 0, st>>>(Y, ldy, X, ldx, w, D, eps);
+    return 0;
+}
+
+extern "C" int sb_rmsnorm_rows_split(float* Y, int ldy, const float* X, int ldx, const float* w,
+                                     int B, int D, float eps, void* hi, void* lo, int ld16,
+                                     cudaStream_t st) {
+    if (B < 1 || D < 1 || !hi) return -1;
+    if (D % 4 || D > RN_MAX * 4 * RN_T || ldx % 4 || ldy % 4 || ld16 % 4 || ((uintptr_t)X & 15) ||
+        ((uintptr_t)Y & 15) || ((uintptr_t)w & 15) || B > 0x7fffffff)
+        return -1;
+    rmsnorm_split_kernel<<<B, RN_T, 0, st>>>(Y, ldy, X, ldx, w, D, eps, (__half*)hi, (__half*)lo,
+                                              ld16);
     return 0;
 }
 extern "C" int sb_silu_mul(float* y, const float* g, const float* u, int n, cudaStream_t st) {

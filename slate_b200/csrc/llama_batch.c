@@ -90,6 +90,9 @@ struct slate_llama_batch {
     /* three-pass stream-K GEMM (gemm_sk.cu): workspace; sk_h: the gate/up
      * GEMM writes its SiLU output also as the down GEMM's f16 hi / lo operand */
     int sk_on, sk_h, sk_min;       /* sk_min: rows from which a GEMM uses it */
+    /* xn_split: the RMSNorm of the step being enqueued also wrote its rows as
+     * op_d's f16 hi / lo pair, so the GEMMs that read xn skip their split */
+    int xn_split;
     float* sk_ws;
     /* tensor parallelism: nq, nkv, F above are this rank's shares, V the full
      * vocabulary of which the LM head holds rows [v0, v0 + V_l) */
@@ -113,11 +116,33 @@ struct slate_llama_batch {
  * rather than gemm_tc.cu's tile-per-CTA kernel. */
 #define SB_SK_MIN_ROWS 128
 
+/* Whether the RMSNorm before a GEMM writes the tensor cores' f16 operand too
+ * (the 3- or 1-pass split paths; the exact-weight path splits with sub-block
+ * sums of its own). */
+static int norm_splits(const slate_llama_batch_t* b, int n) {
+    return b->tc_passes && !b->q4_on && n >= SB_TC_MIN_ROWS && n <= b->op_d.rows &&
+           b->D % 4 == 0 && b->D <= 8192 && b->ld_x % 4 == 0 && b->op_d.ld16 % 4 == 0;
+}
+
+/* RMSNorm of x into xn (and, where the GEMMs take it, into op_d's f16 pair). */
+static int step_norm(slate_llama_batch_t* b, const float* w, int n, cudaStream_t s) {
+    b->xn_split = 0;
+    if (norm_splits(b, n) &&
+        sb_rmsnorm_rows_split(b->xn, b->ld_x, b->x, b->ld_x, w, n, b->D, b->eps, b->op_d.hi,
+                              b->op_d.lo, b->op_d.ld16, s) == 0) {
+        b->xn_split = 1;
+        return 0;
+    }
+    return sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, w, n, b->D, b->eps, s);
+}
+
 /* One weight GEMM of the step on the path chosen for (weight, rows). */
 static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X, int ldx, int n,
                      float* Y, int ldy, int epi, int splits, cudaStream_t s) {
+    /* op_d already holds xn as the f16 pair (RMSNorm wrote it) */
+    const int have_d = X == b->xn && b->xn_split;
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) {
-        int rc = sb_tc_split(X, ldx, n, &b->op_d, s);
+        int rc = have_d ? 0 : sb_tc_split(X, ldx, n, &b->op_d, s);
         return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, &b->op_d, n, Y, ldy, epi, b->tc_err, s);
     }
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
@@ -131,7 +156,8 @@ static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X,
         const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
                                   : W->K == b->op_f.K ? &b->op_f : &b->op_a;
         /* the down GEMM's operand was written by the gate/up GEMM */
-        int rc = X == b->h && b->sk_h ? 0 : sb_tc_split(X, ldx, n, op, s);
+        int rc = (X == b->h && b->sk_h) || (have_d && op == &b->op_d) ? 0
+                                                                      : sb_tc_split(X, ldx, n, op, s);
         const int fuse = epi == SB_EPI_SILU && b->sk_h && Y == b->h;
         return rc ? rc : sb_sk_gemm(W, op, n, b->sk_ws, Y, ldy, epi, fuse ? b->op_f.hi : NULL,
                                     fuse ? b->op_f.lo : NULL, b->op_f.ld16, b->tc_err, s);
@@ -139,7 +165,7 @@ static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X,
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
         const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
                                   : W->K == b->op_f.K ? &b->op_f : &b->op_a;
-        int rc = sb_tc_split(X, ldx, n, op, s);
+        int rc = have_d && op == &b->op_d ? 0 : sb_tc_split(X, ldx, n, op, s);
         return rc ? rc : sb_tc_gemm(W, op, n, b->tc_passes, splits, b->tc_ws, Y, ldy, epi,
                                     b->tc_err, s);
     }
@@ -316,7 +342,7 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, cudaStream_t 
                            b->ld_x, b->row_pos, b->row_slot, b->status, s);
     for (int l = 0; l < b->L && !rc; ++l) {
         const sb_layer* ly = &b->layers[l];
-        rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, ly->attn_norm, n, b->D, b->eps, s);
+        rc |= step_norm(b, ly->attn_norm, n, s);
         rc |= step_gemm(b, &ly->wqkv, b->xn, b->ld_x, n, b->qkv, b->ld_qkv, SB_EPI_STORE, b->sp_qkv, s);
         rc |= sb_rope_append(b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, b->row_pos, b->row_slot,
                              b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
@@ -327,12 +353,12 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, cudaStream_t 
                                  b->tc_err, s);
         rc |= step_gemm(b, &ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, res_epi, b->sp_wo, s);
         if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, b->x, (size_t)n * b->ld_x, s);
-        rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, ly->ffn_norm, n, b->D, b->eps, s);
+        rc |= step_norm(b, ly->ffn_norm, n, s);
         rc |= step_gemm(b, &ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
         rc |= step_gemm(b, &ly->wdown, b->h, b->ld_h, n, b->x, b->ld_x, res_epi, b->sp_dn, s);
         if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, b->x, (size_t)n * b->ld_x, s);
     }
-    rc |= sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, b->out_norm, n, b->D, b->eps, s);
+    rc |= step_norm(b, b->out_norm, n, s);
     rc |= step_gemm(b, &b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE, 1, s);
     if (sample) {
         rc |= sb_sample_rows(b->logits, b->ld_logits, b->V, n, b->d_samp, b->d_rng, b->samp_scratch,
@@ -353,18 +379,20 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, cudaStream_t 
     return sb_cuda_check(cudaGetLastError(), "step launch");
 }
 
-/* Kernel launches step_gemm makes for (W, n rows, epilogue, splits). */
+/* Kernel launches step_gemm makes for (W, n rows, epilogue, splits); xn_in:
+ * the GEMM reads xn (whose f16 split the RMSNorm may have written). */
 static int gemm_launches(const slate_llama_batch_t* b, const sb_matrix* W, int n, int epi,
-                         int splits) {
-    if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return 2;   /* split + GEMM */
+                         int splits, int xn_in) {
+    const int split = xn_in && norm_splits(b, n) ? 0 : 1;
+    if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return split + 1;
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2;                                                               /* split + GEMM */
     if (b->sk_on && W->wtype == SB_WT_Q4K && n >= b->sk_min && W->M_pad % 128 == 0 &&
         (epi != SB_EPI_SILU || W->M % 128 == 0))
-        return (W == &b->layers[0].wdown && b->sk_h ? 0 : 1) +   /* split (down: fused) */
-               sb_sk_kernels(W->M_pad, W->K, n, epi);          /* GEMM (+ output pass) */
+        return (W == &b->layers[0].wdown && b->sk_h ? 0 : split) +   /* split (down: fused) */
+               sb_sk_kernels(W->M_pad, W->K, n, epi);              /* GEMM (+ output pass) */
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
-        return 2 + (splits == 1 && epi != SB_EPI_SILU ? 0 : 1);               /* + finish */
+        return split + 1 + (splits == 1 && epi != SB_EPI_SILU ? 0 : 1);      /* + finish */
     return 1;
 }
 
@@ -373,12 +401,12 @@ int slate_llama_batch_launches_per_step(const slate_llama_batch_t* b, int n) {
     const sb_layer* l0 = &b->layers[0];
     const int res_epi = b->tp > 1 && b->rank != 0 ? SB_EPI_STORE : SB_EPI_ADD;
     const int per_layer = 2 /* rmsnorm x2 */ + 1 /* rope + append */ + 2 /* attention */ +
-                          gemm_launches(b, &l0->wqkv, n, SB_EPI_STORE, b->sp_qkv) +
-                          gemm_launches(b, &l0->wo, n, res_epi, b->sp_wo) +
-                          gemm_launches(b, &l0->wgu, n, SB_EPI_SILU, b->sp_gu) +
-                          gemm_launches(b, &l0->wdown, n, res_epi, b->sp_dn);
+                          gemm_launches(b, &l0->wqkv, n, SB_EPI_STORE, b->sp_qkv, 1) +
+                          gemm_launches(b, &l0->wo, n, res_epi, b->sp_wo, 0) +
+                          gemm_launches(b, &l0->wgu, n, SB_EPI_SILU, b->sp_gu, 1) +
+                          gemm_launches(b, &l0->wdown, n, res_epi, b->sp_dn, 0);
     return 1 /* prologue */ + b->L * per_layer + 1 /* final rmsnorm */ +
-           gemm_launches(b, &b->lm_head, n, SB_EPI_STORE, 1) + (b->tp > 1 ? 2 : 1);
+           gemm_launches(b, &b->lm_head, n, SB_EPI_STORE, 1, 1) + (b->tp > 1 ? 2 : 1);
 }
 
 /* Runs the step for n rows whose metadata is already in d_io. */
