@@ -374,12 +374,15 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     }
 }
 
-// Merge chunk partials: out = Σ_c o_c e^{m_c-M} / Σ_c l_c e^{m_c-M}.
+// Merge chunk partials: out = Σ_c o_c e^{m_c-M} / Σ_c l_c e^{m_c-M}.  With
+// hi != null the rows are also written as the f16 pair hi = f16(out), lo =
+// f16(out - hi) (row stride ld16) that the next tensor-core GEMM takes.
 template <int HD>
 __global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ part, int B, int nq,
                                                     const int32_t* __restrict__ row_pos,
                                                     int nchunk_max, float* __restrict__ att,
-                                                    int ld_att) {
+                                                    int ld_att, __half* __restrict__ hi,
+                                                    __half* __restrict__ lo, int ld16) {
     const int lane = threadIdx.x & 31;
     const long w = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
     const int hq = (int)(w % nq);
@@ -403,18 +406,30 @@ __global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ pa
             const float* r = rec0 + (size_t)c * (HD + 2);
             acc = fmaf(r[2 + d], expf(r[0] - M), acc);
         }
-        att[(size_t)b * ld_att + (size_t)hq * HD + d] = acc * invL;
+        const float o = acc * invL;
+        att[(size_t)b * ld_att + (size_t)hq * HD + d] = o;
+        if (hi) {
+            const __half h = __float2half_rn(o);
+            hi[(size_t)b * ld16 + (size_t)hq * HD + d] = h;
+            if (lo) lo[(size_t)b * ld16 + (size_t)hq * HD + d] = __float2half_rn(o - __half2float(h));
+        }
     }
 }
 
 // prepare != 0: only opt the instantiation into its shared-memory size (the
 // dynamic ring plus static state can exceed the 48 KB default); this happens
 // per device and outside any stream capture.
+struct HiLo {
+    __half* hi;
+    __half* lo;
+    int ld16;
+};
+
 template <int HD, int G, typename KT>
 int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
              int nkv, const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
              int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk,
-             float* scratch, int* err, cudaStream_t st) {
+             float* scratch, int* err, HiLo hl, cudaStream_t st) {
     using S = AttnShape<HD, G, KT>;
     if (prepare) {
         cudaFuncSetAttribute(attn_chunk<HD, G, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -429,7 +444,7 @@ int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
         layer, nchunk, scratch, err);
     const long cw = (long)B * nq;
     attn_combine<HD><<<(unsigned)((cw + 3) / 4), 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att,
-                                                                ld_att);
+                                                                ld_att, hl.hi, hl.lo, hl.ld16);
     return 0;
 }
 
@@ -437,13 +452,13 @@ template <int HD, typename KT>
 int launch_hd(int prepare, int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B,
               int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
               const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
-              int layer, int nchunk, float* scratch, int* err, cudaStream_t st) {
+              int layer, int nchunk, float* scratch, int* err, HiLo hl, cudaStream_t st) {
     switch (G) {
 #define CASE(g)                                                                                  \
     case g:                                                                                      \
         return launch_g<HD, g, KT>(prepare, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
                                    row_slot, page_table, max_pages, pool, n_pages, layer,        \
-                                   nchunk, scratch, err, st);
+                                   nchunk, scratch, err, hl, st);
         CASE(1) CASE(2) CASE(4) CASE(8)
 #undef CASE
     }
@@ -454,13 +469,13 @@ template <typename KT>
 int launch_kt(int prepare, int hd, int G, float* att, int ld_att, const float* qkv, int ld_qkv,
               int B, int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
               const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
-              int layer, int nchunk, float* scratch, int* err, cudaStream_t st) {
+              int layer, int nchunk, float* scratch, int* err, HiLo hl, cudaStream_t st) {
     switch (hd) {
 #define CASE(h)                                                                                  \
     case h:                                                                                      \
         return launch_hd<h, KT>(prepare, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
                                 row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,   \
-                                scratch, err, st);
+                                scratch, err, hl, st);
         CASE(8) CASE(16) CASE(32) CASE(64) CASE(128)
 #undef CASE
     }
@@ -468,14 +483,16 @@ int launch_kt(int prepare, int hd, int G, float* att, int ld_att, const float* q
 }
 
 int combine(int hd, const float* scratch, int B, int nq, const int32_t* row_pos, int nchunk,
-            float* att, int ld_att, cudaStream_t st) {
+            float* att, int ld_att, HiLo hl, cudaStream_t st) {
     const unsigned grid = (unsigned)(((long)B * nq + 3) / 4);
     switch (hd) {
         case 64:
-            attn_combine<64><<<grid, 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att, ld_att);
+            attn_combine<64><<<grid, 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att, ld_att,
+                                                   hl.hi, hl.lo, hl.ld16);
             return 0;
         case 128:
-            attn_combine<128><<<grid, 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att, ld_att);
+            attn_combine<128><<<grid, 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att, ld_att,
+                                                    hl.hi, hl.lo, hl.ld16);
             return 0;
     }
     return -1;
@@ -485,7 +502,7 @@ int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
              int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
              const int32_t* page_table, int max_pages, const void* pool, const void* kvmap,
              int64_t n_pages, int layer, int kv_dtype, int max_seq, float* scratch, int* err,
-             cudaStream_t st) {
+             HiLo hl, cudaStream_t st) {
     if (nkv < 1 || nq % nkv) return -1;
     const int G = nq / nkv;
     const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
@@ -498,16 +515,16 @@ int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
             const int rc = sb_attention_mma(0, kvmap, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot,
                                             page_table, max_pages, n_pages, layer, nchunk, scratch,
                                             err, st);
-            return rc ? rc : combine(hd, scratch, B, nq, row_pos, nchunk, att, ld_att, st);
+            return rc ? rc : combine(hd, scratch, B, nq, row_pos, nchunk, att, ld_att, hl, st);
         }
     }
     return kv_dtype == SLATE_KV_F16
                ? launch_kt<__half>(prepare, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
                                    row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,
-                                   scratch, err, st)
+                                   scratch, err, hl, st)
                : launch_kt<float>(prepare, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
                                   row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,
-                                  scratch, err, st);
+                                  scratch, err, hl, st);
 }
 
 }  // namespace
@@ -519,7 +536,7 @@ extern "C" size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int
 
 extern "C" int sb_attention_prepare(int nq, int nkv, int hd, int kv_dtype) {
     return dispatch(1, nullptr, 0, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr, 0,
-                    nullptr, nullptr, 0, 0, kv_dtype, 0, nullptr, nullptr, 0);
+                    nullptr, nullptr, 0, 0, kv_dtype, 0, nullptr, nullptr, HiLo{nullptr, nullptr, 0}, 0);
 }
 
 extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B,
@@ -530,5 +547,19 @@ extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int 
                                   float* scratch, int* err, cudaStream_t st) {
     if (B < 1 || !err) return -1;
     return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
-                    max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, scratch, err, st);
+                    max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, scratch, err,
+                    HiLo{nullptr, nullptr, 0}, st);
+}
+
+extern "C" int sb_attention_paged_split(float* att, int ld_att, const float* qkv, int ld_qkv, int B,
+                                        int nq, int nkv, int hd, const int32_t* row_pos,
+                                        const int32_t* row_slot, const int32_t* page_table,
+                                        int max_pages, const void* pool, const void* kvmap,
+                                        int64_t n_pages, int layer, int kv_dtype, int max_seq,
+                                        float* scratch, int* err, void* hi, void* lo, int ld16,
+                                        cudaStream_t st) {
+    if (B < 1 || !err || !hi || ld16 < nq * hd) return -1;
+    return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
+                    max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, scratch, err,
+                    HiLo{(__half*)hi, (__half*)lo, ld16}, st);
 }

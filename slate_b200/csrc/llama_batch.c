@@ -93,6 +93,7 @@ struct slate_llama_batch {
     /* xn_split: the RMSNorm of the step being enqueued also wrote its rows as
      * op_d's f16 hi / lo pair, so the GEMMs that read xn skip their split */
     int xn_split;
+    int att_split;                 /* the same for the attention output (op_a) */
     float* sk_ws;
     /* tensor parallelism: nq, nkv, F above are this rank's shares, V the full
      * vocabulary of which the LM head holds rows [v0, v0 + V_l) */
@@ -139,8 +140,10 @@ static int step_norm(slate_llama_batch_t* b, const float* w, int n, cudaStream_t
 /* One weight GEMM of the step on the path chosen for (weight, rows). */
 static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X, int ldx, int n,
                      float* Y, int ldy, int epi, int splits, cudaStream_t s) {
-    /* op_d already holds xn as the f16 pair (RMSNorm wrote it) */
+    /* op_d (op_a) already holds xn (att) as the f16 pair: RMSNorm (the
+     * attention) wrote it */
     const int have_d = X == b->xn && b->xn_split;
+    const int have_a = X == b->att && b->att_split;
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) {
         int rc = have_d ? 0 : sb_tc_split(X, ldx, n, &b->op_d, s);
         return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, &b->op_d, n, Y, ldy, epi, b->tc_err, s);
@@ -156,8 +159,9 @@ static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X,
         const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
                                   : W->K == b->op_f.K ? &b->op_f : &b->op_a;
         /* the down GEMM's operand was written by the gate/up GEMM */
-        int rc = (X == b->h && b->sk_h) || (have_d && op == &b->op_d) ? 0
-                                                                      : sb_tc_split(X, ldx, n, op, s);
+        int rc = (X == b->h && b->sk_h) || (have_d && op == &b->op_d) || (have_a && op == &b->op_a)
+                     ? 0
+                     : sb_tc_split(X, ldx, n, op, s);
         const int fuse = epi == SB_EPI_SILU && b->sk_h && Y == b->h;
         return rc ? rc : sb_sk_gemm(W, op, n, b->sk_ws, Y, ldy, epi, fuse ? b->op_f.hi : NULL,
                                     fuse ? b->op_f.lo : NULL, b->op_f.ld16, b->tc_err, s);
@@ -165,7 +169,9 @@ static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X,
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
         const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
                                   : W->K == b->op_f.K ? &b->op_f : &b->op_a;
-        int rc = have_d && op == &b->op_d ? 0 : sb_tc_split(X, ldx, n, op, s);
+        int rc = (have_d && op == &b->op_d) || (have_a && op == &b->op_a)
+                     ? 0
+                     : sb_tc_split(X, ldx, n, op, s);
         return rc ? rc : sb_tc_gemm(W, op, n, b->tc_passes, splits, b->tc_ws, Y, ldy, epi,
                                     b->tc_err, s);
     }
@@ -347,10 +353,18 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, cudaStream_t 
         rc |= sb_rope_append(b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, b->row_pos, b->row_slot,
                              b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
                              b->rope_cos, b->rope_sin, s);
-        rc |= sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
-                                 b->row_pos, b->row_slot, b->page_table, b->max_pages, b->pool,
-                                 b->kvmap_p, b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch,
-                                 b->tc_err, s);
+        b->att_split = norm_splits(b, n) && b->op_a.ld16 >= b->Dq;
+        if (b->att_split)
+            rc |= sb_attention_paged_split(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv,
+                                           b->hd, b->row_pos, b->row_slot, b->page_table,
+                                           b->max_pages, b->pool, b->kvmap_p, b->n_pages, l,
+                                           b->kv_dtype, b->max_seq, b->scratch, b->tc_err,
+                                           b->op_a.hi, b->op_a.lo, b->op_a.ld16, s);
+        else
+            rc |= sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
+                                     b->row_pos, b->row_slot, b->page_table, b->max_pages, b->pool,
+                                     b->kvmap_p, b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch,
+                                     b->tc_err, s);
         rc |= step_gemm(b, &ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, res_epi, b->sp_wo, s);
         if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, b->x, (size_t)n * b->ld_x, s);
         rc |= step_norm(b, ly->ffn_norm, n, s);
@@ -379,11 +393,12 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, cudaStream_t 
     return sb_cuda_check(cudaGetLastError(), "step launch");
 }
 
-/* Kernel launches step_gemm makes for (W, n rows, epilogue, splits); xn_in:
- * the GEMM reads xn (whose f16 split the RMSNorm may have written). */
+/* Kernel launches step_gemm makes for (W, n rows, epilogue, splits); pre:
+ * the GEMM's input comes from a kernel that can write its f16 split (RMSNorm,
+ * attention). */
 static int gemm_launches(const slate_llama_batch_t* b, const sb_matrix* W, int n, int epi,
-                         int splits, int xn_in) {
-    const int split = xn_in && norm_splits(b, n) ? 0 : 1;
+                         int splits, int pre) {
+    const int split = pre && norm_splits(b, n) ? 0 : 1;
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return split + 1;
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2;                                                               /* split + GEMM */
@@ -402,7 +417,7 @@ int slate_llama_batch_launches_per_step(const slate_llama_batch_t* b, int n) {
     const int res_epi = b->tp > 1 && b->rank != 0 ? SB_EPI_STORE : SB_EPI_ADD;
     const int per_layer = 2 /* rmsnorm x2 */ + 1 /* rope + append */ + 2 /* attention */ +
                           gemm_launches(b, &l0->wqkv, n, SB_EPI_STORE, b->sp_qkv, 1) +
-                          gemm_launches(b, &l0->wo, n, res_epi, b->sp_wo, 0) +
+                          gemm_launches(b, &l0->wo, n, res_epi, b->sp_wo, b->op_a.ld16 >= b->Dq) +
                           gemm_launches(b, &l0->wgu, n, SB_EPI_SILU, b->sp_gu, 1) +
                           gemm_launches(b, &l0->wdown, n, res_epi, b->sp_dn, 0);
     return 1 /* prologue */ + b->L * per_layer + 1 /* final rmsnorm */ +

@@ -106,6 +106,14 @@ int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int
                        const int32_t* page_table, int max_pages, const void* pool,
                        const void* kvmap, int64_t n_pages, int layer, int kv_dtype, int max_seq,
                        float* scratch, int* err, cudaStream_t st);
+/* The same, also writing the output rows as the f16 hi / lo pair (row stride
+ * ld16 >= nq * hd, lo nullable) that the following tensor-core GEMM takes. */
+int sb_attention_paged_split(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
+                             int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
+                             const int32_t* page_table, int max_pages, const void* pool,
+                             const void* kvmap, int64_t n_pages, int layer, int kv_dtype,
+                             int max_seq, float* scratch, int* err, void* hi, void* lo, int ld16,
+                             cudaStream_t st);
 
 /* Tensor-core attention for f16 pools (head_dim 64 or 128, at most 8 query
  * heads per kv head).  The map is an opaque 128-byte CUtensorMap over the
