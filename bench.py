@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--layers", type=int, default=0,
                     help="reduce only for debugging; 0 = the config's (32 for 8b, 80 for 70b)")
+    ap.add_argument("--lanes", type=int, default=1, choices=[1, 2],
+                    help="2: the batch's halves as two lanes on two streams (see slate_cuda_opts_t)")
     ap.add_argument("--gemm-path", type=int, default=0,
                     help="0 auto (tcgen05 3-pass hi/lo split; stream-K kernel from 128 rows), 1 CUDA "
                          "cores, 2 tcgen05 single f16 pass, 3 3-pass tile-per-CTA kernel only, 4 "
@@ -304,7 +306,8 @@ def main():
     tp_id = tp_group_id(dist, world, tp, rank, sb.tp_unique_id) if tp > 1 else b""
     eng = sb.LlamaBatch(path, device=local, max_batch=n, max_slots=n, kv_dtype=kv,
                         max_seq=cfg["max_seq"], gemm_path=args.gemm_path,
-                        attn_path=args.attn_path, tp_size=tp, tp_rank=tp_rank, tp_id=tp_id)
+                        attn_path=args.attn_path, tp_size=tp, tp_rank=tp_rank, tp_id=tp_id,
+                        lanes=args.lanes)
     slots = np.array([eng.open() for _ in range(n)], np.int32)
     assert (slots >= 0).all(), sb.last_error()
     for s, c in zip(slots, ctx):
@@ -421,6 +424,7 @@ def main():
                                  5: "tcgen05 3-pass hi/lo, weights in TMEM, stream-K"}[args.gemm_path],
                    "attn_path": ("mma.sync f16 hi/lo" if args.attn_path == 0 and args.kv == "f16"
                                  else "cuda-core"),
+                   "lanes": args.lanes,
                    "l2": "inputs larger than L2 (KV read per step >> 126 MB)"},
         "roofline": {"bound": "hbm",
                      "kernel": ("attn_chunk_mma+attn_combine" if args.kv == "f16" and args.attn_path == 0

@@ -54,7 +54,7 @@ class CudaOpts(C.Structure):
                 ("kv_dtype", c_int), ("max_seq", c_int), ("kv_pages", c_int64),
                 ("kv_bytes", c_size), ("use_graphs", c_int), ("gemm_path", c_int),
                 ("attn_path", c_int), ("tp_size", c_int), ("tp_rank", c_int),
-                ("tp_id", C.c_ubyte * 128), ("q4k_order", c_int)]
+                ("tp_id", C.c_ubyte * 128), ("q4k_order", c_int), ("lanes", c_int)]
 
 
 class SamplerConfig(C.Structure):
@@ -198,10 +198,11 @@ class LlamaBatch:
 
     def __init__(self, gguf_path: str, *, device=0, max_batch=16, max_slots=0, kv_dtype=KV_F32,
                  max_seq=0, kv_pages=0, kv_bytes=0, use_graphs=True, gemm_path=0, attn_path=0,
-                 tp_size=0, tp_rank=0, tp_id=b"", q4k_order=0):
+                 tp_size=0, tp_rank=0, tp_id=b"", q4k_order=0, lanes=0):
         self.opts = CudaOpts(device, max_batch, max_slots, kv_dtype, max_seq, kv_pages, kv_bytes,
                              int(use_graphs), gemm_path, attn_path, tp_size, tp_rank)
         self.opts.q4k_order = q4k_order
+        self.opts.lanes = lanes
         if tp_id:
             C.memmove(self.opts.tp_id, bytes(tp_id), min(len(tp_id), 128))
         self.h = F["slate_llama_batch_new_gguf"](gguf_path.encode(), C.byref(self.opts))

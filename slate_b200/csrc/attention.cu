@@ -290,7 +290,7 @@ __global__ void prologue_kernel(const int32_t* __restrict__ slots, const int32_t
                                 int32_t* pos, int32_t* page_table, int max_pages,
                                 int32_t* free_stack, int32_t* free_top, int max_slots, int max_seq,
                                 int vocab, const float* __restrict__ emb, int D, float* x, int ldx,
-                                int32_t* row_pos, int32_t* row_slot, int32_t* status) {
+                                int32_t* row_pos, int32_t* row_slot, int32_t* status, int dup_ok) {
     __shared__ int s_ok, s_tok;
     const int b = blockIdx.x;
     if (threadIdx.x == 0) {
@@ -304,6 +304,7 @@ __global__ void prologue_kernel(const int32_t* __restrict__ slots, const int32_t
         int rank = 0;
         if (ok)
             for (int r = 0; r < b; ++r) rank += slots[r] == slot;
+        if (ok && rank && !dup_ok) { set_status(status, -1); ok = 0; }
         if (ok) {
             p = pos[slot] + rank;
             if (p >= max_seq) { set_status(status, -2); ok = 0; }
@@ -537,11 +538,11 @@ extern "C" int sb_step_prologue(const int32_t* slots, const int32_t* tokens, int
                                 int32_t* page_table, int max_pages, int32_t* free_stack,
                                 int32_t* free_top, int max_slots, int max_seq, int vocab,
                                 const float* emb, int D, float* x, int ldx, int32_t* row_pos,
-                                int32_t* row_slot, int32_t* status, cudaStream_t st) {
+                                int32_t* row_slot, int32_t* status, int dup_ok, cudaStream_t st) {
     if (B < 1) return -1;
     prologue_kernel<<<B, 256, 0, st>>>(slots, tokens, pos, page_table, max_pages, free_stack,
                                        free_top, max_slots, max_seq, vocab, emb, D, x, ldx,
-                                       row_pos, row_slot, status);
+                                       row_pos, row_slot, status, dup_ok);
     return 0;
 }
 extern "C" int sb_argmax_pairs(const float* logits, int ldl, int V, int B, int v0, void* pairs,

@@ -24,8 +24,9 @@
 //
 // Operand placement: the dequantised weights go register -> TMEM
 // (tcgen05.st; MMA with A in tensor memory), so shared memory holds only the
-// activation ring, deep enough (3 x 64 KB) to keep the TMA stream ahead of the
-// MMAs, and the tensor core reads only B from shared memory.
+// activation ring, deep enough (3 x 64 KB; 4 x 32 KB for operands of up to
+// 128 rows) to keep the TMA stream ahead of the MMAs, and the tensor core
+// reads only B from shared memory.
 //
 // Roles (512 threads): warps 0-7 dequantise (warp w, lane l: weight row
 // 32 (w % 4) + l, sub-block w / 4 of the K step's two; each thread copies the
@@ -52,16 +53,21 @@ constexpr int BM = 128;                 // weight rows per tile
 constexpr int BN = 256;                 // activation rows per tile (max MMA N)
 constexpr int BK = 64;                  // K per step (one 128-byte swizzle row of f16)
 constexpr int ASTAGES = 4;              // A stages in TMEM
-constexpr int BSTAGES = 3;              // x stages in shared memory
+constexpr int BSTAGES = 4;              // x stages in shared memory (at most; see sk_stages)
 constexpr int NPROD = 256;             // 8 producer warps: two per weight row, one sub-block each
 constexpr int MMA_WARP = 8, TMA_WARP = 9, DRAIN_WARP0 = 12;
 constexpr int NTHREADS = 512;
 constexpr uint32_t COL_A = 256;
-constexpr int B_PART = BN * 128;        // 32 KB: 256 rows x 64 f16
-constexpr int B_STAGE = 2 * B_PART;     // hi | lo
 constexpr int WSTAGES = 3;              // per-thread ring of Q4_K bytes (cp.async)
 constexpr int W_STAGE = 2 * NPROD * 16; // [header | nibbles][producer thread] x 16 B
-constexpr size_t SMEM = (size_t)BSTAGES * B_STAGE + (size_t)WSTAGES * W_STAGE + 1024;
+// x stages: 3 of 64 KB for 256-row operand boxes, 4 of 32 KB for boxes of up
+// to 128 rows -- the latter leave room on the SM for an attention CTA of the
+// other half of the batch.
+__host__ __device__ constexpr int sk_stages(int n_box) { return n_box <= 128 ? 4 : 3; }
+__host__ __device__ constexpr size_t sk_smem(int n_box) {
+    return (size_t)sk_stages(n_box) * 2 * n_box * 128 + (size_t)WSTAGES * W_STAGE + 1024;
+}
+constexpr size_t SMEM_MAX = sk_smem(BN);
 constexpr uint64_t WAIT_NS = 2000000000ull;
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -451,7 +457,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const SkArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* bst = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint4* wring = (uint4*)(bst + (size_t)BSTAGES * B_STAGE);     // [WSTAGES][2][NPROD]
+    const int nbs = sk_stages(a.n_box);
+    const size_t b_part = (size_t)a.n_box * 128, b_stage = 2 * b_part;   // hi | lo
+    uint4* wring = (uint4*)(bst + (size_t)nbs * b_stage);     // [WSTAGES][2][NPROD]
     __shared__ uint64_t a_full[ASTAGES], a_empty[ASTAGES], b_full[BSTAGES], b_empty[BSTAGES];
     __shared__ uint64_t acc_full, acc_empty, done_bar;
     __shared__ uint32_t tmem_slot;
@@ -467,7 +475,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             bar_init(&a_full[s], NPROD / 32);      // one arrival per producer warp
             bar_init(&a_empty[s], 1);
         }
-        for (int s = 0; s < BSTAGES; ++s) {
+        for (int s = 0; s < nbs; ++s) {
             bar_init(&b_full[s], 1);
             bar_init(&b_empty[s], 1);
         }
@@ -553,22 +561,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             while (sg.valid() && ok) {
                 const int n0 = (sg.t % a.NT) * BN;
                 for (int k = sg.ka; k < sg.kb; ++k, ++it) {
-                    const int s = (int)(it % BSTAGES);
-                    if (it >= BSTAGES &&
-                        !bar_wait(&b_empty[s], (uint32_t)(((it / BSTAGES) - 1) & 1), a.err, 32)) {
+                    const int s = (int)(it % nbs);
+                    if (it >= nbs &&
+                        !bar_wait(&b_empty[s], (uint32_t)(((it / nbs) - 1) & 1), a.err, 32)) {
                         ok = false;
                         break;
                     }
-                    unsigned char* st = bst + (size_t)s * B_STAGE;
+                    unsigned char* st = bst + (size_t)s * b_stage;
                     bar_expect(&b_full[s], bytes);
                     tma_2d(st, &xmap_hi, &b_full[s], k * BK, n0);
-                    tma_2d(st + B_PART, &xmap_lo, &b_full[s], k * BK, n0);
+                    tma_2d(st + b_part, &xmap_lo, &b_full[s], k * BK, n0);
                 }
                 sg.next();
             }
             // no copy may still be in flight when the CTA exits
-            for (long long i = it - BSTAGES > 0 ? it - BSTAGES : 0; i < it; ++i)
-                bar_wait_exit(&b_full[i % BSTAGES], (uint32_t)((i / BSTAGES) & 1), a.err);
+            for (long long i = it - nbs > 0 ? it - nbs : 0; i < it; ++i)
+                bar_wait_exit(&b_full[i % nbs], (uint32_t)((i / nbs) & 1), a.err);
         }
     } else if (warp == MMA_WARP) {
         // ---------------- MMA issue ----------------
@@ -588,14 +596,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 tc_fence_after();
                 for (int k = sg.ka; k < sg.kb; ++k, ++it) {
-                    const int sa = (int)(it % ASTAGES), sb = (int)(it % BSTAGES);
+                    const int sa = (int)(it % ASTAGES), sb = (int)(it % nbs);
                     if (!bar_wait(&a_full[sa], (uint32_t)((it / ASTAGES) & 1), a.err, 34) ||
-                        !bar_wait(&b_full[sb], (uint32_t)((it / BSTAGES) & 1), a.err, 35)) {
+                        !bar_wait(&b_full[sb], (uint32_t)((it / nbs) & 1), a.err, 35)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t bh = su32(bst + (size_t)sb * B_STAGE), bl = bh + B_PART;
+                    const uint32_t bh = su32(bst + (size_t)sb * b_stage), bl = bh + (uint32_t)b_part;
                     const uint32_t ah = tmem + COL_A + (uint32_t)(64 * sa), al = ah + 32;
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
@@ -698,7 +706,7 @@ extern "C" int sb_sk_kernels(int M_pad, int K, int n_rows, int epi) {
 }
 
 extern "C" void sb_sk_prepare(void) {
-    cudaFuncSetAttribute(sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+    cudaFuncSetAttribute(sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_MAX);
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess)
         cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
@@ -735,7 +743,7 @@ extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows
     // the output pass: every SiLU tile; shared tiles exist only when some CTA
     // boundary falls inside a tile
     const bool pass = sk_plan(W->M_pad, W->K, n_rows, epi, &C, &U);
-    sk_kernel<<<C, NTHREADS, SMEM, st>>>(*(const CUtensorMap*)X->map_hi,
+    sk_kernel<<<C, NTHREADS, sk_smem(X->n_box), st>>>(*(const CUtensorMap*)X->map_hi,
                                          *(const CUtensorMap*)X->map_lo, a);
     if (pass && epi == SB_EPI_SILU)
         sk_silu_out_kernel<<<dim3((unsigned)(MT * a.NT), 4u), ST, 0, st>>>(a, C, U);

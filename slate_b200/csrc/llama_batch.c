@@ -36,9 +36,29 @@ typedef struct sb_layer {
     sb_matrix wqkv, wo, wgu, wdown;
 } sb_layer;
 
+/* A lane runs the layers of a step for a contiguous range of the batch's rows.
+ * A step runs one lane over all rows, or two lanes over the two halves on two
+ * streams (independent chains: different sequences), so that one half's
+ * attention, bound by HBM, runs beside the other half's projections, bound by
+ * the tensor cores. */
+typedef struct sb_lane {
+    sb_tc_operand own[3];          /* half lanes: operands over the half's rows */
+    const sb_tc_operand *op_d, *op_f, *op_a;   /* GEMM operands (K = D, F, Dq) */
+    float* sk_ws;                  /* stream-K workspace of this lane */
+    int r0;                        /* first row */
+    int xn_split, att_split;       /* enqueue time: the RMSNorm / attention wrote
+                                      the f16 operand of the GEMM that follows */
+} sb_lane;
+
+/* Input of a step GEMM (which producer may already have written its f16 pair). */
+enum { IN_XN, IN_ATT, IN_H, IN_OTHER };
+
 struct slate_llama_batch {
     int device;
     cudaStream_t stream;
+    cudaStream_t stream2;          /* second lane */
+    cudaEvent_t ev_fork, ev_join;
+    cudaEvent_t ev_a, ev_b;        /* lane order: a lane's attention of a layer done */
     pthread_mutex_t lock;
     /* model */
     int L, D, F, nq, nkv, hd, V, kvd, qkv_dim, max_seq;
@@ -90,11 +110,9 @@ struct slate_llama_batch {
     /* three-pass stream-K GEMM (gemm_sk.cu): workspace; sk_h: the gate/up
      * GEMM writes its SiLU output also as the down GEMM's f16 hi / lo operand */
     int sk_on, sk_h, sk_min;       /* sk_min: rows from which a GEMM uses it */
-    /* xn_split: the RMSNorm of the step being enqueued also wrote its rows as
-     * op_d's f16 hi / lo pair, so the GEMMs that read xn skip their split */
-    int xn_split;
-    int att_split;                 /* the same for the attention output (op_a) */
     float* sk_ws;
+    sb_lane full, half[2];         /* the whole batch; the two halves (dual) */
+    int dual, half_rows;           /* dual: steps of > half_rows rows use two lanes */
     /* tensor parallelism: nq, nkv, F above are this rank's shares, V the full
      * vocabulary of which the LM head holds rows [v0, v0 + V_l) */
     int tp, rank, V_l, v0, Dq;     /* Dq = nq * hd (local) */
@@ -109,6 +127,7 @@ struct slate_llama_batch {
     sb_sampler* h_samp;
     uint64_t* h_rng;
     cudaGraphExec_t* graphs_s;
+    cudaGraphExec_t* graphs_c;     /* prompt-chunk steps (repeated slots), per n */
 };
 
 /* Rows from which a Q4_K GEMM runs on the tensor cores (below: CUDA cores). */
@@ -120,33 +139,45 @@ struct slate_llama_batch {
 /* Whether the RMSNorm before a GEMM writes the tensor cores' f16 operand too
  * (the 3- or 1-pass split paths; the exact-weight path splits with sub-block
  * sums of its own). */
-static int norm_splits(const slate_llama_batch_t* b, int n) {
-    return b->tc_passes && !b->q4_on && n >= SB_TC_MIN_ROWS && n <= b->op_d.rows &&
-           b->D % 4 == 0 && b->D <= 8192 && b->ld_x % 4 == 0 && b->op_d.ld16 % 4 == 0;
+static int norm_splits(const slate_llama_batch_t* b, const sb_lane* L, int n) {
+    return b->tc_passes && !b->q4_on && n >= SB_TC_MIN_ROWS && n <= L->op_d->rows &&
+           b->D % 4 == 0 && b->D <= 8192 && b->ld_x % 4 == 0 && L->op_d->ld16 % 4 == 0;
 }
 
-/* RMSNorm of x into xn (and, where the GEMMs take it, into op_d's f16 pair). */
-static int step_norm(slate_llama_batch_t* b, const float* w, int n, cudaStream_t s) {
-    b->xn_split = 0;
-    if (norm_splits(b, n) &&
-        sb_rmsnorm_rows_split(b->xn, b->ld_x, b->x, b->ld_x, w, n, b->D, b->eps, b->op_d.hi,
-                              b->op_d.lo, b->op_d.ld16, s) == 0) {
-        b->xn_split = 1;
+/* RMSNorm of the lane's rows of x into xn (and, where the GEMMs take it, into
+ * the lane's f16 operand). */
+static int step_norm(slate_llama_batch_t* b, sb_lane* L, const float* w, int n, cudaStream_t s) {
+    const size_t ro = (size_t)L->r0 * b->ld_x;
+    L->xn_split = 0;
+    if (norm_splits(b, L, n) &&
+        sb_rmsnorm_rows_split(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps,
+                              L->op_d->hi, L->op_d->lo, L->op_d->ld16, s) == 0) {
+        L->xn_split = 1;
         return 0;
     }
-    return sb_rmsnorm_rows(b->xn, b->ld_x, b->x, b->ld_x, w, n, b->D, b->eps, s);
+    return sb_rmsnorm_rows(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps, s);
 }
 
-/* One weight GEMM of the step on the path chosen for (weight, rows). */
-static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X, int ldx, int n,
-                     float* Y, int ldy, int epi, int splits, cudaStream_t s) {
-    /* op_d (op_a) already holds xn (att) as the f16 pair: RMSNorm (the
+/* Whether a GEMM of this lane runs on the stream-K kernel. */
+static int uses_sk(const slate_llama_batch_t* b, const sb_lane* L, const sb_matrix* W, int n,
+                   int epi) {
+    return b->sk_on && W->wtype == SB_WT_Q4K && W->M_pad % 128 == 0 &&
+           (epi != SB_EPI_SILU || W->M % 128 == 0) &&
+           (n >= b->sk_min || (L != &b->full && n >= SB_TC_MIN_ROWS));
+}
+
+/* One weight GEMM of the step on the path chosen for (weight, rows); X and Y
+ * point at the lane's first row, in names the input (IN_*). */
+static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, const float* X,
+                     int ldx, int in, int n, float* Y, int ldy, int epi, int splits,
+                     cudaStream_t s) {
+    /* the lane's operand already holds xn (att) as the f16 pair: RMSNorm (the
      * attention) wrote it */
-    const int have_d = X == b->xn && b->xn_split;
-    const int have_a = X == b->att && b->att_split;
+    const int have_d = in == IN_XN && L->xn_split;
+    const int have_a = in == IN_ATT && L->att_split;
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) {
-        int rc = have_d ? 0 : sb_tc_split(X, ldx, n, &b->op_d, s);
-        return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, &b->op_d, n, Y, ldy, epi, b->tc_err, s);
+        int rc = have_d ? 0 : sb_tc_split(X, ldx, n, L->op_d, s);
+        return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, L->op_d, n, Y, ldy, epi, b->tc_err, s);
     }
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
         const sb_q4_operand* op = W->K == b->q4_d.K ? &b->q4_d
@@ -154,24 +185,17 @@ static int step_gemm(slate_llama_batch_t* b, const sb_matrix* W, const float* X,
         int rc = sb_q4_split(X, ldx, n, op, s);
         return rc ? rc : sb_q4_gemm(W, op, n, Y, ldy, epi, b->q4_ws, b->q4_cnt, b->tc_err, s);
     }
-    if (b->sk_on && W->wtype == SB_WT_Q4K && n >= b->sk_min && W->M_pad % 128 == 0 &&
-        (epi != SB_EPI_SILU || W->M % 128 == 0)) {
-        const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
-                                  : W->K == b->op_f.K ? &b->op_f : &b->op_a;
+    const sb_tc_operand* op = W->K == L->op_d->K ? L->op_d : W->K == L->op_f->K ? L->op_f : L->op_a;
+    const int pre = (have_d && op->hi == L->op_d->hi) || (have_a && op->hi == L->op_a->hi);
+    if (uses_sk(b, L, W, n, epi)) {
         /* the down GEMM's operand was written by the gate/up GEMM */
-        int rc = (X == b->h && b->sk_h) || (have_d && op == &b->op_d) || (have_a && op == &b->op_a)
-                     ? 0
-                     : sb_tc_split(X, ldx, n, op, s);
-        const int fuse = epi == SB_EPI_SILU && b->sk_h && Y == b->h;
-        return rc ? rc : sb_sk_gemm(W, op, n, b->sk_ws, Y, ldy, epi, fuse ? b->op_f.hi : NULL,
-                                    fuse ? b->op_f.lo : NULL, b->op_f.ld16, b->tc_err, s);
+        int rc = (in == IN_H && b->sk_h) || pre ? 0 : sb_tc_split(X, ldx, n, op, s);
+        const int fuse = epi == SB_EPI_SILU && b->sk_h;
+        return rc ? rc : sb_sk_gemm(W, op, n, L->sk_ws, Y, ldy, epi, fuse ? L->op_f->hi : NULL,
+                                    fuse ? L->op_f->lo : NULL, L->op_f->ld16, b->tc_err, s);
     }
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
-        const sb_tc_operand* op = W->K == b->op_d.K ? &b->op_d
-                                  : W->K == b->op_f.K ? &b->op_f : &b->op_a;
-        int rc = (have_d && op == &b->op_d) || (have_a && op == &b->op_a)
-                     ? 0
-                     : sb_tc_split(X, ldx, n, op, s);
+        int rc = pre ? 0 : sb_tc_split(X, ldx, n, op, s);
         return rc ? rc : sb_tc_gemm(W, op, n, b->tc_passes, splits, b->tc_ws, Y, ldy, epi,
                                     b->tc_err, s);
     }
@@ -330,7 +354,96 @@ static int upload_f32(slate_llama_batch_t* b, float** dst, const void* src, size
 
 /* ---- step enqueue ------------------------------------------------------- */
 
-static int enqueue_step(slate_llama_batch_t* b, int n, int sample, cudaStream_t s) {
+/* Layer l of a step for the lane's n rows (rows r0 .. r0 + n - 1), in three
+ * parts: 0 = RMSNorm, QKV projection, RoPE + KV append; 1 = attention; 2 = Wo
+ * (+ residual), RMSNorm, gate/up (SiLU), down (+ residual). */
+static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int n, cudaStream_t s) {
+    int rc = 0;
+    /* Wo and down add into the residual stream; tensor parallel ranks hold
+     * partial sums that are all-reduced into it, with rank 0 alone adding the
+     * residual itself */
+    const int res_epi = b->tp > 1 && b->rank != 0 ? SB_EPI_STORE : SB_EPI_ADD;
+    const int r0 = L->r0;
+    float* x = b->x + (size_t)r0 * b->ld_x;
+    float* xn = b->xn + (size_t)r0 * b->ld_x;
+    float* qkv = b->qkv + (size_t)r0 * b->ld_qkv;
+    float* att = b->att + (size_t)r0 * b->ld_att;
+    float* h = b->h + (size_t)r0 * b->ld_h;
+    const int32_t* row_pos = b->row_pos + r0;
+    const int32_t* row_slot = b->row_slot + r0;
+    const sb_layer* ly = &b->layers[l];
+    if (part == 0) {
+        rc |= step_norm(b, L, ly->attn_norm, n, s);
+        rc |= step_gemm(b, L, &ly->wqkv, xn, b->ld_x, IN_XN, n, qkv, b->ld_qkv, SB_EPI_STORE,
+                        b->sp_qkv, s);
+        rc |= sb_rope_append(qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, row_pos, row_slot,
+                             b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
+                             b->rope_cos, b->rope_sin, s);
+    } else if (part == 1) {
+        float* scratch = b->scratch + sb_attention_scratch_floats(r0, b->nq, b->hd, b->max_seq);
+        L->att_split = norm_splits(b, L, n) && L->op_a->ld16 >= b->Dq;
+        if (L->att_split)
+            rc |= sb_attention_paged_split(att, b->ld_att, qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
+                                           row_pos, row_slot, b->page_table, b->max_pages, b->pool,
+                                           b->kvmap_p, b->n_pages, l, b->kv_dtype, b->max_seq,
+                                           scratch, b->tc_err, L->op_a->hi, L->op_a->lo,
+                                           L->op_a->ld16, s);
+        else
+            rc |= sb_attention_paged(att, b->ld_att, qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, row_pos,
+                                     row_slot, b->page_table, b->max_pages, b->pool, b->kvmap_p,
+                                     b->n_pages, l, b->kv_dtype, b->max_seq, scratch, b->tc_err, s);
+    } else {
+        rc |= step_gemm(b, L, &ly->wo, att, b->ld_att, IN_ATT, n, x, b->ld_x, res_epi, b->sp_wo, s);
+        if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, x, (size_t)n * b->ld_x, s);
+        rc |= step_norm(b, L, ly->ffn_norm, n, s);
+        rc |= step_gemm(b, L, &ly->wgu, xn, b->ld_x, IN_XN, n, h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
+        rc |= step_gemm(b, L, &ly->wdown, h, b->ld_h, IN_H, n, x, b->ld_x, res_epi, b->sp_dn, s);
+        if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, x, (size_t)n * b->ld_x, s);
+    }
+    return rc;
+}
+
+/* All layers of a step for one lane. */
+static int enqueue_layers(slate_llama_batch_t* b, sb_lane* L, int n, cudaStream_t s) {
+    int rc = 0;
+    for (int l = 0; l < b->L && !rc; ++l)
+        for (int part = 0; part < 3 && !rc; ++part) rc |= enqueue_part(b, L, l, part, n, s);
+    return rc;
+}
+
+/* Two lanes, interleaved: the halves' attentions take turns (A's layer l,
+ * then B's layer l, then A's layer l + 1, ...), so each runs beside the other
+ * half's projections instead of beside the other attention. */
+static int enqueue_lanes(slate_llama_batch_t* b, int n, cudaStream_t s) {
+    sb_lane* A = &b->half[0];
+    sb_lane* Bl = &b->half[1];
+    const int na = b->half_rows, nb = n - b->half_rows;
+    cudaStream_t s2 = b->stream2;
+    int rc = sb_cuda_check(cudaEventRecord(b->ev_fork, s), "fork");
+    rc |= sb_cuda_check(cudaStreamWaitEvent(s2, b->ev_fork, 0), "fork");
+    for (int l = 0; l < b->L && !rc; ++l) {
+        rc |= enqueue_part(b, A, l, 0, na, s);
+        if (l > 0) rc |= sb_cuda_check(cudaStreamWaitEvent(s, b->ev_b, 0), "lane order");
+        rc |= enqueue_part(b, A, l, 1, na, s);
+        rc |= sb_cuda_check(cudaEventRecord(b->ev_a, s), "lane order");
+        rc |= enqueue_part(b, A, l, 2, na, s);
+        rc |= enqueue_part(b, Bl, l, 0, nb, s2);
+        rc |= sb_cuda_check(cudaStreamWaitEvent(s2, b->ev_a, 0), "lane order");
+        rc |= enqueue_part(b, Bl, l, 1, nb, s2);
+        rc |= sb_cuda_check(cudaEventRecord(b->ev_b, s2), "lane order");
+        rc |= enqueue_part(b, Bl, l, 2, nb, s2);
+    }
+    rc |= sb_cuda_check(cudaEventRecord(b->ev_join, s2), "join");
+    rc |= sb_cuda_check(cudaStreamWaitEvent(s, b->ev_join, 0), "join");
+    return rc;
+}
+
+/* Whether a step of n rows runs as two lanes. */
+static int step_dual(const slate_llama_batch_t* b, int n) {
+    return b->dual && n > b->half_rows;
+}
+
+static int enqueue_step(slate_llama_batch_t* b, int n, int sample, int chunk, cudaStream_t s) {
     int rc = 0;
     /* cudaGetLastError() below must only see this step's launches: a failure
      * left by an earlier unchecked call on this thread is cleared here (a
@@ -339,41 +452,18 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, cudaStream_t 
     const int32_t* slots = b->d_io;
     const int32_t* toks = b->d_io + b->max_batch;
     int32_t* out = b->d_io + 2 * b->max_batch;
-    /* Wo and down add into the residual stream; tensor parallel ranks hold
-     * partial sums that are all-reduced into it, with rank 0 alone adding the
-     * residual itself */
-    const int res_epi = b->tp > 1 && b->rank != 0 ? SB_EPI_STORE : SB_EPI_ADD;
     rc |= sb_step_prologue(slots, toks, n, b->pos, b->page_table, b->max_pages, b->free_stack,
                            b->free_top, b->max_slots, b->max_seq, b->V, b->emb, b->D, b->x,
-                           b->ld_x, b->row_pos, b->row_slot, b->status, s);
-    for (int l = 0; l < b->L && !rc; ++l) {
-        const sb_layer* ly = &b->layers[l];
-        rc |= step_norm(b, ly->attn_norm, n, s);
-        rc |= step_gemm(b, &ly->wqkv, b->xn, b->ld_x, n, b->qkv, b->ld_qkv, SB_EPI_STORE, b->sp_qkv, s);
-        rc |= sb_rope_append(b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, b->row_pos, b->row_slot,
-                             b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
-                             b->rope_cos, b->rope_sin, s);
-        b->att_split = norm_splits(b, n) && b->op_a.ld16 >= b->Dq;
-        if (b->att_split)
-            rc |= sb_attention_paged_split(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv,
-                                           b->hd, b->row_pos, b->row_slot, b->page_table,
-                                           b->max_pages, b->pool, b->kvmap_p, b->n_pages, l,
-                                           b->kv_dtype, b->max_seq, b->scratch, b->tc_err,
-                                           b->op_a.hi, b->op_a.lo, b->op_a.ld16, s);
-        else
-            rc |= sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
-                                     b->row_pos, b->row_slot, b->page_table, b->max_pages, b->pool,
-                                     b->kvmap_p, b->n_pages, l, b->kv_dtype, b->max_seq, b->scratch,
-                                     b->tc_err, s);
-        rc |= step_gemm(b, &ly->wo, b->att, b->ld_att, n, b->x, b->ld_x, res_epi, b->sp_wo, s);
-        if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, b->x, (size_t)n * b->ld_x, s);
-        rc |= step_norm(b, ly->ffn_norm, n, s);
-        rc |= step_gemm(b, &ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
-        rc |= step_gemm(b, &ly->wdown, b->h, b->ld_h, n, b->x, b->ld_x, res_epi, b->sp_dn, s);
-        if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, b->x, (size_t)n * b->ld_x, s);
+                           b->ld_x, b->row_pos, b->row_slot, b->status, chunk, s);
+    if (!chunk && step_dual(b, n)) {
+        /* rows [0, half_rows) on this stream, [half_rows, n) on the second */
+        rc |= enqueue_lanes(b, n, s);
+    } else {
+        rc |= enqueue_layers(b, &b->full, n, s);
     }
-    rc |= step_norm(b, b->out_norm, n, s);
-    rc |= step_gemm(b, &b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE, 1, s);
+    rc |= step_norm(b, &b->full, b->out_norm, n, s);
+    rc |= step_gemm(b, &b->full, &b->lm_head, b->xn, b->ld_x, IN_XN, n, b->logits, b->ld_logits,
+                    SB_EPI_STORE, 1, s);
     if (sample) {
         rc |= sb_sample_rows(b->logits, b->ld_logits, b->V, n, b->d_samp, b->d_rng, b->samp_scratch,
                              out, b->row_slot, b->row_pos, b->pos, b->status, b->tc_err, s);
@@ -393,17 +483,16 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, cudaStream_t 
     return sb_cuda_check(cudaGetLastError(), "step launch");
 }
 
-/* Kernel launches step_gemm makes for (W, n rows, epilogue, splits); pre:
- * the GEMM's input comes from a kernel that can write its f16 split (RMSNorm,
- * attention). */
-static int gemm_launches(const slate_llama_batch_t* b, const sb_matrix* W, int n, int epi,
-                         int splits, int pre) {
-    const int split = pre && norm_splits(b, n) ? 0 : 1;
+/* Kernel launches step_gemm makes for (lane, W, n rows, epilogue, splits);
+ * pre: the GEMM's input comes from a kernel that can write its f16 split
+ * (RMSNorm, attention). */
+static int gemm_launches(const slate_llama_batch_t* b, const sb_lane* L, const sb_matrix* W, int n,
+                         int epi, int splits, int pre) {
+    const int split = pre && norm_splits(b, L, n) ? 0 : 1;
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return split + 1;
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2;                                                               /* split + GEMM */
-    if (b->sk_on && W->wtype == SB_WT_Q4K && n >= b->sk_min && W->M_pad % 128 == 0 &&
-        (epi != SB_EPI_SILU || W->M % 128 == 0))
+    if (uses_sk(b, L, W, n, epi))
         return (W == &b->layers[0].wdown && b->sk_h ? 0 : split) +   /* split (down: fused) */
                sb_sk_kernels(W->M_pad, W->K, n, epi);              /* GEMM (+ output pass) */
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
@@ -411,29 +500,39 @@ static int gemm_launches(const slate_llama_batch_t* b, const sb_matrix* W, int n
     return 1;
 }
 
-int slate_llama_batch_launches_per_step(const slate_llama_batch_t* b, int n) {
-    if (!b || n < 1) return 0;
+/* Kernel launches of one lane's layers for n rows. */
+static int layer_launches(const slate_llama_batch_t* b, const sb_lane* L, int n) {
     const sb_layer* l0 = &b->layers[0];
     const int res_epi = b->tp > 1 && b->rank != 0 ? SB_EPI_STORE : SB_EPI_ADD;
-    const int per_layer = 2 /* rmsnorm x2 */ + 1 /* rope + append */ + 2 /* attention */ +
-                          gemm_launches(b, &l0->wqkv, n, SB_EPI_STORE, b->sp_qkv, 1) +
-                          gemm_launches(b, &l0->wo, n, res_epi, b->sp_wo, b->op_a.ld16 >= b->Dq) +
-                          gemm_launches(b, &l0->wgu, n, SB_EPI_SILU, b->sp_gu, 1) +
-                          gemm_launches(b, &l0->wdown, n, res_epi, b->sp_dn, 0);
-    return 1 /* prologue */ + b->L * per_layer + 1 /* final rmsnorm */ +
-           gemm_launches(b, &b->lm_head, n, SB_EPI_STORE, 1, 1) + (b->tp > 1 ? 2 : 1);
+    const int per_layer =
+        2 /* rmsnorm x2 */ + 1 /* rope + append */ + 2 /* attention */ +
+        gemm_launches(b, L, &l0->wqkv, n, SB_EPI_STORE, b->sp_qkv, 1) +
+        gemm_launches(b, L, &l0->wo, n, res_epi, b->sp_wo, L->op_a->ld16 >= b->Dq) +
+        gemm_launches(b, L, &l0->wgu, n, SB_EPI_SILU, b->sp_gu, 1) +
+        gemm_launches(b, L, &l0->wdown, n, res_epi, b->sp_dn, 0);
+    return b->L * per_layer;
 }
 
-/* Runs the step for n rows whose metadata is already in d_io. */
+int slate_llama_batch_launches_per_step(const slate_llama_batch_t* b, int n) {
+    if (!b || n < 1) return 0;
+    const int layers = step_dual(b, n) ? layer_launches(b, &b->half[0], b->half_rows) +
+                                             layer_launches(b, &b->half[1], n - b->half_rows)
+                                       : layer_launches(b, &b->full, n);
+    return 1 /* prologue */ + layers + 1 /* final rmsnorm */ +
+           gemm_launches(b, &b->full, &b->lm_head, n, SB_EPI_STORE, 1, 1) + (b->tp > 1 ? 2 : 1);
+}
+
 /* Runs the step for n rows whose metadata is already in d_io; sample != 0
- * ends it with the stochastic sampler instead of the greedy argmax. */
-static int run_step_mode(slate_llama_batch_t* b, int n, int sample) {
-    if (!b->use_graphs) return enqueue_step(b, n, sample, b->stream);
-    cudaGraphExec_t* slot = sample ? &b->graphs_s[n] : &b->graphs[n];
+ * ends it with the stochastic sampler instead of the greedy argmax; chunk != 0
+ * lets a slot occur several times (a prompt chunk, one lane), otherwise a
+ * repeated slot is rejected (status -1) and the rows may run as two lanes. */
+static int run_step_mode(slate_llama_batch_t* b, int n, int sample, int chunk) {
+    if (!b->use_graphs) return enqueue_step(b, n, sample, chunk, b->stream);
+    cudaGraphExec_t* slot = chunk ? &b->graphs_c[n] : sample ? &b->graphs_s[n] : &b->graphs[n];
     if (!*slot) {
         cudaGraph_t g = NULL;
         SB_CU(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
-        int rc = enqueue_step(b, n, sample, b->stream);
+        int rc = enqueue_step(b, n, sample, chunk, b->stream);
         cudaError_t e = cudaStreamEndCapture(b->stream, &g);
         if (rc) {
             if (g) cudaGraphDestroy(g);
@@ -447,7 +546,7 @@ static int run_step_mode(slate_llama_batch_t* b, int n, int sample) {
     SB_CU(cudaGraphLaunch(*slot, b->stream));
     return 0;
 }
-static int run_step(slate_llama_batch_t* b, int n) { return run_step_mode(b, n, 0); }
+static int run_step(slate_llama_batch_t* b, int n) { return run_step_mode(b, n, 0, 0); }
 
 /* ---- construction ------------------------------------------------------- */
 
@@ -455,6 +554,7 @@ void slate_llama_batch_free(slate_llama_batch_t* b) {
     if (!b) return;
     cudaSetDevice(b->device);
     if (b->stream) cudaStreamSynchronize(b->stream);
+    if (b->stream2) cudaStreamSynchronize(b->stream2);
     if (b->graphs) {
         for (int i = 0; i <= b->max_batch; ++i)
             if (b->graphs[i]) cudaGraphExecDestroy(b->graphs[i]);
@@ -465,6 +565,11 @@ void slate_llama_batch_free(slate_llama_batch_t* b) {
             if (b->graphs_s[i]) cudaGraphExecDestroy(b->graphs_s[i]);
         free(b->graphs_s);
     }
+    if (b->graphs_c) {
+        for (int i = 0; i <= b->max_batch; ++i)
+            if (b->graphs_c[i]) cudaGraphExecDestroy(b->graphs_c[i]);
+        free(b->graphs_c);
+    }
     if (b->h_samp) cudaFreeHost(b->h_samp);
     if (b->h_rng) cudaFreeHost(b->h_rng);
     sb_tc_free_weight(&b->head_tc);
@@ -473,6 +578,11 @@ void slate_llama_batch_free(slate_llama_batch_t* b) {
     free(b->allocs);
     if (b->h_io) cudaFreeHost(b->h_io);
     if (b->stream) cudaStreamDestroy(b->stream);
+    if (b->stream2) cudaStreamDestroy(b->stream2);
+    if (b->ev_fork) cudaEventDestroy(b->ev_fork);
+    if (b->ev_join) cudaEventDestroy(b->ev_join);
+    if (b->ev_a) cudaEventDestroy(b->ev_a);
+    if (b->ev_b) cudaEventDestroy(b->ev_b);
     free(b->layers);
     free(b->h_pos);
     free(b->h_open);
@@ -518,7 +628,14 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
             return NULL;
         }
     }
-    slate_llama_batch_t* b = (slate_llama_batch_t*)calloc(1, sizeof(*b));
+    /* the struct holds TMA descriptors, which must be 64-byte aligned */
+    const size_t bsize = (sizeof(slate_llama_batch_t) + 63) / 64 * 64;
+    slate_llama_batch_t* b = (slate_llama_batch_t*)aligned_alloc(64, bsize);
+    if (!b) {
+        sb_set_error("out of host memory");
+        return NULL;
+    }
+    memset(b, 0, bsize);
     pthread_mutex_init(&b->lock, NULL);
     b->device = o->device;
     b->tp = tp;
@@ -757,6 +874,45 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         }
     }
 
+    /* lanes: the whole batch, and (one GPU, stream-K GEMMs) the two halves,
+     * whose operands view the same f16 buffers from their first row on */
+    b->full.op_d = &b->op_d;
+    b->full.op_f = &b->op_f;
+    b->full.op_a = &b->op_a;
+    b->full.sk_ws = b->sk_ws;
+    b->full.r0 = 0;
+    b->half_rows = b->max_batch / 2;
+    if (b->sk_on && b->tp == 1 && !b->q4_on && o->lanes == 2 && b->half_rows >= SB_TC_MIN_ROWS) {
+        const sb_tc_operand* fo[3] = {&b->op_d, &b->op_f, &b->op_a};
+        for (int hh = 0; hh < 2; ++hh) {
+            sb_lane* L = &b->half[hh];
+            L->r0 = hh ? b->half_rows : 0;
+            const int rows = hh ? b->max_batch - b->half_rows : b->half_rows;
+            for (int i = 0; i < 3; ++i) {
+                if (i == 2 && fo[2]->hi == fo[0]->hi) break;      /* op_a shares op_d */
+                const size_t off = (size_t)L->r0 * fo[i]->ld16 * 2;
+                if (sb_tc_make_operand(&L->own[i], (char*)fo[i]->hi + off,
+                                       fo[i]->lo ? (char*)fo[i]->lo + off : NULL, rows, fo[i]->K,
+                                       fo[i]->ld16))
+                    goto fail;
+            }
+            L->op_d = &L->own[0];
+            L->op_f = &L->own[1];
+            L->op_a = fo[2]->hi == fo[0]->hi ? &L->own[0] : &L->own[2];
+            L->sk_ws = hh ? (float*)dalloc(b, sb_sk_ws_floats(sb_sk_tiles(b->layers[0].wgu.M_pad,
+                                                                          rows)) * 4)
+                          : b->sk_ws;
+            if (!L->sk_ws) goto fail;
+        }
+        if (sb_cuda_check(cudaStreamCreateWithFlags(&b->stream2, cudaStreamNonBlocking), "stream") ||
+            sb_cuda_check(cudaEventCreateWithFlags(&b->ev_fork, cudaEventDisableTiming), "event") ||
+            sb_cuda_check(cudaEventCreateWithFlags(&b->ev_join, cudaEventDisableTiming), "event") ||
+            sb_cuda_check(cudaEventCreateWithFlags(&b->ev_a, cudaEventDisableTiming), "event") ||
+            sb_cuda_check(cudaEventCreateWithFlags(&b->ev_b, cudaEventDisableTiming), "event"))
+            goto fail;
+        b->dual = 1;
+    }
+
     /* KV pool, page tables, free list */
     {
         const size_t esz = b->kv_dtype == SLATE_KV_F16 ? 2 : 4;
@@ -798,6 +954,11 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
     b->h_pos = (int*)calloc((size_t)b->max_slots, sizeof(int));
     b->h_open = (unsigned char*)calloc((size_t)b->max_slots, 1);
     b->graphs = (cudaGraphExec_t*)calloc((size_t)b->max_batch + 1, sizeof(cudaGraphExec_t));
+    b->graphs_c = (cudaGraphExec_t*)calloc((size_t)b->max_batch + 1, sizeof(cudaGraphExec_t));
+    if (!b->graphs || !b->graphs_c) {
+        sb_set_error("out of host memory");
+        goto fail;
+    }
     if (sb_cuda_check(cudaStreamSynchronize(b->stream), "init sync")) goto fail;
     return b;
 fail:
@@ -978,7 +1139,7 @@ static int step_host(slate_llama_batch_t* b, const int32_t* slots, int n, const 
     memcpy(h + b->max_batch, tokens, (size_t)n * 4);
     rc = sb_cuda_check(cudaMemcpyAsync(b->d_io, h, (size_t)2 * b->max_batch * 4,
                                        cudaMemcpyHostToDevice, b->stream), "H2D metadata");
-    if (!rc) rc = run_step(b, n);
+    if (!rc) rc = run_step_mode(b, n, 0, allow_dup);
     if (!rc)
         rc = sb_cuda_check(cudaMemcpyAsync(h + 2 * b->max_batch, b->d_io + 2 * b->max_batch,
                                            (size_t)n * 4, cudaMemcpyDeviceToHost, b->stream),
@@ -1075,7 +1236,7 @@ int slate_llama_batch_step_sample(slate_llama_batch_t* b, const int32_t* slots, 
                                                 cudaMemcpyHostToDevice, b->stream), "H2D sampler");
     if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(b->d_rng, b->h_rng, (size_t)n * 8,
                                                 cudaMemcpyHostToDevice, b->stream), "H2D rng");
-    if (!rc) rc = run_step_mode(b, n, 1);
+    if (!rc) rc = run_step_mode(b, n, 1, 0);
     if (!rc)
         rc = sb_cuda_check(cudaMemcpyAsync(h + 2 * b->max_batch, b->d_io + 2 * b->max_batch,
                                            (size_t)n * 4, cudaMemcpyDeviceToHost, b->stream),
@@ -1228,19 +1389,20 @@ static int enqueue_kernel(slate_llama_batch_t* b, int kernel, int n, int layer, 
                                       b->pool, b->kvmap_p, b->n_pages, layer, b->kv_dtype,
                                       b->max_seq, b->scratch, b->tc_err, s);
         case SLATE_PROF_QKV:
-            return step_gemm(b, &ly->wqkv, b->xn, b->ld_x, n, scratch_y, b->ld_logits, SB_EPI_STORE,
-                             b->sp_qkv, s);
+            return step_gemm(b, &b->full, &ly->wqkv, b->xn, b->ld_x, IN_XN, n, scratch_y,
+                             b->ld_logits, SB_EPI_STORE, b->sp_qkv, s);
         case SLATE_PROF_WO:
-            return step_gemm(b, &ly->wo, b->att, b->ld_att, n, scratch_y, b->ld_logits, SB_EPI_STORE,
-                             b->sp_wo, s);
+            return step_gemm(b, &b->full, &ly->wo, b->att, b->ld_att, IN_ATT, n, scratch_y,
+                             b->ld_logits, SB_EPI_STORE, b->sp_wo, s);
         case SLATE_PROF_GATE_UP:
-            return step_gemm(b, &ly->wgu, b->xn, b->ld_x, n, b->h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
+            return step_gemm(b, &b->full, &ly->wgu, b->xn, b->ld_x, IN_XN, n, b->h, b->ld_h,
+                             SB_EPI_SILU, b->sp_gu, s);
         case SLATE_PROF_DOWN:
-            return step_gemm(b, &ly->wdown, b->h, b->ld_h, n, scratch_y, b->ld_logits, SB_EPI_STORE,
-                             b->sp_dn, s);
+            return step_gemm(b, &b->full, &ly->wdown, b->h, b->ld_h, IN_H, n, scratch_y,
+                             b->ld_logits, SB_EPI_STORE, b->sp_dn, s);
         case SLATE_PROF_LM_HEAD:
-            return step_gemm(b, &b->lm_head, b->xn, b->ld_x, n, b->logits, b->ld_logits, SB_EPI_STORE,
-                             1, s);
+            return step_gemm(b, &b->full, &b->lm_head, b->xn, b->ld_x, IN_XN, n, b->logits,
+                             b->ld_logits, SB_EPI_STORE, 1, s);
         case SLATE_PROF_STEP:
             return run_step(b, n);
     }

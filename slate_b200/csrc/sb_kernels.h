@@ -70,12 +70,14 @@ int sb_attention_step(float* out, const float* q, const float* K, const float* V
 /* Step prologue: validates rows, allocates KV pages on the device free list,
  * records row_pos/row_slot and gathers embeddings x[b] = emb[token[b]].
  * status (device int) receives -3 (bad token), -2 (position/pages) or -1
- * (bad slot) on failure; rows are then left without effect. */
+ * (bad slot) on failure; rows are then left without effect.  dup_ok: a slot
+ * may occur several times (a prompt chunk: its k-th occurrence at position
+ * pos + k); otherwise a repeated slot is a bad slot (-1). */
 int sb_step_prologue(const int32_t* slots, const int32_t* tokens, int B, int32_t* pos,
                      int32_t* page_table, int max_pages, int32_t* free_stack,
                      int32_t* free_top, int max_slots, int max_seq, int vocab,
                      const float* emb, int D, float* x, int ldx, int32_t* row_pos,
-                     int32_t* row_slot, int32_t* status, cudaStream_t st);
+                     int32_t* row_slot, int32_t* status, int dup_ok, cudaStream_t st);
 /* Step epilogue: out_tokens[b] = argmax(logits[b]) (first max), pos[slot]++
  * for every row when *status == 0. */
 int sb_step_epilogue(const float* logits, int ldl, int V, int B, const int32_t* row_slot,

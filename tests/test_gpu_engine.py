@@ -257,6 +257,58 @@ def test_device_step_matches_host_step(sb, workdir):
     assert np.array_equal(res[0], res[1])
 
 
+@pytest.mark.parametrize("kv_dtype,tol", [(0, 1e-4), (1, 2e-3)])
+def test_two_lanes_match_oracle(sb, oracle, workdir, kv_dtype, tol):
+    """With lanes=2 a decode step of more than max_batch / 2 rows runs as two
+    lanes (the halves of the batch on two streams, each with its own GEMM
+    operands and stream-K workspace, their attentions taking turns); with
+    lanes=1 the same steps run as one chain.  Both match the oracle's
+    per-sequence sessions, rows in a rotating order."""
+    path = os.path.join(str(workdir), "paths_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=1024, ffn_hidden=2816, n_heads=16, n_kv_heads=4,
+                      vocab=2000, max_seq=64, q4k=True, seed=11)
+    n, T = 90, 4
+    rng = np.random.default_rng(90 + kv_dtype)
+    feed = rng.integers(0, 2000, (n, T)).astype(np.int32)
+    m = oracle.open(path)
+    ref, _ = m.decode_many(feed)
+    m.close()
+    scale = np.abs(ref).max()
+    for lanes in (2, 1):
+        eng = make_engine(sb, path, max_batch=96, kv_dtype=kv_dtype, lanes=lanes)
+        slots = np.array([eng.open() for _ in range(n)], np.int32)
+        for t in range(T):
+            order = np.roll(np.arange(n), 7 * t)
+            rc, out, lg = eng.step(slots[order], feed[order, t], want_logits=True)
+            assert rc == 0, (lanes, t, sb.last_error())
+            got = lg[np.argsort(order)]
+            err = np.max(np.abs(got - ref[:, t])) / scale
+            assert err < tol, (lanes, t, err)
+        eng.close()
+
+
+def test_device_step_rejects_repeated_slot(sb, workdir):
+    """slate_llama_batch_step_device validates on the device: a slot that
+    occurs twice in one step is a bad slot (-1, as slate_llama_batch_step),
+    and the step leaves positions unchanged."""
+    import torch
+    path = os.path.join(str(workdir), "gqa_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=2,
+                      vocab=512, max_seq=512, q4k=True, seed=7)
+    eng = make_engine(sb, path, max_batch=64)
+    slots = [eng.open() for _ in range(40)]
+    slots[39] = slots[3]
+    d_s = torch.tensor(np.array(slots, np.int32), device="cuda")
+    d_t = torch.zeros(40, dtype=torch.int32, device="cuda")
+    d_o = torch.zeros(40, dtype=torch.int32, device="cuda")
+    assert eng.step_device(d_s.data_ptr(), 40, d_t.data_ptr(), d_o.data_ptr()) == 0
+    assert eng.sync() == -1
+    assert eng.position(slots[3]) == 0
+    eng.close()
+
+
 def test_scheduler_batches_concurrent_callers(sb, oracle, workdir):
     path = os.path.join(str(workdir), "gqa_q4k.gguf")
     if not os.path.exists(path):
