@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(RN_T) rmsnorm_split_kernel(
     float* __restrict__ Y, int ldy, const float* __restrict__ X, int ldx,
     const float* __restrict__ w, int D, float eps, __half* __restrict__ hi, __half* __restrict__ lo,
     int ld16) {
+    asm volatile("griddepcontrol.launch_dependents;");   // the GEMM that follows may start its set-up
     const int n = blockIdx.x, q4 = D / 4;
     const float4* x4 = (const float4*)(X + (size_t)n * ldx);
     float4 v[RN_MAX];

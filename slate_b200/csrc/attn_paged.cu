@@ -383,6 +383,7 @@ __global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ pa
                                                     int nchunk_max, float* __restrict__ att,
                                                     int ld_att, __half* __restrict__ hi,
                                                     __half* __restrict__ lo, int ld16) {
+    asm volatile("griddepcontrol.launch_dependents;");   // the Wo GEMM may start its set-up
     const int lane = threadIdx.x & 31;
     const long w = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
     const int hq = (int)(w % nq);

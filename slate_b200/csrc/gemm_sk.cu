@@ -180,9 +180,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 16 bytes global -> shared without a register (L2 only); completion by group.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+// 16 bytes global -> shared without a register (L2 only; completion by group)
+// with an L2 eviction policy (createpolicy): the weights are read once per
+// GEMM, so they are marked to leave L2 first and the workspace written by the
+// drain stays there for the output pass.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void cp_async16_pol(void* dst, const void* src, uint64_t pol) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(su32(dst)),
+                 "l"(src), "l"(pol)
+                 : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() {
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -190,13 +200,6 @@ __device__ __forceinline__ void cp_async_commit() {
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-// Pulls one 144-byte Q4_K super-block into L2 ahead of use (the lines holding
-// its first, middle and last byte).
-__device__ __forceinline__ void l2_prefetch_block(const unsigned char* p) {
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + 72));
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + 143));
 }
 
 // ---- Q4_K dequantisation (util/quant.c:157-166 scale packing, :187-199 values)
@@ -314,9 +317,12 @@ __device__ __forceinline__ float4* ws_tile(const float* ws, int C, int t) {
     return (float4*)(ws + ((size_t)C * 2 + t) * (BN * BM));
 }
 
-// SiLU(g) * u as the reference forms it (expf, IEEE division).
+// SiLU(g) * u = g / (1 + e^-g) * u (backend_cpu.c:78-87) with the fast
+// exponential and division (__expf, __fdividef: a few ulp of f32 apart from
+// expf and the IEEE quotient); the output pass evaluates it for every FFN unit
+// of every row, and the exact forms made that pass instruction-bound.
 __device__ __forceinline__ float silu_mul(float g, float u) {
-    return g / (1.0f + expf(-g)) * u;
+    return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 __device__ __forceinline__ void store_h(const SkArgs& a, int n, int unit, float h) {
     a.Y[(size_t)n * a.ldy + unit] = h;
@@ -365,18 +371,34 @@ __device__ __forceinline__ void alone_out(const SkArgs& a, uint32_t lane_base, i
 // thread m weight row m; tiles that one CTA of the GEMM computed alone were
 // written by it and are skipped.  The parts of CTAs cf..cl are summed in that
 // order (the result does not depend on timing), then the epilogue is applied.
-__global__ void __launch_bounds__(BM) sk_out_kernel(const SkArgs a, int C, long long U) {
-    const int nk = a.K / BK;
-    const int t = blockIdx.x, g4 = blockIdx.y, m = threadIdx.x;
+// The CTAs whose ranges cover tile t (cf..cl) and the slot holding cf's part
+// (0 if cf's range starts in the tile; every later CTA's part is its first
+// segment, slot 0).  Computed by one thread of the output-pass CTA.
+struct TileSrc {
+    int cf, cl, slot0;
+};
+__device__ TileSrc tile_sources(int t, int nk, int C, long long U) {
     const long long tu0 = (long long)t * nk;
-    const int cf = owner_of(tu0, C, U), cl = owner_of(tu0 + nk - 1, C, U);
+    TileSrc r;
+    r.cf = owner_of(tu0, C, U);
+    r.cl = owner_of(tu0 + nk - 1, C, U);
+    r.slot0 = u_begin(r.cf, C, U) >= tu0 ? 0 : 1;
+    return r;
+}
+
+__global__ void __launch_bounds__(BM) sk_out_kernel(const SkArgs a, int C, long long U) {
+    __shared__ TileSrc ts;
+    const int t = blockIdx.x, g4 = blockIdx.y, m = threadIdx.x;
+    if (m == 0) ts = tile_sources(t, a.K / BK, C, U);
+    __syncthreads();
+    const int cf = ts.cf, cl = ts.cl;
     const int mt = t / a.NT, n0 = (t % a.NT) * BN;
     const int row = mt * BM + m;
     if (cf == cl || n0 + 4 * g4 >= a.n_rows || row >= a.M) return;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
     for (int cc = cf; cc <= cl; ++cc) {
-        const float4* src = ws_slot(a.ws, cc, u_begin(cc, C, U) >= tu0 ? 0 : 1) + (size_t)g4 * BM;
+        const float4* src = ws_slot(a.ws, cc, cc == cf ? ts.slot0 : 0) + (size_t)g4 * BM;
         const float4 p = __ldcg(src + m);
         acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
     }
@@ -397,10 +419,12 @@ __global__ void __launch_bounds__(BM) sk_out_kernel(const SkArgs a, int C, long 
 // thread with their loads issued together.
 constexpr int ST = 256;
 __global__ void __launch_bounds__(ST) sk_silu_out_kernel(const SkArgs a, int C, long long U) {
-    const int nk = a.K / BK;
+    asm volatile("griddepcontrol.launch_dependents;");   // the down GEMM may start its set-up
+    __shared__ TileSrc ts;
     const int t = blockIdx.x, q = blockIdx.y;
-    const long long tu0 = (long long)t * nk;
-    const int cf = owner_of(tu0, C, U), cl = owner_of(tu0 + nk - 1, C, U);
+    if (threadIdx.x == 0) ts = tile_sources(t, a.K / BK, C, U);
+    __syncthreads();
+    const int cf = ts.cf, cl = ts.cl;
     const int mt = t / a.NT, n0 = (t % a.NT) * BN;
     const int groups = (min(a.n_rows - n0, BN) + 3) / 4;
     const int g_lo = q * 16, g_hi = min(groups, g_lo + 16);
@@ -421,7 +445,7 @@ __global__ void __launch_bounds__(ST) sk_silu_out_kernel(const SkArgs a, int C, 
         }
         for (int cc = cf; cc <= cl; ++cc) {
             const float4* src = cf == cl ? ws_tile(a.ws, C, t)
-                                         : ws_slot(a.ws, cc, u_begin(cc, C, U) >= tu0 ? 0 : 1);
+                                         : ws_slot(a.ws, cc, cc == cf ? ts.slot0 : 0);
             float4 p[4], p2[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -501,21 +525,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int m = (warp & 3) * 32 + lane, half = warp >> 2;
         const uint32_t lane_a = tmem + ((uint32_t)((warp & 3) * 32) << 16) + COL_A + 16u * half;
         const size_t row_bytes = (size_t)(a.K / 256) * 144;
+        const uint64_t wpol = l2_evict_first();
         long long it = 0;
         Seg sg;
         sg.start(u0, u1, nk);
         while (sg.valid() && ok) {
             const int mt = sg.t / a.NT;
             const unsigned char* wrow = a.W + (size_t)(mt * BM + m) * row_bytes;
-            const int nsb = a.K / 256;
             // The Q4_K bytes (header, this thread's 16 nibble bytes) of K steps
             // k+1 and k+2 are in flight into this thread's ring slots while
             // step k converts (cp.async: no register waits on the copies).
             auto issue = [&](int kk, long long slot) {
                 const unsigned char* p = wrow + (size_t)(kk >> 2) * 144;
                 uint4* d = wring + (size_t)(slot % WSTAGES) * 2 * NPROD + tid;
-                cp_async16(d, p);
-                cp_async16(d + NPROD, p + 16 + 32 * (kk & 3) + 16 * half);
+                cp_async16_pol(d, p, wpol);
+                cp_async16_pol(d + NPROD, p + 16 + 32 * (kk & 3) + 16 * half, wpol);
             };
             long long wi = 0;                      // ring position of step sg.ka
             for (int j = 0; j < WSTAGES - 1; ++j) {
@@ -530,8 +554,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     ok = false;
                     break;
                 }
-                if (half == 0 && (k & 3) == 0 && (k >> 2) + 2 < nsb)
-                    l2_prefetch_block(wrow + (size_t)((k >> 2) + 2) * 144);
                 if (k + WSTAGES - 1 < sg.kb) issue(k + WSTAGES - 1, wi + WSTAGES - 1);
                 cp_async_commit();
                 cp_async_wait<WSTAGES - 1>();     // step k's copies have landed
@@ -554,6 +576,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else if (warp == TMA_WARP) {
         // ---------------- x hi / lo tiles by TMA ----------------
         if (lane == 0) {
+            // x is the previous kernel's output: wait for that grid (this one
+            // may start early, see sb_sk_gemm)
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             long long it = 0;
             Seg sg;
             sg.start(u0, u1, nk);
@@ -632,6 +657,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // after.
         const int q = warp & 3, m = q * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        asm volatile("griddepcontrol.wait;" ::: "memory");   // Y / workspace: after the previous grid
         long long seg = 0;
         Seg sg;
         sg.start(u0, u1, nk);
@@ -743,8 +769,23 @@ extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows
     // the output pass: every SiLU tile; shared tiles exist only when some CTA
     // boundary falls inside a tile
     const bool pass = sk_plan(W->M_pad, W->K, n_rows, epi, &C, &U);
-    sk_kernel<<<C, NTHREADS, sk_smem(X->n_box), st>>>(*(const CUtensorMap*)X->map_hi,
-                                         *(const CUtensorMap*)X->map_lo, a);
+    // Programmatic dependent launch: the CTAs may start while the previous
+    // kernel of the stream finishes (when it allows it); the weight producers
+    // and the MMA issuer touch nothing that kernel writes, the x loads and the
+    // drain wait for it (griddepcontrol.wait).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)C);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = sk_smem(X->n_box);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, sk_kernel, *(const CUtensorMap*)X->map_hi,
+                           *(const CUtensorMap*)X->map_lo, a) != cudaSuccess)
+        return -1;
     if (pass && epi == SB_EPI_SILU)
         sk_silu_out_kernel<<<dim3((unsigned)(MT * a.NT), 4u), ST, 0, st>>>(a, C, U);
     else if (pass)
