@@ -2,7 +2,7 @@
 // products on the tensor cores (sm_100a warp-level MMA, f16 x f16 -> f32).
 //
 // Same work split and partial-record format as attn_chunk (attn_paged.cu):
-// one CTA per (row, kv head, 512-token chunk), a producer warp and four
+// one CTA per (row, kv head, SB_ATTN_CHUNK-token chunk), a producer warp and four
 // consumer warps that take pages round-robin.  Differences:
 //   * each page's K and V blocks ([16 tokens][head_dim] f16) arrive by tiled
 //     TMA in 64-column boxes with the 128-byte swizzle, so ldmatrix reads them

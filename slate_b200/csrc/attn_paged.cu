@@ -5,7 +5,7 @@
 // so one (page, kv, head) block -- 16 rows of head_dim -- is contiguous
 // (4 KB for f16 / 8 KB for f32 at head_dim 128).
 //
-// One CTA per (row, kv_head, 512-token chunk).  A producer warp streams the
+// One CTA per (row, kv_head, SB_ATTN_CHUNK-token chunk).  A producer warp streams the
 // chunk's pages with cp.async.bulk (TMA bulk copies, one for K and one for V,
 // completion on an mbarrier) into an 8-stage (f16) / 4-stage (f32) ring in
 // shared memory.  Four consumer warps take pages round-robin; each handles

@@ -95,8 +95,10 @@ int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd, const int
 /* Paged GQA attention (llama_infer.c:97-129): att[b][hq*hd+d] for ctx =
  * row_pos[b]+1.  Split over context chunks of SB_ATTN_CHUNK tokens into
  * scratch partials (m, l, o[hd]) of size sb_attention_scratch_floats(), then
- * combined. */
-#define SB_ATTN_CHUNK 512
+ * combined.  1024-token chunks: at the 8B shape with 256 sequences they ran
+ * 2-6% faster per layer than 512 (fewer per-CTA starts and partials) with
+ * ~10K CTAs still in flight; 4096 lost parallelism. */
+#define SB_ATTN_CHUNK 1024
 size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int max_seq);
 /* Opts the (head_dim, group, dtype) kernel into its shared-memory size on the
  * current device; call outside stream capture before the first launch. */
