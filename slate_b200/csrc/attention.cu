@@ -101,6 +101,50 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int ld, int nq, int 
     }
 }
 
+// The same with one CTA per (row, head): blockIdx.y < nq rotates query head
+// y in place, nq <= y < nq + nkv rotates key head y - nq into the cache, the
+// rest copy value heads into the cache; thread j handles the pair (j, j + hd/2)
+// (or, for values, elements j and j + hd/2).  ~(nq + 2 nkv) x rows small CTAs
+// instead of one CTA per row keep the memory system busy.
+template <typename KT>
+__global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int nq, int nkv, int hd,
+                                         const int32_t* __restrict__ row_pos,
+                                         const int32_t* __restrict__ row_slot,
+                                         const int32_t* __restrict__ page_table, int max_pages,
+                                         KT* __restrict__ pool, int64_t n_pages, int layer,
+                                         const float* __restrict__ rc, const float* __restrict__ rs) {
+    const int b = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
+    const int pos = row_pos[b];
+    if (pos < 0) return;
+    const int half = hd / 2;
+    float* r = qkv + (size_t)b * ld + (size_t)h * hd;    // q, k and v heads are contiguous
+    if (h < nq) {
+        const float c = rc[(size_t)pos * half + j], sn = rs[(size_t)pos * half + j];
+        const float a = r[j], bb = r[j + half];
+        r[j] = a * c - bb * sn;
+        r[j + half] = a * sn + bb * c;
+        return;
+    }
+    const int slot = row_slot[b];
+    const int page = page_table[(size_t)slot * max_pages + pos / SB_PAGE_TOKENS];
+    if (page < 0 || page >= n_pages) return;          // never allocated: skip, never fault
+    const int t = pos % SB_PAGE_TOKENS;
+    const size_t head_stride = (size_t)SB_PAGE_TOKENS * hd;
+    KT* kbase = pool + ((size_t)layer * n_pages + page) * (size_t)2 * nkv * head_stride;
+    if (h < nq + nkv) {
+        const float c = rc[(size_t)pos * half + j], sn = rs[(size_t)pos * half + j];
+        const float a = r[j], bb = r[j + half];
+        KT* dst = kbase + (size_t)(h - nq) * head_stride + (size_t)t * hd;
+        from_f(dst[j], a * c - bb * sn);
+        from_f(dst[j + half], a * sn + bb * c);
+    } else {
+        KT* dst = kbase + (size_t)nkv * head_stride + (size_t)(h - nq - nkv) * head_stride +
+                  (size_t)t * hd;
+        from_f(dst[j], r[j]);
+        from_f(dst[j + half], r[j + half]);
+    }
+}
+
 // ------------------------------------------------------------------------
 // Row kernels.
 __global__ void rmsnorm_kernel(float* __restrict__ Y, int ldy, const float* __restrict__ X,
@@ -474,6 +518,18 @@ extern "C" int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd
                               int64_t n_pages, int layer, int kv_dtype, const float* rope_cos,
                               const float* rope_sin, cudaStream_t st) {
     if (B < 1 || hd % 2) return -1;
+    if (hd <= 2048 && B <= 0x7fffffff && nq + 2 * nkv <= 65535) {
+        const dim3 grid((unsigned)B, (unsigned)(nq + 2 * nkv));
+        if (kv_dtype == SLATE_KV_F16)
+            rope_append_heads_kernel<__half><<<grid, hd / 2, 0, st>>>(
+                qkv, ld, nq, nkv, hd, row_pos, row_slot, page_table, max_pages, (__half*)pool,
+                n_pages, layer, rope_cos, rope_sin);
+        else
+            rope_append_heads_kernel<float><<<grid, hd / 2, 0, st>>>(
+                qkv, ld, nq, nkv, hd, row_pos, row_slot, page_table, max_pages, (float*)pool,
+                n_pages, layer, rope_cos, rope_sin);
+        return 0;
+    }
     if (kv_dtype == SLATE_KV_F16)
         rope_append_kernel<__half><<<B, 128, 0, st>>>(qkv, ld, nq, nkv, hd, row_pos, row_slot,
                                                       page_table, max_pages, (__half*)pool, n_pages,
