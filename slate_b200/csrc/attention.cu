@@ -9,6 +9,7 @@
 //
 // The attention kernels themselves live in attn_paged.cu.
 #include "sb_kernels.h"
+#include "sb_pdl.h"
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -113,6 +114,8 @@ __global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int nq
                                          const int32_t* __restrict__ page_table, int max_pages,
                                          KT* __restrict__ pool, int64_t n_pages, int layer,
                                          const float* __restrict__ rc, const float* __restrict__ rs) {
+    sb_grid_release();
+    sb_grid_wait();      // qkv: after the previous kernel (programmatic launch, sb_pdl.h)
     const int b = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
     const int pos = row_pos[b];
     if (pos < 0) return;
@@ -178,7 +181,8 @@ __global__ void __launch_bounds__(RN_T) rmsnorm_split_kernel(
     float* __restrict__ Y, int ldy, const float* __restrict__ X, int ldx,
     const float* __restrict__ w, int D, float eps, __half* __restrict__ hi, __half* __restrict__ lo,
     int ld16) {
-    asm volatile("griddepcontrol.launch_dependents;");   // the GEMM that follows may start its set-up
+    sb_grid_release();   // the GEMM that follows may start its set-up
+    sb_grid_wait();      // x: after the previous kernel (programmatic launch, sb_pdl.h)
     const int n = blockIdx.x, q4 = D / 4;
     const float4* x4 = (const float4*)(X + (size_t)n * ldx);
     float4 v[RN_MAX];
@@ -520,15 +524,15 @@ extern "C" int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd
     if (B < 1 || hd % 2) return -1;
     if (hd <= 2048 && B <= 0x7fffffff && nq + 2 * nkv <= 65535) {
         const dim3 grid((unsigned)B, (unsigned)(nq + 2 * nkv));
-        if (kv_dtype == SLATE_KV_F16)
-            rope_append_heads_kernel<__half><<<grid, hd / 2, 0, st>>>(
-                qkv, ld, nq, nkv, hd, row_pos, row_slot, page_table, max_pages, (__half*)pool,
-                n_pages, layer, rope_cos, rope_sin);
-        else
-            rope_append_heads_kernel<float><<<grid, hd / 2, 0, st>>>(
-                qkv, ld, nq, nkv, hd, row_pos, row_slot, page_table, max_pages, (float*)pool,
-                n_pages, layer, rope_cos, rope_sin);
-        return 0;
+        const cudaError_t e =
+            kv_dtype == SLATE_KV_F16
+                ? sb_launch_pdl(rope_append_heads_kernel<__half>, grid, dim3(hd / 2), 0, st, qkv, ld,
+                                nq, nkv, hd, row_pos, row_slot, page_table, max_pages, (__half*)pool,
+                                n_pages, layer, rope_cos, rope_sin)
+                : sb_launch_pdl(rope_append_heads_kernel<float>, grid, dim3(hd / 2), 0, st, qkv, ld,
+                                nq, nkv, hd, row_pos, row_slot, page_table, max_pages, (float*)pool,
+                                n_pages, layer, rope_cos, rope_sin);
+        return e == cudaSuccess ? 0 : -1;
     }
     if (kv_dtype == SLATE_KV_F16)
         rope_append_kernel<__half><<<B, 128, 0, st>>>(qkv, ld, nq, nkv, hd, row_pos, row_slot,
@@ -555,9 +559,10 @@ extern "C" int sb_rmsnorm_rows_split(float* Y, int ldy, const float* X, int ldx,
     if (D % 4 || D > RN_MAX * 4 * RN_T || ldx % 4 || ldy % 4 || ld16 % 4 || ((uintptr_t)X & 15) ||
         ((uintptr_t)Y & 15) || ((uintptr_t)w & 15) || B > 0x7fffffff)
         return -1;
-    rmsnorm_split_kernel<<<B, RN_T, 0, st>>>(Y, ldy, X, ldx, w, D, eps, (__half*)hi, (__half*)lo,
-                                              ld16);
-    return 0;
+    return sb_launch_pdl(rmsnorm_split_kernel, dim3((unsigned)B), dim3(RN_T), 0, st, Y, ldy, X, ldx,
+                         w, D, eps, (__half*)hi, (__half*)lo, ld16) == cudaSuccess
+               ? 0
+               : -1;
 }
 extern "C" int sb_silu_mul(float* y, const float* g, const float* u, int n, cudaStream_t st) {
     if (n < 1) return -1;

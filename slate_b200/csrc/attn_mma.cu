@@ -27,6 +27,7 @@
 
 #include "sb_internal.h"
 #include "sb_kernels.h"
+#include "sb_pdl.h"
 
 namespace {
 
@@ -134,6 +135,8 @@ __global__ void __launch_bounds__(32 * (NW + 1), 3) attn_chunk_mma(
     __shared__ uint64_t full[STAGES], empty[STAGES];
     __shared__ int pages_s[SB_ATTN_CHUNK / 16];
 
+    sb_grid_release();
+    sb_grid_wait();      // q, positions, pages: after the previous kernel (sb_pdl.h)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t4 = lane & 3;
     const int chunk = blockIdx.x % nchunk_max;
@@ -354,10 +357,11 @@ int launch(int prepare, const void* map, const float* qkv, int ld_qkv, int B, in
     const long ctas = (long)B * nkv * nchunk;
     CUtensorMap m;                      // the caller's copy need not be 64-byte aligned
     memcpy(&m, map, sizeof m);
-    attn_chunk_mma<HD, G><<<(unsigned)ctas, 32 * (NW + 1), smem_bytes<HD, G>(), st>>>(
-        m, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages,
-        n_pages, layer, nchunk, part, err);
-    return 0;
+    return sb_launch_pdl(attn_chunk_mma<HD, G>, dim3((unsigned)ctas), dim3(32 * (NW + 1)),
+                         smem_bytes<HD, G>(), st, m, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
+                         page_table, max_pages, n_pages, layer, nchunk, part, err) == cudaSuccess
+               ? 0
+               : -1;
 }
 
 template <int HD>

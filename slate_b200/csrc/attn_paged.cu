@@ -23,6 +23,7 @@
 #include <math.h>
 
 #include "sb_kernels.h"
+#include "sb_pdl.h"
 
 namespace {
 
@@ -383,7 +384,8 @@ __global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ pa
                                                     int nchunk_max, float* __restrict__ att,
                                                     int ld_att, __half* __restrict__ hi,
                                                     __half* __restrict__ lo, int ld16) {
-    asm volatile("griddepcontrol.launch_dependents;");   // the Wo GEMM may start its set-up
+    sb_grid_release();   // the Wo GEMM may start its set-up
+    sb_grid_wait();      // chunk partials: after the previous kernel (sb_pdl.h)
     const int lane = threadIdx.x & 31;
     const long w = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
     const int hq = (int)(w % nq);
@@ -444,9 +446,11 @@ int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
         qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, (const KT*)pool, n_pages,
         layer, nchunk, scratch, err);
     const long cw = (long)B * nq;
-    attn_combine<HD><<<(unsigned)((cw + 3) / 4), 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att,
-                                                                ld_att, hl.hi, hl.lo, hl.ld16);
-    return 0;
+    return sb_launch_pdl(attn_combine<HD>, dim3((unsigned)((cw + 3) / 4)), dim3(128), 0, st,
+                         (const float*)scratch, B, nq, row_pos, nchunk, att, ld_att, hl.hi, hl.lo,
+                         hl.ld16) == cudaSuccess
+               ? 0
+               : -1;
 }
 
 template <int HD, typename KT>
@@ -488,13 +492,15 @@ int combine(int hd, const float* scratch, int B, int nq, const int32_t* row_pos,
     const unsigned grid = (unsigned)(((long)B * nq + 3) / 4);
     switch (hd) {
         case 64:
-            attn_combine<64><<<grid, 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att, ld_att,
-                                                   hl.hi, hl.lo, hl.ld16);
-            return 0;
+            return sb_launch_pdl(attn_combine<64>, dim3(grid), dim3(128), 0, st, scratch, B, nq,
+                                 row_pos, nchunk, att, ld_att, hl.hi, hl.lo, hl.ld16) == cudaSuccess
+                       ? 0
+                       : -1;
         case 128:
-            attn_combine<128><<<grid, 128, 0, st>>>(scratch, B, nq, row_pos, nchunk, att, ld_att,
-                                                    hl.hi, hl.lo, hl.ld16);
-            return 0;
+            return sb_launch_pdl(attn_combine<128>, dim3(grid), dim3(128), 0, st, scratch, B, nq,
+                                 row_pos, nchunk, att, ld_att, hl.hi, hl.lo, hl.ld16) == cudaSuccess
+                       ? 0
+                       : -1;
     }
     return -1;
 }

@@ -45,6 +45,7 @@
 
 #include "sb_internal.h"
 #include "sb_kernels.h"
+#include "sb_pdl.h"
 #include "sb_tc.h"
 
 namespace {
@@ -387,6 +388,8 @@ __device__ TileSrc tile_sources(int t, int nk, int C, long long U) {
 }
 
 __global__ void __launch_bounds__(BM) sk_out_kernel(const SkArgs a, int C, long long U) {
+    sb_grid_release();
+    sb_grid_wait();      // the GEMM's workspace: after it (sb_pdl.h)
     __shared__ TileSrc ts;
     const int t = blockIdx.x, g4 = blockIdx.y, m = threadIdx.x;
     if (m == 0) ts = tile_sources(t, a.K / BK, C, U);
@@ -419,7 +422,8 @@ __global__ void __launch_bounds__(BM) sk_out_kernel(const SkArgs a, int C, long 
 // thread with their loads issued together.
 constexpr int ST = 256;
 __global__ void __launch_bounds__(ST) sk_silu_out_kernel(const SkArgs a, int C, long long U) {
-    asm volatile("griddepcontrol.launch_dependents;");   // the down GEMM may start its set-up
+    sb_grid_release();   // the down GEMM may start its set-up
+    sb_grid_wait();      // the GEMM's workspace: after it (sb_pdl.h)
     __shared__ TileSrc ts;
     const int t = blockIdx.x, q = blockIdx.y;
     if (threadIdx.x == 0) ts = tile_sources(t, a.K / BK, C, U);
@@ -488,6 +492,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __shared__ uint64_t acc_full, acc_empty, done_bar;
     __shared__ uint32_t tmem_slot;
 
+    sb_grid_release();   // the output pass may be scheduled (it waits for this grid)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = gridDim.x, c = blockIdx.x;
     const int nk = a.K / BK;
@@ -578,7 +583,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) {
             // x is the previous kernel's output: wait for that grid (this one
             // may start early, see sb_sk_gemm)
-            asm volatile("griddepcontrol.wait;" ::: "memory");
+            sb_grid_wait();
             long long it = 0;
             Seg sg;
             sg.start(u0, u1, nk);
@@ -657,7 +662,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // after.
         const int q = warp & 3, m = q * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-        asm volatile("griddepcontrol.wait;" ::: "memory");   // Y / workspace: after the previous grid
+        sb_grid_wait();      // Y / workspace: after the previous grid
         long long seg = 0;
         Seg sg;
         sg.start(u0, u1, nk);
@@ -769,27 +774,21 @@ extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows
     // the output pass: every SiLU tile; shared tiles exist only when some CTA
     // boundary falls inside a tile
     const bool pass = sk_plan(W->M_pad, W->K, n_rows, epi, &C, &U);
-    // Programmatic dependent launch: the CTAs may start while the previous
-    // kernel of the stream finishes (when it allows it); the weight producers
-    // and the MMA issuer touch nothing that kernel writes, the x loads and the
-    // drain wait for it (griddepcontrol.wait).
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)C);
-    cfg.blockDim = dim3(NTHREADS);
-    cfg.dynamicSmemBytes = sk_smem(X->n_box);
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, sk_kernel, *(const CUtensorMap*)X->map_hi,
-                           *(const CUtensorMap*)X->map_lo, a) != cudaSuccess)
+    // Programmatic dependent launch (sb_pdl.h): the weight producers and the
+    // MMA issuer touch nothing earlier kernels write and start at once; the x
+    // loads and the drain wait for the previous grid.
+    if (sb_launch_pdl(sk_kernel, dim3((unsigned)C), dim3(NTHREADS), sk_smem(X->n_box), st,
+                      *(const CUtensorMap*)X->map_hi, *(const CUtensorMap*)X->map_lo, a) !=
+        cudaSuccess)
         return -1;
+    cudaError_t e = cudaSuccess;
     if (pass && epi == SB_EPI_SILU)
-        sk_silu_out_kernel<<<dim3((unsigned)(MT * a.NT), 4u), ST, 0, st>>>(a, C, U);
+        e = sb_launch_pdl(sk_silu_out_kernel, dim3((unsigned)(MT * a.NT), 4u), dim3(ST), 0, st, a, C,
+                          U);
     else if (pass)
-        sk_out_kernel<<<dim3((unsigned)(MT * a.NT), (unsigned)((min(n_rows, BN) + 3) / 4)), BM, 0, st>>>(
-            a, C, U);
+        e = sb_launch_pdl(sk_out_kernel,
+                          dim3((unsigned)(MT * a.NT), (unsigned)((min(n_rows, BN) + 3) / 4)), dim3(BM),
+                          0, st, a, C, U);
+    if (e != cudaSuccess) return -1;
     return 0;
 }
