@@ -163,7 +163,7 @@ class ClockSampler:
                 self.p.kill()
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
+        sm, mx, pw, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.out.splitlines():
             f = [x.strip() for x in line.split(",")]
@@ -174,13 +174,17 @@ class ClockSampler:
                 mx.append(float(f[2]))
             except ValueError:
                 continue
+            try:
+                pw.append(float(f[3]))
+            except ValueError:
+                pass
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "power_w": statistics.median(pw) if pw else None, "samples": len(sm)}
 
 
 # ---------------------------------------------------------------------------
