@@ -336,6 +336,242 @@ __global__ void __launch_bounds__(32 * (NW + 1), 3) attn_chunk_mma(
     }
 }
 
+// ---- causal prefill attention ---------------------------------------------
+// A prompt chunk is a step whose rows are consecutive positions of one
+// sequence.  The decode kernel above would stream every row's whole prefix on
+// its own; here one CTA takes a tile of QT consecutive rows for one kv head and
+// one context chunk, streams each K/V page of the chunk once, and every
+// consumer warp applies it to its 16 query vectors (16 / G rows x G heads):
+//   S = Q K^T with q split into f16 hi and lo (two MMAs, one accumulator),
+//   causal mask (token <= the row's position), online softmax per vector
+//   (two vectors per lane: accumulator rows g and g + 8), O += P V with p
+//   split likewise.  V rows past the chunk's last token are masked in the
+//   ldmatrix registers (the ring stage is shared by all warps).  The partial
+//   records (m, l, o) have the decode kernel's format and layout, so
+//   attn_combine finishes them.
+template <int HD, int G>
+__global__ void __launch_bounds__(32 * (NW + 1), 2) attn_prefill_mma(
+    const __grid_constant__ CUtensorMap kvmap, const float* __restrict__ qkv, int ld_qkv, int B,
+    int nq, int nkv, const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
+    const int32_t* __restrict__ page_table, int max_pages, int64_t n_pages, int layer,
+    int nchunk_max, float* __restrict__ part, int* err) {
+    static_assert(HD % 64 == 0 && 16 % G == 0, "head_dim multiple of 64, G divides 16");
+    constexpr int BLK = 16 * HD * 2;
+    constexpr int KC = HD / 16;
+    constexpr int NT = HD / 8;
+    constexpr int RW = 16 / G;                // rows per consumer warp
+    constexpr int QT = NW * RW;               // rows per CTA
+    sb_grid_release();
+    sb_grid_wait();      // q, positions, pages: after the previous kernel (sb_pdl.h)
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* ring = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t full[STAGES], empty[STAGES];
+    __shared__ int pages_s[SB_ATTN_CHUNK / 16];
+    __shared__ int s_ctx, s_slot;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int chunk = blockIdx.x % nchunk_max;
+    const int rest = blockIdx.x / nchunk_max;
+    const int kvh = rest % nkv, tile = rest / nkv;
+    const int r0 = tile * QT;
+    if (r0 >= B) return;
+    if (tid == 0) {
+        // the tile's rows share one sequence; the chunk is needed up to the
+        // last row's position
+        int ctx = 0, slot = -1;
+        for (int r = r0; r < min(B, r0 + QT); ++r) {
+            const int p = row_pos[r];
+            if (p >= 0) {
+                ctx = max(ctx, p + 1);
+                if (slot < 0) slot = row_slot[r];
+            }
+        }
+        s_ctx = ctx;
+        s_slot = slot;
+        for (int s = 0; s < STAGES; ++s) {
+            bar_init(&full[s], 1);
+            bar_init(&empty[s], NW);            // every consumer warp reads every stage
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const int ctx = s_ctx, slot = s_slot, t0 = chunk * SB_ATTN_CHUNK;
+    if (slot < 0 || t0 >= ctx) return;
+    const int t1 = min(ctx, t0 + SB_ATTN_CHUNK);
+    const int npg = (t1 - t0 + 15) / 16;
+    if (warp == NW) {
+        for (int i = lane; i < npg; i += 32) {
+            int page = page_table[(size_t)slot * max_pages + t0 / 16 + i];
+            if (page < 0 || page >= n_pages) {
+                atomicCAS(err, 0, 6);
+                page = 0;
+            }
+            pages_s[i] = page;
+        }
+    }
+    __syncthreads();
+
+    if (warp == NW) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < npg; ++i) {
+                const int s = i % STAGES;
+                if (i >= STAGES && !bar_wait(&empty[s], ((i / STAGES) - 1) & 1, err, 4)) break;
+                const int row = (pages_s[i] * 2 * nkv + kvh) * 16;
+                const int vrow = row + nkv * 16;
+                unsigned char* st = ring + (size_t)s * 2 * BLK;
+                bar_expect(&full[s], 2 * BLK);
+#pragma unroll
+                for (int h = 0; h < HD / 64; ++h) {
+                    tma_3d(st + h * 2048, &kvmap, &full[s], 64 * h, row, layer);
+                    tma_3d(st + BLK + h * 2048, &kvmap, &full[s], 64 * h, vrow, layer);
+                }
+                issued = i + 1;
+            }
+            for (int i = issued - STAGES > 0 ? issued - STAGES : 0; i < issued; ++i)
+                bar_wait(&full[i % STAGES], (i / STAGES) & 1, err, 5);
+        }
+        return;
+    }
+
+    // ---- consumer warp: vectors v = 0..15 -> row rw0 + v / G, head v % G;
+    // this lane holds vectors g (accumulator rows 0..7) and g + 8 ----
+    const int rw0 = r0 + warp * RW;
+    int vrow[2], vpos[2], vhead[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int v = g + 8 * u;
+        vrow[u] = rw0 + v / G;
+        vhead[u] = kvh * G + v % G;
+        vpos[u] = vrow[u] < B ? row_pos[vrow[u]] : -1;
+    }
+    uint32_t qa_hi[KC][4], qa_lo[KC][4];
+#pragma unroll
+    for (int c = 0; c < KC; ++c) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            float x[4] = {0.f, 0.f, 0.f, 0.f};
+            if (vpos[u] >= 0) {
+                const float* qp = qkv + (size_t)vrow[u] * ld_qkv + (size_t)vhead[u] * HD + 16 * c;
+                x[0] = qp[2 * t4];
+                x[1] = qp[2 * t4 + 1];
+                x[2] = qp[8 + 2 * t4];
+                x[3] = qp[8 + 2 * t4 + 1];
+            }
+            // A registers: 0 = (row g, k 2t..), 1 = (row g+8, k 2t..), 2 = (row g, k 2t+8..),
+            // 3 = (row g+8, k 2t+8..)
+            split2(x[0], x[1], qa_hi[c][u], qa_lo[c][u]);
+            split2(x[2], x[3], qa_hi[c][2 + u], qa_lo[c][2 + u]);
+        }
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    const float scale = 1.0f / sqrtf((float)HD);
+    const int mi = lane >> 3, mr = lane & 7;
+    for (int i = 0; i < npg; ++i) {
+        const int s = i % STAGES;
+        if (!bar_wait(&full[s], (i / STAGES) & 1, err, 7)) break;
+        const unsigned char* kblk = ring + (size_t)s * 2 * BLK;
+        const unsigned char* vblk = kblk + BLK;
+        const int pt0 = t0 + 16 * i;                     // first token of the page
+        const int nval = min(16, t1 - pt0);              // tokens of the page in the chunk
+        // ---- S = Q K^T: two n-tiles of 8 tokens ----
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const uint32_t kbase = su32(kblk);
+#pragma unroll
+        for (int c = 0; c < KC; ++c) {
+            const int r = (mi >> 1) * 8 + mr, d = 16 * c + (mi & 1) * 8;
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4(kbase + swz(r, d), b00, b01, b10, b11);
+            mma16816(sc[0], qa_hi[c][0], qa_hi[c][1], qa_hi[c][2], qa_hi[c][3], b00, b01);
+            mma16816(sc[0], qa_lo[c][0], qa_lo[c][1], qa_lo[c][2], qa_lo[c][3], b00, b01);
+            mma16816(sc[1], qa_hi[c][0], qa_hi[c][1], qa_hi[c][2], qa_hi[c][3], b10, b11);
+            mma16816(sc[1], qa_lo[c][0], qa_lo[c][1], qa_lo[c][2], qa_lo[c][3], b10, b11);
+        }
+        // ---- causal mask, online softmax for vectors g (u = 0) and g + 8 (u = 1) ----
+        float p[2][4];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            float sv[4], mx = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int j = k >> 1, e = k & 1;
+                const int tok = 8 * j + 2 * t4 + e;
+                const bool ok = tok < nval && pt0 + tok <= vpos[u];
+                sv[k] = ok ? sc[j][2 * u + e] * scale : -INFINITY;
+                mx = fmaxf(mx, sv[k]);
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float m_new = fmaxf(m_run[u], mx);
+            // a vector with nothing to attend to yet keeps m = -inf, l = 0, o = 0
+            const float corr = m_new == -INFINITY ? 1.f : expf(m_run[u] - m_new);
+            float ps = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                p[u][k] = sv[k] == -INFINITY ? 0.f : expf(sv[k] - m_new);
+                ps += p[u][k];
+            }
+            ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+            l_run[u] = l_run[u] * corr + ps;
+            m_run[u] = m_new;
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                o[j][2 * u] *= corr;
+                o[j][2 * u + 1] *= corr;
+            }
+        }
+        // P as A fragments (hi / lo): 0 = (g, tok 2t..), 1 = (g+8, tok 2t..),
+        // 2 = (g, tok 8+2t..), 3 = (g+8, tok 8+2t..)
+        uint32_t pa_hi[4], pa_lo[4];
+        split2(p[0][0], p[0][1], pa_hi[0], pa_lo[0]);
+        split2(p[1][0], p[1][1], pa_hi[1], pa_lo[1]);
+        split2(p[0][2], p[0][3], pa_hi[2], pa_lo[2]);
+        split2(p[1][2], p[1][3], pa_hi[3], pa_lo[3]);
+        // V rows past nval may hold stale bits (0 * NaN is NaN): mask them in
+        // the fragments; this lane's B registers hold tokens 2t, 2t+1 (b0)
+        // and 8 + 2t, 9 + 2t (b1)
+        const uint32_t m0 = (2 * t4 < nval ? 0xFFFFu : 0u) | (2 * t4 + 1 < nval ? 0xFFFF0000u : 0u);
+        const uint32_t m1 = (8 + 2 * t4 < nval ? 0xFFFFu : 0u) | (9 + 2 * t4 < nval ? 0xFFFF0000u : 0u);
+        const uint32_t vbase = su32(vblk);
+#pragma unroll
+        for (int j = 0; j < NT; j += 2) {
+            const int r = (mi & 1) * 8 + mr, d = 8 * j + (mi >> 1) * 8;
+            uint32_t v00, v01, v10, v11;
+            ldsm_x4_t(vbase + swz(r, d), v00, v01, v10, v11);
+            v00 &= m0;
+            v01 &= m1;
+            v10 &= m0;
+            v11 &= m1;
+            mma16816(o[j], pa_hi[0], pa_hi[1], pa_hi[2], pa_hi[3], v00, v01);
+            mma16816(o[j], pa_lo[0], pa_lo[1], pa_lo[2], pa_lo[3], v00, v01);
+            mma16816(o[j + 1], pa_hi[0], pa_hi[1], pa_hi[2], pa_hi[3], v10, v11);
+            mma16816(o[j + 1], pa_lo[0], pa_lo[1], pa_lo[2], pa_lo[3], v10, v11);
+        }
+        __syncwarp();
+        if (lane == 0) bar_arrive(&empty[s]);
+    }
+    // ---- partial records of this chunk for the vectors that attend to it ----
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        if (vpos[u] < t0) continue;                 // row invalid or before this chunk
+        float* out = part + (((size_t)vrow[u] * nq + vhead[u]) * nchunk_max + chunk) * (HD + 2);
+        if (t4 == 0) {
+            out[0] = m_run[u];
+            out[1] = l_run[u];
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            out[2 + 8 * j + 2 * t4] = o[j][2 * u];
+            out[2 + 8 * j + 2 * t4 + 1] = o[j][2 * u + 1];
+        }
+    }
+}
+
 template <int HD, int G>
 size_t smem_bytes() {
     const size_t ring = (size_t)STAGES * 2 * 16 * HD * 2;
@@ -364,16 +600,42 @@ int launch(int prepare, const void* map, const float* qkv, int ld_qkv, int B, in
                : -1;
 }
 
+template <int HD, int G>
+int launch_prefill(int prepare, const void* map, const float* qkv, int ld_qkv, int B, int nq,
+                   int nkv, const int32_t* row_pos, const int32_t* row_slot,
+                   const int32_t* page_table, int max_pages, int64_t n_pages, int layer,
+                   int nchunk, float* part, int* err, cudaStream_t st) {
+    const size_t smem = (size_t)STAGES * 2 * 16 * HD * 2 + 1024;
+    if (prepare) {
+        cudaFuncSetAttribute(attn_prefill_mma<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+        return 0;
+    }
+    constexpr int QT = NW * (16 / G);
+    const long ctas = (long)((B + QT - 1) / QT) * nkv * nchunk;
+    CUtensorMap m;
+    memcpy(&m, map, sizeof m);
+    return sb_launch_pdl(attn_prefill_mma<HD, G>, dim3((unsigned)ctas), dim3(32 * (NW + 1)), smem,
+                         st, m, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages,
+                         n_pages, layer, nchunk, part, err) == cudaSuccess
+               ? 0
+               : -1;
+}
+
 template <int HD>
-int launch_hd(int prepare, int G, const void* map, const float* qkv, int ld_qkv, int B, int nq,
-              int nkv, const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
-              int max_pages, int64_t n_pages, int layer, int nchunk, float* part, int* err,
-              cudaStream_t st) {
+int launch_hd(int prepare, int prefill, int G, const void* map, const float* qkv, int ld_qkv,
+              int B, int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
+              const int32_t* page_table, int max_pages, int64_t n_pages, int layer, int nchunk,
+              float* part, int* err, cudaStream_t st) {
     switch (G) {
 #define CASE(g)                                                                                 \
     case g:                                                                                     \
-        return launch<HD, g>(prepare, map, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,          \
-                             page_table, max_pages, n_pages, layer, nchunk, part, err, st);
+        return prefill ? launch_prefill<HD, g>(prepare, map, qkv, ld_qkv, B, nq, nkv, row_pos,  \
+                                               row_slot, page_table, max_pages, n_pages, layer, \
+                                               nchunk, part, err, st)                           \
+                       : launch<HD, g>(prepare, map, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, \
+                                       page_table, max_pages, n_pages, layer, nchunk, part, err, \
+                                       st);
         CASE(1) CASE(2) CASE(4) CASE(8)
 #undef CASE
     }
@@ -421,19 +683,44 @@ extern "C" int sb_attention_make_map(void* map, void* pool, int64_t n_pages, int
     return 0;
 }
 
+static int attention_mma(int prepare, int prefill, const void* map, const float* qkv, int ld_qkv,
+                         int B, int nq, int nkv, int hd, const int32_t* row_pos,
+                         const int32_t* row_slot, const int32_t* page_table, int max_pages,
+                         int64_t n_pages, int layer, int nchunk, float* part, int* err,
+                         cudaStream_t st) {
+    const int G = nq / nkv;
+    switch (hd) {
+        case 64:
+            return launch_hd<64>(prepare, prefill, G, map, qkv, ld_qkv, B, nq, nkv, row_pos,
+                                 row_slot, page_table, max_pages, n_pages, layer, nchunk, part,
+                                 err, st);
+        case 128:
+            return launch_hd<128>(prepare, prefill, G, map, qkv, ld_qkv, B, nq, nkv, row_pos,
+                                  row_slot, page_table, max_pages, n_pages, layer, nchunk, part,
+                                  err, st);
+    }
+    return -1;
+}
+
 extern "C" int sb_attention_mma(int prepare, const void* map, const float* qkv, int ld_qkv, int B,
                                 int nq, int nkv, int hd, const int32_t* row_pos,
                                 const int32_t* row_slot, const int32_t* page_table, int max_pages,
                                 int64_t n_pages, int layer, int nchunk, float* part, int* err,
                                 cudaStream_t st) {
-    const int G = nq / nkv;
-    switch (hd) {
-        case 64:
-            return launch_hd<64>(prepare, G, map, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
-                                 page_table, max_pages, n_pages, layer, nchunk, part, err, st);
-        case 128:
-            return launch_hd<128>(prepare, G, map, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
-                                  page_table, max_pages, n_pages, layer, nchunk, part, err, st);
-    }
-    return -1;
+    if (prepare)   // both kernels' shared-memory attributes
+        return attention_mma(1, 0, nullptr, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr,
+                             0, 0, 0, 0, nullptr, nullptr, 0) |
+               attention_mma(1, 1, nullptr, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr,
+                             0, 0, 0, 0, nullptr, nullptr, 0);
+    return attention_mma(0, 0, map, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
+                         max_pages, n_pages, layer, nchunk, part, err, st);
+}
+
+extern "C" int sb_attention_prefill_mma(const void* map, const float* qkv, int ld_qkv, int B,
+                                        int nq, int nkv, int hd, const int32_t* row_pos,
+                                        const int32_t* row_slot, const int32_t* page_table,
+                                        int max_pages, int64_t n_pages, int layer, int nchunk,
+                                        float* part, int* err, cudaStream_t st) {
+    return attention_mma(0, 1, map, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
+                         max_pages, n_pages, layer, nchunk, part, err, st);
 }

@@ -558,6 +558,26 @@ extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int 
                     HiLo{nullptr, nullptr, 0}, st);
 }
 
+extern "C" int sb_attention_paged_prefill(float* att, int ld_att, const float* qkv, int ld_qkv,
+                                          int B, int nq, int nkv, int hd, const int32_t* row_pos,
+                                          const int32_t* row_slot, const int32_t* page_table,
+                                          int max_pages, const void* pool, const void* kvmap,
+                                          int64_t n_pages, int layer, int kv_dtype, int max_seq,
+                                          float* scratch, int* err, void* hi, void* lo, int ld16,
+                                          cudaStream_t st) {
+    if (B < 1 || !err || (hi && ld16 < nq * hd)) return -1;
+    const HiLo hl{(__half*)hi, (__half*)lo, hi ? ld16 : 0};
+    if (!kvmap || !sb_attention_mma_supported(nq, nkv, hd, kv_dtype))
+        return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
+                        max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, scratch, err, hl,
+                        st);
+    const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
+    const int rc = sb_attention_prefill_mma(kvmap, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot,
+                                            page_table, max_pages, n_pages, layer, nchunk, scratch,
+                                            err, st);
+    return rc ? rc : combine(hd, scratch, B, nq, row_pos, nchunk, att, ld_att, hl, st);
+}
+
 extern "C" int sb_attention_paged_split(float* att, int ld_att, const float* qkv, int ld_qkv, int B,
                                         int nq, int nkv, int hd, const int32_t* row_pos,
                                         const int32_t* row_slot, const int32_t* page_table,

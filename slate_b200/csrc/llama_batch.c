@@ -113,6 +113,7 @@ struct slate_llama_batch {
     float* sk_ws;
     sb_lane full, half[2];         /* the whole batch; the two halves (dual) */
     int dual, half_rows;           /* dual: steps of > half_rows rows use two lanes */
+    int chunk_step;                /* enqueue time: the step is a prompt chunk */
     /* tensor parallelism: nq, nkv, F above are this rank's shares, V the full
      * vocabulary of which the LM head holds rows [v0, v0 + V_l) */
     int tp, rank, V_l, v0, Dq;     /* Dq = nq * hd (local) */
@@ -382,7 +383,14 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
     } else if (part == 1) {
         float* scratch = b->scratch + sb_attention_scratch_floats(r0, b->nq, b->hd, b->max_seq);
         L->att_split = norm_splits(b, L, n) && L->op_a->ld16 >= b->Dq;
-        if (L->att_split)
+        if (b->chunk_step)   /* rows: consecutive positions of one sequence */
+            rc |= sb_attention_paged_prefill(att, b->ld_att, qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
+                                             row_pos, row_slot, b->page_table, b->max_pages,
+                                             b->pool, b->kvmap_p, b->n_pages, l, b->kv_dtype,
+                                             b->max_seq, scratch, b->tc_err,
+                                             L->att_split ? L->op_a->hi : NULL,
+                                             L->att_split ? L->op_a->lo : NULL, L->op_a->ld16, s);
+        else if (L->att_split)
             rc |= sb_attention_paged_split(att, b->ld_att, qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
                                            row_pos, row_slot, b->page_table, b->max_pages, b->pool,
                                            b->kvmap_p, b->n_pages, l, b->kv_dtype, b->max_seq,
@@ -455,6 +463,7 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, int chunk, cu
     rc |= sb_step_prologue(slots, toks, n, b->pos, b->page_table, b->max_pages, b->free_stack,
                            b->free_top, b->max_slots, b->max_seq, b->V, b->emb, b->D, b->x,
                            b->ld_x, b->row_pos, b->row_slot, b->status, chunk, s);
+    b->chunk_step = chunk;
     if (!chunk && step_dual(b, n)) {
         /* rows [0, half_rows) on this stream, [half_rows, n) on the second */
         rc |= enqueue_lanes(b, n, s);

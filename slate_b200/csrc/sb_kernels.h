@@ -131,6 +131,23 @@ int sb_attention_mma(int prepare, const void* map, const float* qkv, int ld_qkv,
                      int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
                      const int32_t* page_table, int max_pages, int64_t n_pages, int layer,
                      int nchunk, float* part, int* err, cudaStream_t st);
+/* The causal prefill form of the same (attn_mma.cu): the B rows are
+ * consecutive positions of one sequence (a prompt chunk); tiles of rows share
+ * each streamed K/V page.  Same partial records. */
+int sb_attention_prefill_mma(const void* map, const float* qkv, int ld_qkv, int B, int nq, int nkv,
+                             int hd, const int32_t* row_pos, const int32_t* row_slot,
+                             const int32_t* page_table, int max_pages, int64_t n_pages, int layer,
+                             int nchunk, float* part, int* err, cudaStream_t st);
+/* Paged attention for a prompt chunk (rows = consecutive positions of one
+ * sequence) with the prefill kernel where the KV shape allows it (f16 KV,
+ * a tensor map), else the decode kernels; output as sb_attention_paged_split
+ * (hi may be null: f32 rows only). */
+int sb_attention_paged_prefill(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
+                               int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
+                               const int32_t* page_table, int max_pages, const void* pool,
+                               const void* kvmap, int64_t n_pages, int layer, int kv_dtype,
+                               int max_seq, float* scratch, int* err, void* hi, void* lo, int ld16,
+                               cudaStream_t st);
 
 /* Tensor parallelism.  Per row, the (max logit, global index) pair of this
  * rank's vocabulary slice [v0, v0 + V) -> pairs[B] (8 bytes each); after an

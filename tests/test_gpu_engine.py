@@ -377,6 +377,51 @@ def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
         eng.close()
 
 
+@pytest.mark.parametrize("max_batch", [64, 256])
+def test_prefill_attention_long_prompt(sb, oracle, workdir, max_batch):
+    """The causal prefill attention (f16 KV, head_dim 128, four query heads per
+    kv head -- the 8B head geometry) on prompts that cross the 1024-token
+    context chunks and 16-token pages inside a step, two sequences prefilled
+    one after the other; the last prompt logits and three decoded steps
+    against the oracle's token-by-token sessions (2e-3 of scale, the f16-KV
+    tolerance)."""
+    path = os.path.join(str(workdir), "prefill_hd128.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=1024, ffn_hidden=2048, n_heads=8, n_kv_heads=2,
+                      vocab=1000, max_seq=2048, theta_base=500000.0, q4k=True, seed=23)
+    rng = np.random.default_rng(max_batch)
+    lens = [1300, 1037]
+    prompts = [rng.integers(0, 1000, L).astype(np.int32) for L in lens]
+    eng = make_engine(sb, path, max_batch=max_batch, max_slots=2, kv_dtype=1)
+    slots = [eng.open() for _ in lens]
+    last = []
+    for s, p in zip(slots, prompts):
+        rc, lg = eng.prefill(s, p)
+        assert rc == 0, sb.last_error()
+        last.append(lg)
+    toks = np.array([int(np.argmax(l)) for l in last], np.int32)
+    streams = [[t] for t in toks]
+    dec = []
+    for _ in range(3):
+        rc, out, lg = eng.step(np.array(slots, np.int32), toks, want_logits=True)
+        assert rc == 0, sb.last_error()
+        dec.append(lg)
+        toks = out
+        for i, t in enumerate(out):
+            streams[i].append(int(t))
+    eng.close()
+    m = oracle.open(path)
+    for i, p in enumerate(prompts):
+        feed = np.array(list(p) + streams[i][:-1], np.int32)
+        ref, _ = m.decode_many(feed[None, :])
+        ref = ref[0]
+        scale = np.abs(ref).max()
+        assert np.max(np.abs(last[i] - ref[len(p) - 1])) / scale <= 2e-3, (i, "prefill")
+        for t in range(3):
+            assert np.max(np.abs(dec[t][i] - ref[len(p) + t])) / scale <= 2e-3, (i, t)
+    m.close()
+
+
 @pytest.mark.parametrize("kv_dtype,tol", [(0, 1e-4), (1, 2e-3)])
 @pytest.mark.parametrize("max_batch", [16, 64])
 def test_batched_prefill_matches_oracle(sb, oracle, workdir, kv_dtype, tol, max_batch):
