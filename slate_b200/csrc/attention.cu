@@ -397,6 +397,15 @@ __global__ void epilogue_kernel(const float* logits, int ldl, int V, const int32
     }
 }
 
+// Position advance of a step without an LM head (a prompt chunk whose logits
+// nobody reads): pos[slot] = max(pos[slot], row_pos + 1) for every row when the
+// step was accepted, as the epilogue does beside the argmax.
+__global__ void advance_kernel(const int32_t* row_slot, const int32_t* row_pos, int32_t* pos,
+                               const int32_t* status, int B) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < B && *status == 0 && row_pos[r] >= 0) atomicMax(&pos[row_slot[r]], row_pos[r] + 1);
+}
+
 // Tensor parallelism: each rank holds a vocabulary slice [v0, v0 + V) of the LM
 // head; it reduces its logits to one (max, global index) pair per row, the pairs
 // of all ranks are gathered, and every rank picks the same winner: the larger
@@ -611,6 +620,13 @@ extern "C" int sb_argmax_pairs(const float* logits, int ldl, int V, int B, int v
                                cudaStream_t st) {
     if (B < 1 || V < 1) return -1;
     argmax_pairs_kernel<<<B, 512, 0, st>>>(logits, ldl, V, v0, (sb_vi*)pairs);
+    return 0;
+}
+
+extern "C" int sb_step_advance(const int32_t* row_slot, const int32_t* row_pos, int32_t* pos,
+                               const int32_t* status, int B, cudaStream_t st) {
+    if (B < 1) return -1;
+    advance_kernel<<<(B + 127) / 128, 128, 0, st>>>(row_slot, row_pos, pos, status, B);
     return 0;
 }
 

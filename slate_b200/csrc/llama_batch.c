@@ -129,6 +129,7 @@ struct slate_llama_batch {
     uint64_t* h_rng;
     cudaGraphExec_t* graphs_s;
     cudaGraphExec_t* graphs_c;     /* prompt-chunk steps (repeated slots), per n */
+    cudaGraphExec_t* graphs_p;     /* the same without LM head (logits not wanted) */
 };
 
 /* Rows from which a Q4_K GEMM runs on the tensor cores (below: CUDA cores). */
@@ -451,7 +452,8 @@ static int step_dual(const slate_llama_batch_t* b, int n) {
     return b->dual && n > b->half_rows;
 }
 
-static int enqueue_step(slate_llama_batch_t* b, int n, int sample, int chunk, cudaStream_t s) {
+static int enqueue_step(slate_llama_batch_t* b, int n, int sample, int chunk, int head,
+                        cudaStream_t s) {
     int rc = 0;
     /* cudaGetLastError() below must only see this step's launches: a failure
      * left by an earlier unchecked call on this thread is cleared here (a
@@ -469,6 +471,15 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, int chunk, cu
         rc |= enqueue_lanes(b, n, s);
     } else {
         rc |= enqueue_layers(b, &b->full, n, s);
+    }
+    if (!head) {
+        /* a prompt chunk whose logits nobody reads: positions only */
+        rc |= sb_step_advance(b->row_slot, b->row_pos, b->pos, b->status, n, s);
+        if (rc) {
+            sb_set_error("kernel launch rejected its arguments");
+            return -1;
+        }
+        return sb_cuda_check(cudaGetLastError(), "step launch");
     }
     rc |= step_norm(b, &b->full, b->out_norm, n, s);
     rc |= step_gemm(b, &b->full, &b->lm_head, b->xn, b->ld_x, IN_XN, n, b->logits, b->ld_logits,
@@ -535,13 +546,14 @@ int slate_llama_batch_launches_per_step(const slate_llama_batch_t* b, int n) {
  * ends it with the stochastic sampler instead of the greedy argmax; chunk != 0
  * lets a slot occur several times (a prompt chunk, one lane), otherwise a
  * repeated slot is rejected (status -1) and the rows may run as two lanes. */
-static int run_step_mode(slate_llama_batch_t* b, int n, int sample, int chunk) {
-    if (!b->use_graphs) return enqueue_step(b, n, sample, chunk, b->stream);
-    cudaGraphExec_t* slot = chunk ? &b->graphs_c[n] : sample ? &b->graphs_s[n] : &b->graphs[n];
+static int run_step_mode(slate_llama_batch_t* b, int n, int sample, int chunk, int head) {
+    if (!b->use_graphs) return enqueue_step(b, n, sample, chunk, head, b->stream);
+    cudaGraphExec_t* slot = chunk ? (head ? &b->graphs_c[n] : &b->graphs_p[n])
+                            : sample ? &b->graphs_s[n] : &b->graphs[n];
     if (!*slot) {
         cudaGraph_t g = NULL;
         SB_CU(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
-        int rc = enqueue_step(b, n, sample, chunk, b->stream);
+        int rc = enqueue_step(b, n, sample, chunk, head, b->stream);
         cudaError_t e = cudaStreamEndCapture(b->stream, &g);
         if (rc) {
             if (g) cudaGraphDestroy(g);
@@ -555,7 +567,7 @@ static int run_step_mode(slate_llama_batch_t* b, int n, int sample, int chunk) {
     SB_CU(cudaGraphLaunch(*slot, b->stream));
     return 0;
 }
-static int run_step(slate_llama_batch_t* b, int n) { return run_step_mode(b, n, 0, 0); }
+static int run_step(slate_llama_batch_t* b, int n) { return run_step_mode(b, n, 0, 0, 1); }
 
 /* ---- construction ------------------------------------------------------- */
 
@@ -578,6 +590,11 @@ void slate_llama_batch_free(slate_llama_batch_t* b) {
         for (int i = 0; i <= b->max_batch; ++i)
             if (b->graphs_c[i]) cudaGraphExecDestroy(b->graphs_c[i]);
         free(b->graphs_c);
+    }
+    if (b->graphs_p) {
+        for (int i = 0; i <= b->max_batch; ++i)
+            if (b->graphs_p[i]) cudaGraphExecDestroy(b->graphs_p[i]);
+        free(b->graphs_p);
     }
     if (b->h_samp) cudaFreeHost(b->h_samp);
     if (b->h_rng) cudaFreeHost(b->h_rng);
@@ -964,7 +981,8 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
     b->h_open = (unsigned char*)calloc((size_t)b->max_slots, 1);
     b->graphs = (cudaGraphExec_t*)calloc((size_t)b->max_batch + 1, sizeof(cudaGraphExec_t));
     b->graphs_c = (cudaGraphExec_t*)calloc((size_t)b->max_batch + 1, sizeof(cudaGraphExec_t));
-    if (!b->graphs || !b->graphs_c) {
+    b->graphs_p = (cudaGraphExec_t*)calloc((size_t)b->max_batch + 1, sizeof(cudaGraphExec_t));
+    if (!b->graphs || !b->graphs_c || !b->graphs_p) {
         sb_set_error("out of host memory");
         goto fail;
     }
@@ -1148,7 +1166,11 @@ static int step_host(slate_llama_batch_t* b, const int32_t* slots, int n, const 
     memcpy(h + b->max_batch, tokens, (size_t)n * 4);
     rc = sb_cuda_check(cudaMemcpyAsync(b->d_io, h, (size_t)2 * b->max_batch * 4,
                                        cudaMemcpyHostToDevice, b->stream), "H2D metadata");
-    if (!rc) rc = run_step_mode(b, n, 0, allow_dup);
+    /* a prompt chunk whose logits nobody reads runs without the LM head; tensor-
+     * parallel ranks keep it, so that their collectives stay in step whatever
+     * buffers each rank passes */
+    const int head = !allow_dup || b->tp > 1 || out_tokens || out_logits || last_logits;
+    if (!rc) rc = run_step_mode(b, n, 0, allow_dup, head);
     if (!rc)
         rc = sb_cuda_check(cudaMemcpyAsync(h + 2 * b->max_batch, b->d_io + 2 * b->max_batch,
                                            (size_t)n * 4, cudaMemcpyDeviceToHost, b->stream),
@@ -1245,7 +1267,7 @@ int slate_llama_batch_step_sample(slate_llama_batch_t* b, const int32_t* slots, 
                                                 cudaMemcpyHostToDevice, b->stream), "H2D sampler");
     if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(b->d_rng, b->h_rng, (size_t)n * 8,
                                                 cudaMemcpyHostToDevice, b->stream), "H2D rng");
-    if (!rc) rc = run_step_mode(b, n, 1, 0);
+    if (!rc) rc = run_step_mode(b, n, 1, 0, 1);
     if (!rc)
         rc = sb_cuda_check(cudaMemcpyAsync(h + 2 * b->max_batch, b->d_io + 2 * b->max_batch,
                                            (size_t)n * 4, cudaMemcpyDeviceToHost, b->stream),

@@ -73,6 +73,10 @@ int sb_attention_step(float* out, const float* q, const float* K, const float* V
  * (bad slot) on failure; rows are then left without effect.  dup_ok: a slot
  * may occur several times (a prompt chunk: its k-th occurrence at position
  * pos + k); otherwise a repeated slot is a bad slot (-1). */
+/* Positions of a step without LM head: pos[slot] = max(pos[slot], row_pos + 1)
+ * per row when *status == 0. */
+int sb_step_advance(const int32_t* row_slot, const int32_t* row_pos, int32_t* pos,
+                    const int32_t* status, int B, cudaStream_t st);
 int sb_step_prologue(const int32_t* slots, const int32_t* tokens, int B, int32_t* pos,
                      int32_t* page_table, int max_pages, int32_t* free_stack,
                      int32_t* free_top, int max_slots, int max_seq, int vocab,
