@@ -53,10 +53,10 @@ MODELS = {"8b": dict(cfg=CFG3, metric=METRIC, batch=256, prompt=(128, 4096), per
                       workload="llama3-70b-shape q4k tensor-parallel decode (BASELINE config 5)")}
 # DRAM bytes (read + write) per algorithmic byte of one attn_chunk_mma launch, from
 # an ncu capture of 32 rows at the 8B shape (profiles/attn_chunk_mma_8b_b32.md:
-# 300.40 MB read + 6.63 MB written for 300.74 MB of K/V, q and output).  Traffic
-# scales with the K/V tokens read, so the full launch's traffic is this ratio times
-# its algorithmic bytes.
-ATTN_MMA_TRAFFIC_RATIO = 1.0209
+# 300.39 MB read + 5.20 MB written for 300.74 MB of K/V, q and output, 1024-token
+# chunks).  Traffic scales with the K/V tokens read, so the full launch's traffic is
+# this ratio times its algorithmic bytes.
+ATTN_MMA_TRAFFIC_RATIO = 1.0161
 
 
 def parse():
