@@ -88,7 +88,7 @@ def parse():
                     help="cap every context (profiling captures of the GEMMs on a small device "
                          "footprint; 0 = the config's distribution)")
     ap.add_argument("--e2e-steps", type=int, default=-1,
-                    help="host-API steps for the e2e figure (default max(3, steps/2))")
+                    help="host-API steps for the e2e figure (default: --steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     return ap.parse_args()
@@ -355,6 +355,23 @@ def main():
     replicas = world // tp
     value = n * replicas * args.steps / (tot_ms / 1000.0)
 
+    # end to end through the host-buffer API: H2D slots+tokens, D2H greedy tokens;
+    # right after the timed region, so that both run in the same power state
+    host_tok = d_tok[args.steps & 1 ^ (args.warmup & 1)].cpu().numpy()
+    e2e_steps = args.e2e_steps if args.e2e_steps >= 0 else args.steps
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        rc, host_tok, _ = eng.step(slots, host_tok)
+        assert rc == 0, sb.last_error()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = n * replicas * e2e_steps / e2e_s if e2e_steps else None
+
     # per-kernel timing of the dominant kernels on the same state and stream
     layer = cfg["n_layers"] // 2
     kt = {name: eng.profile(k, n, layer, iters=10) for name, k in
@@ -365,7 +382,7 @@ def main():
     D, L, V = cfg["d_model"], cfg["n_layers"], cfg["vocab"]
     hd = D // cfg["n_heads"]
     nq, nkv, F = cfg["n_heads"] // tp, cfg["n_kv_heads"] // tp, cfg["ffn_hidden"] // tp
-    ctx_now = ctx + total_steps                        # contexts seen by the profiled launch
+    ctx_now = ctx + total_steps + e2e_steps            # contexts seen by the profiled launch
     attn_bytes = float(ctx_now.sum()) * 2 * nkv * hd * esz + n * nq * hd * 4 * 3
     q4k = 144 / 256
     w_layer = (D * (nq + 2 * nkv) * hd + nq * hd * D + 3 * D * F) * q4k
@@ -384,21 +401,6 @@ def main():
         traffic = ATTN_MMA_TRAFFIC_RATIO * attn_bytes
     step_s = tot_ms / 1000.0 / args.steps
 
-    # end to end through the host-buffer API: H2D slots+tokens, D2H greedy tokens
-    host_tok = d_tok[args.steps & 1 ^ (args.warmup & 1)].cpu().numpy()
-    e2e_steps = args.e2e_steps if args.e2e_steps >= 0 else max(3, args.steps // 2)
-    torch.cuda.synchronize()
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        rc, host_tok, _ = eng.step(slots, host_tok)
-        assert rc == 0, sb.last_error()
-    e2e_s = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = n * replicas * e2e_steps / e2e_s if e2e_steps else None
 
     # prompt prefill through slate_llama_batch_prefill (chunks of max_batch
     # prompt rows with the causal prefill attention): one sequence's slot is
