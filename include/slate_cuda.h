@@ -101,8 +101,11 @@ typedef struct slate_backend_cuda {
      * passes 1 = f16 x f16 operands, 3 = f16 hi/lo split of both operands
      * (f32-level products), both for 16 <= B; 2 = exact f16 weights (sc*q)
      * against x as f16 hi/lo with the Q4_K block scales applied per
-     * super-block (f32-level products), any B >= 1.  M % 128 == 0,
-     * K % 256 == 0.
+     * super-block (f32-level products), any B >= 1; 4 = the small-batch
+     * kernel: the 4-bit quants (exact in f16) against x as f16 hi/lo through
+     * mma.sync, per 32-element sub-block d*sc*sum(q*x) - dmin*m*sum(x) in f32
+     * (the reference's own structure, util/quant.c:210-304), 1 <= B <= 16.
+     * M % 128 == 0, K % 256 == 0.
      * Synchronous: returns -5 if the device reported a pipeline timeout. */
     int (*matmul_q4k_batch_tc)(float* Y, const void* A_q4k, const float* X, int B, int M, int K,
                                int passes);

@@ -2,7 +2,7 @@
 // products on the tensor cores (sm_100a warp-level MMA, f16 x f16 -> f32).
 //
 // Same work split and partial-record format as attn_chunk (attn_paged.cu):
-// one CTA per (row, kv head, SB_ATTN_CHUNK-token chunk), a producer warp and four
+// one CTA per (row, kv head, chunk of ct tokens), a producer warp and four
 // consumer warps that take pages round-robin.  Differences:
 //   * each page's K and V blocks ([16 tokens][head_dim] f16) arrive by tiled
 //     TMA in 64-column boxes with the 128-byte swizzle, so ldmatrix reads them
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), 3) attn_chunk_mma(
     const __grid_constant__ CUtensorMap kvmap, const float* __restrict__ qkv, int ld_qkv, int B,
     int nq, int nkv, const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ page_table, int max_pages, int64_t n_pages, int layer,
-    int nchunk_max, float* __restrict__ part, int* err) {
+    int nchunk_max, int ct, float* __restrict__ part, int* err) {
     static_assert(HD % 64 == 0 && G <= 8, "head_dim multiple of 64, at most 8 heads per group");
     constexpr int BLK = 16 * HD * 2;          // one K or V block, bytes
     constexpr int KC = HD / 16;               // 16-wide k chunks of head_dim
@@ -145,9 +145,9 @@ __global__ void __launch_bounds__(32 * (NW + 1), 3) attn_chunk_mma(
     if (b >= B) return;
     const int pos = row_pos[b];
     if (pos < 0) return;
-    const int ctx = pos + 1, t0 = chunk * SB_ATTN_CHUNK;
+    const int ctx = pos + 1, t0 = chunk * ct;
     if (t0 >= ctx) return;
-    const int t1 = min(ctx, t0 + SB_ATTN_CHUNK);
+    const int t1 = min(ctx, t0 + ct);
     const int npg = (t1 - t0 + 15) / 16;
     const int slot = row_slot[b];
 
@@ -582,7 +582,7 @@ size_t smem_bytes() {
 template <int HD, int G>
 int launch(int prepare, const void* map, const float* qkv, int ld_qkv, int B, int nq, int nkv,
            const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
-           int max_pages, int64_t n_pages, int layer, int nchunk, float* part, int* err,
+           int max_pages, int64_t n_pages, int layer, int nchunk, int ct, float* part, int* err,
            cudaStream_t st) {
     if (prepare) {
         cudaFuncSetAttribute(attn_chunk_mma<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -595,7 +595,7 @@ int launch(int prepare, const void* map, const float* qkv, int ld_qkv, int B, in
     memcpy(&m, map, sizeof m);
     return sb_launch_pdl(attn_chunk_mma<HD, G>, dim3((unsigned)ctas), dim3(32 * (NW + 1)),
                          smem_bytes<HD, G>(), st, m, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot,
-                         page_table, max_pages, n_pages, layer, nchunk, part, err) == cudaSuccess
+                         page_table, max_pages, n_pages, layer, nchunk, ct, part, err) == cudaSuccess
                ? 0
                : -1;
 }
@@ -626,7 +626,7 @@ template <int HD>
 int launch_hd(int prepare, int prefill, int G, const void* map, const float* qkv, int ld_qkv,
               int B, int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
               const int32_t* page_table, int max_pages, int64_t n_pages, int layer, int nchunk,
-              float* part, int* err, cudaStream_t st) {
+              int ct, float* part, int* err, cudaStream_t st) {
     switch (G) {
 #define CASE(g)                                                                                 \
     case g:                                                                                     \
@@ -634,8 +634,8 @@ int launch_hd(int prepare, int prefill, int G, const void* map, const float* qkv
                                                row_slot, page_table, max_pages, n_pages, layer, \
                                                nchunk, part, err, st)                           \
                        : launch<HD, g>(prepare, map, qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, \
-                                       page_table, max_pages, n_pages, layer, nchunk, part, err, \
-                                       st);
+                                       page_table, max_pages, n_pages, layer, nchunk, ct, part,  \
+                                       err, st);
         CASE(1) CASE(2) CASE(4) CASE(8)
 #undef CASE
     }
@@ -686,18 +686,18 @@ extern "C" int sb_attention_make_map(void* map, void* pool, int64_t n_pages, int
 static int attention_mma(int prepare, int prefill, const void* map, const float* qkv, int ld_qkv,
                          int B, int nq, int nkv, int hd, const int32_t* row_pos,
                          const int32_t* row_slot, const int32_t* page_table, int max_pages,
-                         int64_t n_pages, int layer, int nchunk, float* part, int* err,
+                         int64_t n_pages, int layer, int nchunk, int ct, float* part, int* err,
                          cudaStream_t st) {
     const int G = nq / nkv;
     switch (hd) {
         case 64:
             return launch_hd<64>(prepare, prefill, G, map, qkv, ld_qkv, B, nq, nkv, row_pos,
-                                 row_slot, page_table, max_pages, n_pages, layer, nchunk, part,
-                                 err, st);
+                                 row_slot, page_table, max_pages, n_pages, layer, nchunk, ct,
+                                 part, err, st);
         case 128:
             return launch_hd<128>(prepare, prefill, G, map, qkv, ld_qkv, B, nq, nkv, row_pos,
-                                  row_slot, page_table, max_pages, n_pages, layer, nchunk, part,
-                                  err, st);
+                                  row_slot, page_table, max_pages, n_pages, layer, nchunk, ct,
+                                  part, err, st);
     }
     return -1;
 }
@@ -705,15 +705,16 @@ static int attention_mma(int prepare, int prefill, const void* map, const float*
 extern "C" int sb_attention_mma(int prepare, const void* map, const float* qkv, int ld_qkv, int B,
                                 int nq, int nkv, int hd, const int32_t* row_pos,
                                 const int32_t* row_slot, const int32_t* page_table, int max_pages,
-                                int64_t n_pages, int layer, int nchunk, float* part, int* err,
-                                cudaStream_t st) {
+                                int64_t n_pages, int layer, int nchunk, int ct, float* part,
+                                int* err, cudaStream_t st) {
     if (prepare)   // both kernels' shared-memory attributes
         return attention_mma(1, 0, nullptr, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr,
-                             0, 0, 0, 0, nullptr, nullptr, 0) |
+                             0, 0, 0, 0, 0, nullptr, nullptr, 0) |
                attention_mma(1, 1, nullptr, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr,
-                             0, 0, 0, 0, nullptr, nullptr, 0);
+                             0, 0, 0, 0, 0, nullptr, nullptr, 0);
+    if (ct < 16 || ct > SB_ATTN_CHUNK || ct % 16) return -1;
     return attention_mma(0, 0, map, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
-                         max_pages, n_pages, layer, nchunk, part, err, st);
+                         max_pages, n_pages, layer, nchunk, ct, part, err, st);
 }
 
 extern "C" int sb_attention_prefill_mma(const void* map, const float* qkv, int ld_qkv, int B,
@@ -722,5 +723,5 @@ extern "C" int sb_attention_prefill_mma(const void* map, const float* qkv, int l
                                         int max_pages, int64_t n_pages, int layer, int nchunk,
                                         float* part, int* err, cudaStream_t st) {
     return attention_mma(0, 1, map, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
-                         max_pages, n_pages, layer, nchunk, part, err, st);
+                         max_pages, n_pages, layer, nchunk, SB_ATTN_CHUNK, part, err, st);
 }

@@ -70,11 +70,16 @@ extern "C" int slate_cuda_attention_paged_gqa_noalloc(float* out, const float* q
         return -1;
     }
     const int max_seq = max_pages * 16;
-    const size_t need = sb_attention_scratch_floats(B, nq, hd, max_seq);
+    // the engine's chunk for B rows, lengthened until the partials fit
+    int ct = sb_attention_chunk_tokens(B);
+    while (ct < SB_ATTN_CHUNK &&
+           sb_attention_scratch_rows(B, nq, hd, max_seq, ct) > (size_t)SLATE_CUDA_NOALLOC_SCRATCH_FLOATS)
+        ct *= 2;
+    const size_t need = sb_attention_scratch_rows(B, nq, hd, max_seq, ct);
     if (need > (size_t)SLATE_CUDA_NOALLOC_SCRATCH_FLOATS) {
         sb_set_error("attention (no-alloc): %zu scratch floats needed (B %d x heads %d x %d chunks "
                      "x %d), limit %zu",
-                     need, B, nq, (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK, hd + 2,
+                     need, B, nq, (max_seq + ct - 1) / ct, hd + 2,
                      (size_t)SLATE_CUDA_NOALLOC_SCRATCH_FLOATS);
         return -1;
     }
@@ -98,8 +103,8 @@ extern "C" int slate_cuda_attention_paged_gqa_noalloc(float* out, const float* q
         mapp = map;
     }
     if (sb_attention_paged(out, nq * hd, q, nq * hd, B, nq, nkv, hd, pos, row_slot, page_table,
-                           max_pages, kv_pool, mapp, n_pages, layer, kv_dtype, max_seq, scr, err,
-                           st)) {
+                           max_pages, kv_pool, mapp, n_pages, layer, kv_dtype, max_seq, ct, scr,
+                           err, st)) {
         sb_set_error("attention (no-alloc): unsupported shape");
         return -1;
     }

@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     const float* __restrict__ qkv, int ld_qkv, int B, int nq, int nkv,
     const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ page_table, int max_pages, const KT* __restrict__ pool,
-    int64_t n_pages, int layer, int nchunk_max, float* __restrict__ part, int* err) {
+    int64_t n_pages, int layer, int nchunk_max, int ct, float* __restrict__ part, int* err) {
     using S = AttnShape<HD, G, KT>;
     constexpr int DPL = S::DPL, STAGES = S::STAGES, TOK = S::TOK, NV = S::NV, VPL = S::VPL,
                   SH = S::SH, GL = S::GL;
@@ -182,9 +182,9 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     if (b >= B) return;
     const int pos = row_pos[b];
     if (pos < 0) return;
-    const int ctx = pos + 1, t0 = chunk * SB_ATTN_CHUNK;
+    const int ctx = pos + 1, t0 = chunk * ct;
     if (t0 >= ctx) return;
-    const int t1 = min(ctx, t0 + SB_ATTN_CHUNK);
+    const int t1 = min(ctx, t0 + ct);
     const int npg = (t1 - t0 + 15) / 16;
     const int slot = row_slot[b];
 
@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
 template <int HD>
 __global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ part, int B, int nq,
                                                     const int32_t* __restrict__ row_pos,
-                                                    int nchunk_max, float* __restrict__ att,
+                                                    int nchunk_max, int ct, float* __restrict__ att,
                                                     int ld_att, __half* __restrict__ hi,
                                                     __half* __restrict__ lo, int ld16) {
     sb_grid_release();   // the Wo GEMM may start its set-up
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ pa
     if (b >= B) return;
     const int pos = row_pos[b];
     if (pos < 0) return;
-    const int nch = (pos + SB_ATTN_CHUNK) / SB_ATTN_CHUNK;  // ceil((pos+1)/CHUNK)
+    const int nch = (pos + ct) / ct;                      // ceil((pos + 1) / ct)
     const float* rec0 = part + ((size_t)b * nq + hq) * nchunk_max * (HD + 2);
     float M = -INFINITY;
     for (int c = 0; c < nch; ++c) M = fmaxf(M, rec0[(size_t)c * (HD + 2)]);
@@ -431,7 +431,7 @@ struct HiLo {
 template <int HD, int G, typename KT>
 int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
              int nkv, const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
-             int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk,
+             int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk, int ct,
              float* scratch, int* err, HiLo hl, cudaStream_t st) {
     using S = AttnShape<HD, G, KT>;
     if (prepare) {
@@ -444,11 +444,11 @@ int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
     const long ctas = (long)B * nkv * nchunk;
     attn_chunk<HD, G, KT><<<(unsigned)ctas, 32 * (NW + 1), S::SMEM, st>>>(
         qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, (const KT*)pool, n_pages,
-        layer, nchunk, scratch, err);
+        layer, nchunk, ct, scratch, err);
     const long cw = (long)B * nq;
     return sb_launch_pdl(attn_combine<HD>, dim3((unsigned)((cw + 3) / 4)), dim3(128), 0, st,
-                         (const float*)scratch, B, nq, row_pos, nchunk, att, ld_att, hl.hi, hl.lo,
-                         hl.ld16) == cudaSuccess
+                         (const float*)scratch, B, nq, row_pos, nchunk, ct, att, ld_att, hl.hi,
+                         hl.lo, hl.ld16) == cudaSuccess
                ? 0
                : -1;
 }
@@ -457,13 +457,13 @@ template <int HD, typename KT>
 int launch_hd(int prepare, int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B,
               int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
               const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
-              int layer, int nchunk, float* scratch, int* err, HiLo hl, cudaStream_t st) {
+              int layer, int nchunk, int ct, float* scratch, int* err, HiLo hl, cudaStream_t st) {
     switch (G) {
 #define CASE(g)                                                                                  \
     case g:                                                                                      \
         return launch_g<HD, g, KT>(prepare, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
                                    row_slot, page_table, max_pages, pool, n_pages, layer,        \
-                                   nchunk, scratch, err, hl, st);
+                                   nchunk, ct, scratch, err, hl, st);
         CASE(1) CASE(2) CASE(4) CASE(8)
 #undef CASE
     }
@@ -474,13 +474,13 @@ template <typename KT>
 int launch_kt(int prepare, int hd, int G, float* att, int ld_att, const float* qkv, int ld_qkv,
               int B, int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
               const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
-              int layer, int nchunk, float* scratch, int* err, HiLo hl, cudaStream_t st) {
+              int layer, int nchunk, int ct, float* scratch, int* err, HiLo hl, cudaStream_t st) {
     switch (hd) {
 #define CASE(h)                                                                                  \
     case h:                                                                                      \
         return launch_hd<h, KT>(prepare, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
                                 row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,   \
-                                scratch, err, hl, st);
+                                ct, scratch, err, hl, st);
         CASE(8) CASE(16) CASE(32) CASE(64) CASE(128)
 #undef CASE
     }
@@ -488,17 +488,17 @@ int launch_kt(int prepare, int hd, int G, float* att, int ld_att, const float* q
 }
 
 int combine(int hd, const float* scratch, int B, int nq, const int32_t* row_pos, int nchunk,
-            float* att, int ld_att, HiLo hl, cudaStream_t st) {
+            int ct, float* att, int ld_att, HiLo hl, cudaStream_t st) {
     const unsigned grid = (unsigned)(((long)B * nq + 3) / 4);
     switch (hd) {
         case 64:
             return sb_launch_pdl(attn_combine<64>, dim3(grid), dim3(128), 0, st, scratch, B, nq,
-                                 row_pos, nchunk, att, ld_att, hl.hi, hl.lo, hl.ld16) == cudaSuccess
+                                 row_pos, nchunk, ct, att, ld_att, hl.hi, hl.lo, hl.ld16) == cudaSuccess
                        ? 0
                        : -1;
         case 128:
             return sb_launch_pdl(attn_combine<128>, dim3(grid), dim3(128), 0, st, scratch, B, nq,
-                                 row_pos, nchunk, att, ld_att, hl.hi, hl.lo, hl.ld16) == cudaSuccess
+                                 row_pos, nchunk, ct, att, ld_att, hl.hi, hl.lo, hl.ld16) == cudaSuccess
                        ? 0
                        : -1;
     }
@@ -508,53 +508,69 @@ int combine(int hd, const float* scratch, int B, int nq, const int32_t* row_pos,
 int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
              int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
              const int32_t* page_table, int max_pages, const void* pool, const void* kvmap,
-             int64_t n_pages, int layer, int kv_dtype, int max_seq, float* scratch, int* err,
-             HiLo hl, cudaStream_t st) {
+             int64_t n_pages, int layer, int kv_dtype, int max_seq, int ct, float* scratch,
+             int* err, HiLo hl, cudaStream_t st) {
     if (nkv < 1 || nq % nkv) return -1;
     const int G = nq / nkv;
-    const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
+    if (ct <= 0) ct = sb_attention_chunk_tokens(B);
+    if (ct < 16 || ct > SB_ATTN_CHUNK || ct % 16) return -1;
+    const int nchunk = (max_seq + ct - 1) / ct;
     if (sb_attention_mma_supported(nq, nkv, hd, kv_dtype)) {
         if (prepare) {
             const int rc = sb_attention_mma(1, nullptr, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr,
-                                            nullptr, 0, 0, 0, 0, nullptr, nullptr, 0);
+                                            nullptr, 0, 0, 0, 0, 0, nullptr, nullptr, 0);
             if (rc) return rc;          // the CUDA-core kernel is prepared too (calls without a map)
         } else if (kvmap) {
             const int rc = sb_attention_mma(0, kvmap, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot,
-                                            page_table, max_pages, n_pages, layer, nchunk, scratch,
-                                            err, st);
-            return rc ? rc : combine(hd, scratch, B, nq, row_pos, nchunk, att, ld_att, hl, st);
+                                            page_table, max_pages, n_pages, layer, nchunk, ct,
+                                            scratch, err, st);
+            return rc ? rc : combine(hd, scratch, B, nq, row_pos, nchunk, ct, att, ld_att, hl, st);
         }
     }
     return kv_dtype == SLATE_KV_F16
                ? launch_kt<__half>(prepare, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
                                    row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,
-                                   scratch, err, hl, st)
+                                   ct, scratch, err, hl, st)
                : launch_kt<float>(prepare, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
                                   row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,
-                                  scratch, err, hl, st);
+                                  ct, scratch, err, hl, st);
 }
 
 }  // namespace
 
+extern "C" int sb_attention_chunk_tokens(int B) {
+    return B >= 64 ? SB_ATTN_CHUNK : B >= 32 ? SB_ATTN_CHUNK / 2 : B >= 16 ? SB_ATTN_CHUNK / 4
+                                                                          : SB_ATTN_CHUNK / 8;
+}
+
+extern "C" size_t sb_attention_scratch_rows(int B, int nq, int hd, int max_seq, int ct) {
+    return (size_t)B * nq * ((max_seq + ct - 1) / ct) * (hd + 2);
+}
+
 extern "C" size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int max_seq) {
-    const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
-    return (size_t)max_batch * nq * nchunk * (hd + 2);
+    size_t best = 0;
+    for (int B = 1; B <= max_batch; ++B) {
+        const size_t f = sb_attention_scratch_rows(B, nq, hd, max_seq, sb_attention_chunk_tokens(B));
+        if (f > best) best = f;
+    }
+    return best;
 }
 
 extern "C" int sb_attention_prepare(int nq, int nkv, int hd, int kv_dtype) {
     return dispatch(1, nullptr, 0, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr, 0,
-                    nullptr, nullptr, 0, 0, kv_dtype, 0, nullptr, nullptr, HiLo{nullptr, nullptr, 0}, 0);
+                    nullptr, nullptr, 0, 0, kv_dtype, 0, SB_ATTN_CHUNK, nullptr, nullptr,
+                    HiLo{nullptr, nullptr, 0}, 0);
 }
 
 extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B,
                                   int nq, int nkv, int hd, const int32_t* row_pos,
                                   const int32_t* row_slot, const int32_t* page_table,
                                   int max_pages, const void* pool, const void* kvmap,
-                                  int64_t n_pages, int layer, int kv_dtype, int max_seq,
+                                  int64_t n_pages, int layer, int kv_dtype, int max_seq, int ct,
                                   float* scratch, int* err, cudaStream_t st) {
     if (B < 1 || !err) return -1;
     return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
-                    max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, scratch, err,
+                    max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, ct, scratch, err,
                     HiLo{nullptr, nullptr, 0}, st);
 }
 
@@ -569,13 +585,14 @@ extern "C" int sb_attention_paged_prefill(float* att, int ld_att, const float* q
     const HiLo hl{(__half*)hi, (__half*)lo, hi ? ld16 : 0};
     if (!kvmap || !sb_attention_mma_supported(nq, nkv, hd, kv_dtype))
         return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
-                        max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, scratch, err, hl,
-                        st);
+                        max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, 0, scratch, err,
+                        hl, st);
     const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
     const int rc = sb_attention_prefill_mma(kvmap, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot,
                                             page_table, max_pages, n_pages, layer, nchunk, scratch,
                                             err, st);
-    return rc ? rc : combine(hd, scratch, B, nq, row_pos, nchunk, att, ld_att, hl, st);
+    return rc ? rc : combine(hd, scratch, B, nq, row_pos, nchunk, SB_ATTN_CHUNK, att, ld_att, hl,
+                             st);
 }
 
 extern "C" int sb_attention_paged_split(float* att, int ld_att, const float* qkv, int ld_qkv, int B,
@@ -587,6 +604,6 @@ extern "C" int sb_attention_paged_split(float* att, int ld_att, const float* qkv
                                         cudaStream_t st) {
     if (B < 1 || !err || !hi || ld16 < nq * hd) return -1;
     return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
-                    max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, scratch, err,
+                    max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, 0, scratch, err,
                     HiLo{(__half*)hi, (__half*)lo, ld16}, st);
 }

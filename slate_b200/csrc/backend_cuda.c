@@ -168,7 +168,7 @@ static int be_attention_paged(float* out, const float* q, const int32_t* pos,
     if (!rc)
         rc = fin(sb_attention_paged(out, nq * hd, q, nq * hd, B, nq, nkv, hd, pos, row_slot,
                                     page_table, max_pages, pool, mapp, n_pages, layer, kv_dtype,
-                                    max_seq, scr, err, g_stream),
+                                    max_seq, 0, scr, err, g_stream),
                  "attention_paged_gqa");
     if (!rc) rc = sb_cuda_check(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, g_stream), "err");
     if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "attention_paged_gqa");
@@ -247,8 +247,32 @@ static int be_matmul_q4k_sk(float* Y, const void* A, const float* X, int B, int 
     return rc;
 }
 
+/* passes 4: the small-batch kernel (gemm_mv.cu), 1 <= B <= 16 */
+static int be_matmul_q4k_mv(float* Y, const void* A, const float* X, int B, int M, int K) {
+    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0};
+    const size_t wsf = sb_mv_ws_floats(M, K);
+    void *ws = NULL, *cnt = NULL;
+    int rc = sb_cuda_check(cudaMallocAsync(&ws, wsf * 4 + 16, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMallocAsync(&cnt, (size_t)M / 128 * 4, g_stream), "alloc");
+    if (!rc) rc = sb_cuda_check(cudaMemsetAsync(cnt, 0, (size_t)M / 128 * 4, g_stream), "memset");
+    if (!rc) rc = fin(sb_mv_gemm(&W, X, K, B, Y, M, SB_EPI_STORE, (float*)ws, (int*)cnt, g_stream),
+                      "matmul_q4k_batch_tc");
+    if (!rc) rc = sb_cuda_check(cudaStreamSynchronize(g_stream), "matmul_q4k_batch_tc");
+    if (ws) cudaFreeAsync(ws, g_stream);
+    if (cnt) cudaFreeAsync(cnt, g_stream);
+    return rc;
+}
+
 static int be_matmul_q4k_tc(float* Y, const void* A, const float* X, int B, int M, int K,
                             int passes) {
+    if (passes == 4) {
+        if (M % 128 || K % 256 || B < 1 || B > SB_MV_MAX_ROWS) {
+            sb_set_error("matmul_q4k_batch_tc: passes 4 takes 1 <= B <= %d, M %% 128 == 0",
+                         SB_MV_MAX_ROWS);
+            return -1;
+        }
+        return be_matmul_q4k_mv(Y, A, X, B, M, K);
+    }
     if (passes == 2 && M % 128 == 0 && K % 256 == 0 && B >= 1 && K % 4 == 0)
         return be_matmul_q4k_exact(Y, A, X, B, M, K);
     {

@@ -1,0 +1,417 @@
+// gemm_mv.cu -- Q4_K weight GEMM for small batches (1..16 activation rows):
+// the weights stream from HBM once, the tensor cores (mma.sync m16n8k16) do
+// the multiply-adds.
+//
+//   Y[n][m] (op)= sum_k X[n][k] * W[m][k]       n <= 16; op: store, residual
+//                                               add, or SiLU(gate) * up
+//
+// Numerics follow the structure of the reference's Q4_K dot product
+// (src/util/quant.c:210-304): per 32-element sub-block j of a super-block it
+// forms sum(q * x) and sum(x) and combines them as
+//     d * sc_j * sum(q * x) - dmin * m_j * sum(x).
+// The 4-bit quants q (0..15) are exact in f16, so the tensor cores form
+// sum(q * x) per sub-block with x as an f16 hi + lo pair (two MMAs; every
+// product q * hi and q * lo is exact, the sums are f32), and the CUDA cores
+// apply d * sc_j (exact in f32) and subtract dmin * m_j * sum(x) in f32.  No
+// weight is dequantised to floating point, so the per-weight work is a mask,
+// an OR and one packed f16 subtraction per two weights.  Each activation row
+// is scaled by a power of two per K chunk (largest |x| just below 2^14) before
+// the split, so small activations keep their low bits in the lo half; the
+// scale is divided out exactly at the end.
+//
+// Work decomposition: a CTA (4 warps) owns 128 weight rows and a K chunk of
+// KC columns (a multiple of 256); a warp owns 32 rows (two m16 tiles) and
+// walks the chunk's super-blocks, holding the next super-block's quants in
+// registers while it computes the current one.  Lane (g, t) of a warp loads
+// 32-bit word t of every sub-block of rows g and g + 8 of each tile: the low
+// nibbles of that word are the lane's four A elements of the sub-block's
+// first MMA, the high nibbles those of its second, so every MMA covers
+// exactly one sub-block (the k order inside a sub-block is permuted the same
+// way in A and in the staged x fragments).  The header of each row's
+// super-block is decoded once per warp (lane l: row l) into shared memory.
+// With more than one K chunk, each CTA writes its 128 x n partial sums to a
+// workspace and the last CTA of the row block (an atomic counter; no CTA
+// waits on another) sums the chunks in chunk order -- results do not depend
+// on timing -- and applies the epilogue.
+//
+// The weights of the first super-block are requested before the grid waits
+// for the previous kernel of the stream (programmatic dependent launch), so
+// the weight stream starts while the producer of X finishes.
+#include <cuda_fp16.h>
+
+#include "sb_internal.h"
+#include "sb_kernels.h"
+#include "sb_pdl.h"
+
+namespace {
+
+constexpr int WARPS = 4;
+constexpr int NTHREADS = 32 * WARPS;
+constexpr int ROWS = 32 * WARPS;        // weight rows per CTA
+constexpr int TROW = 132;               // output tile row stride (floats): conflict-free stores
+constexpr int SROW = 9;                 // scale scratch row stride (float2): conflict-free loads
+constexpr int MAX_KC = 2048;
+
+struct MvArgs {
+    const unsigned char* W;
+    int M, K;
+    const float* X;
+    int ldx, n;
+    float* Y;
+    int ldy;
+    float* ws;
+    int* cnt;
+    int KC, nkc;
+};
+
+__device__ __forceinline__ uint32_t ldg32(const unsigned char* p) {
+    return __ldg(reinterpret_cast<const unsigned int*>(p));
+}
+
+// (1024 + n) with n in bits 0-3 / 16-19 -> exact n in both halves.
+__device__ __forceinline__ uint32_t nib_lo(uint32_t q) {
+    uint32_t h = (q & 0x000F000Fu) | 0x64006400u;
+    __half2 r = __hsub2(*reinterpret_cast<__half2*>(&h), __half2half2(__ushort_as_half(0x6400)));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+// (1024 + 16 n) with n in bits 4-7 / 20-23 -> (1024 + 16 n) / 16 - 64 = n, exact.
+__device__ __forceinline__ uint32_t nib_hi(uint32_t q) {
+    uint32_t h = (q & 0x00F000F0u) | 0x64006400u;
+    __half2 r = __hfma2(*reinterpret_cast<__half2*>(&h), __half2half2(__ushort_as_half(0x2C00)),
+                        __half2half2(__ushort_as_half(0xD400)));   // x * 1/16 - 64
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float byte_f(uint32_t w, int i) { return (float)((w >> (8 * i)) & 0xffu); }
+
+// Effective scale d*sc_j and min dmin*m_j of the 8 sub-blocks of a super-block
+// header (f16 d, f16 dmin, 12 packed 6-bit scale / min bytes;
+// src/util/quant.c:157-166).
+__device__ __forceinline__ void decode_header(uint4 h, float2* out) {
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffffu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const uint32_t sc03 = h.y & 0x3F3F3F3Fu, m03 = h.z & 0x3F3F3F3Fu;
+    const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        out[i] = make_float2(d * byte_f(sc03, i), dmin * byte_f(m03, i));
+        out[4 + i] = make_float2(d * byte_f(sc47, i), dmin * byte_f(m47, i));
+    }
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+// Quants (one word per sub-block) of rows g and g + 8 of both m16 tiles, and
+// the header of row `lane` of the warp, for one super-block.
+struct Quants {
+    uint32_t q[2][2][8];   // [tile][row g / g + 8][sub-block]
+    uint4 hdr;
+};
+
+__device__ __forceinline__ void load_quants(Quants& Q, const unsigned char* wrow0, size_t rb,
+                                            int kb, int g, int t, int lane) {
+    const unsigned char* blk = wrow0 + (size_t)kb * 144;
+#pragma unroll
+    for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const unsigned char* p = blk + (size_t)(16 * rt + 8 * h + g) * rb + 16 + 4 * t;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) Q.q[rt][h][j] = ldg32(p + 16 * j);
+        }
+    Q.hdr = __ldg(reinterpret_cast<const uint4*>(blk + (size_t)lane * rb));
+}
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int KC = a.KC;
+    const int nsub = KC / 32;
+    uint4* xf = reinterpret_cast<uint4*>(smem);                               // [nsub][2][NT][32]
+    float* xs = reinterpret_cast<float*>(smem + (size_t)nsub * 2 * NT * 512);  // [nsub][8 NT]
+    float2* sc = reinterpret_cast<float2*>(xs + nsub * 8 * NT);               // [WARPS][32][SROW]
+    float* cs = reinterpret_cast<float*>(sc + WARPS * 32 * SROW);             // [8 NT] x scale
+    float* tile = reinterpret_cast<float*>(smem);                             // [8 NT][TROW], after the loop
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int rb = blockIdx.x, kc = blockIdx.y;
+    const int row0 = rb * ROWS;
+    const int k0 = kc * KC;
+    const size_t rbytes = (size_t)(a.K / 256) * 144;
+    const unsigned char* wrow0 = a.W + (size_t)(row0 + 32 * warp) * rbytes;
+    const int kb0 = k0 / 256, nsb = KC / 256;
+
+    // weights of the first super-block: independent of the previous kernel
+    Quants cur;
+    load_quants(cur, wrow0, rbytes, kb0, g, t, lane);
+    sb_grid_release();
+    sb_grid_wait();
+
+    // ---- activations of the chunk: per-row power-of-two scale, f16 hi/lo
+    // fragments in MMA order, sub-block sums
+    for (int c = warp; c < 8 * NT; c += WARPS) {
+        float m = 0.f;
+        if (c < a.n) {
+            const float4* xr = reinterpret_cast<const float4*>(a.X + (size_t)c * a.ldx + k0);
+            for (int i = lane; i < KC / 4; i += 32) {
+                float4 v = xr[i];
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) {
+            int e = 0;
+            const bool ok = m > 0.f && m <= 3.0e38f;
+            if (ok) {
+                frexpf(m, &e);                       // m < 2^e
+                e = max(-100, min(100, e));
+            }
+            cs[c] = ok ? ldexpf(1.0f, 14 - e) : 1.0f;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < nsub * 2 * NT * 32; i += NTHREADS) {
+        const int ln = i & 31, nt = (i >> 5) % NT, hs = (i >> 5) / NT;   // hs = 2 * sub + half
+        const int c = nt * 8 + (ln >> 2);
+        uint4 f = make_uint4(0u, 0u, 0u, 0u);
+        if (c < a.n) {
+            const float s = cs[c];
+            float4 v = *reinterpret_cast<const float4*>(a.X + (size_t)c * a.ldx + k0 + 16 * hs +
+                                                        4 * (ln & 3));
+            v.x *= s; v.y *= s; v.z *= s; v.w *= s;
+            // k slots (2t, 2t+1) <- elements (0, 2); (2t+8, 2t+9) <- (1, 3)
+            __half2 h02 = __floats2half2_rn(v.x, v.z), h13 = __floats2half2_rn(v.y, v.w);
+            float2 r02 = __half22float2(h02), r13 = __half22float2(h13);
+            __half2 l02 = __floats2half2_rn(v.x - r02.x, v.z - r02.y);
+            __half2 l13 = __floats2half2_rn(v.y - r13.x, v.w - r13.y);
+            f.x = *reinterpret_cast<uint32_t*>(&h02);
+            f.y = *reinterpret_cast<uint32_t*>(&h13);
+            f.z = *reinterpret_cast<uint32_t*>(&l02);
+            f.w = *reinterpret_cast<uint32_t*>(&l13);
+        }
+        xf[i] = f;
+    }
+    for (int i = tid; i < nsub * 8 * NT; i += NTHREADS) {
+        const int j = i / (8 * NT), c = i % (8 * NT);
+        float sum = 0.f;
+        if (c < a.n) {
+            const float s = cs[c];
+            const float4* xr = reinterpret_cast<const float4*>(a.X + (size_t)c * a.ldx + k0 + 32 * j);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                float4 v = xr[q];
+                sum += v.x * s;
+                sum += v.y * s;
+                sum += v.z * s;
+                sum += v.w * s;
+            }
+        }
+        xs[i] = sum;
+    }
+    __syncthreads();
+
+    float acc[2][NT][4];
+#pragma unroll
+    for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[rt][nt][c] = 0.f;
+
+    float2* wsc = sc + warp * 32 * SROW;
+    for (int sb = 0; sb < nsb; ++sb) {
+        Quants nxt;
+        if (sb + 1 < nsb) load_quants(nxt, wrow0, rbytes, kb0 + sb + 1, g, t, lane);
+        float2 dm[8];
+        decode_header(cur.hdr, dm);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wsc[lane * SROW + j] = dm[j];
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int sub = sb * 8 + j;
+            uint4 xb[2][NT];
+            float2 xsum[NT];
+#pragma unroll
+            for (int hs = 0; hs < 2; ++hs)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) xb[hs][nt] = xf[((2 * sub + hs) * NT + nt) * 32 + lane];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+                xsum[nt] = *reinterpret_cast<const float2*>(xs + sub * 8 * NT + nt * 8 + 2 * t);
+#pragma unroll
+            for (int rt = 0; rt < 2; ++rt) {
+                const uint32_t q0 = cur.q[rt][0][j], q1 = cur.q[rt][1][j];
+                const uint32_t q0s = q0 >> 8, q1s = q1 >> 8;
+                const uint32_t alo[4] = {nib_lo(q0), nib_lo(q1), nib_lo(q0s), nib_lo(q1s)};
+                const uint32_t ahi[4] = {nib_hi(q0), nib_hi(q1), nib_hi(q0s), nib_hi(q1s)};
+                const float2 s0 = wsc[(16 * rt + g) * SROW + j];
+                const float2 s1 = wsc[(16 * rt + g + 8) * SROW + j];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    float d[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(d, alo, xb[0][nt].x, xb[0][nt].y);
+                    mma16816(d, alo, xb[0][nt].z, xb[0][nt].w);
+                    mma16816(d, ahi, xb[1][nt].x, xb[1][nt].y);
+                    mma16816(d, ahi, xb[1][nt].z, xb[1][nt].w);
+                    acc[rt][nt][0] = fmaf(s0.x, d[0], fmaf(-s0.y, xsum[nt].x, acc[rt][nt][0]));
+                    acc[rt][nt][1] = fmaf(s0.x, d[1], fmaf(-s0.y, xsum[nt].y, acc[rt][nt][1]));
+                    acc[rt][nt][2] = fmaf(s1.x, d[2], fmaf(-s1.y, xsum[nt].x, acc[rt][nt][2]));
+                    acc[rt][nt][3] = fmaf(s1.x, d[3], fmaf(-s1.y, xsum[nt].y, acc[rt][nt][3]));
+                }
+            }
+        }
+        if (sb + 1 < nsb) cur = nxt;
+    }
+
+    // ---- partial sums of the CTA -> tile[col][row] (x scale divided out)
+    __syncthreads();   // the x fragments are dead; the tile reuses their space
+#pragma unroll
+    for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int col = nt * 8 + 2 * t + (c & 1);
+                const int r = 32 * warp + 16 * rt + g + 8 * (c >> 1);
+                tile[col * TROW + r] = acc[rt][nt][c] / cs[col];
+            }
+    __syncthreads();
+
+    if (a.nkc > 1) {
+        // write this chunk's part; the last CTA of the row block sums them
+        float* part = a.ws + ((size_t)kc * gridDim.x + rb) * (8 * NT) * ROWS;
+        for (int col = 0; col < 8 * NT; ++col) part[col * ROWS + tid] = tile[col * TROW + tid];
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) s_last = atomicAdd(&a.cnt[rb], 1) == a.nkc - 1;
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        for (int col = 0; col < 8 * NT; ++col) {
+            float v = 0.f;
+            for (int c = 0; c < a.nkc; ++c)
+                v += __ldcg(a.ws + (((size_t)c * gridDim.x + rb) * (8 * NT) + col) * ROWS + tid);
+            tile[col * TROW + tid] = v;
+        }
+        if (tid == 0) a.cnt[rb] = 0;     // every CTA of the row block has counted
+        __syncthreads();
+    }
+
+    // ---- epilogue: thread = row of the block (SiLU: output of the block)
+    if (EPI == SB_EPI_SILU) {
+        if (tid < 64) {
+            const int o = rb * 64 + tid;
+            if (o < a.M / 2)
+                for (int col = 0; col < a.n; ++col)
+                    a.Y[(size_t)col * a.ldy + o] =
+                        silu_mul(tile[col * TROW + tid], tile[col * TROW + 64 + tid]);
+        }
+    } else {
+        const int m = row0 + tid;
+        if (m < a.M)
+            for (int col = 0; col < a.n; ++col) {
+                float* y = a.Y + (size_t)col * a.ldy + m;
+                const float v = tile[col * TROW + tid];
+                *y = EPI == SB_EPI_ADD ? *y + v : v;
+            }
+    }
+}
+
+size_t mv_smem(int KC, int NT) {
+    const size_t nsub = KC / 32;
+    size_t loop = nsub * 2 * NT * 512 + nsub * 8 * NT * 4 + WARPS * 32 * SROW * 8 + 8 * NT * 4;
+    size_t out = (size_t)8 * NT * TROW * 4;
+    return loop > out ? loop : out;
+}
+
+// K chunk: a multiple of 256 dividing K, at most MAX_KC / NT, chosen so that
+// the grid has at least two CTAs per SM where the matrix allows it.
+int mv_plan(int M_pad, int K, int NT) {
+    const int blocks = M_pad / ROWS, nsb = K / 256, kmax = MAX_KC / NT / 256;
+    int best = 0;
+    for (int s = 1; s <= nsb && s <= kmax; ++s) {
+        if (nsb % s) continue;
+        if (best == 0 || (long)blocks * (nsb / s) >= 296) best = s;
+    }
+    return best * 256;
+}
+
+template <int NT, int EPI>
+int launch(const MvArgs& a, int blocks, cudaStream_t st) {
+    const size_t smem = mv_smem(a.KC, NT);
+    static unsigned long long ready = 0;     // per device ordinal (< 64)
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    if (!(__atomic_load_n(&ready, __ATOMIC_RELAXED) >> dev & 1ull)) {
+        if (cudaFuncSetAttribute(mv_kernel<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)mv_smem(MAX_KC / NT, NT)) != cudaSuccess)
+            return -1;
+        __atomic_fetch_or(&ready, 1ull << dev, __ATOMIC_RELAXED);
+    }
+    return sb_launch_pdl(mv_kernel<NT, EPI>, dim3(blocks, a.nkc), dim3(NTHREADS), smem, st, a) ==
+                   cudaSuccess
+               ? 0
+               : -1;
+}
+
+template <int NT>
+int dispatch(const MvArgs& a, int blocks, int epi, cudaStream_t st) {
+    switch (epi) {
+        case SB_EPI_STORE: return launch<NT, SB_EPI_STORE>(a, blocks, st);
+        case SB_EPI_ADD: return launch<NT, SB_EPI_ADD>(a, blocks, st);
+        case SB_EPI_SILU: return launch<NT, SB_EPI_SILU>(a, blocks, st);
+    }
+    return -1;
+}
+
+}  // namespace
+
+extern "C" size_t sb_mv_ws_floats(int M_pad, int K) {
+    if (M_pad % ROWS || K % 256) return 0;
+    size_t best = 0;
+    for (int NT = 1; NT <= 2; ++NT) {
+        const int KC = mv_plan(M_pad, K, NT);
+        const size_t f = (size_t)(K / KC) * M_pad * 8 * NT;
+        if (f > best) best = f;
+    }
+    return best;
+}
+
+extern "C" int sb_mv_gemm(const sb_matrix* W, const float* X, int ldx, int n, float* Y, int ldy,
+                          int epi, float* ws, int* cnt, cudaStream_t st) {
+    if (!W || !X || !Y || !ws || !cnt || n < 1 || n > SB_MV_MAX_ROWS) return -1;
+    if (W->wtype != SB_WT_Q4K || W->K % 256 || W->M_pad % ROWS || ldx % 4 ||
+        (reinterpret_cast<uintptr_t>(X) & 15))
+        return -1;
+    const int NT = n <= 8 ? 1 : 2;
+    MvArgs a;
+    a.W = static_cast<const unsigned char*>(W->data);
+    a.M = W->M;
+    a.K = W->K;
+    a.X = X;
+    a.ldx = ldx;
+    a.n = n;
+    a.Y = Y;
+    a.ldy = ldy;
+    a.ws = ws;
+    a.cnt = cnt;
+    a.KC = mv_plan(W->M_pad, W->K, NT);
+    if (a.KC == 0) return -1;
+    a.nkc = W->K / a.KC;
+    const int blocks = W->M_pad / ROWS;
+    return NT == 1 ? dispatch<1>(a, blocks, epi, st) : dispatch<2>(a, blocks, epi, st);
+}

@@ -45,6 +45,8 @@ typedef struct sb_lane {
     sb_tc_operand own[3];          /* half lanes: operands over the half's rows */
     const sb_tc_operand *op_d, *op_f, *op_a;   /* GEMM operands (K = D, F, Dq) */
     float* sk_ws;                  /* stream-K workspace of this lane */
+    float* mv_ws;                  /* small-batch GEMM partials and counters */
+    int* mv_cnt;
     int r0;                        /* first row */
     int xn_split, att_split;       /* enqueue time: the RMSNorm / attention wrote
                                       the f16 operand of the GEMM that follows */
@@ -143,6 +145,7 @@ struct slate_llama_batch {
  * sums of its own). */
 static int norm_splits(const slate_llama_batch_t* b, const sb_lane* L, int n) {
     return b->tc_passes && !b->q4_on && n >= SB_TC_MIN_ROWS && n <= L->op_d->rows &&
+           !(L->mv_ws && n <= SB_MV_MAX_ROWS) &&
            b->D % 4 == 0 && b->D <= 8192 && b->ld_x % 4 == 0 && L->op_d->ld16 % 4 == 0;
 }
 
@@ -181,6 +184,10 @@ static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, con
         int rc = have_d ? 0 : sb_tc_split(X, ldx, n, L->op_d, s);
         return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, L->op_d, n, Y, ldy, epi, b->tc_err, s);
     }
+    /* a few rows: weight streaming bound, gemm_mv.cu */
+    if (L->mv_ws && W->wtype == SB_WT_Q4K && n <= SB_MV_MAX_ROWS &&
+        sb_mv_gemm(W, X, ldx, n, Y, ldy, epi, L->mv_ws, L->mv_cnt, s) == 0)
+        return 0;
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
         const sb_q4_operand* op = W->K == b->q4_d.K ? &b->q4_d
                                   : W->K == b->q4_f.K ? &b->q4_f : &b->q4_a;
@@ -382,7 +389,10 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
                              b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
                              b->rope_cos, b->rope_sin, s);
     } else if (part == 1) {
-        float* scratch = b->scratch + sb_attention_scratch_floats(r0, b->nq, b->hd, b->max_seq);
+        /* the second lane's partials sit after a whole batch's */
+        float* scratch = b->scratch + (r0 ? sb_attention_scratch_floats(b->max_batch, b->nq, b->hd,
+                                                                         b->max_seq)
+                                          : 0);
         L->att_split = norm_splits(b, L, n) && L->op_a->ld16 >= b->Dq;
         if (b->chunk_step)   /* rows: consecutive positions of one sequence */
             rc |= sb_attention_paged_prefill(att, b->ld_att, qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
@@ -400,7 +410,8 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
         else
             rc |= sb_attention_paged(att, b->ld_att, qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, row_pos,
                                      row_slot, b->page_table, b->max_pages, b->pool, b->kvmap_p,
-                                     b->n_pages, l, b->kv_dtype, b->max_seq, scratch, b->tc_err, s);
+                                     b->n_pages, l, b->kv_dtype, b->max_seq, 0, scratch, b->tc_err,
+                                     s);
     } else {
         rc |= step_gemm(b, L, &ly->wo, att, b->ld_att, IN_ATT, n, x, b->ld_x, res_epi, b->sp_wo, s);
         if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, x, (size_t)n * b->ld_x, s);
@@ -510,6 +521,7 @@ static int gemm_launches(const slate_llama_batch_t* b, const sb_lane* L, const s
                          int epi, int splits, int pre) {
     const int split = pre && norm_splits(b, L, n) ? 0 : 1;
     if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return split + 1;
+    if (L->mv_ws && W->wtype == SB_WT_Q4K && n <= SB_MV_MAX_ROWS) return 1;
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2;                                                               /* split + GEMM */
     if (uses_sk(b, L, W, n, epi))
@@ -774,7 +786,8 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         b->ld_qkv = round_up(b->layers[0].wqkv.M_pad, 4);
         b->ld_h = round_up(b->layers[0].wgu.M_pad / 2, 128);
         b->ld_logits = round_up(b->lm_head.M_pad, 4);
-        size_t scr = sb_attention_scratch_floats(B, b->nq, hd, b->max_seq);
+        /* attention partials: one batch's, twice when the halves may run as lanes */
+        size_t scr = sb_attention_scratch_floats(B, b->nq, hd, b->max_seq) * (o->lanes == 2 ? 2 : 1);
         b->x = (float*)dalloc(b, (size_t)B * b->ld_x * 4);
         b->xn = (float*)dalloc(b, (size_t)B * b->ld_x * 4);
         b->att = (float*)dalloc(b, (size_t)B * b->ld_att * 4);
@@ -937,6 +950,34 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
             sb_cuda_check(cudaEventCreateWithFlags(&b->ev_b, cudaEventDisableTiming), "event"))
             goto fail;
         b->dual = 1;
+    }
+
+    /* small-batch Q4_K GEMMs (default path): partials and row-block counters
+     * per lane that can run beside another (the full lane and the first half
+     * never run at the same time) */
+    if (o->gemm_path == 0 && b->layers[0].wqkv.wtype == SB_WT_Q4K) {
+        const sb_matrix* mats[5] = {&b->layers[0].wqkv, &b->layers[0].wo, &b->layers[0].wgu,
+                                    &b->layers[0].wdown, &b->lm_head};
+        size_t wsf = 0;
+        int blocks = 0;
+        for (int i = 0; i < 5; ++i) {
+            if (mats[i]->wtype != SB_WT_Q4K) continue;
+            const size_t f = sb_mv_ws_floats(mats[i]->M_pad, mats[i]->K);
+            if (f > wsf) wsf = f;
+            if (mats[i]->M_pad / 128 > blocks) blocks = mats[i]->M_pad / 128;
+        }
+        sb_lane* lanes[2] = {&b->full, b->dual ? &b->half[1] : NULL};
+        for (int i = 0; i < 2 && wsf && lanes[i]; ++i) {
+            lanes[i]->mv_ws = (float*)dalloc(b, wsf * 4);
+            lanes[i]->mv_cnt = (int*)dalloc(b, (size_t)blocks * 4);
+            if (!lanes[i]->mv_ws || !lanes[i]->mv_cnt ||
+                sb_cuda_check(cudaMemset(lanes[i]->mv_cnt, 0, (size_t)blocks * 4), "memset"))
+                goto fail;
+        }
+        if (b->dual) {
+            b->half[0].mv_ws = b->full.mv_ws;
+            b->half[0].mv_cnt = b->full.mv_cnt;
+        }
     }
 
     /* KV pool, page tables, free list */
@@ -1418,7 +1459,7 @@ static int enqueue_kernel(slate_llama_batch_t* b, int kernel, int n, int layer, 
             return sb_attention_paged(b->att, b->ld_att, b->qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd,
                                       b->row_pos, b->row_slot, b->page_table, b->max_pages,
                                       b->pool, b->kvmap_p, b->n_pages, layer, b->kv_dtype,
-                                      b->max_seq, b->scratch, b->tc_err, s);
+                                      b->max_seq, 0, b->scratch, b->tc_err, s);
         case SLATE_PROF_QKV:
             return step_gemm(b, &b->full, &ly->wqkv, b->xn, b->ld_x, IN_XN, n, scratch_y,
                              b->ld_logits, SB_EPI_STORE, b->sp_qkv, s);

@@ -42,6 +42,16 @@ typedef struct sb_matrix {
 /* Y[n][·] (epi) X[n][0..K) · W[m][0..K)  for n < B.
  * X row stride ldx (floats); for f32 weights X must be zero in [K, ldw).
  * path: 0 = auto (GEMV for B <= 8, tiled otherwise), 1 = tiled only. */
+/* Small batches (gemm_mv.cu): Q4_K weights, 1..SB_MV_MAX_ROWS activation
+ * rows, tensor cores through mma.sync, weights streamed once.  ws holds
+ * sb_mv_ws_floats(M_pad, K) floats; cnt M_pad / 128 zeroed ints (left zeroed).
+ * X 16-byte aligned with ldx % 4 == 0.  Returns -1 (nothing launched) for
+ * shapes it does not take. */
+#define SB_MV_MAX_ROWS 16
+size_t sb_mv_ws_floats(int M_pad, int K);
+int sb_mv_gemm(const sb_matrix* W, const float* X, int ldx, int n, float* Y, int ldy, int epi,
+               float* ws, int* cnt, cudaStream_t st);
+
 int sb_gemm(const sb_matrix* W, const float* X, int ldx, int B, float* Y, int ldy,
             int epi, int path, cudaStream_t st);
 
@@ -97,25 +107,34 @@ int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd, const int
                    const float* rope_cos, const float* rope_sin, cudaStream_t st);
 
 /* Paged GQA attention (llama_infer.c:97-129): att[b][hq*hd+d] for ctx =
- * row_pos[b]+1.  Split over context chunks of SB_ATTN_CHUNK tokens into
- * scratch partials (m, l, o[hd]) of size sb_attention_scratch_floats(), then
- * combined.  1024-token chunks: at the 8B shape with 256 sequences they ran
- * 2-6% faster per layer than 512 (fewer per-CTA starts and partials) with
- * ~10K CTAs still in flight; 4096 lost parallelism. */
+ * row_pos[b]+1.  Split over context chunks of ct tokens (one CTA per row, kv
+ * head and chunk) into scratch partials (m, l, o[hd]), then combined.
+ * sb_attention_chunk_tokens(B) picks ct from the row count: SB_ATTN_CHUNK from
+ * 64 rows (at the 8B shape with 256 sequences 1024-token chunks ran 2-6%
+ * faster per layer than 512, fewer per-CTA starts and partials, with ~10K
+ * CTAs in flight; 4096 lost parallelism), halving per halving of the rows down
+ * to 128 tokens below 16 rows, so that a few sequences still spread over the
+ * GPU.  sb_attention_scratch_rows() is the scratch of B rows at chunk ct;
+ * sb_attention_scratch_floats(max_batch) covers every B <= max_batch at its
+ * own chunk (and any B <= max_batch at a longer chunk). */
 #define SB_ATTN_CHUNK 1024
+int sb_attention_chunk_tokens(int B);
+size_t sb_attention_scratch_rows(int B, int nq, int hd, int max_seq, int ct);
 size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int max_seq);
 /* Opts the (head_dim, group, dtype) kernel into its shared-memory size on the
  * current device; call outside stream capture before the first launch. */
 int sb_attention_prepare(int nq, int nkv, int hd, int kv_dtype);
 /* kvmap: NULL, or a tensor map of the pool from sb_attention_make_map(); with
- * one, f16 pools of supported shapes take the tensor-core kernel. */
+ * one, f16 pools of supported shapes take the tensor-core kernel.  ct: chunk
+ * tokens (a multiple of 16 up to SB_ATTN_CHUNK), 0 = sb_attention_chunk_tokens(B). */
 int sb_attention_paged(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
                        int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
                        const int32_t* page_table, int max_pages, const void* pool,
                        const void* kvmap, int64_t n_pages, int layer, int kv_dtype, int max_seq,
-                       float* scratch, int* err, cudaStream_t st);
-/* The same, also writing the output rows as the f16 hi / lo pair (row stride
- * ld16 >= nq * hd, lo nullable) that the following tensor-core GEMM takes. */
+                       int ct, float* scratch, int* err, cudaStream_t st);
+/* The same (chunks of sb_attention_chunk_tokens(B)), also writing the output
+ * rows as the f16 hi / lo pair (row stride ld16 >= nq * hd, lo nullable) that
+ * the following tensor-core GEMM takes. */
 int sb_attention_paged_split(float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
                              int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
                              const int32_t* page_table, int max_pages, const void* pool,
@@ -130,11 +149,12 @@ int sb_attention_paged_split(float* att, int ld_att, const float* qkv, int ld_qk
 int sb_attention_mma_supported(int nq, int nkv, int hd, int kv_dtype);
 int sb_attention_make_map(void* map, void* pool, int64_t n_pages, int layers, int nkv, int hd);
 /* Chunk stage only (partials into `part`, same records as the CUDA-core
- * kernel); prepare != 0 sets the shared-memory attributes instead. */
+ * kernel; chunks of ct tokens, nchunk per row); prepare != 0 sets the
+ * shared-memory attributes instead. */
 int sb_attention_mma(int prepare, const void* map, const float* qkv, int ld_qkv, int B, int nq,
                      int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
                      const int32_t* page_table, int max_pages, int64_t n_pages, int layer,
-                     int nchunk, float* part, int* err, cudaStream_t st);
+                     int nchunk, int ct, float* part, int* err, cudaStream_t st);
 /* The causal prefill form of the same (attn_mma.cu): the B rows are
  * consecutive positions of one sequence (a prompt chunk); tiles of rows share
  * each streamed K/V page.  Same partial records. */

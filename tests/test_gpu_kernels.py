@@ -274,6 +274,49 @@ def test_matmul_q4k_streamk(be, oracle, sb, monkeypatch, B, M, K):
         assert scale_err(got, want) < 1e-5, rep
 
 
+@pytest.mark.parametrize("B", [1, 3, 8, 9, 16])
+@pytest.mark.parametrize("M,K", [(128, 256), (384, 1024), (6144, 4096), (4096, 4096),
+                                 (256, 14336), (28672, 4096)])
+def test_matmul_q4k_small_batch(be, oracle, sb, B, M, K):
+    """passes=4, the small-batch kernel: the quants q enter the mma.sync
+    tensor cores exactly, x as f16 hi + lo after a power-of-two scale per row
+    and K chunk, and each sub-block's sum(q*x) is scaled by d*sc with
+    dmin*m*sum(x) subtracted in f32.  Shapes with one K chunk and with up to 16
+    chunks summed by the last CTA of a row block; two calls (the row-block
+    counters must be left at zero)."""
+    rng = np.random.default_rng(B * 13 + M + K)
+    q = sb.quantize_q4k(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    X = rng.normal(0, 1, (B, K)).astype(np.float32)
+    Y = be.empty(B * M * 4)
+    Wd = oracle.dequant_q4k(q, M * K).reshape(M, K).astype(np.float64)
+    want = X.astype(np.float64) @ Wd.T
+    for rep in range(2):
+        rc = be.matmul_q4k_batch_tc(Y, be.dev(q), be.dev(X), B, M, K, 4)
+        assert rc == 0, be.sb.last_error()
+        got = be.host(Y, (B, M))
+        assert scale_err(got, want) < 1e-5, rep
+
+
+def test_matmul_q4k_small_batch_magnitudes(be, oracle, sb):
+    """Rows of very different size (1e-4 .. 1e4, one all-zero row) keep f32-level
+    accuracy each: the hi/lo split happens after each row's own power-of-two
+    scale, so small activations do not fall into f16 subnormals."""
+    M, K, B = 512, 2048, 6
+    rng = np.random.default_rng(77)
+    q = sb.quantize_q4k(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    X = rng.normal(0, 1, (B, K)).astype(np.float32)
+    X *= np.array([1e-4, 1e-2, 1.0, 1e2, 1e4, 0.0], np.float32)[:, None]
+    Y = be.empty(B * M * 4)
+    rc = be.matmul_q4k_batch_tc(Y, be.dev(q), be.dev(X), B, M, K, 4)
+    assert rc == 0, be.sb.last_error()
+    got = be.host(Y, (B, M))
+    Wd = oracle.dequant_q4k(q, M * K).reshape(M, K).astype(np.float64)
+    want = X.astype(np.float64) @ Wd.T
+    for r in range(B - 1):
+        assert scale_err(got[r], want[r]) < 1e-5, r
+    assert not got[B - 1].any()
+
+
 def run_attention(be, monkeypatch, path, q, pool, table, pos, nq, nkv, hd, kv_dtype, layer, n_pages):
     """attention_paged_gqa with the kernel picked by SLATE_CUDA_ATTN_PATH
     ("0": tensor cores where the f16 shape allows, "1": CUDA cores)."""
