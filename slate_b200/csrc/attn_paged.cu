@@ -539,8 +539,8 @@ int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
 }  // namespace
 
 extern "C" int sb_attention_chunk_tokens(int B) {
-    return B >= 64 ? SB_ATTN_CHUNK : B >= 32 ? SB_ATTN_CHUNK / 2 : B >= 16 ? SB_ATTN_CHUNK / 4
-                                                                          : SB_ATTN_CHUNK / 8;
+    return B >= 16 ? SB_ATTN_CHUNK : B >= 8 ? SB_ATTN_CHUNK / 2 : B >= 4 ? SB_ATTN_CHUNK / 4
+                                                                       : SB_ATTN_CHUNK / 8;
 }
 
 extern "C" size_t sb_attention_scratch_rows(int B, int nq, int hd, int max_seq, int ct) {

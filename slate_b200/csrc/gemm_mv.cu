@@ -21,20 +21,22 @@
 //
 // Work decomposition: a CTA (4 warps) owns 128 weight rows and a K chunk of
 // KC columns (a multiple of 256); a warp owns 32 rows (two m16 tiles) and
-// walks the chunk's super-blocks, holding the next super-block's quants in
-// registers while it computes the current one.  Lane (g, t) of a warp loads
-// 32-bit word t of every sub-block of rows g and g + 8 of each tile: the low
-// nibbles of that word are the lane's four A elements of the sub-block's
-// first MMA, the high nibbles those of its second, so every MMA covers
-// exactly one sub-block (the k order inside a sub-block is permuted the same
-// way in A and in the staged x fragments).  The header of each row's
-// super-block is decoded once per warp (lane l: row l) into shared memory.
+// walks the chunk's super-blocks through a ring of three shared-memory stages
+// (32 rows x 144 bytes each, copied with coalesced 16-byte cp.async, two
+// super-blocks ahead of the one being computed).  Lane (g, t) reads 32-bit
+// word t of every sub-block of rows g and g + 8 of each tile (bank-conflict
+// free at the 144-byte row stride): the low nibbles of that word are the
+// lane's four A elements of the sub-block's first MMA, the high nibbles those
+// of its second, so every MMA covers exactly one sub-block (the k order inside
+// a sub-block is permuted the same way in A and in the staged x fragments).
+// The header of each row's super-block is decoded once per warp (lane l: row
+// l) into shared memory.
 // With more than one K chunk, each CTA writes its 128 x n partial sums to a
 // workspace and the last CTA of the row block (an atomic counter; no CTA
 // waits on another) sums the chunks in chunk order -- results do not depend
 // on timing -- and applies the epilogue.
 //
-// The weights of the first super-block are requested before the grid waits
+// The weights of the first two super-blocks are requested before the grid waits
 // for the previous kernel of the stream (programmatic dependent launch), so
 // the weight stream starts while the producer of X finishes.
 #include <cuda_fp16.h>
@@ -50,7 +52,9 @@ constexpr int NTHREADS = 32 * WARPS;
 constexpr int ROWS = 32 * WARPS;        // weight rows per CTA
 constexpr int TROW = 132;               // output tile row stride (floats): conflict-free stores
 constexpr int SROW = 9;                 // scale scratch row stride (float2): conflict-free loads
-constexpr int MAX_KC = 2048;
+constexpr int MAX_KC = 1024;             // x fragments of a chunk: 32 KB of shared memory
+constexpr int WSTAGES = 3;              // weight ring stages per warp
+constexpr int WSTAGE = 32 * 144;        // bytes: 32 rows x one super-block
 
 struct MvArgs {
     const unsigned char* W;
@@ -63,10 +67,6 @@ struct MvArgs {
     int* cnt;
     int KC, nkc;
 };
-
-__device__ __forceinline__ uint32_t ldg32(const unsigned char* p) {
-    return __ldg(reinterpret_cast<const unsigned int*>(p));
-}
 
 // (1024 + n) with n in bits 0-3 / 16-19 -> exact n in both halves.
 __device__ __forceinline__ uint32_t nib_lo(uint32_t q) {
@@ -110,25 +110,24 @@ __device__ __forceinline__ void decode_header(uint4 h, float2* out) {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
-// Quants (one word per sub-block) of rows g and g + 8 of both m16 tiles, and
-// the header of row `lane` of the warp, for one super-block.
-struct Quants {
-    uint32_t q[2][2][8];   // [tile][row g / g + 8][sub-block]
-    uint4 hdr;
-};
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__device__ __forceinline__ void load_quants(Quants& Q, const unsigned char* wrow0, size_t rb,
-                                            int kb, int g, int t, int lane) {
-    const unsigned char* blk = wrow0 + (size_t)kb * 144;
+// Super-block kb of the warp's 32 rows -> stage (row r at r * 144): 288
+// 16-byte pieces, 9 per lane, consecutive lanes on consecutive pieces.
+__device__ __forceinline__ void stage_weights(unsigned char* stage, const unsigned char* wrow0,
+                                              size_t rb, int kb, int lane) {
+    const unsigned char* src = wrow0 + (size_t)kb * 144;
 #pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const unsigned char* p = blk + (size_t)(16 * rt + 8 * h + g) * rb + 16 + 4 * t;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) Q.q[rt][h][j] = ldg32(p + 16 * j);
-        }
-    Q.hdr = __ldg(reinterpret_cast<const uint4*>(blk + (size_t)lane * rb));
+    for (int k = 0; k < 9; ++k) {
+        const int i = lane + 32 * k, r = i / 9, c = i - 9 * r;
+        cp_async16(stage + r * 144 + 16 * c, src + (size_t)r * rb + 16 * c);
+    }
 }
 
 template <int NT, int EPI>
@@ -140,6 +139,7 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
     float* xs = reinterpret_cast<float*>(smem + (size_t)nsub * 2 * NT * 512);  // [nsub][8 NT]
     float2* sc = reinterpret_cast<float2*>(xs + nsub * 8 * NT);               // [WARPS][32][SROW]
     float* cs = reinterpret_cast<float*>(sc + WARPS * 32 * SROW);             // [8 NT] x scale
+    unsigned char* ring = reinterpret_cast<unsigned char*>(cs + 16);          // [WARPS][WSTAGES][WSTAGE]
     float* tile = reinterpret_cast<float*>(smem);                             // [8 NT][TROW], after the loop
     __shared__ int s_last;
 
@@ -152,9 +152,13 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
     const unsigned char* wrow0 = a.W + (size_t)(row0 + 32 * warp) * rbytes;
     const int kb0 = k0 / 256, nsb = KC / 256;
 
-    // weights of the first super-block: independent of the previous kernel
-    Quants cur;
-    load_quants(cur, wrow0, rbytes, kb0, g, t, lane);
+    // weights of the first two super-blocks: independent of the previous kernel
+    unsigned char* wring = ring + (size_t)warp * WSTAGES * WSTAGE;
+#pragma unroll
+    for (int p = 0; p < WSTAGES - 1; ++p) {
+        if (p < nsb) stage_weights(wring + p * WSTAGE, wrow0, rbytes, kb0 + p, lane);
+        cp_commit();
+    }
     sb_grid_release();
     sb_grid_wait();
 
@@ -232,11 +236,15 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
 
     float2* wsc = sc + warp * 32 * SROW;
     for (int sb = 0; sb < nsb; ++sb) {
-        Quants nxt;
-        if (sb + 1 < nsb) load_quants(nxt, wrow0, rbytes, kb0 + sb + 1, g, t, lane);
+        cp_wait<WSTAGES - 2>();   // this lane's pieces of super-block sb have landed
+        __syncwarp();             // ... and every lane's; stage (sb - 1) is free again
+        if (sb + WSTAGES - 1 < nsb)
+            stage_weights(wring + ((sb + WSTAGES - 1) % WSTAGES) * WSTAGE, wrow0, rbytes,
+                          kb0 + sb + WSTAGES - 1, lane);
+        cp_commit();
+        const unsigned char* cur = wring + (sb % WSTAGES) * WSTAGE;
         float2 dm[8];
-        decode_header(cur.hdr, dm);
-        __syncwarp();
+        decode_header(*reinterpret_cast<const uint4*>(cur + lane * 144), dm);
 #pragma unroll
         for (int j = 0; j < 8; ++j) wsc[lane * SROW + j] = dm[j];
         __syncwarp();
@@ -254,7 +262,10 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
                 xsum[nt] = *reinterpret_cast<const float2*>(xs + sub * 8 * NT + nt * 8 + 2 * t);
 #pragma unroll
             for (int rt = 0; rt < 2; ++rt) {
-                const uint32_t q0 = cur.q[rt][0][j], q1 = cur.q[rt][1][j];
+                const uint32_t q0 = *reinterpret_cast<const uint32_t*>(
+                    cur + (16 * rt + g) * 144 + 16 + 16 * j + 4 * t);
+                const uint32_t q1 = *reinterpret_cast<const uint32_t*>(
+                    cur + (16 * rt + g + 8) * 144 + 16 + 16 * j + 4 * t);
                 const uint32_t q0s = q0 >> 8, q1s = q1 >> 8;
                 const uint32_t alo[4] = {nib_lo(q0), nib_lo(q1), nib_lo(q0s), nib_lo(q1s)};
                 const uint32_t ahi[4] = {nib_hi(q0), nib_hi(q1), nib_hi(q0s), nib_hi(q1s)};
@@ -274,8 +285,8 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
                 }
             }
         }
-        if (sb + 1 < nsb) cur = nxt;
     }
+    cp_wait<0>();
 
     // ---- partial sums of the CTA -> tile[col][row] (x scale divided out)
     __syncthreads();   // the x fragments are dead; the tile reuses their space
@@ -333,19 +344,28 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
 
 size_t mv_smem(int KC, int NT) {
     const size_t nsub = KC / 32;
-    size_t loop = nsub * 2 * NT * 512 + nsub * 8 * NT * 4 + WARPS * 32 * SROW * 8 + 8 * NT * 4;
+    size_t loop = nsub * 2 * NT * 512 + nsub * 8 * NT * 4 + WARPS * 32 * SROW * 8 + 16 * 4 +
+                  (size_t)WARPS * WSTAGES * WSTAGE;
     size_t out = (size_t)8 * NT * TROW * 4;
     return loop > out ? loop : out;
 }
 
-// K chunk: a multiple of 256 dividing K, at most MAX_KC / NT, chosen so that
-// the grid has at least two CTAs per SM where the matrix allows it.
+// K chunk: s super-blocks, s dividing K / 256, at most MAX_KC / NT columns;
+// the s with the least (waves of 2 CTAs per SM) x (s + 1 super-block times,
+// the one for staging x and the partial sums), larger s on ties.
 int mv_plan(int M_pad, int K, int NT) {
+    const long slots = 2L * 148;
     const int blocks = M_pad / ROWS, nsb = K / 256, kmax = MAX_KC / NT / 256;
     int best = 0;
+    long best_cost = 0;
     for (int s = 1; s <= nsb && s <= kmax; ++s) {
         if (nsb % s) continue;
-        if (best == 0 || (long)blocks * (nsb / s) >= 296) best = s;
+        const long ctas = (long)blocks * (nsb / s);
+        const long cost = (ctas + slots - 1) / slots * (s + 1);
+        if (best == 0 || cost <= best_cost) {
+            best = s;
+            best_cost = cost;
+        }
     }
     return best * 256;
 }

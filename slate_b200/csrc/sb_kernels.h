@@ -110,11 +110,12 @@ int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd, const int
  * row_pos[b]+1.  Split over context chunks of ct tokens (one CTA per row, kv
  * head and chunk) into scratch partials (m, l, o[hd]), then combined.
  * sb_attention_chunk_tokens(B) picks ct from the row count: SB_ATTN_CHUNK from
- * 64 rows (at the 8B shape with 256 sequences 1024-token chunks ran 2-6%
+ * 16 rows (at the 8B shape with 256 sequences 1024-token chunks ran 2-6%
  * faster per layer than 512, fewer per-CTA starts and partials, with ~10K
- * CTAs in flight; 4096 lost parallelism), halving per halving of the rows down
- * to 128 tokens below 16 rows, so that a few sequences still spread over the
- * GPU.  sb_attention_scratch_rows() is the scratch of B rows at chunk ct;
+ * CTAs in flight; 4096 lost parallelism; at 16 rows 256-token chunks, 2.6
+ * waves of CTAs, were slower than 1024), halving per halving of the rows down
+ * to 128 tokens below 4 rows, so that a few sequences still fill about one
+ * wave of CTAs.  sb_attention_scratch_rows() is the scratch of B rows at chunk ct;
  * sb_attention_scratch_floats(max_batch) covers every B <= max_batch at its
  * own chunk (and any B <= max_batch at a longer chunk). */
 #define SB_ATTN_CHUNK 1024
