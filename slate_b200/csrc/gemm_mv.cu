@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
     unsigned char* ring = reinterpret_cast<unsigned char*>(cs + 16);          // [WARPS][WSTAGES][WSTAGE]
     float* tile = reinterpret_cast<float*>(smem);                             // [8 NT][TROW], after the loop
     __shared__ int s_last;
+    __shared__ int rmax[16];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -163,66 +164,74 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
     sb_grid_wait();
 
     // ---- activations of the chunk: per-row power-of-two scale, f16 hi/lo
-    // fragments in MMA order, sub-block sums
-    for (int c = warp; c < 8 * NT; c += WARPS) {
-        float m = 0.f;
-        if (c < a.n) {
-            const float4* xr = reinterpret_cast<const float4*>(a.X + (size_t)c * a.ldx + k0);
-            for (int i = lane; i < KC / 4; i += 32) {
-                float4 v = xr[i];
-                m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-            }
-        }
+    // fragments in MMA order, sub-block sums.  A thread's float4s of the chunk
+    // (rows < n; at most 16: 8 NT rows x KC / 4) are all requested at once.
+    constexpr int U = 8 * NT * (MAX_KC / NT) / 4 / NTHREADS;
+    const int q4 = KC / 4, total = a.n * q4;
+    for (int i = tid; i < nsub * 2 * NT * 32; i += NTHREADS) xf[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < nsub * 8 * NT; i += NTHREADS) xs[i] = 0.f;
+    if (tid < 8 * NT) rmax[tid] = 0;
+    float4 v[U];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) {
-            int e = 0;
-            const bool ok = m > 0.f && m <= 3.0e38f;
-            if (ok) {
-                frexpf(m, &e);                       // m < 2^e
-                e = max(-100, min(100, e));
-            }
-            cs[c] = ok ? ldexpf(1.0f, 14 - e) : 1.0f;
+    for (int u = 0; u < U; ++u) {
+        const int f = tid + NTHREADS * u;
+        if (f < total) {
+            const int c = f / q4, e = 4 * (f - c * q4);
+            v[u] = *reinterpret_cast<const float4*>(a.X + (size_t)c * a.ldx + k0 + e);
         }
     }
     __syncthreads();
-    for (int i = tid; i < nsub * 2 * NT * 32; i += NTHREADS) {
-        const int ln = i & 31, nt = (i >> 5) % NT, hs = (i >> 5) / NT;   // hs = 2 * sub + half
-        const int c = nt * 8 + (ln >> 2);
-        uint4 f = make_uint4(0u, 0u, 0u, 0u);
-        if (c < a.n) {
-            const float s = cs[c];
-            float4 v = *reinterpret_cast<const float4*>(a.X + (size_t)c * a.ldx + k0 + 16 * hs +
-                                                        4 * (ln & 3));
-            v.x *= s; v.y *= s; v.z *= s; v.w *= s;
-            // k slots (2t, 2t+1) <- elements (0, 2); (2t+8, 2t+9) <- (1, 3)
-            __half2 h02 = __floats2half2_rn(v.x, v.z), h13 = __floats2half2_rn(v.y, v.w);
-            float2 r02 = __half22float2(h02), r13 = __half22float2(h13);
-            __half2 l02 = __floats2half2_rn(v.x - r02.x, v.z - r02.y);
-            __half2 l13 = __floats2half2_rn(v.y - r13.x, v.w - r13.y);
-            f.x = *reinterpret_cast<uint32_t*>(&h02);
-            f.y = *reinterpret_cast<uint32_t*>(&h13);
-            f.z = *reinterpret_cast<uint32_t*>(&l02);
-            f.w = *reinterpret_cast<uint32_t*>(&l13);
-        }
-        xf[i] = f;
-    }
-    for (int i = tid; i < nsub * 8 * NT; i += NTHREADS) {
-        const int j = i / (8 * NT), c = i % (8 * NT);
-        float sum = 0.f;
-        if (c < a.n) {
-            const float s = cs[c];
-            const float4* xr = reinterpret_cast<const float4*>(a.X + (size_t)c * a.ldx + k0 + 32 * j);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                float4 v = xr[q];
-                sum += v.x * s;
-                sum += v.y * s;
-                sum += v.z * s;
-                sum += v.w * s;
-            }
+    for (int u = 0; u < U; ++u) {
+        const int f = tid + NTHREADS * u;
+        if (f < total) {
+            const float m = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+            atomicMax(&rmax[f / q4], __float_as_int(m));     // m >= 0: int order = float order
         }
-        xs[i] = sum;
+    }
+    __syncthreads();
+    if (tid < 8 * NT) {
+        const float m = __int_as_float(rmax[tid]);
+        int e = 0;
+        const bool ok = m > 0.f && m <= 3.0e38f;
+        if (ok) {
+            frexpf(m, &e);                       // m < 2^e
+            e = max(-100, min(100, e));
+        }
+        cs[tid] = ok ? ldexpf(1.0f, 14 - e) : 1.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int f = tid + NTHREADS * u;
+        // the 8 float4s of a sub-block sit in 8 consecutive lanes (q4 % 8 == 0),
+        // all inside or all outside the chunk
+        float ps = 0.f;
+        int c = 0, e = 0;
+        if (f < total) {
+            c = f / q4;
+            e = 4 * (f - c * q4);
+            const float sc_ = cs[c];
+            float4 x = v[u];
+            x.x *= sc_; x.y *= sc_; x.z *= sc_; x.w *= sc_;
+            ps = ((x.x + x.y) + x.z) + x.w;
+            // k slots (2t, 2t+1) <- elements (0, 2); (2t+8, 2t+9) <- (1, 3)
+            __half2 h02 = __floats2half2_rn(x.x, x.z), h13 = __floats2half2_rn(x.y, x.w);
+            float2 r02 = __half22float2(h02), r13 = __half22float2(h13);
+            __half2 l02 = __floats2half2_rn(x.x - r02.x, x.z - r02.y);
+            __half2 l13 = __floats2half2_rn(x.y - r13.x, x.w - r13.y);
+            uint4 fr;
+            fr.x = *reinterpret_cast<uint32_t*>(&h02);
+            fr.y = *reinterpret_cast<uint32_t*>(&h13);
+            fr.z = *reinterpret_cast<uint32_t*>(&l02);
+            fr.w = *reinterpret_cast<uint32_t*>(&l13);
+            // fragment (2 * sub + half, nt, lane g * 4 + t) holds x[nt * 8 + g][16 * hs + 4 t ..]
+            xf[((e >> 4) * NT + (c >> 3)) * 32 + (c & 7) * 4 + ((e >> 2) & 3)] = fr;
+        }
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+        if (f < total && (lane & 7) == 0) xs[(e >> 5) * 8 * NT + c] = ps;
     }
     __syncthreads();
 
@@ -305,19 +314,34 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
     if (a.nkc > 1) {
         // write this chunk's part; the last CTA of the row block sums them
         float* part = a.ws + ((size_t)kc * gridDim.x + rb) * (8 * NT) * ROWS;
-        for (int col = 0; col < 8 * NT; ++col) part[col * ROWS + tid] = tile[col * TROW + tid];
+        for (int col = 0; col < a.n; ++col) part[col * ROWS + tid] = tile[col * TROW + tid];
         __threadfence();
         __syncthreads();
         if (tid == 0) s_last = atomicAdd(&a.cnt[rb], 1) == a.nkc - 1;
         __syncthreads();
         if (!s_last) return;
         __threadfence();
-        for (int col = 0; col < 8 * NT; ++col) {
-            float v = 0.f;
-            for (int c = 0; c < a.nkc; ++c)
-                v += __ldcg(a.ws + (((size_t)c * gridDim.x + rb) * (8 * NT) + col) * ROWS + tid);
-            tile[col * TROW + tid] = v;
+        float sum[8 * NT];
+#pragma unroll
+        for (int col = 0; col < 8 * NT; ++col) sum[col] = 0.f;
+        for (int c0 = 0; c0 < a.nkc; c0 += 4) {      // chunk order; 4 x 8 NT loads in flight
+            float pv[4][8 * NT];
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+                for (int col = 0; col < 8 * NT; ++col)
+                    pv[cc][col] = (c0 + cc < a.nkc && col < a.n)
+                                      ? __ldcg(a.ws + (((size_t)(c0 + cc) * gridDim.x + rb) * (8 * NT) +
+                                                       col) * ROWS + tid)
+                                      : 0.f;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+                for (int col = 0; col < 8 * NT; ++col) sum[col] += pv[cc][col];
         }
+#pragma unroll
+        for (int col = 0; col < 8 * NT; ++col)
+            if (col < a.n) tile[col * TROW + tid] = sum[col];
         if (tid == 0) a.cnt[rb] = 0;     // every CTA of the row block has counted
         __syncthreads();
     }
