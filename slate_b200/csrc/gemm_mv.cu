@@ -19,11 +19,11 @@
 // the split, so small activations keep their low bits in the lo half; the
 // scale is divided out exactly at the end.
 //
-// Work decomposition: a CTA (4 warps) owns 128 weight rows and a K chunk of
+// Work decomposition: a CTA (8 warps) owns 256 weight rows and a K chunk of
 // KC columns (a multiple of 256); a warp owns 32 rows (two m16 tiles) and
-// walks the chunk's super-blocks through a ring of three shared-memory stages
-// (32 rows x 144 bytes each, copied with coalesced 16-byte cp.async, two
-// super-blocks ahead of the one being computed).  Lane (g, t) reads 32-bit
+// walks the chunk's super-blocks through a ring of two shared-memory stages
+// (32 rows x 144 bytes each, copied with coalesced 16-byte cp.async, one
+// super-block ahead of the one being computed; 16 warps per SM hide the rest).  Lane (g, t) reads 32-bit
 // word t of every sub-block of rows g and g + 8 of each tile (bank-conflict
 // free at the 144-byte row stride): the low nibbles of that word are the
 // lane's four A elements of the sub-block's first MMA, the high nibbles those
@@ -36,7 +36,7 @@
 // waits on another) sums the chunks in chunk order -- results do not depend
 // on timing -- and applies the epilogue.
 //
-// The weights of the first two super-blocks are requested before the grid waits
+// The weights of the first super-block are requested before the grid waits
 // for the previous kernel of the stream (programmatic dependent launch), so
 // the weight stream starts while the producer of X finishes.
 #include <cuda_fp16.h>
@@ -47,18 +47,18 @@
 
 namespace {
 
-constexpr int WARPS = 4;
+constexpr int WARPS = 8;
 constexpr int NTHREADS = 32 * WARPS;
 constexpr int ROWS = 32 * WARPS;        // weight rows per CTA
-constexpr int TROW = 132;               // output tile row stride (floats): conflict-free stores
+constexpr int TROW = ROWS + 4;          // output tile row stride (floats): conflict-free stores
 constexpr int SROW = 9;                 // scale scratch row stride (float2): conflict-free loads
-constexpr int MAX_KC = 1024;             // x fragments of a chunk: 32 KB of shared memory
-constexpr int WSTAGES = 3;              // weight ring stages per warp
+constexpr int MAX_KC = 512;             // x fragments of a chunk: 16 KB of shared memory
+constexpr int WSTAGES = 2;              // weight ring stages per warp
 constexpr int WSTAGE = 32 * 144;        // bytes: 32 rows x one super-block
 
 struct MvArgs {
     const unsigned char* W;
-    int M, K;
+    int M, M_pad, K;
     const float* X;
     int ldx, n;
     float* Y;
@@ -119,15 +119,13 @@ template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Super-block kb of the warp's 32 rows -> stage (row r at r * 144): 288
-// 16-byte pieces, 9 per lane, consecutive lanes on consecutive pieces.
+// 16-byte pieces, 9 per lane, consecutive lanes on consecutive pieces (piece
+// i = 9 r + c lands at 16 i; off[k] is its offset in the matrix).
 __device__ __forceinline__ void stage_weights(unsigned char* stage, const unsigned char* wrow0,
-                                              size_t rb, int kb, int lane) {
+                                              const uint32_t (&off)[9], int kb, int lane) {
     const unsigned char* src = wrow0 + (size_t)kb * 144;
 #pragma unroll
-    for (int k = 0; k < 9; ++k) {
-        const int i = lane + 32 * k, r = i / 9, c = i - 9 * r;
-        cp_async16(stage + r * 144 + 16 * c, src + (size_t)r * rb + 16 * c);
-    }
+    for (int k = 0; k < 9; ++k) cp_async16(stage + 16 * (lane + 32 * k), src + off[k]);
 }
 
 template <int NT, int EPI>
@@ -152,12 +150,19 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
     const size_t rbytes = (size_t)(a.K / 256) * 144;
     const unsigned char* wrow0 = a.W + (size_t)(row0 + 32 * warp) * rbytes;
     const int kb0 = k0 / 256, nsb = KC / 256;
+    const bool wvalid = row0 + 32 * warp < a.M_pad;   // the last CTA may hold 128 rows only
+    uint32_t off[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+        const int i = lane + 32 * k, r = i / 9;
+        off[k] = (uint32_t)(r * rbytes + 16 * (i - 9 * r));
+    }
 
     // weights of the first two super-blocks: independent of the previous kernel
     unsigned char* wring = ring + (size_t)warp * WSTAGES * WSTAGE;
 #pragma unroll
     for (int p = 0; p < WSTAGES - 1; ++p) {
-        if (p < nsb) stage_weights(wring + p * WSTAGE, wrow0, rbytes, kb0 + p, lane);
+        if (wvalid && p < nsb) stage_weights(wring + p * WSTAGE, wrow0, off, kb0 + p, lane);
         cp_commit();
     }
     sb_grid_release();
@@ -166,7 +171,7 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
     // ---- activations of the chunk: per-row power-of-two scale, f16 hi/lo
     // fragments in MMA order, sub-block sums.  A thread's float4s of the chunk
     // (rows < n; at most 16: 8 NT rows x KC / 4) are all requested at once.
-    constexpr int U = 8 * NT * (MAX_KC / NT) / 4 / NTHREADS;
+    constexpr int U = (8 * NT * (MAX_KC / NT) / 4 + NTHREADS - 1) / NTHREADS;
     const int q4 = KC / 4, total = a.n * q4;
     for (int i = tid; i < nsub * 2 * NT * 32; i += NTHREADS) xf[i] = make_uint4(0u, 0u, 0u, 0u);
     for (int i = tid; i < nsub * 8 * NT; i += NTHREADS) xs[i] = 0.f;
@@ -244,11 +249,11 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
             for (int c = 0; c < 4; ++c) acc[rt][nt][c] = 0.f;
 
     float2* wsc = sc + warp * 32 * SROW;
-    for (int sb = 0; sb < nsb; ++sb) {
+    for (int sb = 0; sb < (wvalid ? nsb : 0); ++sb) {
         cp_wait<WSTAGES - 2>();   // this lane's pieces of super-block sb have landed
         __syncwarp();             // ... and every lane's; stage (sb - 1) is free again
         if (sb + WSTAGES - 1 < nsb)
-            stage_weights(wring + ((sb + WSTAGES - 1) % WSTAGES) * WSTAGE, wrow0, rbytes,
+            stage_weights(wring + ((sb + WSTAGES - 1) % WSTAGES) * WSTAGE, wrow0, off,
                           kb0 + sb + WSTAGES - 1, lane);
         cp_commit();
         const unsigned char* cur = wring + (sb % WSTAGES) * WSTAGE;
@@ -348,12 +353,14 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
 
     // ---- epilogue: thread = row of the block (SiLU: output of the block)
     if (EPI == SB_EPI_SILU) {
-        if (tid < 64) {
-            const int o = rb * 64 + tid;
+        // 128-row groups (gate rows 0-63, up rows 64-127): ROWS / 2 outputs
+        if (tid < ROWS / 2) {
+            const int o = rb * (ROWS / 2) + tid;
+            const int gr = (tid / 64) * 128 + tid % 64;
             if (o < a.M / 2)
                 for (int col = 0; col < a.n; ++col)
                     a.Y[(size_t)col * a.ldy + o] =
-                        silu_mul(tile[col * TROW + tid], tile[col * TROW + 64 + tid]);
+                        silu_mul(tile[col * TROW + gr], tile[col * TROW + gr + 64]);
         }
     } else {
         const int m = row0 + tid;
@@ -379,7 +386,7 @@ size_t mv_smem(int KC, int NT) {
 // the one for staging x and the partial sums), larger s on ties.
 int mv_plan(int M_pad, int K, int NT) {
     const long slots = 2L * 148;
-    const int blocks = M_pad / ROWS, nsb = K / 256, kmax = MAX_KC / NT / 256;
+    const int blocks = (M_pad + ROWS - 1) / ROWS, nsb = K / 256, kmax = MAX_KC / NT / 256;
     int best = 0;
     long best_cost = 0;
     for (int s = 1; s <= nsb && s <= kmax; ++s) {
@@ -425,11 +432,12 @@ int dispatch(const MvArgs& a, int blocks, int epi, cudaStream_t st) {
 }  // namespace
 
 extern "C" size_t sb_mv_ws_floats(int M_pad, int K) {
-    if (M_pad % ROWS || K % 256) return 0;
+    if (M_pad % 128 || K % 256) return 0;
+    const size_t blocks = (M_pad + ROWS - 1) / ROWS;
     size_t best = 0;
     for (int NT = 1; NT <= 2; ++NT) {
         const int KC = mv_plan(M_pad, K, NT);
-        const size_t f = (size_t)(K / KC) * M_pad * 8 * NT;
+        const size_t f = (size_t)(K / KC) * blocks * ROWS * 8 * NT;
         if (f > best) best = f;
     }
     return best;
@@ -438,13 +446,14 @@ extern "C" size_t sb_mv_ws_floats(int M_pad, int K) {
 extern "C" int sb_mv_gemm(const sb_matrix* W, const float* X, int ldx, int n, float* Y, int ldy,
                           int epi, float* ws, int* cnt, cudaStream_t st) {
     if (!W || !X || !Y || !ws || !cnt || n < 1 || n > SB_MV_MAX_ROWS) return -1;
-    if (W->wtype != SB_WT_Q4K || W->K % 256 || W->M_pad % ROWS || ldx % 4 ||
+    if (W->wtype != SB_WT_Q4K || W->K % 256 || W->M_pad % 128 || ldx % 4 ||
         (reinterpret_cast<uintptr_t>(X) & 15))
         return -1;
     const int NT = n <= 8 ? 1 : 2;
     MvArgs a;
     a.W = static_cast<const unsigned char*>(W->data);
     a.M = W->M;
+    a.M_pad = W->M_pad;
     a.K = W->K;
     a.X = X;
     a.ldx = ldx;
@@ -456,6 +465,6 @@ extern "C" int sb_mv_gemm(const sb_matrix* W, const float* X, int ldx, int n, fl
     a.KC = mv_plan(W->M_pad, W->K, NT);
     if (a.KC == 0) return -1;
     a.nkc = W->K / a.KC;
-    const int blocks = W->M_pad / ROWS;
+    const int blocks = (W->M_pad + ROWS - 1) / ROWS;
     return NT == 1 ? dispatch<1>(a, blocks, epi, st) : dispatch<2>(a, blocks, epi, st);
 }
