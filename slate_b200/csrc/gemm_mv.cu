@@ -23,15 +23,16 @@
 // KC columns (a multiple of 256); a warp owns 32 rows (two m16 tiles) and
 // walks the chunk's super-blocks through a ring of two shared-memory stages
 // (32 rows x 144 bytes each, copied with coalesced 16-byte cp.async, one
-// super-block ahead of the one being computed; 16 warps per SM hide the rest).  Lane (g, t) reads 32-bit
-// word t of every sub-block of rows g and g + 8 of each tile (bank-conflict
+// super-block ahead of the one being computed; 16 warps per SM hide the
+// rest).  Lane (g, t) reads 32-bit word t of every sub-block of rows g and
+// g + 8 of each tile (bank-conflict
 // free at the 144-byte row stride): the low nibbles of that word are the
 // lane's four A elements of the sub-block's first MMA, the high nibbles those
 // of its second, so every MMA covers exactly one sub-block (the k order inside
 // a sub-block is permuted the same way in A and in the staged x fragments).
 // The header of each row's super-block is decoded once per warp (lane l: row
 // l) into shared memory.
-// With more than one K chunk, each CTA writes its 128 x n partial sums to a
+// With more than one K chunk, each CTA writes its 256 x n partial sums to a
 // workspace and the last CTA of the row block (an atomic counter; no CTA
 // waits on another) sums the chunks in chunk order -- results do not depend
 // on timing -- and applies the epilogue.
@@ -129,7 +130,7 @@ __device__ __forceinline__ void stage_weights(unsigned char* stage, const unsign
 }
 
 template <int NT, int EPI>
-__global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
+__global__ void __launch_bounds__(NTHREADS, 2) mv_kernel(const MvArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int KC = a.KC;
     const int nsub = KC / 32;
@@ -320,12 +321,17 @@ __global__ void __launch_bounds__(NTHREADS) mv_kernel(const MvArgs a) {
         // write this chunk's part; the last CTA of the row block sums them
         float* part = a.ws + ((size_t)kc * gridDim.x + rb) * (8 * NT) * ROWS;
         for (int col = 0; col < a.n; ++col) part[col * ROWS + tid] = tile[col * TROW + tid];
-        __threadfence();
+        // the CTA's writes reach thread 0 through the barrier; its GPU-scope
+        // fence orders them (cumulatively) before the count, and after the
+        // count for the CTA that finishes the row block
         __syncthreads();
-        if (tid == 0) s_last = atomicAdd(&a.cnt[rb], 1) == a.nkc - 1;
+        if (tid == 0) {
+            __threadfence();
+            s_last = atomicAdd(&a.cnt[rb], 1) == a.nkc - 1;
+            if (s_last) __threadfence();
+        }
         __syncthreads();
         if (!s_last) return;
-        __threadfence();
         float sum[8 * NT];
 #pragma unroll
         for (int col = 0; col < 8 * NT; ++col) sum[col] = 0.f;
