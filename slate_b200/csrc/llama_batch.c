@@ -163,6 +163,14 @@ static int step_norm(slate_llama_batch_t* b, sb_lane* L, const float* w, int n, 
     return sb_rmsnorm_rows(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps, s);
 }
 
+/* Whether the f32 LM head runs on the tensor cores as its f16 hi/lo pair: from
+ * SB_TC_MIN_ROWS rows, and from 4 rows where the operand's row box is small
+ * (an engine of at most 64 rows), since the CUDA-core GEMV is FMA-bound from
+ * about 4 rows while the tensor-core pass costs the same up to its box. */
+static int head_on_tc(const slate_llama_batch_t* b, const sb_lane* L, int n) {
+    return b->head_tc.hi && (n >= SB_TC_MIN_ROWS || (n >= 4 && L->op_d->n_box <= 64));
+}
+
 /* Whether a GEMM of this lane runs on the stream-K kernel. */
 static int uses_sk(const slate_llama_batch_t* b, const sb_lane* L, const sb_matrix* W, int n,
                    int epi) {
@@ -180,7 +188,7 @@ static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, con
      * attention) wrote it */
     const int have_d = in == IN_XN && L->xn_split;
     const int have_a = in == IN_ATT && L->att_split;
-    if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) {
+    if (W == &b->lm_head && head_on_tc(b, L, n)) {
         int rc = have_d ? 0 : sb_tc_split(X, ldx, n, L->op_d, s);
         return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, L->op_d, n, Y, ldy, epi, b->tc_err, s);
     }
@@ -520,7 +528,7 @@ static int enqueue_step(slate_llama_batch_t* b, int n, int sample, int chunk, in
 static int gemm_launches(const slate_llama_batch_t* b, const sb_lane* L, const sb_matrix* W, int n,
                          int epi, int splits, int pre) {
     const int split = pre && norm_splits(b, L, n) ? 0 : 1;
-    if (W == &b->lm_head && b->head_tc.hi && n >= SB_TC_MIN_ROWS) return split + 1;
+    if (W == &b->lm_head && head_on_tc(b, L, n)) return split + 1;
     if (L->mv_ws && W->wtype == SB_WT_Q4K && n <= SB_MV_MAX_ROWS) return 1;
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2;                                                               /* split + GEMM */
