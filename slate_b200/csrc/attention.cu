@@ -174,7 +174,7 @@ __global__ void rmsnorm_kernel(float* __restrict__ Y, int ldy, const float* __re
 // The same normalisation with the row held in registers (float4, up to
 // RN_MAX * 4 * RN_T elements) and, besides the f32 row, the row as the f16
 // hi / lo pair (hi = f16(y), lo = f16(y - hi)) that the tensor-core GEMMs take
-// as their operand (lo may be null).  Sum of squares: f32 per thread, double
+// as their operand (hi null: f32 row only; lo may be null).  Sum of squares: f32 per thread, double
 // across the block, as above.
 constexpr int RN_T = 256, RN_MAX = 8;
 __global__ void __launch_bounds__(RN_T) rmsnorm_split_kernel(
@@ -210,8 +210,8 @@ __global__ void __launch_bounds__(RN_T) rmsnorm_split_kernel(
     const float inv = 1.0f / sqrtf((float)(red[0] / (double)D) + eps);
     const float4* w4 = (const float4*)w;
     float4* y4 = (float4*)(Y + (size_t)n * ldy);
-    uint2* h2 = (uint2*)(hi + (size_t)n * ld16);
-    uint2* l2 = lo ? (uint2*)(lo + (size_t)n * ld16) : nullptr;
+    uint2* h2 = hi ? (uint2*)(hi + (size_t)n * ld16) : nullptr;
+    uint2* l2 = hi && lo ? (uint2*)(lo + (size_t)n * ld16) : nullptr;
 #pragma unroll
     for (int j = 0; j < RN_MAX; ++j) {
         const int i = threadIdx.x + j * RN_T;
@@ -220,6 +220,7 @@ __global__ void __launch_bounds__(RN_T) rmsnorm_split_kernel(
         const float4 y = make_float4(v[j].x * g.x * inv, v[j].y * g.y * inv, v[j].z * g.z * inv,
                                      v[j].w * g.w * inv);
         y4[i] = y;
+        if (!h2) continue;
         const __half2 a = __floats2half2_rn(y.x, y.y), b = __floats2half2_rn(y.z, y.w);
         h2[i] = make_uint2(*(const uint32_t*)&a, *(const uint32_t*)&b);
         if (l2) {
@@ -564,7 +565,7 @@ extern "C" int sb_rmsnorm_rows(float* Y, int ldy, const float* X, int ldx, const
 extern "C" int sb_rmsnorm_rows_split(float* Y, int ldy, const float* X, int ldx, const float* w,
                                      int B, int D, float eps, void* hi, void* lo, int ld16,
                                      cudaStream_t st) {
-    if (B < 1 || D < 1 || !hi) return -1;
+    if (B < 1 || D < 1) return -1;
     if (D % 4 || D > RN_MAX * 4 * RN_T || ldx % 4 || ldy % 4 || ld16 % 4 || ((uintptr_t)X & 15) ||
         ((uintptr_t)Y & 15) || ((uintptr_t)w & 15) || B > 0x7fffffff)
         return -1;

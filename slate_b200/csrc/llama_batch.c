@@ -160,6 +160,12 @@ static int step_norm(slate_llama_batch_t* b, sb_lane* L, const float* w, int n, 
         L->xn_split = 1;
         return 0;
     }
+    /* f32 rows only, through the same kernel where the shape allows: it stays in
+     * the programmatic launch chain, so the GEMM after it starts streaming its
+     * weights while it runs */
+    if (sb_rmsnorm_rows_split(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps, NULL,
+                              NULL, 0, s) == 0)
+        return 0;
     return sb_rmsnorm_rows(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps, s);
 }
 
