@@ -12,16 +12,22 @@ CUDA graph); `value` = tokens/s over all ranks with inputs already in HBM,
 Contexts: prompt U[128, 4096] plus a uniform offset of U[0, 256) already-decoded
 tokens (the steady state of 256-token budgets under continuous refill), seeded
 on the device as synthetic K/V.  The timed window is shorter than a budget, so
-no sequence finishes inside it.  The KV read per step (~75 GB f16) exceeds the
-126 MB L2, so no flush is needed between steps.
+no sequence finishes inside it.  The KV cache is f32 by default, the
+reference's own dtype (llama_infer.c:225-226); the same measurement with an f16
+cache is reported as the labelled extra `variant_kv_f16`.  The KV read per step
+(~150 GB f32, ~75 GB f16) exceeds the 126 MB L2, so no flush is needed between
+steps.
 
 Multi-GPU: sequences are independent, so each rank is a replica running its own
 256 sequences (weak scaling, no collective on the data path); torch.distributed
 (nccl) only provides the barrier and the max-over-ranks timing.
 
 --impl reference: the reference's own CPU path (oracle/_ref, the unmodified
-slate sources) on this host's cores, one slate_llama_decode_step session per
-thread, timed at a few context lengths and fitted per token as a + b*ctx.
+slate sources) on this host's cores: one slate_llama_decode_step session per
+thread, each holding a seeded history of the benchmark's own context
+distribution; a step = every session decodes one greedy token.  The process
+maps only oracle/ libraries (the workload file is written by the CPU-only
+writer in oracle/build).
 """
 from __future__ import annotations
 
@@ -51,12 +57,12 @@ MODELS = {"8b": dict(cfg=CFG3, metric=METRIC, batch=256, prompt=(128, 4096), per
                      workload="llama3-8b-shape q4k continuous-batching decode (BASELINE config 3)"),
           "70b": dict(cfg=CFG5, metric=METRIC70, batch=512, prompt=(256, 2048), period=8,
                       workload="llama3-70b-shape q4k tensor-parallel decode (BASELINE config 5)")}
-# DRAM bytes (read + write) per algorithmic byte of one attn_chunk_mma launch, from
-# an ncu capture of 32 rows at the 8B shape (profiles/attn_chunk_mma_8b_b32.md:
-# 300.39 MB read + 5.20 MB written for 300.74 MB of K/V, q and output, 1024-token
-# chunks).  Traffic scales with the K/V tokens read, so the full launch's traffic is
-# this ratio times its algorithmic bytes.
-ATTN_MMA_TRAFFIC_RATIO = 1.0161
+# DRAM bytes (read + write) per algorithmic byte of one attention launch, from ncu
+# captures of 32 rows at the 8B shape with 1024-token chunks (dram__bytes_read.sum +
+# dram__bytes_write.sum over K/V + q + output bytes).  f16 KV (attn_chunk_mma):
+# 300.39 MB read + 5.20 MB written for 300.74 MB.  Traffic scales with the K/V
+# tokens read, so a full launch's traffic is the ratio times its algorithmic bytes.
+ATTN_TRAFFIC_RATIO = {"f16": 1.0161, "f32": None}
 
 
 def parse():
@@ -65,7 +71,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
+    ap.add_argument("--kv", default="f32", choices=["f16", "f32"],
+                    help="KV cache dtype of the headline (f32: the reference's)")
+    ap.add_argument("--variant-kv", default="auto", choices=["auto", "none", "f16", "f32"],
+                    help="also time the other KV dtype and report it as variant_kv_<dtype> "
+                         "(auto: f16 when the headline is f32)")
     ap.add_argument("--model", default="8b", choices=list(MODELS),
                     help="8b: the headline (config 3, replicas); 70b: config 5 with --tp")
     ap.add_argument("--tp", type=int, default=1,
@@ -90,7 +100,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=-1,
                     help="host-API steps for the e2e figure (default: --steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--cpu-steps", type=int, default=4,
+                    help="decode steps of the reference sessions for cpu_baseline (after 1 warm-up)")
+    ap.add_argument("--cpu-threads", type=int, default=0, help="reference sessions (0: all cores)")
     return ap.parse_args()
 
 
@@ -103,15 +115,16 @@ def model_path(args, cfg) -> str:
     return os.path.join("/tmp", tag)
 
 
-def ensure_model(args, cfg, rank, barrier) -> str:
-    import slate_b200 as sb
+def ensure_model(args, cfg, barrier, writer) -> str:
+    """The benchmark's GGUF, written once per host by `writer` (the product's
+    slate_b200.synth_gguf, or oracle.synth_gguf -- the same bytes -- in the
+    reference arm, which must not map the product library)."""
     path = model_path(args, cfg)
     if int(os.environ.get("LOCAL_RANK", "0")) == 0 and not os.path.exists(path):
         tmp = path + f".{os.getpid()}.tmp"
         # the 70B file repeats a period of 8 distinct random layers (written in
         # about a minute instead of ten); the engine still holds every layer
-        sb.synth_gguf(tmp, q4k=True, seed=args.seed, layer_period=MODELS[args.model]["period"],
-                      **cfg)
+        writer(tmp, q4k=True, seed=args.seed, layer_period=MODELS[args.model]["period"], **cfg)
         os.rename(tmp, path)
     barrier()
     return path
@@ -189,129 +202,126 @@ class ClockSampler:
                 "power_w": statistics.median(pw) if pw else None, "samples": len(sm)}
 
 
+def kv_dtype_name(args) -> str:
+    """The headline KV dtype: --kv, except that the 70B shape at 2-way tensor
+    parallelism keeps f16 (its f32 cache would need ~214 GB per GPU)."""
+    if args.model == "70b" and args.tp < 4 and "--kv" not in " ".join(sys.argv):
+        return "f16"
+    return args.kv
+
+
 # ---------------------------------------------------------------------------
-# reference CPU baseline (oracle/_ref: the reference's own sources)
+# reference CPU path (oracle/_ref: the reference's own sources)
 # ---------------------------------------------------------------------------
-def reference_cpu(path, cfg, budget_s, threads=None):
-    """Per-token time of slate_llama_decode_step at a few context lengths, one
-    reference session per thread.  A session's dense KV cache is calloc'd by
-    the reference (llama_infer.c:225-226); to decode at context c its position
-    field (struct slate_llama_session, llama_infer.c:53-59: model, backend,
-    position, ...) is set to c, so attention reads c zero-initialised rows --
-    the same work as a real c-token history (the CPU attention has no
-    data-dependent shortcuts).  Fits t = a + b*ctx."""
-    import ctypes as C
+def reference_cpu(path, ctx, seeds, warmup, steps, threads=0):
+    """Greedy decode through the reference's slate_llama_decode_step
+    (src/loader/llama_infer.c:274-279), one session per host thread.
+
+    The reference's LLaMA path is single-threaded and unbatched
+    (util/quant.c:306-313, backend/backend_cpu.c:33-36), so one session per
+    core is its best host throughput.  Session i holds a seeded history of
+    ctx[i] tokens (slate_ref_session_seed_context: the values the CUDA engine
+    seeds for the same seed) and decodes warmup + steps tokens, each fed its
+    previous greedy token; a step ends when every session has its token.  The
+    session count is capped by host memory (each session callocs a dense f32
+    KV cache of 2 * layers * max_seq * kv_dim floats, llama_infer.c:225-226)."""
     import oracle as O
     ref = O.Reference()
     g, m = ref.open(path)
-    V = ref.config(m)["vocab"]
-    n_thr = threads or os.cpu_count() or 1
-    pts = [128, 2048, 4096]
-    per_pt = []
-    t_start = time.time()
-    for ctx in pts:
-        if time.time() - t_start > budget_s and per_pt:
+    c = ref.config(m)
+    V = c["vocab"]
+    sess_bytes = 2 * c["n_layers"] * c["max_seq"] * c["n_kv_heads"] * c["head_dim"] * 4
+    n = threads or os.cpu_count() or 1
+    try:
+        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+        n = max(1, min(n, int(0.6 * avail // sess_bytes)))
+    except (ValueError, OSError):
+        pass
+    n = min(n, len(ctx))
+    sess = [None] * n
+    out = [np.zeros(V, np.float32) for _ in range(n)]
+    tok = [int(t) for t in np.random.default_rng(int(seeds[0])).integers(0, V, n)]
+    rcs = [0] * n
+    t_seed = time.time()
+
+    def make(i):
+        sess[i] = ref.session(m, int(ctx[i]), int(seeds[i]))
+
+    th = [threading.Thread(target=make, args=(i,)) for i in range(n)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    t_seed = time.time() - t_seed
+    gate = threading.Barrier(n + 1)
+    stop = []
+
+    def worker(i):
+        while True:
+            gate.wait()
+            if stop:
+                return
+            rcs[i] = ref.decode(sess[i], tok[i], out[i])
+            tok[i] = int(np.argmax(out[i]))
+            gate.wait()
+
+    th = [threading.Thread(target=worker, args=(i,)) for i in range(n)]
+    for t in th:
+        t.start()
+    step_s = []
+    for k in range(warmup + steps):
+        t0 = time.perf_counter()
+        gate.wait()
+        gate.wait()
+        if k >= warmup:
+            step_s.append(time.perf_counter() - t0)
+        if any(rcs):
             break
-        times = [0.0] * n_thr
-
-        def work(i):
-            s = ref.lib.slate_llama_session_new(m)
-            C.c_int.from_address(s + 16).value = ctx        # position
-            out = np.zeros(V, np.float32)
-            t0 = time.perf_counter()
-            rc = ref.lib.slate_llama_decode_step(s, 1, out.ctypes.data_as(C.POINTER(C.c_float)))
-            times[i] = time.perf_counter() - t0 if rc == 0 else float("nan")
-            ref.lib.slate_llama_session_free(s)
-
-        th = [threading.Thread(target=work, args=(i,)) for i in range(n_thr)]
-        for t in th:
-            t.start()
-        for t in th:
-            t.join()
-        per_pt.append((ctx, float(np.nanmedian(times))))
+    stop.append(True)
+    gate.wait()
+    for t in th:
+        t.join()
+    for s in sess:
+        ref.lib.slate_llama_session_free(s)
     ref.close(g, m)
-    x = np.array([p[0] for p in per_pt], float)
-    y = np.array([p[1] for p in per_pt], float)
-    b = float(np.polyfit(x, y, 1)[0]) if len(x) > 1 else 0.0
-    a = float(y.mean() - b * x.mean())
-    mean_ctx = (128 + 4096) / 2 + 128          # prompt U[128,4096] + half a 256-token budget
-    t_tok = a + b * mean_ctx
-    return {"value": n_thr / t_tok, "unit": "tok/s", "cores": n_thr, "kind": "reference",
-            "sample": (f"{n_thr} concurrent reference sessions (one per thread), 1 decode token each "
-                       f"at ctx {[p[0] for p in per_pt]}; per-token s {[round(p[1], 3) for p in per_pt]}; "
-                       f"extrapolated to mean ctx {mean_ctx:.0f} as t = a + b*ctx"),
-            "seconds": round(time.time() - t_start, 1)}
+    if any(rcs) or len(step_s) < steps:
+        raise RuntimeError(f"reference decode failed: rc {sorted(set(rcs))}")
+    tot = sum(step_s)
+    used = np.asarray(ctx[:n], np.float64)
+    return {"value": n * steps / tot, "unit": "tok/s", "cores": n, "kind": "reference",
+            "ms_per_step": 1000.0 * tot / steps, "p50_step_ms": 1000.0 * float(np.median(step_s)),
+            "steps": steps, "warmup": warmup, "sessions": n, "mean_ctx": float(used.mean()),
+            "sample": (f"{n} reference sessions in parallel (one per host thread, the unbatched "
+                       f"slate_llama_decode_step), histories of {int(used.min())}-{int(used.max())} "
+                       f"tokens (mean {used.mean():.0f}) seeded from the benchmark's context "
+                       f"distribution, {warmup} warm-up + {steps} timed greedy tokens each"),
+            "seed_s": round(t_seed, 1)}
 
 
-def main():
-    args = parse()
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    spec = MODELS[args.model]
-    cfg = dict(spec["cfg"])
-    if args.layers:
-        cfg["n_layers"] = args.layers
-    if not args.batch:
-        args.batch = spec["batch"]
-    tp = max(1, args.tp)
-    if world % tp:
-        raise SystemExit(f"--tp {tp} must divide the {world} ranks")
-    replica, tp_rank = rank // tp, rank % tp
-
-    if args.impl == "reference":
-        if rank != 0:
-            return 0
-        if args.model != "8b":
-            print(json.dumps({"impl": "reference", "unavailable":
-                              "the reference CPU arm is timed on the 8b headline config only"}))
-            return 0
-        import oracle as O
-        if not O.Reference.available():
-            print(json.dumps({"impl": "reference", "unavailable":
-                              "oracle/_ref/libslate_ref.so was not built (reference sources absent at build time)"}))
-            return 0
-        path = ensure_model(args, cfg, rank, lambda: None)
-        t0 = time.time()
-        cpu = reference_cpu(path, cfg, args.cpu_seconds)
-        line = {"metric": METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / (cpu["value"] / cpu["cores"]),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic", "impl": "reference",
-                "config": {"workload": "llama3-8b-shape q4k decode, reference CPU sessions", "seqs": cpu["cores"],
-                           "kv_dtype": "f32", "contexts": "sampled, extrapolated"},
-                "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
-                "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0},
-                "wall_s": round(time.time() - t0, 1)}
-        print(json.dumps(line))
-        return 0
-
+# ---------------------------------------------------------------------------
+# one measurement of the CUDA engine
+# ---------------------------------------------------------------------------
+def measure(args, cfg, path, kv_name, env, full=True):
+    """Warm-up + timed decode steps of one engine with a KV cache of `kv_name`;
+    with `full`, also the e2e figure, per-kernel times and the prompt prefill."""
     import torch
     import slate_b200 as sb
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
-
-        def barrier():
-            dist.barrier()
-    else:
-        dist = None
-
-        def barrier():
-            pass
-
-    path = ensure_model(args, cfg, rank, barrier)
-    kv = sb.KV_F16 if args.kv == "f16" else sb.KV_F32
+    dist, barrier, world, local, tp, tp_rank, replica, tp_id = (
+        env[k] for k in ("dist", "barrier", "world", "local", "tp", "tp_rank", "replica", "tp_id"))
+    kv = sb.KV_F16 if kv_name == "f16" else sb.KV_F32
+    esz = 2 if kv == sb.KV_F16 else 4
     n = args.batch
     total_steps = args.warmup + args.steps
+    e2e_steps = (args.e2e_steps if args.e2e_steps >= 0 else args.steps) if full else 0
     ctx = contexts(args, cfg, n, replica, 3 * total_steps + 4)
-    tp_id = tp_group_id(dist, world, tp, rank, sb.tp_unique_id) if tp > 1 else b""
+    D, L, V = cfg["d_model"], cfg["n_layers"], cfg["vocab"]
+    hd = D // cfg["n_heads"]
+    nq, nkv, F = cfg["n_heads"] // tp, cfg["n_kv_heads"] // tp, cfg["ffn_hidden"] // tp
+    # pool: every sequence's pages through the last step, the two prefill prompts
+    pf = args.prefill_tokens if full and 0 < args.prefill_tokens < cfg["max_seq"] else 0
+    pages = int(sum((int(c) + total_steps + e2e_steps + 2) // 16 + 1 for c in ctx)) + 2 * (pf // 16 + 2) + 64
     eng = sb.LlamaBatch(path, device=local, max_batch=n, max_slots=n, kv_dtype=kv,
-                        max_seq=cfg["max_seq"], gemm_path=args.gemm_path,
+                        max_seq=cfg["max_seq"], kv_pages=pages, gemm_path=args.gemm_path,
                         attn_path=args.attn_path, tp_size=tp, tp_rank=tp_rank, tp_id=tp_id,
                         lanes=args.lanes)
     slots = np.array([eng.open() for _ in range(n)], np.int32)
@@ -322,7 +332,7 @@ def main():
     stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
     d_slots = torch.tensor(slots, device="cuda")
     rng = np.random.default_rng(args.seed + replica)     # one token stream per TP group
-    d_tok = [torch.tensor(rng.integers(0, cfg["vocab"], n).astype(np.int32), device="cuda"),
+    d_tok = [torch.tensor(rng.integers(0, V, n).astype(np.int32), device="cuda"),
              torch.zeros(n, dtype=torch.int32, device="cuda")]
 
     def dstep(i):
@@ -353,65 +363,54 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         tot_ms = float(t.item())
     replicas = world // tp
-    value = n * replicas * args.steps / (tot_ms / 1000.0)
+    res = {"kv": kv_name, "value": n * replicas * args.steps / (tot_ms / 1000.0), "tot_ms": tot_ms,
+           "step_ms": step_ms, "ctx": ctx, "replicas": replicas, "clocks": clk.summary(),
+           "launches": eng.launches_per_step(n) * args.steps}
 
     # end to end through the host-buffer API: H2D slots+tokens, D2H greedy tokens;
     # right after the timed region, so that both run in the same power state
-    host_tok = d_tok[args.steps & 1 ^ (args.warmup & 1)].cpu().numpy()
-    e2e_steps = args.e2e_steps if args.e2e_steps >= 0 else args.steps
-    torch.cuda.synchronize()
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        rc, host_tok, _ = eng.step(slots, host_tok)
-        assert rc == 0, sb.last_error()
-    e2e_s = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = n * replicas * e2e_steps / e2e_s if e2e_steps else None
+    if e2e_steps:
+        host_tok = d_tok[args.steps & 1 ^ (args.warmup & 1)].cpu().numpy()
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            rc, host_tok, _ = eng.step(slots, host_tok)
+            assert rc == 0, sb.last_error()
+        e2e_s = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        res["e2e"] = {"value": n * replicas * e2e_steps / e2e_s, "unit": "tok/s",
+                      "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": n * 4}
 
     # per-kernel timing of the dominant kernels on the same state and stream
     layer = cfg["n_layers"] // 2
-    kt = {name: eng.profile(k, n, layer, iters=10) for name, k in
-          [("attention", sb.PROF_ATTENTION), ("qkv", sb.PROF_QKV), ("wo", sb.PROF_WO),
-           ("gate_up", sb.PROF_GATE_UP), ("down", sb.PROF_DOWN), ("lm_head", sb.PROF_LM_HEAD)]}
-    esz = 2 if kv == sb.KV_F16 else 4
-    # per-rank shares (tp = 1: the whole model)
-    D, L, V = cfg["d_model"], cfg["n_layers"], cfg["vocab"]
-    hd = D // cfg["n_heads"]
-    nq, nkv, F = cfg["n_heads"] // tp, cfg["n_kv_heads"] // tp, cfg["ffn_hidden"] // tp
+    groups = [("attention", sb.PROF_ATTENTION)]
+    if full:
+        groups += [("qkv", sb.PROF_QKV), ("wo", sb.PROF_WO), ("gate_up", sb.PROF_GATE_UP),
+                   ("down", sb.PROF_DOWN), ("lm_head", sb.PROF_LM_HEAD)]
+    kt = {name: eng.profile(k, n, layer, iters=10) for name, k in groups}
+    res["kernel_ms"] = kt
     ctx_now = ctx + total_steps + e2e_steps            # contexts seen by the profiled launch
-    attn_bytes = float(ctx_now.sum()) * 2 * nkv * hd * esz + n * nq * hd * 4 * 3
+    res["attn_bytes"] = float(ctx_now.sum()) * 2 * nkv * hd * esz + n * nq * hd * 4 * 3
     q4k = 144 / 256
     w_layer = (D * (nq + 2 * nkv) * hd + nq * hd * D + 3 * D * F) * q4k
     head = V // tp * D * 4
     kv_read_step = float((ctx + total_steps - args.steps // 2).sum()) * 2 * nkv * hd * esz * L
-    step_bytes = w_layer * L + head + kv_read_step + n * 2 * nkv * hd * esz * L
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        peak, peak_src = float(peaks["hbm_gbs"]), "measured"
-    except Exception:
-        peak, peak_src = 6650.0, "fallback"
-    achieved = attn_bytes / (kt["attention"] / 1000.0) / 1e9
-    traffic = None
-    if args.kv == "f16" and args.attn_path == 0:
-        traffic = ATTN_MMA_TRAFFIC_RATIO * attn_bytes
-    step_s = tot_ms / 1000.0 / args.steps
-
+    res["step_bytes"] = w_layer * L + head + kv_read_step + n * 2 * nkv * hd * esz * L
 
     # prompt prefill through slate_llama_batch_prefill (chunks of max_batch
     # prompt rows with the causal prefill attention): one sequence's slot is
     # released and a fresh prompt of --prefill-tokens tokens admitted into it
-    prefill = None
-    if args.prefill_tokens > 0 and args.prefill_tokens < cfg["max_seq"] and n >= 2:
+    res["prefill"] = None
+    if pf and n >= 2:
         for s in slots[:2]:
             assert eng.release(int(s)) == 0, sb.last_error()
         warm, ps = eng.open(), eng.open()
-        rng = np.random.default_rng(args.seed)
-        prompts = [rng.integers(0, cfg["vocab"], args.prefill_tokens).astype(np.int32) for _ in range(2)]
+        prng = np.random.default_rng(args.seed)
+        prompts = [prng.integers(0, V, pf).astype(np.int32) for _ in range(2)]
         rc, _ = eng.prefill(warm, prompts[0], want_logits=False)   # captures the chunk graphs
         assert rc == 0, sb.last_error()
         torch.cuda.synchronize()
@@ -419,60 +418,172 @@ def main():
         rc, _ = eng.prefill(ps, prompts[1], want_logits=False)
         pf_s = time.perf_counter() - t0
         assert rc == 0, sb.last_error()
-        prefill = {"tokens": args.prefill_tokens, "ms": pf_s * 1e3,
-                   "tok_s": args.prefill_tokens / pf_s, "rows_per_step": n,
-                   "note": "one prompt into a released slot through the host API (wall clock, "
-                           "chunk graphs already captured by a first prompt)"}
+        res["prefill"] = {"tokens": pf, "ms": pf_s * 1e3, "tok_s": pf / pf_s, "rows_per_step": n,
+                          "note": "one prompt into a released slot through the host API (wall "
+                                  "clock, chunk graphs already captured by a first prompt)"}
+    eng.close()
+    return res
+
+
+def attn_kernel_name(kv_name, args):
+    return ("attn_chunk_mma+attn_combine" if kv_name == "f16" and args.attn_path == 0
+            else "attn_chunk+attn_combine") + " (paged GQA attention, one layer)"
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    spec = MODELS[args.model]
+    cfg = dict(spec["cfg"])
+    if args.layers:
+        cfg["n_layers"] = args.layers
+    if not args.batch:
+        args.batch = spec["batch"]
+    tp = max(1, args.tp)
+    if world % tp:
+        raise SystemExit(f"--tp {tp} must divide the {world} ranks")
+    replica, tp_rank = rank // tp, rank % tp
+    kv_name = kv_dtype_name(args)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        if args.model != "8b":
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference CPU arm is timed on the 8b headline config only"}))
+            return 0
+        import oracle as O
+        if not O.Reference.available():
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "oracle/_ref/libslate_ref.so was not built (reference sources absent at build time)"}))
+            return 0
+        t0 = time.time()
+        path = ensure_model(args, cfg, lambda: None, O.synth_gguf)
+        ctx = contexts(args, cfg, args.batch, 0, 3 * (args.warmup + args.steps) + 4)
+        cpu = reference_cpu(path, ctx, [args.seed + i for i in range(len(ctx))], args.warmup,
+                            args.steps, args.cpu_threads)
+        line = {"metric": METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": cpu["ms_per_step"],
+                "p50_step_ms": cpu["p50_step_ms"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": {"workload": "llama3-8b-shape q4k greedy decode, reference CPU sessions "
+                                       "(BASELINE config 3 contexts)",
+                           "seqs": cpu["sessions"], "kv_dtype": "f32", "mean_ctx": cpu["mean_ctx"],
+                           "step": "every session decodes one token"},
+                "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "wall_s": round(time.time() - t0, 1)}
+        print(json.dumps(line))
+        return 0
+
+    import torch
+    import slate_b200 as sb
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+        def barrier():
+            dist.barrier()
+    else:
+        dist = None
+
+        def barrier():
+            pass
+
+    path = ensure_model(args, cfg, barrier, sb.synth_gguf)
+    tp_id = tp_group_id(dist, world, tp, rank, sb.tp_unique_id) if tp > 1 else b""
+    env = dict(dist=dist, barrier=barrier, world=world, local=local, tp=tp, tp_rank=tp_rank,
+               replica=replica, tp_id=tp_id)
+    main_res = measure(args, cfg, path, kv_name, env, full=True)
+    variant = args.variant_kv
+    if variant == "auto":
+        variant = "f16" if kv_name == "f32" and args.model == "8b" else "none"
+    var_res = None
+    if variant != "none" and variant != kv_name:
+        if tp > 1:                      # a fresh NCCL group for the second engine
+            env["tp_id"] = tp_group_id(dist, world, tp, rank, sb.tp_unique_id)
+        var_res = measure(args, cfg, path, variant, env, full=False)
 
     cpu = None
     if rank == 0 and world == 1 and args.model == "8b" and not args.no_cpu_baseline:
         import oracle as O
         if O.Reference.available():
-            cpu = reference_cpu(path, cfg, args.cpu_seconds)
-    launches = eng.launches_per_step(n) * args.steps
-    clocks = clk.summary()
-    eng.close()
+            ctx = main_res["ctx"]
+            cpu = reference_cpu(path, ctx, [args.seed + i for i in range(len(ctx))], 1,
+                                args.cpu_steps, args.cpu_threads)
     if dist:
         barrier()
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak, peak_src = float(peaks["hbm_gbs"]), "measured"
+    except Exception:
+        peak, peak_src = 6650.0, "fallback"
+
+    def step_roofline(r):
+        step_s = r["tot_ms"] / 1000.0 / args.steps
+        return {"bytes_per_step": r["step_bytes"], "achieved_GBps": r["step_bytes"] / step_s / 1e9,
+                "frac_of_measured": r["step_bytes"] / step_s / 1e9 / peak,
+                "frac_of_8TBps": r["step_bytes"] / step_s / 8e12}
+
+    def attn_roofline(r):
+        ms = r["kernel_ms"]["attention"]
+        achieved = r["attn_bytes"] / (ms / 1000.0) / 1e9
+        ratio = ATTN_TRAFFIC_RATIO.get(r["kv"]) if args.attn_path == 0 or r["kv"] == "f32" else None
+        return {"bound": "hbm", "kernel": attn_kernel_name(r["kv"], args), "achieved": achieved,
+                "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": None if ratio is None else ratio * r["attn_bytes"],
+                "algorithmic_bytes_per_launch": r["attn_bytes"], "launch_ms": ms}
+
+    r = main_res
+    replicas = r["replicas"]
+    n = args.batch
     line = {
-        "metric": spec["metric"], "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
-        "p50_step_ms": float(np.median(step_ms)), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "metric": spec["metric"], "value": r["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["tot_ms"] / args.steps,
+        "p50_step_ms": float(np.median(r["step_ms"])), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32" if kv_name == "f32" else "f32 (KV cache stored as f16)", "data": "synthetic",
         "config": {"workload": spec["workload"],
                    "model": f"llama3-{args.model}-shape random N(0,0.02) Q4_K", "layers": cfg["n_layers"],
-                   "global_batch": n * replicas, "seqs_per_replica": n, "kv_dtype": args.kv,
-                   "mean_ctx": float(ctx.mean()),
+                   "global_batch": n * replicas, "seqs_per_replica": n, "kv_dtype": kv_name,
+                   "mean_ctx": float(r["ctx"].mean()),
                    "parallelism": f"replicas x{replicas}" + (f", tensor parallel {tp}" if tp > 1 else ""),
                    "gemm_path": {0: "tcgen05 3-pass hi/lo, stream-K (weights in TMEM) from 128 rows",
                                  1: "cuda-core f32", 2: "tcgen05 1-pass f16",
                                  3: "tcgen05 3-pass hi/lo, tile per CTA",
                                  4: "tcgen05 exact f16 weights, 2-pass x, stream-K",
                                  5: "tcgen05 3-pass hi/lo, weights in TMEM, stream-K"}[args.gemm_path],
-                   "attn_path": ("mma.sync f16 hi/lo" if args.attn_path == 0 and args.kv == "f16"
+                   "attn_path": ("mma.sync f16 hi/lo" if args.attn_path == 0 and kv_name == "f16"
                                  else "cuda-core"),
                    "lanes": args.lanes,
                    "l2": "inputs larger than L2 (KV read per step >> 126 MB)"},
-        "roofline": {"bound": "hbm",
-                     "kernel": ("attn_chunk_mma+attn_combine" if args.kv == "f16" and args.attn_path == 0
-                                else "attn_chunk+attn_combine") + " (paged GQA attention, one layer)",
-                     "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": kt["attention"]},
-        "step_roofline": {"bytes_per_step": step_bytes, "achieved_GBps": step_bytes / step_s / 1e9,
-                          "frac_of_measured": step_bytes / step_s / 1e9 / peak,
-                          "frac_of_8TBps": step_bytes / step_s / 8e12},
-        "kernel_ms": kt,
-        "e2e": None if e2e is None else {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": n * 8,
-                                         "d2h_bytes_per_step": n * 4},
-        "gpu_launches": launches,
-        "prefill": prefill,
-        "clocks": clocks,
+        "roofline": attn_roofline(r),
+        "step_roofline": step_roofline(r),
+        "kernel_ms": r["kernel_ms"],
+        "e2e": r.get("e2e"),
+        "gpu_launches": r["launches"],
+        "prefill": r["prefill"],
+        "clocks": r["clocks"],
         "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
     }
+    if var_res is not None:
+        v = var_res
+        line[f"variant_kv_{v['kv']}"] = {
+            "value": v["value"], "unit": "tok/s", "ms_per_step": v["tot_ms"] / args.steps,
+            "p50_step_ms": float(np.median(v["step_ms"])), "kv_dtype": v["kv"],
+            "note": "same workload, seeds and steps with the KV cache in " + v["kv"],
+            "roofline": attn_roofline(v), "step_roofline": step_roofline(v), "clocks": v["clocks"],
+            "gpu_launches": v["launches"]}
     print(json.dumps(line))
     return 0
 

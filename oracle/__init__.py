@@ -1,6 +1,6 @@
 """oracle -- TEST INFRASTRUCTURE: CPU checkers for the CUDA decode path.
 
-Two checkers, both loaded with ctypes:
+Two checkers and one workload writer, all loaded with ctypes:
   * `Oracle`    -- build/liboracle.so, the C restatement in slate_oracle.c of
                    the reference's LLaMA Q4_K decode (each function cites the
                    reference file:line it follows);
@@ -8,6 +8,10 @@ Two checkers, both loaded with ctypes:
                    (eating-and-drinking/slate) compiled unmodified by
                    oracle/Makefile; absent where the reference tree was never
                    available to build it.
+  * `synth_gguf` -- build/libslate_synth.so, the synthetic-model writer of
+                   slate_b200/csrc/synth.c compiled alone (no CUDA), so a
+                   process that times the reference on the CPU writes the same
+                   workload file without mapping the product library.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
 package; the product library never links or calls it.
@@ -22,6 +26,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "build", "liboracle.so")
+SYNTH_SO = os.path.join(HERE, "build", "libslate_synth.so")
 REF_SO = os.path.join(HERE, "_ref", "libslate_ref.so")
 
 Pf = C.POINTER(C.c_float)
@@ -34,6 +39,33 @@ def build(ref_root: str | None = None) -> None:
     if ref_root:
         args.append(f"REF={ref_root}")
     subprocess.run(args, check=True, stdout=subprocess.DEVNULL)
+
+
+class SynthConfig(C.Structure):
+    """slate_synth_config_t (include/slate_cuda.h)."""
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d_model", "ffn_hidden", "n_heads", "n_kv_heads",
+                                       "vocab", "max_seq")] + [
+        ("theta_base", C.c_float), ("rms_eps", C.c_float), ("q4k", C.c_int), ("tied_output", C.c_int),
+        ("seed", C.c_uint64), ("n_threads", C.c_int), ("layer_period", C.c_int), ("q4k_order", C.c_int),
+        ("embd_f16", C.c_int)]
+
+
+def synth_gguf(path: str, *, n_layers, d_model, ffn_hidden, n_heads, n_kv_heads, vocab, max_seq,
+               theta_base=10000.0, rms_eps=1e-5, q4k=True, tied_output=False, seed=0,
+               n_threads=0, layer_period=0, q4k_order=0, embd_f16=0) -> None:
+    """slate_synth_llama_gguf from build/libslate_synth.so: the same bytes as
+    slate_b200.synth_gguf for the same arguments."""
+    if not os.path.exists(SYNTH_SO):
+        build()
+    lib = C.CDLL(SYNTH_SO)
+    lib.slate_synth_llama_gguf.restype = C.c_int
+    lib.slate_synth_llama_gguf.argtypes = [C.c_char_p, C.POINTER(SynthConfig)]
+    cfg = SynthConfig(n_layers, d_model, ffn_hidden, n_heads, n_kv_heads, vocab, max_seq,
+                      theta_base, rms_eps, int(q4k), int(tied_output), seed, n_threads,
+                      layer_period, q4k_order, embd_f16)
+    rc = lib.slate_synth_llama_gguf(path.encode(), C.byref(cfg))
+    if rc:
+        raise OSError(f"slate_synth_llama_gguf({path}) rc={rc}")
 
 
 def _f(a):
@@ -247,6 +279,8 @@ class Reference:
             ("slate_llama_session_position", C.c_int, [C.c_void_p]),
             ("slate_llama_prefill", C.c_int, [C.c_void_p, Pi, C.c_int, Pf]),
             ("slate_llama_decode_step", C.c_int, [C.c_void_p, C.c_int32, Pf]),
+            ("slate_ref_session_set_position", C.c_int, [C.c_void_p, C.c_int]),
+            ("slate_ref_session_seed_context", C.c_int, [C.c_void_p, C.c_int, C.c_uint64]),
             ("slate_dequant_q4_k", None, [Pf, C.c_void_p, C.c_int64]),
             ("slate_dot_q4_k_f32", C.c_float, [C.c_void_p, Pf, C.c_int64]),
             ("slate_q4_k_matvec", None, [Pf, C.c_void_p, Pf, C.c_int, C.c_int]),
@@ -285,3 +319,19 @@ class Reference:
     def close(self, g, m):
         self.lib.slate_llama_free(m)
         self.lib.slate_gguf_close(g)
+
+    def session(self, m, context=0, seed=0):
+        """A reference session (slate_llama_session_new) with a seeded
+        `context`-token history (slate_ref_session_seed_context: the values the
+        CUDA engine's seed_context writes for the same seed)."""
+        s = self.lib.slate_llama_session_new(m)
+        if not s:
+            raise MemoryError("slate_llama_session_new failed")
+        if context and self.lib.slate_ref_session_seed_context(s, int(context), int(seed)) != 0:
+            self.lib.slate_llama_session_free(s)
+            raise ValueError(f"context {context} does not fit the session")
+        return s
+
+    def decode(self, s, token, out):
+        """slate_llama_decode_step into the f32 array `out` (vocab long)."""
+        return self.lib.slate_llama_decode_step(s, int(token), out.ctypes.data_as(Pf))

@@ -19,10 +19,14 @@
  * hashes of (seed, t, i/2) -- so any thread count writes the same bytes.
  * Norm gains are 1.0 as in the reference fixtures
  * (make_tiny_llama_q4k_gguf.py:117,122,127).
+ *
+ * Self-contained (libc, libm, pthreads): besides libslate_cuda.so, the oracle's
+ * Makefile compiles this file alone into a CPU-only library, so that a process
+ * timing the reference on the host can write the same workload file without
+ * mapping the CUDA library.
  */
 #define _GNU_SOURCE
 #include "slate_cuda.h"
-#include "sb_internal.h"
 
 #include <fcntl.h>
 #include <fenv.h>
@@ -50,6 +54,15 @@ static uint16_t f64_to_f16(double x) {
     int E = e - 1 + 15;
     if (E >= 31) return sign | 0x7c00u;
     return sign | (uint16_t)(E << 10) | (uint16_t)((uint32_t)q & 0x3ffu);
+}
+
+/* ---- binary16 -> f64, exact (subnormals included) ---- */
+static double f16_to_f64(uint16_t h) {
+    const int e = (h >> 10) & 0x1f, m = h & 0x3ff;
+    double v = e == 0 ? ldexp((double)m, -24)
+             : e == 31 ? (m ? NAN : INFINITY)
+                       : ldexp((double)(m | 0x400), e - 25);
+    return (h & 0x8000u) ? -v : v;
 }
 
 static void quant_block(uint8_t* out, const float* w) {
@@ -229,7 +242,7 @@ static void* writer(void* arg) {
                 row_bytes = (size_t)t->cols * 2;
                 bytes = row_bytes * (size_t)nr;
             } else if (t->kind == 2 && j->embd_f16 == 2) {   /* f32 of f16-rounded values */
-                for (int64_t i = 0; i < n; ++i) f[i] = sb_f16_to_f32(f64_to_f16((double)f[i]));
+                for (int64_t i = 0; i < n; ++i) f[i] = (float)f16_to_f64(f64_to_f16((double)f[i]));
             }
             off_t at = (off_t)(j->data_off + t->off + (uint64_t)r * row_bytes);
             if (pwrite(j->fd, src, bytes, at) != (ssize_t)bytes) j->rc = -6;

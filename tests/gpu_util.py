@@ -70,6 +70,23 @@ class Backend:
         self.live = []
 
 
+def seeded_kv(seed, n, n_layers, kv_dim):
+    """The history slate_llama_batch_seed_context writes for `seed`: element i of
+    the [layer][K|V][token][kv_dim] order is 2*u - 1 in f32, u the top 53 bits of
+    splitmix64(seed ^ i * 0x9e3779b97f4a7c15) scaled to [0, 1).  Returns
+    (K, V), each [n_layers, n, kv_dim] f32."""
+    with np.errstate(over="ignore"):
+        i = np.arange(n_layers * 2 * n * kv_dim, dtype=np.uint64)
+        z = np.uint64(seed) ^ (i * np.uint64(0x9E3779B97F4A7C15))
+        z = z + np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        z = z ^ (z >> np.uint64(31))
+    u = ((z >> np.uint64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)).astype(np.float32)
+    kv = (u * np.float32(2.0) - np.float32(1.0)).reshape(n_layers, 2, n, kv_dim)
+    return np.ascontiguousarray(kv[:, 0]), np.ascontiguousarray(kv[:, 1])
+
+
 def scale_err(got, want):
     """max |got - want| relative to the reference's largest magnitude."""
     return float(np.max(np.abs(np.asarray(got, np.float64) - want)) / max(np.abs(want).max(), 1e-30))

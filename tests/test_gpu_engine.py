@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 
 from conftest import golden
-from gpu_util import greedy_agrees, scale_err
+from gpu_util import greedy_agrees, scale_err, seeded_kv
 from test_golden import TINY, read_ref_logits
 
 pytestmark = pytest.mark.gpu
@@ -188,6 +188,27 @@ def test_page_pool_exhaustion(sb, workdir):
     assert eng.step([a, b], [4, 5])[0] == 0                  # existing pages keep working
     assert eng.release(a) == 0
     assert eng.step([c], [3])[0] == 0                        # page came back
+    eng.close()
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+def test_seeded_context_is_the_documented_generator(sb, workdir, kv_dtype):
+    """seed_context writes the generator the reference-side timing reproduces
+    (tests/gpu_util.seeded_kv, oracle/ref_session.c): exactly in an f32 cache,
+    its f16 rounding in an f16 cache."""
+    path = os.path.join(str(workdir), "gqa_q4k.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=2,
+                      vocab=512, max_seq=512, q4k=True, seed=7)
+    eng = make_engine(sb, path, max_batch=4, max_seq=1024, kv_dtype=kv_dtype)
+    s = eng.open()
+    assert eng.seed_context(s, 333, seed=987654321) == 0
+    rc, K, V = eng.read_kv(s, 333, 2, 128)
+    assert rc == 0, sb.last_error()
+    Kw, Vw = seeded_kv(987654321, 333, 2, 128)
+    if kv_dtype == 1:
+        Kw, Vw = Kw.astype(np.float16).astype(np.float32), Vw.astype(np.float16).astype(np.float32)
+    assert np.array_equal(K, Kw) and np.array_equal(V, Vw)
     eng.close()
 
 

@@ -1,0 +1,166 @@
+"""Full-depth parity at the headline configuration.
+
+The model is bench.py's: all 32 layers of the LLaMA-3-8B shape (d_model 4096,
+32 query / 8 KV heads, head_dim 128, FFN 14336, vocab 128256, RoPE theta 5e5,
+Q4_K linear weights from N(0, 0.02), f32 embedding and LM head).  One engine of
+256 rows holds 8 checked sequences with histories of 128..4300 tokens at
+scattered batch rows among 248 short ones.  Independent oracle sessions (the C
+restatement of decode_one, src/loader/llama_infer.c:134-206, itself pinned to
+the reference library) hold the same f32 history and decode the same tokens,
+teacher-forced with the oracle's greedy token so every engine variant sees one
+token stream.  Each variant runs four steps:
+
+  steps 1-2: all 256 rows   (stream-K tcgen05 GEMM, tensor-core LM head)
+  step 3:    64 rows        (tile-per-CTA tcgen05 GEMM)
+  step 4:    8 rows         (small-batch mma.sync GEMM)
+
+Tolerances, over every logit of the checked rows, as max |engine - oracle|
+relative to max |oracle|:
+  * f32 KV cache, f32-level GEMM products (the default 3-pass f16 hi/lo split,
+    and the exact-weight 2-pass kernel, gemm_path 4): 1e-4
+  * f16 KV cache, default GEMMs: 1e-3 (north_star's bound; the f16 cache holds
+    the f16 rounding of the oracle's f32 history and of every new K/V row)
+  * single-pass f16 GEMM (gemm_path 2, an opt-in speed mode): 2e-3, the bound
+    north_star gives where reduced-precision tensor-core products are used.
+Greedy ids: the oracle's argmax, except near-ties (the oracle's own top-2 gap
+within the tolerance), of which at most ceil(tokens / 1000) are accepted per
+variant -- one in this test's 32 checked tokens.  The measured error and the
+near-tie count of every variant are printed (`pytest -s`).
+"""
+import math
+import os
+import shutil
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+import pytest
+
+from gpu_util import greedy_agrees
+
+pytestmark = pytest.mark.gpu
+
+CFG3 = dict(n_layers=32, d_model=4096, ffn_hidden=14336, n_heads=32, n_kv_heads=8, vocab=128256,
+            max_seq=4352, theta_base=500000.0, rms_eps=1e-5)
+SEED = 1234                              # bench.py's default: the same file serves both
+CHECK_CTX = [128, 700, 1500, 2222, 3000, 3600, 4096, 4300]
+CHECK_ROWS = [0, 37, 90, 129, 170, 201, 230, 255]
+N_ROWS = 256
+STEPS = [list(range(N_ROWS)), list(range(N_ROWS)), "mid", "checked"]
+
+VARIANTS = [  # (name, kv_dtype, gemm_path, tolerance)
+    ("f32kv_exact", 0, 0, 1e-4),
+    ("f16kv_exact", 1, 0, 1e-3),
+    ("f32kv_exact_weight_2pass", 0, 4, 1e-4),
+    ("f32kv_single_pass_f16", 0, 2, 2e-3),
+]
+
+
+def model_file(sb, workdir):
+    name = f"slate_b200_8b_L32_s{SEED}.gguf"
+    for d in (os.environ.get("SLATE_BENCH_DIR"), "/dev/shm"):
+        if d and os.path.isdir(d) and shutil.disk_usage(d).free > (9 << 30):
+            path = os.path.join(d, name)
+            break
+    else:
+        path = os.path.join(str(workdir), name)
+    if not os.path.exists(path):
+        tmp = path + f".{os.getpid()}.tmp"
+        sb.synth_gguf(tmp, q4k=True, seed=SEED, **CFG3)
+        os.rename(tmp, path)
+    return path
+
+
+def step_rows(kind):
+    if kind == "checked":
+        return list(CHECK_ROWS)
+    if kind == "mid":
+        others = [r for r in range(N_ROWS) if r not in CHECK_ROWS][:64 - len(CHECK_ROWS)]
+        return sorted(CHECK_ROWS + others)
+    return kind
+
+
+def contexts():
+    rng = np.random.default_rng(7)
+    ctx = rng.integers(1, 48, N_ROWS)
+    for r, c in zip(CHECK_ROWS, CHECK_CTX):
+        ctx[r] = c
+    return ctx
+
+
+def new_engine(sb, path, kv, gemm_path):
+    ctx = contexts()
+    pages = int(sum((int(c) + len(STEPS) + 2) // 16 + 1 for c in ctx)) + 16
+    eng = sb.LlamaBatch(path, max_batch=N_ROWS, max_slots=N_ROWS, kv_dtype=kv,
+                        max_seq=CFG3["max_seq"], kv_pages=pages, gemm_path=gemm_path)
+    slots = [eng.open() for _ in range(N_ROWS)]
+    assert min(slots) >= 0, sb.last_error()
+    for r, s in enumerate(slots):
+        assert eng.seed_context(s, int(ctx[r]), 9000 + r) == 0, sb.last_error()
+    return eng, slots
+
+
+@pytest.fixture(scope="module")
+def reference_run(sb, oracle, workdir):
+    """The oracle's logits for the checked rows at every step, and the token
+    stream (row -> token per step) every engine variant is fed."""
+    path = model_file(sb, workdir)
+    L, kvd = CFG3["n_layers"], CFG3["n_kv_heads"] * CFG3["d_model"] // CFG3["n_heads"]
+    eng, slots = new_engine(sb, path, 0, 0)
+    m = oracle.open(path)
+    sess = []
+    for r, c in zip(CHECK_ROWS, CHECK_CTX):
+        rc, K, V = eng.read_kv(slots[r], c, L, kvd)
+        assert rc == 0, sb.last_error()
+        o = m.session(max_seq=CFG3["max_seq"])
+        assert o.seed_kv(K, V) == 0
+        sess.append(o)
+        del K, V
+    eng.close()
+    rng = np.random.default_rng(11)
+    tokens = rng.integers(0, CFG3["vocab"], (len(STEPS), N_ROWS)).astype(np.int32)
+    ref = np.zeros((len(STEPS), len(CHECK_ROWS), CFG3["vocab"]), np.float32)
+    pool = ThreadPoolExecutor(max_workers=len(sess))
+    for t in range(len(STEPS)):
+        outs = list(pool.map(lambda i: sess[i].decode(int(tokens[t, CHECK_ROWS[i]])),
+                             range(len(sess))))
+        for i, (rc, lg) in enumerate(outs):
+            assert rc == 0
+            ref[t, i] = lg
+            if t + 1 < len(STEPS):
+                tokens[t + 1, CHECK_ROWS[i]] = int(np.argmax(lg))
+    for o in sess:
+        o.close()
+    m.close()
+    return path, tokens, ref
+
+
+@pytest.mark.parametrize("name,kv,gemm_path,tol", VARIANTS, ids=[v[0] for v in VARIANTS])
+def test_full_depth_8b(sb, reference_run, name, kv, gemm_path, tol):
+    path, tokens, ref = reference_run
+    eng, slots = new_engine(sb, path, kv, gemm_path)
+    worst, n_tie, n_tok, per_step, wrong = 0.0, 0, 0, [], []
+    for t, kind in enumerate(STEPS):
+        rows = step_rows(kind)
+        rc, out, lg = eng.step([slots[r] for r in rows], tokens[t, rows], want_logits=True)
+        assert rc == 0, sb.last_error()
+        step_worst = 0.0
+        for i, r in enumerate(CHECK_ROWS):
+            j = rows.index(r)
+            want = ref[t, i]
+            scale = float(np.abs(want).max())
+            err = float(np.max(np.abs(lg[j].astype(np.float64) - want))) / scale
+            step_worst = max(step_worst, err)
+            ok, tie = greedy_agrees(int(out[j]), want, tol * scale)
+            if not ok:
+                wrong.append((t, r, int(out[j]), int(np.argmax(want))))
+            n_tie += tie
+            n_tok += 1
+        per_step.append(step_worst)
+        worst = max(worst, step_worst)
+    eng.close()
+    print(f"\nfull-depth 8B {name}: worst logit error {worst:.3e} of scale "
+          f"(per step {', '.join(f'{e:.2e}' for e in per_step)}; rows {[len(step_rows(k)) for k in STEPS]}), "
+          f"near-ties {n_tie} of {n_tok} tokens, other mismatches {len(wrong)}")
+    assert not wrong, (name, wrong)
+    assert worst <= tol, (name, worst, per_step)
+    assert n_tie <= math.ceil(n_tok / 1000), (name, n_tie, n_tok)

@@ -191,3 +191,41 @@ def test_synth_llama_cpp_order_and_f16_tables(sb, oracle, workdir):
     assert th["token_embd.weight"][0] == 1 and tr["token_embd.weight"][0] == 0
     assert np.array_equal(th["token_embd.weight"][2].view(np.float16).astype(np.float32),
                           tr["token_embd.weight"][2].view(np.float32))
+
+
+def test_cpu_writer_matches_product_writer(sb, workdir):
+    """oracle.synth_gguf (synth.c built without CUDA, used where the reference is
+    timed) writes the same bytes as the product library's writer."""
+    import oracle as O
+    a, b = os.path.join(str(workdir), "w_oracle.gguf"), os.path.join(str(workdir), "w_product.gguf")
+    for cfg in (SYNTH["gqa_q4k"], dict(SYNTH["tiny_f32"], embd_f16=2)):
+        O.synth_gguf(a, **cfg)
+        sb.synth_gguf(b, **cfg)
+        assert open(a, "rb").read() == open(b, "rb").read()
+
+
+def test_reference_seeded_history_matches_engine_generator(reference, oracle, synth_models):
+    """slate_ref_session_seed_context (oracle/ref_session.c) gives a reference
+    session the history the CUDA engine's seed_context writes: a session seeded
+    that way decodes like an oracle session given the generator's K/V."""
+    from gpu_util import seeded_kv
+    path = synth_models["gqa_q4k"]
+    g, m = reference.open(path)
+    c = reference.config(m)
+    kvd = c["n_kv_heads"] * c["head_dim"]
+    n, seed, tok = 37, 4242, 11
+    s = reference.session(m, n, seed)
+    assert reference.lib.slate_llama_session_position(s) == n
+    got = np.zeros(c["vocab"], np.float32)
+    assert reference.decode(s, tok, got) == 0
+    reference.lib.slate_llama_session_free(s)
+    reference.close(g, m)
+    om = oracle.open(path)
+    o = om.session()
+    K, V = seeded_kv(seed, n, c["n_layers"], kvd)
+    assert o.seed_kv(K, V) == 0
+    rc, want = o.decode(tok)
+    assert rc == 0
+    o.close()
+    om.close()
+    assert np.max(np.abs(got - want)) <= 1e-5 * np.abs(want).max()
