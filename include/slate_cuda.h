@@ -122,6 +122,18 @@ const slate_backend_t* slate_backend_cuda(void);
  * call wins; later calls with another device return NULL). */
 const slate_backend_cuda_t* slate_backend_cuda_create(int device);
 
+/* The 13 reference entries in a host-coherent form, for callers written
+ * against the CPU backend's semantics -- the reference's GPT-style inference
+ * engine (src/infer/engine.c: host memset / memcpy on alloc'd buffers at
+ * :276-277, 411-412, 586-591; host weight, scratch and logits pointers passed
+ * to the entries; results read without sync()).  alloc returns managed memory,
+ * copies accept any pointers, and every entry returns only after its kernel has
+ * finished; kernels read host pointers directly, so this form exists only on a
+ * device that can access pageable host memory (HMM / ATS): NULL otherwise,
+ * with the reason in slate_cuda_last_error().  Same device and stream as
+ * slate_backend_cuda_create(device), on which it calls first. */
+const slate_backend_t* slate_backend_cuda_host_coherent(int device);
+
 /* Text of the last device-side or argument error seen by this library on the
  * calling thread ("" if none). */
 const char* slate_cuda_last_error(void);
@@ -142,11 +154,15 @@ int slate_cuda_sample_rows(int32_t* out_tokens, const float* logits, int ld, int
  * legacy default stream, which the call synchronises before returning).
  * Its scratch is one fixed device array per device of
  * SLATE_CUDA_NOALLOC_SCRATCH_FLOATS floats (8 MiB); a call needs
- * B * nq * ceil(max_pages * 16 / 512) * (hd + 2) of them and is rejected with
- * -1 beyond that.  All calls on a device share the array, so calls that
- * overlap on the GPU race: serialise them.  The first call on a device
- * resolves the array's address (cudaGetSymbolAddress) with that device
- * current; make it before any stream capture.  No cudaMalloc/cudaFree. */
+ * B * nq * ceil(max_pages * 16 / ct) * (hd + 2) of them, ct being the engine's
+ * attention chunk for B rows (128 tokens below 4 rows up to 1024 from 16),
+ * doubled up to 1024 tokens until the partials fit, and is rejected with -1
+ * when even 1024-token chunks do not fit.  All calls on a device share the
+ * array, so calls that overlap on the GPU race: serialise them.  The first
+ * call on a device resolves the array's address (cudaGetSymbolAddress) with
+ * that device current; make it before any stream capture.  Each call waits
+ * for its stream before returning (it reads the kernels' error word).  No
+ * cudaMalloc/cudaFree. */
 #define SLATE_CUDA_NOALLOC_SCRATCH_FLOATS (1u << 21)
 int slate_cuda_attention_paged_gqa_noalloc(float* out, const float* q, const int32_t* pos,
                                            const int32_t* row_slot, const int32_t* page_table,

@@ -8,6 +8,7 @@
 // index serves every layer.  Pages come from a device-side free stack.
 //
 // The attention kernels themselves live in attn_paged.cu.
+#include "sb_internal.h"
 #include "sb_kernels.h"
 #include "sb_pdl.h"
 #include <cuda_fp16.h>
@@ -569,10 +570,9 @@ extern "C" int sb_rmsnorm_rows_split(float* Y, int ldy, const float* X, int ldx,
     if (D % 4 || D > RN_MAX * 4 * RN_T || ldx % 4 || ldy % 4 || ld16 % 4 || ((uintptr_t)X & 15) ||
         ((uintptr_t)Y & 15) || ((uintptr_t)w & 15) || B > 0x7fffffff)
         return -1;
-    return sb_launch_pdl(rmsnorm_split_kernel, dim3((unsigned)B), dim3(RN_T), 0, st, Y, ldy, X, ldx,
-                         w, D, eps, (__half*)hi, (__half*)lo, ld16) == cudaSuccess
-               ? 0
-               : -1;
+    return sb_cuda_check(sb_launch_pdl(rmsnorm_split_kernel, dim3((unsigned)B), dim3(RN_T), 0, st,
+                                       Y, ldy, X, ldx, w, D, eps, (__half*)hi, (__half*)lo, ld16),
+                         "rmsnorm launch");
 }
 extern "C" int sb_silu_mul(float* y, const float* g, const float* u, int n, cudaStream_t st) {
     if (n < 1) return -1;

@@ -8,16 +8,20 @@
 // synchronise or grow a memory pool mid-step.  This entry point runs the same
 // kernels with their scratch in a fixed file-scope device array instead.
 //
-// Scratch: SLATE_CUDA_NOALLOC_SCRATCH_FLOATS floats of partial records
-// (B * n_heads * ceil(max_pages * 16 / 512) * (head_dim + 2) of them per
-// call) plus one error word.  Requests beyond that are rejected with -1 and a
-// message before any device work.  Every call on a device shares the one
+// Scratch: SLATE_CUDA_NOALLOC_SCRATCH_FLOATS floats of partial records plus
+// one error word.  A call needs B * n_heads * ceil(max_pages * 16 / ct) *
+// (head_dim + 2) floats, ct being the engine's attention chunk for B rows
+// (sb_attention_chunk_tokens: 128 tokens below 4 rows up to 1024 from 16),
+// doubled up to 1024 tokens until the partials fit; a request that does not
+// fit even with 1024-token chunks is rejected with -1 and a message before
+// any device work.  Every call on a device shares the one
 // array: calls whose kernels overlap on the GPU (two host threads, or two
 // streams) race on it, so the caller serialises them.
 //
 // Set-up: the first call on a device (with that device current) resolves the
 // array's device address with cudaGetSymbolAddress and keeps it; make that
-// first call before any stream capture.  The error word is cleared on the
+// first call before any stream capture.  Every call is synchronous: it waits
+// for its stream to read the kernels' error word before it returns.  The error word is cleared on the
 // stream before each launch; the partials need no clearing (each record the
 // combine reads is written first by the same call).
 #include <cuda_runtime.h>

@@ -403,6 +403,98 @@ const slate_backend_cuda_t* slate_backend_cuda_create(int device) {
     return r;
 }
 
+/* ---- host-coherent form ------------------------------------------------
+ * The reference's GPT engine (src/infer/engine.c) uses its backend the way the
+ * CPU backend allows: it memset()s and memcpy()s buffers returned by alloc on
+ * the host (:276-277, 411-412, 586-591), hands host pointers to the entries
+ * (the module's weights, calloc'd scratch at :446, the caller's logits) and
+ * reads results right after a call without sync().  This form serves such a
+ * caller unchanged: alloc returns managed memory (host and device see one
+ * address), the copies go through cudaMemcpyDefault, and every entry waits for
+ * its kernel before returning.  The kernels read the host pointers directly,
+ * so the form is offered only where the device can access pageable host
+ * memory (cudaDevAttrPageableMemoryAccess: HMM or ATS); its entries use plain
+ * loads only (no TMA), and it shares the device and stream of the main
+ * singleton. */
+static slate_backend_t g_hc;
+
+static void* hc_alloc(size_t bytes) {
+    if (bytes == 0) return NULL;
+    void* p = NULL;
+    if (sb_cuda_check(cudaMallocManaged(&p, bytes, cudaMemAttachGlobal), "alloc (managed)"))
+        return NULL;
+    return p;
+}
+static void hc_copy(void* dst, const void* src, size_t bytes) {
+    sb_cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, g_stream), "copy");
+    be_sync();
+}
+static void hc_matvec(float* y, const float* A, const float* x, int M, int K) {
+    note(sb_matvec_f32_generic(y, A, x, M, K, g_stream), "matvec");
+    be_sync();
+}
+static void hc_linear_batch(float* C, const float* X, const float* W, int B, int K, int N) {
+    be_linear_batch(C, X, W, B, K, N);
+    be_sync();
+}
+static void hc_matvec_q4k(float* y, const void* A, const float* x, int M, int K) {
+    be_matvec_q4k(y, A, x, M, K);
+    be_sync();
+}
+static void hc_rmsnorm_row(float* y, const float* x, const float* w, int D, float eps) {
+    be_rmsnorm_row(y, x, w, D, eps);
+    be_sync();
+}
+static void hc_silu_mul(float* y, const float* g, const float* u, int H) {
+    be_silu_mul(y, g, u, H);
+    be_sync();
+}
+static void hc_add(float* y, const float* x, int D) {
+    be_add(y, x, D);
+    be_sync();
+}
+static void hc_embed(float* y, const float* W, int token, int D) {
+    be_embed(y, W, token, D);
+    be_sync();
+}
+static void hc_attention_step(float* out, const float* q, const float* K, const float* V,
+                              float* scores, int L, int D) {
+    be_attention_step(out, q, K, V, scores, L, D);
+    be_sync();
+}
+
+const slate_backend_t* slate_backend_cuda_host_coherent(int device) {
+    if (!slate_backend_cuda_create(device)) return NULL;
+    int pageable = 0;
+    if (sb_cuda_check(cudaDeviceGetAttribute(&pageable, cudaDevAttrPageableMemoryAccess, device),
+                      "cudaDeviceGetAttribute"))
+        return NULL;
+    if (!pageable) {
+        sb_set_error("device %d cannot read pageable host memory (no HMM / ATS): the host-coherent "
+                     "backend is unavailable", device);
+        return NULL;
+    }
+    pthread_mutex_lock(&g_init);
+    if (!g_hc.name) {
+        g_hc.alloc = hc_alloc;
+        g_hc.release = be_release;
+        g_hc.copy_h2d = hc_copy;
+        g_hc.copy_d2h = hc_copy;
+        g_hc.matvec = hc_matvec;
+        g_hc.linear_batch = hc_linear_batch;
+        g_hc.matvec_q4k = hc_matvec_q4k;
+        g_hc.rmsnorm_row = hc_rmsnorm_row;
+        g_hc.silu_mul = hc_silu_mul;
+        g_hc.add_inplace = hc_add;
+        g_hc.embed_lookup = hc_embed;
+        g_hc.attention_step = hc_attention_step;
+        g_hc.sync = be_sync;
+        g_hc.name = "cuda-host-coherent";
+    }
+    pthread_mutex_unlock(&g_init);
+    return &g_hc;
+}
+
 const slate_backend_t* slate_backend_cuda(void) {
     const char* e = getenv("SLATE_CUDA_BACKEND");
     if (!e || strcmp(e, "1") != 0) return NULL;

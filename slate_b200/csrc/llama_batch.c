@@ -154,18 +154,21 @@ static int norm_splits(const slate_llama_batch_t* b, const sb_lane* L, int n) {
 static int step_norm(slate_llama_batch_t* b, sb_lane* L, const float* w, int n, cudaStream_t s) {
     const size_t ro = (size_t)L->r0 * b->ld_x;
     L->xn_split = 0;
-    if (norm_splits(b, L, n) &&
-        sb_rmsnorm_rows_split(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps,
-                              L->op_d->hi, L->op_d->lo, L->op_d->ld16, s) == 0) {
-        L->xn_split = 1;
-        return 0;
+    /* -1 from the split kernel means the shape does not fit it (nothing was
+     * launched) and the next form is tried; a failed launch is returned */
+    int rc = -1;
+    if (norm_splits(b, L, n)) {
+        rc = sb_rmsnorm_rows_split(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps,
+                                   L->op_d->hi, L->op_d->lo, L->op_d->ld16, s);
+        if (rc == 0) L->xn_split = 1;
+        if (rc != -1) return rc;
     }
     /* f32 rows only, through the same kernel where the shape allows: it stays in
      * the programmatic launch chain, so the GEMM after it starts streaming its
      * weights while it runs */
-    if (sb_rmsnorm_rows_split(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps, NULL,
-                              NULL, 0, s) == 0)
-        return 0;
+    rc = sb_rmsnorm_rows_split(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps, NULL,
+                               NULL, 0, s);
+    if (rc != -1) return rc;
     return sb_rmsnorm_rows(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps, s);
 }
 

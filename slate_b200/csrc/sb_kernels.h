@@ -68,7 +68,8 @@ int sb_rmsnorm_rows(float* Y, int ldy, const float* X, int ldx, const float* w, 
 /* The same rows also written as an f16 hi / lo pair (row stride ld16, lo
  * nullable; hi null: the f32 rows only) for the tensor-core GEMM operand, as a
  * programmatic dependent launch; D % 4 == 0, D <= 8192, ldx / ldy / ld16
- * multiples of 4 and 16-byte aligned X, Y, w (else -1). */
+ * multiples of 4 and 16-byte aligned X, Y, w (else -1, nothing launched); -5
+ * when the launch itself fails. */
 int sb_rmsnorm_rows_split(float* Y, int ldy, const float* X, int ldx, const float* w, int B, int D,
                           float eps, void* hi, void* lo, int ld16, cudaStream_t st);
 int sb_silu_mul(float* y, const float* g, const float* u, int n, cudaStream_t st);

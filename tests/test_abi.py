@@ -58,7 +58,7 @@ def test_vtable_layout_matches_reference(sb):
 def test_header_compiles_with_reference_header_first(tmp_path):
     """A translation unit that includes the reference's backend.h first and
     then slate_cuda.h sees one struct slate_backend (the reference's)."""
-    ref_inc = "/root/reference/include"
+    ref_inc = os.path.join(os.environ.get("SLATE_REFERENCE_ROOT", "/root/reference"), "include")
     if not os.path.isdir(ref_inc):
         pytest.skip("reference headers unavailable")
     src = tmp_path / "t.c"

@@ -70,7 +70,7 @@ def test_noalloc_rejects_oversized_request(sb):
     device work (so this runs without a GPU)."""
     noalloc = sb.F["slate_cuda_attention_paged_gqa_noalloc"]
     dummy = C.c_void_p(256)             # never dereferenced: the size check comes first
-    # 1024 rows x 32 heads x 9 chunks x 130 floats > 2^21
+    # 1024 rows x 32 heads x 5 chunks of 1024 tokens (4352-token cap) x 130 floats > 2^21
     rc = noalloc(dummy, dummy, dummy, dummy, dummy, 272, dummy, 1000, 0, 1024, 32, 8, 128, 1, None)
     assert rc == -1
     assert "limit" in sb.last_error()
