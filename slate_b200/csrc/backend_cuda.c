@@ -54,7 +54,7 @@ static int aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 static void be_matvec(float* y, const float* A, const float* x, int M, int K) {
     int rc;
     if (K % 128 == 0 && aligned16(A) && aligned16(x)) {
-        sb_matrix W = {SB_WT_F32, A, M, M, K, K};
+        sb_matrix W = {SB_WT_F32, A, M, M, K, K, 0};
         rc = sb_gemm(&W, x, K, 1, y, M, SB_EPI_STORE, 0, g_stream);
     } else {
         rc = sb_matvec_f32_generic(y, A, x, M, K, g_stream);
@@ -98,7 +98,7 @@ static int be_matmul_q4k(float* Y, const void* A, const float* X, int B, int M, 
 }
 static int be_matmul_f32(float* Y, const float* A, const float* X, int B, int M, int K) {
     if (K % 128 == 0 && aligned16(A) && aligned16(X)) {
-        sb_matrix W = {SB_WT_F32, A, M, M, K, K};
+        sb_matrix W = {SB_WT_F32, A, M, M, K, K, 0};
         return fin(sb_gemm(&W, X, K, B, Y, M, SB_EPI_STORE, 0, g_stream), "matmul_f32_batch");
     }
     int rc = 0;
@@ -182,7 +182,7 @@ static int be_attention_paged(float* out, const float* q, const int32_t* pos,
 
 /* passes 2: the exact-weight kernel (gemm_q4k.cu), any B >= 1 */
 static int be_matmul_q4k_exact(float* Y, const void* A, const float* X, int B, int M, int K) {
-    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0};
+    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0, 0};
     sb_q4_prepare();
     const int r_pad = (B + 127) / 128 * 128;
     const size_t xs_bytes = (size_t)((K / 256 + 1) & ~1) * r_pad * 8 * 2;
@@ -219,7 +219,7 @@ static int be_matmul_q4k_exact(float* Y, const void* A, const float* X, int B, i
 
 /* passes 3 on the stream-K kernel (gemm_sk.cu) */
 static int be_matmul_q4k_sk(float* Y, const void* A, const float* X, int B, int M, int K) {
-    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0};
+    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0, 0};
     sb_sk_prepare();
     void *hi = NULL, *lo = NULL, *ws = NULL, *err = NULL;
     int rc = sb_cuda_check(cudaMallocAsync(&hi, (size_t)B * K * 2, g_stream), "alloc");
@@ -249,7 +249,7 @@ static int be_matmul_q4k_sk(float* Y, const void* A, const float* X, int B, int 
 
 /* passes 4: the small-batch kernel (gemm_mv.cu), 1 <= B <= 16 */
 static int be_matmul_q4k_mv(float* Y, const void* A, const float* X, int B, int M, int K) {
-    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0};
+    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0, 0};
     const size_t wsf = sb_mv_ws_floats(M, K);
     void *ws = NULL, *cnt = NULL;
     int rc = sb_cuda_check(cudaMallocAsync(&ws, wsf * 4 + 16, g_stream), "alloc");
@@ -285,7 +285,7 @@ static int be_matmul_q4k_tc(float* Y, const void* A, const float* X, int B, int 
         sb_set_error("matmul_q4k_batch_tc: unsupported shape or passes");
         return -1;
     }
-    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0};
+    sb_matrix W = {SB_WT_Q4K, A, M, M, K, 0, 0};
     const int splits = sb_tc_splits_for(M, K);
     void *hi = NULL, *lo = NULL, *ws = NULL, *err = NULL;
     int rc = sb_cuda_check(cudaMallocAsync(&hi, (size_t)B * K * 2, g_stream), "alloc");

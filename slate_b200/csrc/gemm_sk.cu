@@ -9,7 +9,9 @@
 // (x = hi + lo to ~22 bits) by sb_tc_split().  Each weight is also split into
 // f16 hi + lo, and the tensor cores accumulate hi*hi + hi*lo + lo*hi in f32,
 // which reproduces f32 products to ~1e-6 relative (the same numerics as
-// gemm_tc.cu's three-pass kernel).
+// gemm_tc.cu's three-pass kernel).  The weights are split as w * 2^wexp (a
+// power of two per matrix, chosen at upload) so that their lo halves stay
+// normal f16 numbers; the drain scales the accumulator back by 2^-wexp.
 //
 // Work decomposition: a tile is 128 weight rows (TMEM lanes) x up to 256
 // activation rows (MMA N); the (tile, 64-wide K step) space is cut into one
@@ -303,6 +305,7 @@ struct SkArgs {
     __half* h_lo;
     int* err;
     int M, M_pad, K, n_rows, NT, n_box, ldy, epi, ld16;
+    float wscale, wunscale;   // 2^wexp applied to the weights before the split, 2^-wexp after
 };
 
 // Workspace: a 128 x 256 tile is stored as [BN/4][BM] float4 (column group
@@ -355,7 +358,10 @@ __device__ __forceinline__ void alone_out(const SkArgs& a, uint32_t lane_base, i
         tmem_ld16(lane_base + (uint32_t)c0, v);
         float o[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = a.epi == SB_EPI_ADD ? y[i] + v[i] : v[i];
+        for (int i = 0; i < 16; ++i) {
+            const float r = v[i] * a.wunscale;
+            o[i] = a.epi == SB_EPI_ADD ? y[i] + r : r;
+        }
         if (a.epi == SB_EPI_ADD && c0 + 16 < n_mma) load_y(c0 + 16);
         if (live) {
 #pragma unroll
@@ -567,7 +573,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 uint32_t hi[16], lo[16];
                 float sd, sm;
                 sub_scale(h0, (k & 3) * 2 + half, sd, sm);
-                dequant_sub(q0, sd, sm, hi, lo);
+                dequant_sub(q0, sd * a.wscale, sm * a.wscale, hi, lo);
                 tmem_st16(lane_a + (uint32_t)(64 * s), hi);
                 tmem_st16(lane_a + (uint32_t)(64 * s + 32), lo);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -682,10 +688,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 for (int c0 = 0; c0 < n_mma; c0 += 16) {
                     float v[16];
                     tmem_ld16(lane_base + (uint32_t)c0, v);
+                    const float u = a.wunscale;
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        wsp[(size_t)((c0 >> 2) + j) * BM] =
-                            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        wsp[(size_t)((c0 >> 2) + j) * BM] = make_float4(
+                            v[4 * j] * u, v[4 * j + 1] * u, v[4 * j + 2] * u, v[4 * j + 3] * u);
                 }
             }
             tc_fence_before();
@@ -768,6 +775,8 @@ extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows
     a.h_hi = (__half*)h_hi;
     a.h_lo = (__half*)h_lo;
     a.ld16 = ld16;
+    a.wscale = ldexpf(1.0f, W->wexp);
+    a.wunscale = ldexpf(1.0f, -W->wexp);
     const int MT = W->M_pad / BM;
     int C = 0;
     long long U = 0;

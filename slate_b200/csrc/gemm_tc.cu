@@ -28,6 +28,8 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
+#include <math.h>
+#include <string.h>
 
 #include "sb_internal.h"
 #include "sb_kernels.h"
@@ -214,8 +216,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const __grid_constant__ CUtensorMap amap_hi, const __grid_constant__ CUtensorMap amap_lo,
               const unsigned char* __restrict__ W, int M, int M_pad, int K, int n_rows, int n_box,
               int splits, float* __restrict__ ws, float* __restrict__ Y, int ldy, int direct,
-              int* err) {
+              int* err, int wexp) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // weights enter the split as w * 2^wexp (exact); the epilogue scales back
+    const float wsc = ldexpf(1.0f, wexp), wun = ldexpf(1.0f, -wexp);
     // 1024-aligned carve-up: per stage [A_hi | A_lo | B_hi | B_lo]
     unsigned char* base = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     constexpr int PARTS = PASSES == 3 ? 2 : 1;
@@ -309,11 +313,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 float sd, sm;
                 uint32_t h16[16], l16[16];
                 sub_scale(hdr, j0, sd, sm);
-                dequant32<PASSES>(q0, sd, sm, h16, l16);
+                dequant32<PASSES>(q0, sd * wsc, sm * wsc, h16, l16);
 #pragma unroll
                 for (int c = 0; c < 16; ++c) { hi[c] = h16[c]; lo[c] = l16[c]; }
                 sub_scale(hdr, j0 + 1, sd, sm);
-                dequant32<PASSES>(q1, sd, sm, h16, l16);
+                dequant32<PASSES>(q1, sd * wsc, sm * wsc, h16, l16);
 #pragma unroll
                 for (int c = 0; c < 16; ++c) { hi[16 + c] = h16[c]; lo[16 + c] = l16[c]; }
             }
@@ -370,6 +374,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int c0 = 0; c0 < n_mma; c0 += 16) {
                 float v[16];
                 tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] *= wun;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int n = c0 + j;
@@ -445,12 +451,13 @@ __global__ void split_f16_rows_kernel(const float* __restrict__ X, int ldx, int 
 
 // Scalar form of the same split, for any strides and alignment.
 __global__ void split_f16_kernel(const float* __restrict__ X, int ldx, int n_rows, int K,
-                                 __half* __restrict__ hi, __half* __restrict__ lo, int ld16) {
+                                 __half* __restrict__ hi, __half* __restrict__ lo, int ld16,
+                                 float scale) {
     const long total = (long)n_rows * K;
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (long)gridDim.x * blockDim.x) {
         const int n = (int)(i / K), k = (int)(i % K);
-        const float x = X[(size_t)n * ldx + k];
+        const float x = X[(size_t)n * ldx + k] * scale;
         const __half h = __float2half_rn(x);
         hi[(size_t)n * ld16 + k] = h;
         if (lo) lo[(size_t)n * ld16 + k] = __float2half_rn(x - __half2float(h));
@@ -522,8 +529,21 @@ extern "C" int sb_tc_split(const float* X, int ldx, int n_rows, const sb_tc_oper
     const long total = (long)n_rows * op->K;
     const int grid = (int)((total + 255) / 256 < 2368 ? (total + 255) / 256 : 2368);
     split_f16_kernel<<<grid, 256, 0, st>>>(X, ldx, n_rows, op->K, (__half*)op->hi,
-                                           (__half*)op->lo, op->ld16);
+                                           (__half*)op->lo, op->ld16, 1.0f);
     return 0;
+}
+
+// max |W| over M rows of K (row stride ldw) as the bits of a non-negative
+// float (their order is the floats' order), for the weight pair's scale.
+__global__ void absmax_kernel(const float* __restrict__ W, int ldw, int M, int K,
+                              unsigned int* __restrict__ out) {
+    float mx = 0.f;
+    const long total = (long)M * K;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long)gridDim.x * blockDim.x)
+        mx = fmaxf(mx, fabsf(W[(size_t)(i / K) * ldw + i % K]));
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(mx));
 }
 
 extern "C" int sb_tc_make_weight(sb_tc_weight* w, const float* W32, int ldw, int M, int K,
@@ -541,8 +561,34 @@ extern "C" int sb_tc_make_weight(sb_tc_weight* w, const float* W32, int ldw, int
     cudaMemsetAsync(hi, 0, (size_t)M_pad * K * 2, st);
     cudaMemsetAsync(lo, 0, (size_t)M_pad * K * 2, st);
     const long total = (long)M * K;
-    split_f16_kernel<<<(int)((total + 255) / 256 < 4736 ? (total + 255) / 256 : 4736), 256, 0, st>>>(
-        W32, ldw, M, K, (__half*)hi, (__half*)lo, K);
+    const int grid = (int)((total + 255) / 256 < 4736 ? (total + 255) / 256 : 4736);
+    // the pair holds W * 2^wexp (exact), the largest power of two that keeps
+    // every weight below 2^13, so that the lo halves stay normal f16 numbers
+    // (a lo half of a weight near 0.02 is subnormal unscaled); the GEMM's
+    // epilogue scales back by 2^-wexp
+    unsigned int* d_mx = nullptr;
+    unsigned int h_mx = 0;
+    if (cudaMallocAsync((void**)&d_mx, sizeof(unsigned int), st) != cudaSuccess) {
+        cudaFree(hi);
+        cudaFree(lo);
+        return -5;
+    }
+    cudaMemsetAsync(d_mx, 0, sizeof(unsigned int), st);
+    absmax_kernel<<<grid, 256, 0, st>>>(W32, ldw, M, K, d_mx);
+    cudaMemcpyAsync(&h_mx, d_mx, sizeof(unsigned int), cudaMemcpyDeviceToHost, st);
+    cudaFreeAsync(d_mx, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) {
+        cudaFree(hi);
+        cudaFree(lo);
+        return -5;
+    }
+    float mx;
+    memcpy(&mx, &h_mx, 4);
+    int wexp = (mx > 0.f && isfinite(mx)) ? (int)floorf(log2f(8192.0f / mx)) : 0;
+    wexp = wexp < 0 ? 0 : wexp > 24 ? 24 : wexp;
+    split_f16_kernel<<<grid, 256, 0, st>>>(W32, ldw, M, K, (__half*)hi, (__half*)lo, K,
+                                           ldexpf(1.0f, wexp));
+    w->wexp = wexp;
     w->hi = hi;
     w->lo = lo;
     w->M = M;
@@ -581,7 +627,7 @@ extern "C" int sb_tc_gemm_f16w(const sb_tc_weight* W, const sb_tc_operand* X, in
     tc_kernel<3, stages_for<3>(), 1><<<grid, NTHREADS, smem_for<3>(X->n_box), st>>>(
         *(const CUtensorMap*)X->map_hi, *(const CUtensorMap*)X->map_lo,
         *(const CUtensorMap*)W->map_hi, *(const CUtensorMap*)W->map_lo, nullptr, W->M, W->M_pad,
-        W->K, n_rows, X->n_box, 1, nullptr, Y, ldy, epi == SB_EPI_ADD ? 2 : 1, err);
+        W->K, n_rows, X->n_box, 1, nullptr, Y, ldy, epi == SB_EPI_ADD ? 2 : 1, err, W->wexp);
     return 0;
 }
 
@@ -618,11 +664,11 @@ extern "C" int sb_tc_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows
     if (passes == 1)
         tc_kernel<1, stages_for<1>(), 0><<<grid, NTHREADS, smem_for<1>(X->n_box), st>>>(
             *xh, *xl, *xh, *xh, w, W->M, W->M_pad, W->K, n_rows, X->n_box, splits, ws, Y, ldy,
-            direct, err);
+            direct, err, W->wexp);
     else
         tc_kernel<3, stages_for<3>(), 0><<<grid, NTHREADS, smem_for<3>(X->n_box), st>>>(
             *xh, *xl, *xh, *xh, w, W->M, W->M_pad, W->K, n_rows, X->n_box, splits, ws, Y, ldy,
-            direct, err);
+            direct, err, W->wexp);
     if (direct) return 0;
     const int n_out = epi == SB_EPI_SILU ? W->M / 2 : W->M;
     const long total = (long)n_rows * n_out;

@@ -286,6 +286,25 @@ static void q4k_from_ggml(uint8_t* dst, const uint8_t* src) {
         for (int i = 0; i < 16; ++i) dst[16 + 16 * sb + i] = (uint8_t)(e[sb][i] | (e[sb][i + 16] << 4));
 }
 
+/* Exponent e (0..24) for the tensor-core split of a Q4_K matrix: the largest
+ * with every weight below 2^13 after scaling by 2^e, from the block headers
+ * (|d*sc*q - dmin*m| <= |d|*63*15 + |dmin|*63).  An f16 lo half of a weight
+ * near 0.02 (~1e-5) is subnormal and keeps ~7 of its 11 bits; scaled, it
+ * keeps all of them. */
+static int q4k_wexp(const unsigned char* p, size_t nblocks) {
+    float mx = 0.f;
+    for (size_t i = 0; i < nblocks; ++i) {
+        uint16_t dh, mh;
+        memcpy(&dh, p + 144 * i, 2);
+        memcpy(&mh, p + 144 * i + 2, 2);
+        const float bnd = fabsf(sb_f16_to_f32(dh)) * 945.0f + fabsf(sb_f16_to_f32(mh)) * 63.0f;
+        if (bnd > mx) mx = bnd;
+    }
+    if (!(mx > 0.f) || !isfinite(mx)) return 0;
+    const int e = (int)floorf(log2f(8192.0f / mx));
+    return e < 0 ? 0 : e > 24 ? 24 : e;
+}
+
 static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, const src_part* parts,
                        int nparts, int K, int interleave64) {
     int all_q4k = 1, M = 0;
@@ -309,6 +328,7 @@ static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, cons
     out->M_pad = M_pad;
     out->K = K;
     out->ldw = all_q4k ? 0 : round_up(K, 128);
+    out->wexp = 0;
     const size_t row_bytes = all_q4k ? q4k_row_bytes(K) : (size_t)out->ldw * 4;
     const size_t bytes = row_bytes * (size_t)M_pad;
     if (nparts == 1 && !interleave64 && parts[0].src_k == K && !(all_q4k && b->q4k_order) &&
@@ -316,8 +336,9 @@ static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, cons
         /* already in the device layout: copy rows straight from the source */
         unsigned char* dptr = (unsigned char*)dalloc(b, bytes);
         if (!dptr) return -5;
-        SB_CU(cudaMemcpy(dptr, (const unsigned char*)parts[0].p + (size_t)parts[0].row0 * row_bytes,
-                         row_bytes * (size_t)M, cudaMemcpyHostToDevice));
+        const unsigned char* src = (const unsigned char*)parts[0].p + (size_t)parts[0].row0 * row_bytes;
+        if (all_q4k) out->wexp = q4k_wexp(src, (size_t)M * (K / 256));
+        SB_CU(cudaMemcpy(dptr, src, row_bytes * (size_t)M, cudaMemcpyHostToDevice));
         if (M_pad > M) SB_CU(cudaMemset(dptr + row_bytes * (size_t)M, 0, row_bytes * (size_t)(M_pad - M)));
         out->data = dptr;
         return 0;
@@ -364,6 +385,7 @@ static int pack_matrix(slate_llama_batch_t* b, stage_t* st, sb_matrix* out, cons
         }
         base += sp->rows;
     }
+    if (all_q4k) out->wexp = q4k_wexp(h, (size_t)M_pad * (K / 256));
     void* dptr = dalloc(b, bytes);
     if (!dptr) return -5;
     SB_CU(cudaMemcpy(dptr, h, bytes, cudaMemcpyHostToDevice));
@@ -743,7 +765,7 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
     if (m->output == m->token_embd && m->output_dtype == m->token_embd_dtype && D % 128 == 0 &&
         b->V_l % 128 == 0) {
         /* tied: share the table (this rank's vocabulary rows) */
-        b->lm_head = (sb_matrix){SB_WT_F32, b->emb + (size_t)b->v0 * D, b->V_l, b->V_l, D, D};
+        b->lm_head = (sb_matrix){SB_WT_F32, b->emb + (size_t)b->v0 * D, b->V_l, b->V_l, D, D, 0};
     } else {
         src_part p = {m->output, m->output_dtype, b->V_l, b->v0, D, 0};
         if (pack_matrix(b, &stg, &b->lm_head, &p, 1, D, 0)) goto fail;

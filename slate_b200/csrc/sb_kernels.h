@@ -37,6 +37,10 @@ typedef struct sb_matrix {
     int M_pad;   /* physical rows, multiple of 128                         */
     int K;       /* reduction length                                       */
     int ldw;     /* f32 row stride (floats); ignored for Q4_K              */
+    int wexp;    /* Q4_K on the tensor cores (f16 hi/lo split of each weight):
+                    weights are formed as w * 2^wexp -- exact, a power of two --
+                    so that the lo halves stay normal f16 numbers, and the
+                    accumulator is scaled by 2^-wexp; 0 = unscaled             */
 } sb_matrix;
 
 /* Y[n][·] (epi) X[n][0..K) · W[m][0..K)  for n < B.

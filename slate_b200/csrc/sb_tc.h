@@ -48,6 +48,7 @@ typedef struct sb_tc_weight {
     void* hi;
     void* lo;
     int M, M_pad, K;
+    int wexp;    /* the pair holds W * 2^wexp (exact; keeps the lo halves normal) */
 } sb_tc_weight;
 /* Splits the device f32 matrix W32 (row stride ldw) into a new pair. */
 int sb_tc_make_weight(sb_tc_weight* w, const float* W32, int ldw, int M, int K, cudaStream_t st);
