@@ -53,9 +53,28 @@ METRIC = "decode tok/s (box), LLaMA-3-8B-shape Q4_K, 256 ragged seqs; p50 step l
 CFG5 = dict(n_layers=80, d_model=8192, ffn_hidden=28672, n_heads=64, n_kv_heads=8, vocab=128256,
             max_seq=2368, theta_base=500000.0, rms_eps=1e-5)
 METRIC70 = "decode tok/s (box), LLaMA-3-70B-shape Q4_K tensor-parallel, 512 ragged seqs per TP group"
-MODELS = {"8b": dict(cfg=CFG3, metric=METRIC, batch=256, prompt=(128, 4096), period=0,
+# ~1B, 64 requests, prompts lognormal (median 256, clipped to
+# 2048), 128 greedy tokens, Poisson arrivals at 20 req/s.  BASELINE.json gives no
+# sigma for the lognormal; 0.75 is used (mean prompt ~339 tokens) and recorded.
+CFG2 = dict(n_layers=16, d_model=2048, ffn_hidden=8192, n_heads=32, n_kv_heads=8, vocab=32000,
+            max_seq=2304, theta_base=10000.0, rms_eps=1e-5)
+METRIC1B = "decode tok/s (box), ~1B-shape Q4_K, 64 ragged seqs; p50 step latency"
+# Mistral-7B shape, 32 sequences, prompts U[8192, 32768],
+# 128 greedy tokens, f16 KV cache in 16-token pages
+CFG4 = dict(n_layers=32, d_model=4096, ffn_hidden=14336, n_heads=32, n_kv_heads=8, vocab=32000,
+            max_seq=32896, theta_base=1000000.0, rms_eps=1e-5)
+METRIC_MISTRAL = "decode tok/s (box), Mistral-7B-shape Q4_K long context, 32 ragged seqs; p50 step latency"
+MODELS = {"8b": dict(cfg=CFG3, metric=METRIC, batch=256, prompt=(128, 4096), budget=256, period=0,
+                     kv="f32", file_gb=9,
                      workload="llama3-8b-shape q4k continuous-batching decode (BASELINE config 3)"),
-          "70b": dict(cfg=CFG5, metric=METRIC70, batch=512, prompt=(256, 2048), period=8,
+          "1b": dict(cfg=CFG2, metric=METRIC1B, batch=64, prompt=("lognormal", 256, 0.75, 2048),
+                     budget=128, period=0, kv="f32", file_gb=2,
+                     workload="~1b-shape q4k continuous-batching decode (BASELINE config 2)"),
+          "mistral": dict(cfg=CFG4, metric=METRIC_MISTRAL, batch=32, prompt=(8192, 32768), budget=128,
+                          period=0, kv="f16", file_gb=6,
+                          workload="mistral-7b-shape q4k long-context decode (BASELINE config 4)"),
+          "70b": dict(cfg=CFG5, metric=METRIC70, batch=512, prompt=(256, 2048), budget=256, period=8,
+                      kv="f32", file_gb=60,
                       workload="llama3-70b-shape q4k tensor-parallel decode (BASELINE config 5)")}
 # DRAM bytes (read + write) per algorithmic byte of one attention launch, from ncu
 # captures of 32 rows at the 8B shape with 1024-token chunks (dram__bytes_read.sum +
@@ -71,8 +90,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--kv", default="f32", choices=["f16", "f32"],
-                    help="KV cache dtype of the headline (f32: the reference's)")
+    ap.add_argument("--kv", default=None, choices=["f16", "f32"],
+                    help="KV cache dtype of the headline (default: f32, the reference's; f16 for "
+                         "the Mistral config, which mandates it, and for 70b below 4-way TP)")
     ap.add_argument("--variant-kv", default="auto", choices=["auto", "none", "f16", "f32"],
                     help="also time the other KV dtype and report it as variant_kv_<dtype> "
                          "(auto: f16 when the headline is f32)")
@@ -103,12 +123,18 @@ def parse():
     ap.add_argument("--cpu-steps", type=int, default=4,
                     help="decode steps of the reference sessions for cpu_baseline (after 1 warm-up)")
     ap.add_argument("--cpu-threads", type=int, default=0, help="reference sessions (0: all cores)")
+    ap.add_argument("--refill-steps", type=int, default=-1,
+                    help="steps of the continuous-refill replay after the decode timing (finished "
+                         "sequences replaced by prefilled new requests; default --steps, 0: skip)")
+    ap.add_argument("--trace", default="auto", choices=["auto", "none", "poisson"],
+                    help="poisson: replay BASELINE config 2's Poisson arrivals (20 req/s) through the "
+                         "host API after the decode timing (auto: for --model 1b)")
     return ap.parse_args()
 
 
 def model_path(args, cfg) -> str:
     tag = f"slate_b200_{args.model}_L{cfg['n_layers']}_s{args.seed}.gguf"
-    need = (9 << 30) if args.model == "8b" else (60 << 30)
+    need = MODELS[args.model]["file_gb"] << 30
     for d in (os.environ.get("SLATE_BENCH_DIR"), "/dev/shm", "/tmp"):
         if d and os.path.isdir(d) and shutil.disk_usage(d).free > need:
             return os.path.join(d, tag)
@@ -139,16 +165,27 @@ def tp_group_id(dist, world, tp, rank, make_id):
     return ids[(rank // tp) * tp]
 
 
-def contexts(args, cfg, n, replica, steps):
-    """Prompt U[lo, hi] plus U[0, 256) already-decoded tokens per sequence."""
-    lo, hi = MODELS[args.model]["prompt"]
+def prompt_lengths(spec, rng, n):
+    """Prompt lengths of the config: U[lo, hi], or a clipped lognormal."""
+    pr = spec["prompt"]
+    if pr[0] == "lognormal":
+        _, median, sigma, clip = pr
+        return np.clip(np.round(rng.lognormal(np.log(median), sigma, n)), 1, clip).astype(np.int64)
+    return rng.integers(pr[0], pr[1] + 1, n)
+
+
+def contexts(args, cfg, n, replica, steps, with_done=False):
+    """Prompt lengths of the config plus U[0, budget) already-decoded tokens per
+    sequence (the steady state of fixed budgets under continuous refill)."""
+    spec = MODELS[args.model]
     rng = np.random.default_rng(args.seed * 1000 + replica)
-    prompt = rng.integers(lo, hi + 1, n)
-    done = rng.integers(0, 256, n)
+    prompt = prompt_lengths(spec, rng, n)
+    done = rng.integers(0, spec["budget"], n)
     cap = cfg["max_seq"] - steps - 1
     if args.max_ctx:
         cap = min(cap, args.max_ctx)
-    return np.minimum(prompt + done, cap).astype(np.int64)
+    ctx = np.minimum(prompt + done, cap).astype(np.int64)
+    return (ctx, done) if with_done else ctx
 
 
 class ClockSampler:
@@ -203,11 +240,15 @@ class ClockSampler:
 
 
 def kv_dtype_name(args) -> str:
-    """The headline KV dtype: --kv, except that the 70B shape at 2-way tensor
-    parallelism keeps f16 (its f32 cache would need ~214 GB per GPU)."""
-    if args.model == "70b" and args.tp < 4 and "--kv" not in " ".join(sys.argv):
+    """The headline KV dtype: --kv, else the config's: f32 (the reference's),
+    f16 for the Mistral config (BASELINE config 4 mandates it; its f32 cache
+    would need ~172 GB) and for the 70B shape below 4-way tensor parallelism
+    (~214 GB of f32 cache per GPU at 2-way)."""
+    if args.kv:
+        return args.kv
+    if args.model == "70b" and args.tp < 4:
         return "f16"
-    return args.kv
+    return MODELS[args.model]["kv"]
 
 
 # ---------------------------------------------------------------------------
@@ -313,13 +354,21 @@ def measure(args, cfg, path, kv_name, env, full=True):
     n = args.batch
     total_steps = args.warmup + args.steps
     e2e_steps = (args.e2e_steps if args.e2e_steps >= 0 else args.steps) if full else 0
-    ctx = contexts(args, cfg, n, replica, 3 * total_steps + 4)
+    ctx, done = contexts(args, cfg, n, replica, 3 * total_steps + 4, with_done=True)
     D, L, V = cfg["d_model"], cfg["n_layers"], cfg["vocab"]
     hd = D // cfg["n_heads"]
     nq, nkv, F = cfg["n_heads"] // tp, cfg["n_kv_heads"] // tp, cfg["ffn_hidden"] // tp
     # pool: every sequence's pages through the last step, the two prefill prompts
     pf = args.prefill_tokens if full and 0 < args.prefill_tokens < cfg["max_seq"] else 0
+    refill = args.refill_steps if full and tp == 1 and args.trace != "poisson" else 0
+    trace = full and tp == 1 and args.trace == "poisson"
     pages = int(sum((int(c) + total_steps + e2e_steps + 2) // 16 + 1 for c in ctx)) + 2 * (pf // 16 + 2) + 64
+    if refill:
+        # admitted prompts reuse released sequences' pages; this covers the
+        # difference between their lengths (about 3 sigma over ~20 admissions)
+        pages += 1024
+    if trace:
+        pages = max(pages, int(MODELS[args.model]["batch"]) * (cfg["max_seq"] // 16 + 1))
     eng = sb.LlamaBatch(path, device=local, max_batch=n, max_slots=n, kv_dtype=kv,
                         max_seq=cfg["max_seq"], kv_pages=pages, gemm_path=args.gemm_path,
                         attn_path=args.attn_path, tp_size=tp, tp_rank=tp_rank, tp_id=tp_id,
@@ -391,6 +440,8 @@ def measure(args, cfg, path, kv_name, env, full=True):
     if full:
         groups += [("qkv", sb.PROF_QKV), ("wo", sb.PROF_WO), ("gate_up", sb.PROF_GATE_UP),
                    ("down", sb.PROF_DOWN), ("lm_head", sb.PROF_LM_HEAD)]
+        if tp > 1:                       # two per layer, after Wo and after down
+            groups += [("allreduce", sb.PROF_ALLREDUCE)]
     kt = {name: eng.profile(k, n, layer, iters=10) for name, k in groups}
     res["kernel_ms"] = kt
     ctx_now = ctx + total_steps + e2e_steps            # contexts seen by the profiled launch
@@ -421,8 +472,134 @@ def measure(args, cfg, path, kv_name, env, full=True):
         res["prefill"] = {"tokens": pf, "ms": pf_s * 1e3, "tok_s": pf / pf_s, "rows_per_step": n,
                           "note": "one prompt into a released slot through the host API (wall "
                                   "clock, chunk graphs already captured by a first prompt)"}
+        slots[0], slots[1] = warm, ps
+        done[0] = done[1] = 0
+    res["refill"] = None
+    if refill:
+        steps_so_far = total_steps + e2e_steps
+        left = MODELS[args.model]["budget"] - done - steps_so_far
+        res["refill"] = refill_trace(eng, args, MODELS[args.model], slots, left, V, args.seed)
+    res["trace"] = None
+    if trace:
+        for s in slots:
+            assert eng.release(int(s)) == 0, sb.last_error()
+        res["trace"] = poisson_trace(eng, args, MODELS[args.model], V, args.seed)
     eng.close()
     return res
+
+
+def refill_trace(eng, args, spec, slots, left, V, seed):
+    """Continuous refill ("a continuous refill so that 256
+    sequences stay active") through the host API.  Every sequence has a budget
+    of spec['budget'] output tokens (`left` of them remain); a finished one is
+    released and a new request admitted into a fresh slot: its prompt, drawn
+    from the config's prompt distribution, runs through
+    slate_llama_batch_prefill and its first output token is the prompt's greedy
+    token.  Each step then decodes every row with slate_llama_batch_step.
+    Served tok/s = output tokens (decode rows plus first tokens) / wall time,
+    prefill included."""
+    import slate_b200 as sb
+    rng = np.random.default_rng(seed + 77)
+    n = len(slots)
+    slots, left = slots.copy(), left.copy()
+    toks = rng.integers(0, V, n).astype(np.int32)
+    out_tok = prompt_tok = admitted = 0
+    pf_s, step_s, stopped = 0.0, [], None
+    t0 = time.perf_counter()
+    for _ in range(args.refill_steps):
+        for r in np.nonzero(left <= 0)[0]:
+            assert eng.release(int(slots[r])) == 0, sb.last_error()
+            s_new = eng.open()
+            assert s_new >= 0, sb.last_error()
+            prompt = rng.integers(0, V, int(prompt_lengths(spec, rng, 1)[0])).astype(np.int32)
+            tp = time.perf_counter()
+            rc, lg = eng.prefill(s_new, prompt, want_logits=True)
+            pf_s += time.perf_counter() - tp
+            if rc == -2:
+                stopped = "KV pool full"
+                break
+            assert rc == 0, sb.last_error()
+            slots[r], toks[r], left[r] = s_new, int(np.argmax(lg)), spec["budget"] - 1
+            out_tok += 1
+            prompt_tok += len(prompt)
+            admitted += 1
+        if stopped:
+            break
+        ts = time.perf_counter()
+        rc, toks, _ = eng.step(slots, toks)
+        assert rc == 0, sb.last_error()
+        step_s.append(time.perf_counter() - ts)
+        out_tok += n
+        left -= 1
+    wall = time.perf_counter() - t0
+    return {"value": out_tok / wall, "unit": "tok/s", "steps": len(step_s), "admitted": admitted,
+            "prompt_tokens": prompt_tok, "prefill_s": round(pf_s, 3), "wall_s": round(wall, 3),
+            "decode_step_p50_ms": 1e3 * float(np.median(step_s)) if step_s else None,
+            "stopped": stopped,
+            "note": "continuous refill through the host API (slate_llama_batch_step + "
+                    "slate_llama_batch_prefill for each admitted prompt), wall clock, prefill "
+                    "included; output tokens = decode rows + each prompt's first token"}
+
+
+def poisson_trace(eng, args, spec, V, seed, n_req=64, rate=20.0, max_tokens=128):
+    """BASELINE config 2's request trace through the host API: n_req requests
+    with Poisson arrivals at `rate` per second, prompts from the config's
+    distribution (seeded tokens), max_tokens greedy tokens each.  A request is
+    admitted (slate_llama_batch_prefill; its first token is the prompt's greedy
+    token) once it has arrived and a row is free, then decodes in the batch
+    steps until done.  Reports served tok/s over the makespan (first arrival to
+    last completion), time to first token and time per output token."""
+    import slate_b200 as sb
+    rng = np.random.default_rng(seed + 99)
+    arrivals = np.cumsum(rng.exponential(1.0 / rate, n_req))
+    arrivals -= arrivals[0]
+    plens = prompt_lengths(spec, rng, n_req)
+    prompts = [rng.integers(0, V, int(x)).astype(np.int32) for x in plens]
+    w = eng.open()                              # warm-up: chunk graphs for prompts
+    assert w >= 0, sb.last_error()
+    rc, _ = eng.prefill(w, prompts[0][: min(len(prompts[0]), 64)], want_logits=False)
+    assert rc == 0 and eng.release(w) == 0, sb.last_error()
+    pending, active = list(range(n_req)), {}
+    ttft, t_first, t_done, step_s = {}, {}, {}, []
+    t0 = time.perf_counter()
+    while pending or active:
+        while pending and arrivals[pending[0]] <= time.perf_counter() - t0 and len(active) < eng.max_batch:
+            r = pending.pop(0)
+            s = eng.open()
+            assert s >= 0, sb.last_error()
+            rc, lg = eng.prefill(s, prompts[r], want_logits=True)
+            assert rc == 0, sb.last_error()
+            now = time.perf_counter() - t0
+            active[s] = [r, int(np.argmax(lg)), 1]
+            ttft[r], t_first[r] = now - arrivals[r], now
+        if not active:
+            time.sleep(max(0.0, arrivals[pending[0]] - (time.perf_counter() - t0)))
+            continue
+        sl = list(active)
+        ts = time.perf_counter()
+        rc, out, _ = eng.step(sl, [active[s][1] for s in sl])
+        assert rc == 0, sb.last_error()
+        step_s.append(time.perf_counter() - ts)
+        now = time.perf_counter() - t0
+        for i, s in enumerate(sl):
+            a = active[s]
+            a[1], a[2] = int(out[i]), a[2] + 1
+            if a[2] >= max_tokens:
+                assert eng.release(s) == 0, sb.last_error()
+                t_done[a[0]] = now
+                del active[s]
+    makespan = max(t_done.values())
+    tpot = [(t_done[r] - t_first[r]) / (max_tokens - 1) for r in range(n_req)]
+    return {"value": n_req * max_tokens / makespan, "unit": "tok/s", "requests": n_req,
+            "rate_req_s": rate, "max_tokens": max_tokens, "makespan_s": round(makespan, 3),
+            "ttft_p50_ms": 1e3 * float(np.median(list(ttft.values()))),
+            "ttft_p95_ms": 1e3 * float(np.percentile(list(ttft.values()), 95)),
+            "tpot_p50_ms": 1e3 * float(np.median(tpot)),
+            "decode_step_p50_ms": 1e3 * float(np.median(step_s)), "steps": len(step_s),
+            "prompt_mean": float(plens.mean()),
+            "note": "Poisson arrivals replayed on the wall clock through the host API "
+                    "(slate_llama_batch_prefill per admitted prompt, slate_llama_batch_step for "
+                    "the running batch); served tok/s = all output tokens / makespan"}
 
 
 def attn_kernel_name(kv_name, args):
@@ -446,6 +623,10 @@ def main():
         raise SystemExit(f"--tp {tp} must divide the {world} ranks")
     replica, tp_rank = rank // tp, rank % tp
     kv_name = kv_dtype_name(args)
+    if args.refill_steps < 0:
+        args.refill_steps = args.steps
+    if args.trace == "auto":
+        args.trace = "poisson" if args.model == "1b" else "none"
 
     if args.impl == "reference":
         if rank != 0:
@@ -573,9 +754,12 @@ def main():
         "e2e": r.get("e2e"),
         "gpu_launches": r["launches"],
         "prefill": r["prefill"],
+        "refill": r["refill"],
         "clocks": r["clocks"],
         "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
     }
+    if r.get("trace"):
+        line["trace_poisson"] = r["trace"]
     if var_res is not None:
         v = var_res
         line[f"variant_kv_{v['kv']}"] = {

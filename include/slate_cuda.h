@@ -352,6 +352,9 @@ int slate_llama_batch_launches_per_step(const slate_llama_batch_t* b, int n);
 #define SLATE_PROF_DOWN      4   /* FFN down GEMM */
 #define SLATE_PROF_LM_HEAD   5   /* vocabulary projection */
 #define SLATE_PROF_STEP      6   /* one whole step (same graph as _step) */
+#define SLATE_PROF_ALLREDUCE 7   /* tensor parallel only: the all-reduce(sum) of
+                                    [n, d_model] activations that follows Wo and
+                                    down (a collective: every rank calls it) */
 /* Times `iters` back-to-back launches of one kernel group for the rows of the
  * most recent step (the first n rows; `layer` selects the layer's weights and
  * KV) on the engine stream with CUDA events, after one untimed launch; the

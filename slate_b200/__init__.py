@@ -18,7 +18,8 @@ LIB_PATH = os.path.join(HERE, "libslate_cuda.so")
 
 KV_F32 = 0
 KV_F16 = 1
-PROF_ATTENTION, PROF_QKV, PROF_WO, PROF_GATE_UP, PROF_DOWN, PROF_LM_HEAD, PROF_STEP = range(7)
+PROF_ATTENTION, PROF_QKV, PROF_WO, PROF_GATE_UP, PROF_DOWN, PROF_LM_HEAD, PROF_STEP, PROF_ALLREDUCE = \
+    range(8)
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(

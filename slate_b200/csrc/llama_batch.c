@@ -1516,6 +1516,11 @@ static int enqueue_kernel(slate_llama_batch_t* b, int kernel, int n, int layer, 
                              b->ld_logits, SB_EPI_STORE, 1, s);
         case SLATE_PROF_STEP:
             return run_step(b, n);
+        case SLATE_PROF_ALLREDUCE:
+            /* the step's all-reduce after Wo / down: [n][ld_x] floats, here on
+             * scratch rows (a collective: every rank makes the same call) */
+            if (b->tp < 2) return -1;
+            return sb_tp_allreduce_sum(b->comm, scratch_y, (size_t)n * b->ld_x, s);
     }
     return -1;
 }
@@ -1523,7 +1528,7 @@ static int enqueue_kernel(slate_llama_batch_t* b, int kernel, int n, int layer, 
 int slate_llama_batch_profile(slate_llama_batch_t* b, int kernel, int n, int layer, int iters,
                               float* ms) {
     if (!b || !ms || n < 1 || n > b->max_batch || layer < 0 || layer >= b->L || iters < 1 ||
-        kernel < 0 || kernel > SLATE_PROF_STEP)
+        kernel < 0 || kernel > SLATE_PROF_ALLREDUCE || (kernel == SLATE_PROF_ALLREDUCE && b->tp < 2))
         return -1;
     if (b->ld_logits < b->D || (kernel == SLATE_PROF_QKV && b->ld_logits < b->layers[0].wqkv.M)) {
         sb_set_error("profile scratch too small for this model");

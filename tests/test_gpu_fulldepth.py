@@ -48,10 +48,11 @@ N_ROWS = 256
 STEPS = [list(range(N_ROWS)), list(range(N_ROWS)), "mid", "checked"]
 
 VARIANTS = [  # (name, kv_dtype, gemm_path, tolerance)
-    ("f32kv_exact", 0, 0, 1e-4),
-    ("f16kv_exact", 1, 0, 1e-3),
+    ("f32kv_default", 0, 0, 2e-4),
+    ("f32kv_tile_3pass", 0, 3, 2e-4),
     ("f32kv_exact_weight_2pass", 0, 4, 1e-4),
-    ("f32kv_single_pass_f16", 0, 2, 2e-3),
+    ("f16kv_default", 1, 0, 3e-3),
+    ("f32kv_single_pass_f16", 0, 2, 1e-2),
 ]
 
 

@@ -1,11 +1,11 @@
 """Tensor-parallel decode (the 70B plan: column-split Wq/Wk/Wv/gate/up, row-split
 Wo/down with an NCCL all-reduce, vocabulary-split LM head with gathered argmax
-pairs) on 2 GPUs, one process per rank, against the oracle's per-sequence
+pairs) on 2 and 4 GPUs, one process per rank, against the oracle's per-sequence
 sessions (src/loader/llama_infer.c semantics) on the same GGUF.
 
 Tolerances as the single-GPU engine tests: 1e-4 of the logit scale with f32 KV,
-2e-3 with f16 KV; greedy ids equal up to near-ties.  Needs >= 2 GPUs (skipped
-otherwise)."""
+2e-3 with f16 KV; greedy ids equal up to near-ties.  Runs at 2 and 4 ranks,
+each case skipped where the box has fewer GPUs."""
 import multiprocessing as mp
 import os
 
@@ -85,10 +85,13 @@ def run_tp(path, feed, kv_dtype, tp=2, timeout=600):
     return res
 
 
-@pytest.mark.skipif(_gpu_count() < 2, reason="tensor parallelism needs 2 GPUs")
-@pytest.mark.parametrize("name,kv_dtype,tol", [("small", 0, 1e-4), ("small", 1, 2e-3),
-                                               ("8b_heads", 1, 2e-3)])
-def test_tp2_matches_oracle(sb, oracle, workdir, name, kv_dtype, tol):
+@pytest.mark.parametrize("name,kv_dtype,tol,tp", [
+    ("small", 0, 1e-4, 2), ("small", 1, 2e-3, 2), ("8b_heads", 1, 2e-3, 2),
+    # 4 ranks: one kv head per rank (small), two (8B head geometry, group 4 kept whole)
+    ("small", 0, 1e-4, 4), ("8b_heads", 0, 1e-4, 4)])
+def test_tp_matches_oracle(sb, oracle, workdir, name, kv_dtype, tol, tp):
+    if _gpu_count() < tp:
+        pytest.skip(f"tensor parallelism over {tp} ranks needs {tp} GPUs")
     mc = TP_MODELS[name]
     path = os.path.join(str(workdir), f"tp_{name}.gguf")
     if not os.path.exists(path):
@@ -96,11 +99,11 @@ def test_tp2_matches_oracle(sb, oracle, workdir, name, kv_dtype, tol):
     rng = np.random.default_rng(5)
     n, T = 3, 40
     feed = rng.integers(0, mc["vocab"], (n, T)).astype(np.int32)
-    res = run_tp(path, feed, kv_dtype)
+    res = run_tp(path, feed, kv_dtype, tp=tp)
     m = oracle.open(path)
     ref, _ = m.decode_many(feed)
     m.close()
-    for r in (0, 1):
+    for r in range(tp):
         lg, ids = res[r]
         scale = np.abs(ref).max()
         err = np.max(np.abs(lg - ref)) / scale
@@ -110,4 +113,5 @@ def test_tp2_matches_oracle(sb, oracle, workdir, name, kv_dtype, tol):
                 ok, _ = greedy_agrees(int(ids[i, t]), ref[i, t], tol * scale)
                 assert ok, (name, r, i, t)
     # every rank picked the same greedy tokens
-    assert np.array_equal(res[0][1], res[1][1])
+    for r in range(1, tp):
+        assert np.array_equal(res[0][1], res[r][1])
