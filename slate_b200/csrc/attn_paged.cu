@@ -161,7 +161,7 @@ struct AttnShape {
 };
 
 template <int HD, int G, typename KT>
-__global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
+__global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 4) attn_chunk(
     const float* __restrict__ qkv, int ld_qkv, int B, int nq, int nkv,
     const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ page_table, int max_pages, const KT* __restrict__ pool,

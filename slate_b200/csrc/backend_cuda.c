@@ -231,7 +231,7 @@ static int be_matmul_q4k_sk(float* Y, const void* A, const float* X, int B, int 
     sb_tc_operand op;
     if (!rc && sb_tc_make_operand(&op, hi, lo, B, K, K)) rc = -1;
     if (!rc) rc = fin(sb_tc_split(X, K, B, &op, g_stream), "tc split");
-    if (!rc) rc = fin(sb_sk_gemm(&W, &op, B, (float*)ws, Y, M, SB_EPI_STORE, NULL, NULL, 0, (int*)err,
+    if (!rc) rc = fin(sb_sk_gemm(&W, &op, B, (float*)ws, Y, M, SB_EPI_STORE, NULL, NULL, 0, NULL, (int*)err,
                                  g_stream),
                       "matmul_q4k_batch_tc");
     int e = 0;

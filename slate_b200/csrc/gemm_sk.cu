@@ -297,6 +297,18 @@ struct Seg {
     }
 };
 
+// RoPE + paged-cache epilogue of the fused Q|K|V projection (SB_EPI_ROPE).
+struct SkRope {
+    const int32_t* row_pos;
+    const int32_t* row_slot;
+    const int32_t* page_table;
+    void* pool;
+    const float* rcos;
+    const float* rsin;
+    long long n_pages;
+    int max_pages, layer, kv_f16, nq, nkv, hd;
+};
+
 struct SkArgs {
     const unsigned char* W;   // Q4_K rows [M_pad][K/256 * 144]
     float* Y;
@@ -306,6 +318,7 @@ struct SkArgs {
     int* err;
     int M, M_pad, K, n_rows, NT, n_box, ldy, epi, ld16;
     float wscale, wunscale;   // 2^wexp applied to the weights before the split, 2^-wexp after
+    SkRope r;                 // SB_EPI_ROPE only
 };
 
 // Workspace: a 128 x 256 tile is stored as [BN/4][BM] float4 (column group
@@ -482,6 +495,80 @@ __global__ void __launch_bounds__(ST) sk_silu_out_kernel(const SkArgs a, int C, 
                 const int n = n0 + 4 * g4[j] + e;
                 if (n < a.n_rows) store_h(a, n, unit, silu_mul(v[e], u[e]));
             }
+        }
+    }
+}
+
+// RoPE epilogue of the fused Q|K|V projection (src/loader/llama_infer.c:160-174):
+// CTA (t, g4) finishes columns [4 g4, 4 g4 + 4) of tile t, thread m weight row
+// m.  Every tile goes through the workspace (a tile computed alone in its own
+// area, the parts of a shared one in the CTAs' slots), and a 128-row tile holds
+// 128 / head_dim whole heads, so the NeoX pair (d, d + head_dim / 2) of a head
+// is in the tile: query heads are rotated in place in Y, key heads rotated and
+// value heads copied into the paged cache at each row's position, exactly as
+// rope_append_heads_kernel does with the projection written out first.
+__global__ void __launch_bounds__(BM) sk_rope_out_kernel(const SkArgs a, int C, long long U) {
+    sb_grid_release();   // the attention may start its set-up
+    sb_grid_wait();      // the GEMM's workspace: after it (sb_pdl.h)
+    __shared__ TileSrc ts;
+    __shared__ float xs[BM][4];
+    const int t = blockIdx.x, g4 = blockIdx.y, m = threadIdx.x;
+    if (m == 0) ts = tile_sources(t, a.K / BK, C, U);
+    __syncthreads();
+    const int cf = ts.cf, cl = ts.cl;
+    const int mt = t / a.NT, n0 = (t % a.NT) * BN;
+    if (n0 + 4 * g4 >= a.n_rows) return;          // the same for every thread of the CTA
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int cc = cf; cc <= cl; ++cc) {
+        const float4* src = (cf == cl ? ws_tile(a.ws, C, t) : ws_slot(a.ws, cc, cc == cf ? ts.slot0 : 0)) +
+                            (size_t)g4 * BM;
+        const float4 p = __ldcg(src + m);
+        acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    }
+    xs[m][0] = acc.x;
+    xs[m][1] = acc.y;
+    xs[m][2] = acc.z;
+    xs[m][3] = acc.w;
+    __syncthreads();
+    const SkRope& r = a.r;
+    const int row = mt * BM + m;
+    if (row >= a.M) return;                       // zero padding rows
+    const int hd = r.hd, half = hd / 2, h = row / hd, d = row % hd;
+    const bool rotate = h < r.nq + r.nkv;
+    if (rotate && d >= half) return;              // the pair is the thread of element d - half
+    const size_t hs = (size_t)SB_PAGE_TOKENS * hd;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int n = n0 + 4 * g4 + j;
+        if (n >= a.n_rows) break;
+        const int pos = r.row_pos[n];
+        if (pos < 0) continue;
+        float o0 = xs[m][j], o1 = 0.f;
+        if (rotate) {
+            const float c = r.rcos[(size_t)pos * half + d], sn = r.rsin[(size_t)pos * half + d];
+            const float x0 = xs[m][j], x1 = xs[m + half][j];
+            o0 = x0 * c - x1 * sn;
+            o1 = x0 * sn + x1 * c;
+            if (h < r.nq) {
+                a.Y[(size_t)n * a.ldy + row] = o0;
+                a.Y[(size_t)n * a.ldy + row + half] = o1;
+                continue;
+            }
+        }
+        const int slot = r.row_slot[n];
+        const int page = r.page_table[(size_t)slot * r.max_pages + pos / SB_PAGE_TOKENS];
+        if (page < 0 || page >= r.n_pages) continue;   // never allocated: skip, never fault
+        const int kv = rotate ? 0 : 1, hk = rotate ? h - r.nq : h - r.nq - r.nkv;
+        const size_t off = ((((size_t)r.layer * r.n_pages + page) * 2 + kv) * r.nkv + hk) * hs +
+                           (size_t)(pos % SB_PAGE_TOKENS) * hd + d;
+        if (r.kv_f16) {
+            __half* dst = (__half*)r.pool + off;
+            dst[0] = __float2half_rn(o0);
+            if (rotate) dst[half] = __float2half_rn(o1);
+        } else {
+            float* dst = (float*)r.pool + off;
+            dst[0] = o0;
+            if (rotate) dst[half] = o1;
         }
     }
 }
@@ -680,7 +767,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (!have) ok = false;
             tc_fence_after();
             const bool alone = sg.ka == 0 && sg.kb == nk;
-            if (have && alone && a.epi != SB_EPI_SILU) {
+            if (have && alone && a.epi != SB_EPI_SILU && a.epi != SB_EPI_ROPE) {
                 alone_out(a, lane_base, mt, n0, n_mma, m);
             } else if (have) {
                 float4* wsp = (alone ? ws_tile(a.ws, C, t)
@@ -731,7 +818,7 @@ static bool sk_plan(int M_pad, int K, int n_rows, int epi, int* C_out, long long
     const int NT = (n_rows + BN - 1) / BN, nk = K / BK;
     const long long U = (long long)(M_pad / BM) * NT * nk;
     const int C = (int)(U < g_sms ? U : g_sms);
-    bool pass = epi == SB_EPI_SILU;
+    bool pass = epi == SB_EPI_SILU || epi == SB_EPI_ROPE;
     for (int c = 1; c < C && !pass; ++c) pass = (U * c / C) % nk != 0;
     if (C_out) *C_out = C;
     if (U_out) *U_out = U;
@@ -751,12 +838,17 @@ extern "C" void sb_sk_prepare(void) {
 }
 
 extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows, float* ws,
-                          float* Y, int ldy, int epi, void* h_hi, void* h_lo, int ld16, int* err,
-                          cudaStream_t st) {
+                          float* Y, int ldy, int epi, void* h_hi, void* h_lo, int ld16,
+                          const sb_rope_args* rope, int* err, cudaStream_t st) {
     if (!W || !X || !X->lo || W->wtype != SB_WT_Q4K || W->M_pad % BM || W->K % 256 ||
         W->K != X->K || n_rows < 1 || n_rows > X->rows || !ws || !Y || !err ||
-        (epi != SB_EPI_STORE && epi != SB_EPI_ADD && epi != SB_EPI_SILU) ||
+        (epi != SB_EPI_STORE && epi != SB_EPI_ADD && epi != SB_EPI_SILU && epi != SB_EPI_ROPE) ||
         (epi == SB_EPI_SILU && W->M % 128) || (h_hi && (!h_lo || epi != SB_EPI_SILU || ld16 < W->M / 2)))
+        return -1;
+    if (epi == SB_EPI_ROPE &&
+        (!rope || rope->hd < 2 || rope->hd % 2 || BM % rope->hd ||
+         W->M != (rope->nq + 2 * rope->nkv) * rope->hd || !rope->pool || !rope->row_pos ||
+         !rope->row_slot || !rope->page_table || !rope->rope_cos || !rope->rope_sin))
         return -1;
     if (!g_sms) sb_sk_prepare();
     SkArgs a;
@@ -777,6 +869,11 @@ extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows
     a.ld16 = ld16;
     a.wscale = ldexpf(1.0f, W->wexp);
     a.wunscale = ldexpf(1.0f, -W->wexp);
+    a.r = SkRope{};
+    if (epi == SB_EPI_ROPE)
+        a.r = SkRope{rope->row_pos, rope->row_slot, rope->page_table, rope->pool, rope->rope_cos,
+                     rope->rope_sin, (long long)rope->n_pages, rope->max_pages, rope->layer,
+                     rope->kv_dtype == SLATE_KV_F16, rope->nq, rope->nkv, rope->hd};
     const int MT = W->M_pad / BM;
     int C = 0;
     long long U = 0;
@@ -791,7 +888,11 @@ extern "C" int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows
         cudaSuccess)
         return -1;
     cudaError_t e = cudaSuccess;
-    if (pass && epi == SB_EPI_SILU)
+    if (epi == SB_EPI_ROPE)
+        e = sb_launch_pdl(sk_rope_out_kernel,
+                          dim3((unsigned)(MT * a.NT), (unsigned)((min(n_rows, BN) + 3) / 4)), dim3(BM),
+                          0, st, a, C, U);
+    else if (pass && epi == SB_EPI_SILU)
         e = sb_launch_pdl(sk_silu_out_kernel, dim3((unsigned)(MT * a.NT), 4u), dim3(ST), 0, st, a, C,
                           U);
     else if (pass)

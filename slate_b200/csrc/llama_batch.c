@@ -188,6 +188,16 @@ static int uses_sk(const slate_llama_batch_t* b, const sb_lane* L, const sb_matr
            (n >= b->sk_min || (L != &b->full && n >= SB_TC_MIN_ROWS));
 }
 
+/* Whether the lane's QKV projection of n rows carries RoPE and the paged KV
+ * append in its output pass: it runs on the stream-K kernel, whose 128-row
+ * tiles then hold whole heads. */
+static int qkv_rope_fused(const slate_llama_batch_t* b, const sb_lane* L, int n) {
+    const sb_matrix* W = &b->layers[0].wqkv;
+    return uses_sk(b, L, W, n, SB_EPI_ROPE) && 128 % b->hd == 0 && b->hd % 2 == 0 &&
+           L->op_d->K == W->K && W->M == (b->nq + 2 * b->nkv) * b->hd &&
+           sb_sk_tiles(W->M_pad, n) <= sb_sk_tiles(b->layers[0].wgu.M_pad, n);
+}
+
 /* One weight GEMM of the step on the path chosen for (weight, rows); X and Y
  * point at the lane's first row, in names the input (IN_*). */
 static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, const float* X,
@@ -218,7 +228,7 @@ static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, con
         int rc = (in == IN_H && b->sk_h) || pre ? 0 : sb_tc_split(X, ldx, n, op, s);
         const int fuse = epi == SB_EPI_SILU && b->sk_h;
         return rc ? rc : sb_sk_gemm(W, op, n, L->sk_ws, Y, ldy, epi, fuse ? L->op_f->hi : NULL,
-                                    fuse ? L->op_f->lo : NULL, L->op_f->ld16, b->tc_err, s);
+                                    fuse ? L->op_f->lo : NULL, L->op_f->ld16, NULL, b->tc_err, s);
     }
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
         int rc = pre ? 0 : sb_tc_split(X, ldx, n, op, s);
@@ -422,11 +432,22 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
     const sb_layer* ly = &b->layers[l];
     if (part == 0) {
         rc |= step_norm(b, L, ly->attn_norm, n, s);
-        rc |= step_gemm(b, L, &ly->wqkv, xn, b->ld_x, IN_XN, n, qkv, b->ld_qkv, SB_EPI_STORE,
-                        b->sp_qkv, s);
-        rc |= sb_rope_append(qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, row_pos, row_slot,
-                             b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
-                             b->rope_cos, b->rope_sin, s);
+        if (qkv_rope_fused(b, L, n)) {
+            /* RoPE and the KV append in the stream-K GEMM's output pass */
+            const sb_tc_operand* op = L->op_d;
+            const sb_rope_args ra = {row_pos, row_slot, b->page_table, b->pool, b->rope_cos,
+                                     b->rope_sin, b->n_pages, b->max_pages, l, b->kv_dtype,
+                                     b->nq, b->nkv, b->hd};
+            if (!L->xn_split) rc |= sb_tc_split(xn, b->ld_x, n, op, s);
+            rc |= sb_sk_gemm(&ly->wqkv, op, n, L->sk_ws, qkv, b->ld_qkv, SB_EPI_ROPE, NULL, NULL, 0,
+                             &ra, b->tc_err, s);
+        } else {
+            rc |= step_gemm(b, L, &ly->wqkv, xn, b->ld_x, IN_XN, n, qkv, b->ld_qkv, SB_EPI_STORE,
+                            b->sp_qkv, s);
+            rc |= sb_rope_append(qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, row_pos, row_slot,
+                                 b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
+                                 b->rope_cos, b->rope_sin, s);
+        }
     } else if (part == 1) {
         /* the second lane's partials sit after a whole batch's */
         float* scratch = b->scratch + (r0 ? sb_attention_scratch_floats(b->max_batch, b->nq, b->hd,
@@ -575,9 +596,13 @@ static int gemm_launches(const slate_llama_batch_t* b, const sb_lane* L, const s
 static int layer_launches(const slate_llama_batch_t* b, const sb_lane* L, int n) {
     const sb_layer* l0 = &b->layers[0];
     const int res_epi = b->tp > 1 && b->rank != 0 ? SB_EPI_STORE : SB_EPI_ADD;
+    const int qkv = qkv_rope_fused(b, L, n)
+                        ? (norm_splits(b, L, n) ? 0 : 1) + sb_sk_kernels(l0->wqkv.M_pad, l0->wqkv.K, n,
+                                                                         SB_EPI_ROPE)
+                        : 1 /* rope + append */ + gemm_launches(b, L, &l0->wqkv, n, SB_EPI_STORE,
+                                                                b->sp_qkv, 1);
     const int per_layer =
-        2 /* rmsnorm x2 */ + 1 /* rope + append */ + 2 /* attention */ +
-        gemm_launches(b, L, &l0->wqkv, n, SB_EPI_STORE, b->sp_qkv, 1) +
+        2 /* rmsnorm x2 */ + 2 /* attention */ + qkv +
         gemm_launches(b, L, &l0->wo, n, res_epi, b->sp_wo, L->op_a->ld16 >= b->Dq) +
         gemm_launches(b, L, &l0->wgu, n, SB_EPI_SILU, b->sp_gu, 1) +
         gemm_launches(b, L, &l0->wdown, n, res_epi, b->sp_dn, 0);

@@ -24,7 +24,26 @@ extern "C" {
 #define SB_EPI_SILU  2   /* rows interleaved by 64 (gate | up) per 128-row
                             tile: Y[n][t*64+r] = silu(g)*u (backend_cpu.c:78) */
 
+#define SB_EPI_ROPE  3   /* fused Q|K|V projection: RoPE (llama_infer.c:77-92)
+                            on the query heads in place, key heads rotated and
+                            value heads copied into the paged cache at each
+                            row's position (llama_infer.c:167-174) */
+
 #define SB_PAGE_TOKENS 16
+
+/* What the SB_EPI_ROPE epilogue needs: the rows' positions and slots, the
+ * page table and KV pool (layout of slate_llama_batch_new_desc), the RoPE
+ * tables [pos][head_dim/2], and the head counts of the projection. */
+typedef struct sb_rope_args {
+    const int32_t* row_pos;
+    const int32_t* row_slot;
+    const int32_t* page_table;
+    void* pool;
+    const float* rope_cos;
+    const float* rope_sin;
+    int64_t n_pages;
+    int max_pages, layer, kv_dtype, nq, nkv, hd;
+} sb_rope_args;
 
 /* Weight matrix as the GEMMs consume it (packed once at upload):
  *   Q4_K: rows of K/256 super-blocks of 144 bytes (Slate's nibble order),

@@ -94,9 +94,13 @@ void sb_q4_prepare(void);
  * SiLU weight it is used with (0 if none).  SiLU needs W->M % 128 == 0 (gate rows 0-63 and up
  * rows 64-127 of every 128-row tile) and may also write the result as an f16
  * hi / lo pair (h_hi / h_lo, row stride ld16; NULL: not written), the operand
- * of the GEMM that follows. */
+ * of the GEMM that follows.  SB_EPI_ROPE (the fused Q|K|V weight, `rope`
+ * non-NULL, 128 % head_dim == 0) rotates the query heads in place in Y and
+ * writes the rotated keys and the values into the paged cache instead of Y;
+ * its tiles also need the workspace's tile areas (t >= the QKV tiles). */
 int sb_sk_gemm(const sb_matrix* W, const sb_tc_operand* X, int n_rows, float* ws, float* Y,
-               int ldy, int epi, void* h_hi, void* h_lo, int ld16, int* err, cudaStream_t st);
+               int ldy, int epi, void* h_hi, void* h_lo, int ld16, const sb_rope_args* rope,
+               int* err, cudaStream_t st);
 size_t sb_sk_ws_floats(int max_silu_tiles);
 /* Kernel launches of one sb_sk_gemm call (1, or 2 with the output pass). */
 int sb_sk_kernels(int M_pad, int K, int n_rows, int epi);
