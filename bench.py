@@ -369,7 +369,10 @@ def measure(args, cfg, path, kv_name, env, full=True):
         pages += 1024
     if trace:
         pages = max(pages, int(MODELS[args.model]["batch"]) * (cfg["max_seq"] // 16 + 1))
-    eng = sb.LlamaBatch(path, device=local, max_batch=n, max_slots=n, kv_dtype=kv,
+    # prompts run in chunks of max_batch rows: engines that prefill get a box of
+    # at least 256 rows (the decode graph of n rows is the same whatever the box)
+    box = max(n, 256) if (pf or refill or trace) else n
+    eng = sb.LlamaBatch(path, device=local, max_batch=box, max_slots=n, kv_dtype=kv,
                         max_seq=cfg["max_seq"], kv_pages=pages, gemm_path=args.gemm_path,
                         attn_path=args.attn_path, tp_size=tp, tp_rank=tp_rank, tp_id=tp_id,
                         lanes=args.lanes)
@@ -469,15 +472,19 @@ def measure(args, cfg, path, kv_name, env, full=True):
         rc, _ = eng.prefill(ps, prompts[1], want_logits=False)
         pf_s = time.perf_counter() - t0
         assert rc == 0, sb.last_error()
-        res["prefill"] = {"tokens": pf, "ms": pf_s * 1e3, "tok_s": pf / pf_s, "rows_per_step": n,
+        res["prefill"] = {"tokens": pf, "ms": pf_s * 1e3, "tok_s": pf / pf_s, "rows_per_step": box,
                           "note": "one prompt into a released slot through the host API (wall "
                                   "clock, chunk graphs already captured by a first prompt)"}
         slots[0], slots[1] = warm, ps
         done[0] = done[1] = 0
     res["refill"] = None
     if refill:
-        steps_so_far = total_steps + e2e_steps
-        left = MODELS[args.model]["budget"] - done - steps_so_far
+        # remaining budgets of a steady state: the seeded decoded counts advanced
+        # by the steps run so far, wrapped at the budget (a sequence past its
+        # budget stands for its successor), so admissions arrive at the steady
+        # rate of rows / budget per step rather than in one burst
+        budget = MODELS[args.model]["budget"]
+        left = budget - (done + total_steps + e2e_steps) % budget
         res["refill"] = refill_trace(eng, args, MODELS[args.model], slots, left, V, args.seed)
     res["trace"] = None
     if trace:

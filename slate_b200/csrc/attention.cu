@@ -256,7 +256,24 @@ __device__ __forceinline__ void am_merge(float& bv, int& bi, float v, int i) {
 __device__ void block_argmax(const float* row, int V, float& out_v, int& out_i) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) am_merge(bv, bi, row[i], i);
+    if (((uintptr_t)row & 15) == 0) {
+        // 16-byte loads, four in flight per thread (the logits are read once:
+        // streaming loads); am_merge keeps the lowest index of the maximum
+        // whatever order the elements arrive in
+        const int V4 = V / 4;
+        const float4* r4 = (const float4*)row;
+#pragma unroll 4
+        for (int j = threadIdx.x; j < V4; j += blockDim.x) {
+            const float4 x = __ldcs(r4 + j);
+            am_merge(bv, bi, x.x, 4 * j);
+            am_merge(bv, bi, x.y, 4 * j + 1);
+            am_merge(bv, bi, x.z, 4 * j + 2);
+            am_merge(bv, bi, x.w, 4 * j + 3);
+        }
+        for (int i = 4 * V4 + threadIdx.x; i < V; i += blockDim.x) am_merge(bv, bi, row[i], i);
+    } else {
+        for (int i = threadIdx.x; i < V; i += blockDim.x) am_merge(bv, bi, row[i], i);
+    }
     for (int o = 16; o > 0; o >>= 1) {
         float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
         int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
