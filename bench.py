@@ -81,7 +81,9 @@ MODELS = {"8b": dict(cfg=CFG3, metric=METRIC, batch=256, prompt=(128, 4096), bud
 # dram__bytes_write.sum over K/V + q + output bytes).  f16 KV (attn_chunk_mma):
 # 300.39 MB read + 5.20 MB written for 300.74 MB.  Traffic scales with the K/V
 # tokens read, so a full launch's traffic is the ratio times its algorithmic bytes.
-ATTN_TRAFFIC_RATIO = {"f16": 1.0161, "f32": None}
+# f32 KV (attn_chunk, 256 rows, contexts capped at 1024, mean 956): 2040.80 MB read
+# + 11.49 MB written for 2019.67 MB.
+ATTN_TRAFFIC_RATIO = {"f16": 1.0161, "f32": 1.0161}
 
 
 def parse():

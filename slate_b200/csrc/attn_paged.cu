@@ -161,7 +161,7 @@ struct AttnShape {
 };
 
 template <int HD, int G, typename KT>
-__global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 4) attn_chunk(
+__global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     const float* __restrict__ qkv, int ld_qkv, int B, int nq, int nkv,
     const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ page_table, int max_pages, const KT* __restrict__ pool,
@@ -271,10 +271,21 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 4) attn_chunk(
                     for (int h = 0; h < G; ++h)
 #pragma unroll
                         for (int t = 0; t < TOK; ++t) {
-                            float a = 0.f;
+                            if constexpr (DPL % 2 == 0) {
+                                // dims in pairs on the paired f32 pipe (FMUL2 / FFMA2)
+                                float2 a2 = __fmul2_rn(make_float2(q[h][0], q[h][1]),
+                                                       make_float2(kr[t][0], kr[t][1]));
 #pragma unroll
-                            for (int c = 0; c < DPL; ++c) a = fmaf(q[h][c], kr[t][c], a);
-                            part_s[h * TOK + t] = a;
+                                for (int c = 2; c < DPL; c += 2)
+                                    a2 = __ffma2_rn(make_float2(q[h][c], q[h][c + 1]),
+                                                    make_float2(kr[t][c], kr[t][c + 1]), a2);
+                                part_s[h * TOK + t] = a2.x + a2.y;
+                            } else {
+                                float a = 0.f;
+#pragma unroll
+                                for (int c = 0; c < DPL; ++c) a = fmaf(q[h][c], kr[t][c], a);
+                                part_s[h * TOK + t] = a;
+                            }
                         }
                 }
                 float sv[VPL];
@@ -313,8 +324,18 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 4) attn_chunk(
                     const float sm = __shfl_sync(0xffffffffu, psum, h * GL);
                     const float corr = expf(m[h] - mn);
                     l[h] = l[h] * corr + sm;
+                    if constexpr (DPL % 2 == 0) {
 #pragma unroll
-                    for (int c = 0; c < DPL; ++c) o[h][c] *= corr;
+                        for (int c = 0; c < DPL; c += 2) {
+                            const float2 r2 = __fmul2_rn(make_float2(o[h][c], o[h][c + 1]),
+                                                         make_float2(corr, corr));
+                            o[h][c] = r2.x;
+                            o[h][c + 1] = r2.y;
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < DPL; ++c) o[h][c] *= corr;
+                    }
                     m[h] = mn;
                 }
                 __syncwarp();
@@ -328,8 +349,18 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 4) attn_chunk(
 #pragma unroll
                     for (int h = 0; h < G; ++h) {
                         const float p = p_s[warp][t * G + h];
+                        if constexpr (DPL % 2 == 0) {
 #pragma unroll
-                        for (int c = 0; c < DPL; ++c) o[h][c] = fmaf(p, vr[c], o[h][c]);
+                            for (int c = 0; c < DPL; c += 2) {
+                                const float2 r2 = __ffma2_rn(make_float2(p, p), make_float2(vr[c], vr[c + 1]),
+                                                             make_float2(o[h][c], o[h][c + 1]));
+                                o[h][c] = r2.x;
+                                o[h][c + 1] = r2.y;
+                            }
+                        } else {
+#pragma unroll
+                            for (int c = 0; c < DPL; ++c) o[h][c] = fmaf(p, vr[c], o[h][c]);
+                        }
                     }
                 }
                 __syncwarp();

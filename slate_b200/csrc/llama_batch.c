@@ -112,6 +112,7 @@ struct slate_llama_batch {
     /* three-pass stream-K GEMM (gemm_sk.cu): workspace; sk_h: the gate/up
      * GEMM writes its SiLU output also as the down GEMM's f16 hi / lo operand */
     int sk_on, sk_h, sk_min;       /* sk_min: rows from which a GEMM uses it */
+    int gv_on;                     /* Q4_K GEMMs of 1-2 rows on the CUDA-core GEMV */
     float* sk_ws;
     sb_lane full, half[2];         /* the whole batch; the two halves (dual) */
     int dual, half_rows;           /* dual: steps of > half_rows rows use two lanes */
@@ -211,6 +212,9 @@ static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, con
         int rc = have_d ? 0 : sb_tc_split(X, ldx, n, L->op_d, s);
         return rc ? rc : sb_tc_gemm_f16w(&b->head_tc, L->op_d, n, Y, ldy, epi, b->tc_err, s);
     }
+    /* one or two rows: the CUDA-core GEMV (gemm_gv.cu), weight streaming bound */
+    if (b->gv_on && n <= SB_GV_MAX_ROWS && sb_gv_supported(W, n, epi))
+        return sb_gv_gemm(W, X, ldx, n, Y, ldy, epi, s);
     /* a few rows: weight streaming bound, gemm_mv.cu */
     if (L->mv_ws && W->wtype == SB_WT_Q4K && n <= SB_MV_MAX_ROWS &&
         sb_mv_gemm(W, X, ldx, n, Y, ldy, epi, L->mv_ws, L->mv_cnt, s) == 0)
@@ -581,6 +585,7 @@ static int gemm_launches(const slate_llama_batch_t* b, const sb_lane* L, const s
                          int epi, int splits, int pre) {
     const int split = pre && norm_splits(b, L, n) ? 0 : 1;
     if (W == &b->lm_head && head_on_tc(b, L, n)) return split + 1;
+    if (b->gv_on && n <= SB_GV_MAX_ROWS && sb_gv_supported(W, n, epi)) return 1;
     if (L->mv_ws && W->wtype == SB_WT_Q4K && n <= SB_MV_MAX_ROWS) return 1;
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0)
         return 2;                                                               /* split + GEMM */
@@ -769,6 +774,8 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
     if (tp > 1 && sb_tp_init(&b->comm, tp, rank, o->tp_id)) goto fail;
     sb_gemm_prepare();
     sb_tc_prepare();
+    sb_gv_prepare();
+    b->gv_on = o->gemm_path == 0;
     if (sb_attention_prepare(b->nq, b->nkv, hd, b->kv_dtype)) {
         sb_set_error("no attention kernel for head_dim %d, group %d", hd, nq / nkv);
         goto fail;

@@ -7,8 +7,8 @@ exact per-layer shapes (d_model 4096, 32/8 heads, head_dim 128, FFN 14336,
 vocab 128256 / 32000, theta 5e5 / 1e6) with fewer layers; the ~1B model runs
 at full depth.  Histories of up to 4350 (8B) and 32760 (Mistral) tokens are
 seeded on the device, read back and given to the oracle sessions, then every
-sequence decodes in one batch (tiled GEMM path) and then a 4-row batch (GEMV
-path).  Tolerances as in test_gpu_engine: 1e-4 (f32 KV) / 2e-3 (f16 KV) of the
+sequence decodes in one batch (tiled GEMM path), then a 4-row batch (the
+small-batch MMA kernel), a 1-row and a 2-row batch (the CUDA-core GEMV).  Tolerances as in test_gpu_engine: 1e-4 (f32 KV) / 2e-3 (f16 KV) of the
 logit scale, greedy ids exact except for reported near-ties.
 """
 import os
@@ -75,7 +75,9 @@ def test_real_shapes(sb, oracle, workdir, name):
     toks = rng.integers(0, mc["vocab"], len(slots)).astype(np.int32)
     n_tie = 0
     pool = ThreadPoolExecutor(max_workers=os.cpu_count() or 8)
-    for rows in (list(range(len(slots))), list(range(0, len(slots), 2))[:4]):
+    # every sequence (tiled / tensor-core GEMMs), 4 rows (the small-batch MMA
+    # kernel), then 1 and 2 rows (the CUDA-core GEMV)
+    for rows in (list(range(len(slots))), list(range(0, len(slots), 2))[:4], [1], [0, len(slots) - 1]):
         rc, out, lg = eng.step([slots[r] for r in rows], toks[rows], want_logits=True)
         assert rc == 0, sb.last_error()
         refs = list(pool.map(lambda r: sess[r].decode(int(toks[r])), rows))
