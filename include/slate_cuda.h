@@ -128,11 +128,15 @@ const slate_backend_cuda_t* slate_backend_cuda_create(int device);
  * :276-277, 411-412, 586-591; host weight, scratch and logits pointers passed
  * to the entries; results read without sync()).  alloc returns managed memory,
  * copies accept any pointers, and every entry returns only after its kernel has
- * finished; kernels read host pointers directly, so this form exists only on a
- * device that can access pageable host memory (HMM / ATS): NULL otherwise,
- * with the reason in slate_cuda_last_error().  Same device and stream as
+ * finished.  Kernels read the pointers they are given directly: memory from
+ * this alloc, pinned / registered host memory, or -- only where
+ * slate_cuda_pageable_memory_access(device) is 1 (HMM / ATS) -- any host
+ * memory, such as a module's own weights.  Same device and stream as
  * slate_backend_cuda_create(device), on which it calls first. */
 const slate_backend_t* slate_backend_cuda_host_coherent(int device);
+/* 1 if kernels on `device` may read pageable host memory (HMM / ATS), 0 if
+ * not, -5 on error. */
+int slate_cuda_pageable_memory_access(int device);
 
 /* Text of the last device-side or argument error seen by this library on the
  * calling thread ("" if none). */

@@ -104,6 +104,7 @@ EXPORTS = {
     "slate_backend_cuda": (P,),
     "slate_backend_cuda_create": (C.POINTER(BackendCuda), c_int),
     "slate_backend_cuda_host_coherent": (P, c_int),
+    "slate_cuda_pageable_memory_access": (c_int, c_int),
     "slate_cuda_last_error": (C.c_char_p,),
     "slate_cuda_tp_unique_id": (c_int, P, c_size),
     "slate_cuda_sample_rows": (c_int, Pi32, P, c_int, c_int, c_int, P, C.POINTER(c_u64)),

@@ -411,11 +411,12 @@ const slate_backend_cuda_t* slate_backend_cuda_create(int device) {
  * reads results right after a call without sync().  This form serves such a
  * caller unchanged: alloc returns managed memory (host and device see one
  * address), the copies go through cudaMemcpyDefault, and every entry waits for
- * its kernel before returning.  The kernels read the host pointers directly,
- * so the form is offered only where the device can access pageable host
- * memory (cudaDevAttrPageableMemoryAccess: HMM or ATS); its entries use plain
- * loads only (no TMA), and it shares the device and stream of the main
- * singleton. */
+ * its kernel before returning.  The kernels read the pointers they are given
+ * directly, with plain loads only (no TMA): memory from this table's alloc,
+ * pinned or registered host memory, or -- on a device that can access pageable
+ * host memory (cudaDevAttrPageableMemoryAccess: HMM or ATS,
+ * slate_cuda_pageable_memory_access) -- any host memory.  It shares the device
+ * and stream of the main singleton. */
 static slate_backend_t g_hc;
 
 static void* hc_alloc(size_t bytes) {
@@ -463,17 +464,16 @@ static void hc_attention_step(float* out, const float* q, const float* K, const 
     be_sync();
 }
 
+int slate_cuda_pageable_memory_access(int device) {
+    int v = 0;
+    if (sb_cuda_check(cudaDeviceGetAttribute(&v, cudaDevAttrPageableMemoryAccess, device),
+                      "cudaDeviceGetAttribute"))
+        return -5;
+    return v ? 1 : 0;
+}
+
 const slate_backend_t* slate_backend_cuda_host_coherent(int device) {
     if (!slate_backend_cuda_create(device)) return NULL;
-    int pageable = 0;
-    if (sb_cuda_check(cudaDeviceGetAttribute(&pageable, cudaDevAttrPageableMemoryAccess, device),
-                      "cudaDeviceGetAttribute"))
-        return NULL;
-    if (!pageable) {
-        sb_set_error("device %d cannot read pageable host memory (no HMM / ATS): the host-coherent "
-                     "backend is unavailable", device);
-        return NULL;
-    }
     pthread_mutex_lock(&g_init);
     if (!g_hc.name) {
         g_hc.alloc = hc_alloc;
