@@ -176,8 +176,10 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     __shared__ int pages_s[SB_ATTN_CHUNK / 16];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int chunk = blockIdx.x % nchunk_max;
-    const int rest = blockIdx.x / nchunk_max;
+    // chunk-major order: every row's first chunk is scheduled first, and the
+    // shorter (partial or empty) later chunks fill the last waves
+    const int chunk = blockIdx.x / (B * nkv);
+    const int rest = blockIdx.x % (B * nkv);
     const int kvh = rest % nkv, b = rest / nkv;
     if (b >= B) return;
     const int pos = row_pos[b];
