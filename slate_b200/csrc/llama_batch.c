@@ -214,7 +214,7 @@ static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, con
     }
     /* one or two rows: the CUDA-core GEMV (gemm_gv.cu), weight streaming bound */
     if (b->gv_on && n <= SB_GV_MAX_ROWS && sb_gv_supported(W, n, epi))
-        return sb_gv_gemm(W, X, ldx, n, Y, ldy, epi, s);
+        return sb_gv_gemm(W, X, ldx, n, Y, ldy, epi, b->tc_err, s);
     /* a few rows: weight streaming bound, gemm_mv.cu */
     if (L->mv_ws && W->wtype == SB_WT_Q4K && n <= SB_MV_MAX_ROWS &&
         sb_mv_gemm(W, X, ldx, n, Y, ldy, epi, L->mv_ws, L->mv_cnt, s) == 0)
