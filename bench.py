@@ -113,7 +113,8 @@ def parse():
     ap.add_argument("--gemm-path", type=int, default=0,
                     help="0 auto (tcgen05 3-pass hi/lo split; stream-K kernel from 128 rows), 1 CUDA "
                          "cores, 2 tcgen05 single f16 pass, 3 3-pass tile-per-CTA kernel only, 4 "
-                         "exact-weight stream-K kernel, 5 3-pass stream-K kernel from 16 rows")
+                         "exact-weight stream-K kernel, 5 3-pass stream-K kernel from 16 rows, 6 "
+                         "exact-weight kernel with x rounded once to f16")
     ap.add_argument("--attn-path", type=int, default=0,
                     help="0: tensor-core attention for f16 KV (mma.sync), 1: CUDA-core kernel")
     ap.add_argument("--max-ctx", type=int, default=0,
@@ -752,7 +753,8 @@ def main():
                                  1: "cuda-core f32", 2: "tcgen05 1-pass f16",
                                  3: "tcgen05 3-pass hi/lo, tile per CTA",
                                  4: "tcgen05 exact f16 weights, 2-pass x, stream-K",
-                                 5: "tcgen05 3-pass hi/lo, weights in TMEM, stream-K"}[args.gemm_path],
+                                 5: "tcgen05 3-pass hi/lo, weights in TMEM, stream-K",
+                                 6: "tcgen05 exact f16 weights, 1-pass f16 x, stream-K"}[args.gemm_path],
                    "attn_path": ("mma.sync f16 hi/lo" if args.attn_path == 0 and kv_name == "f16"
                                  else "cuda-core"),
                    "lanes": args.lanes,

@@ -223,7 +223,8 @@ typedef struct slate_cuda_opts {
                             1 CUDA-core kernels only, 2 tcgen05 1-pass f16, 3 the
                             3-pass tile-per-CTA kernel only, 4 Q4_K on the
                             exact-weight stream-K tcgen05 kernel (2 f16 passes),
-                            5 Q4_K on the 3-pass stream-K kernel from 16 rows */
+                            5 Q4_K on the 3-pass stream-K kernel from 16 rows,
+                            6 as 4 with x rounded once to f16 (1 pass) */
     int attn_path;       /* 0 auto (tensor cores for f16 KV where the shape allows),
                             1 CUDA-core attention only */
     /* Tensor parallelism (the 70B plan): tp_size ranks, one process or thread

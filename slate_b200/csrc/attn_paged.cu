@@ -176,6 +176,8 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     __shared__ int pages_s[SB_ATTN_CHUNK / 16];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    sb_grid_release();   // the combine kernel may start its set-up
+    sb_grid_wait();      // q, positions, pages, the appended K/V: after the previous kernel (sb_pdl.h)
     // chunk-major order: every row's first chunk is scheduled first, and the
     // shorter (partial or empty) later chunks fill the last waves
     const int chunk = blockIdx.x / (B * nkv);
@@ -475,9 +477,10 @@ int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
         return 0;
     }
     const long ctas = (long)B * nkv * nchunk;
-    attn_chunk<HD, G, KT><<<(unsigned)ctas, 32 * (NW + 1), S::SMEM, st>>>(
-        qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages, (const KT*)pool, n_pages,
-        layer, nchunk, ct, scratch, err);
+    if (sb_launch_pdl(attn_chunk<HD, G, KT>, dim3((unsigned)ctas), dim3(32 * (NW + 1)), S::SMEM, st,
+                      qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages,
+                      (const KT*)pool, n_pages, layer, nchunk, ct, scratch, err) != cudaSuccess)
+        return -1;
     const long cw = (long)B * nq;
     return sb_launch_pdl(attn_combine<HD>, dim3((unsigned)((cw + 3) / 4)), dim3(128), 0, st,
                          (const float*)scratch, B, nq, row_pos, nchunk, ct, att, ld_att, hl.hi,

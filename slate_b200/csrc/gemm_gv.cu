@@ -26,7 +26,9 @@
 // kernel of the stream (programmatic dependent launch), since weights are not
 // written by it.  x (NR rows of K floats, stored 64-float groups 68 floats
 // apart so the consumers' loads hit distinct banks) and its 32-element sums
-// are staged once per CTA.
+// are staged once per CTA; with a norm weight, the staged rows are RMSNorm-ed
+// in place first (the step's RMSNorm launch before this GEMM is then not
+// needed).
 //
 // Consumers: NG groups of 8 warps take the stages in turn.  In a stage, WPR
 // warps share a row (WPR = the power of two >= K/4096), each summing a
@@ -61,6 +63,8 @@ struct GvArgs {
     const float* X;
     float* Y;
     int* err;
+    const float* nw;          // RMSNorm weight applied to X while it is staged (null: none)
+    float eps;
     int ldx, ldy, M, K, nb;
     int RS, WPR, CH;          // rows per stage, warps per row, super-blocks per part
     int n_stages, NS;         // stages in the matrix, ring depth
@@ -219,6 +223,40 @@ __global__ void __launch_bounds__(NTHREADS, 1) gv_kernel(const GvArgs a) {
         }
     }
     cons_sync();
+    if (a.nw) {
+        // RMSNorm of each staged row (llama_infer.c:157, 186): y = x * w / sqrt(mean(x^2) + eps),
+        // the sum of squares in f32 per thread and in double across the block
+        __shared__ double red[CW * NG][NR];
+        __shared__ float inv_s[NR];
+        for (int nr = 0; nr < NR; ++nr) {
+            const float* xd = xs + (size_t)nr * xsn;
+            float sq = 0.f;
+            for (int k = threadIdx.x; k < a.K; k += NCONS) {
+                const float v = xd[(k >> 6) * 68 + (k & 63)];
+                sq = fmaf(v, v, sq);
+            }
+            double sd = sq;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sd += __shfl_xor_sync(0xffffffffu, sd, o);
+            if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5][nr] = sd;
+        }
+        cons_sync();
+        if (threadIdx.x < NR) {
+            double t = 0.0;
+            for (int w = 0; w < CW * NG; ++w) t += red[w][threadIdx.x];
+            inv_s[threadIdx.x] = 1.0f / sqrtf((float)(t / (double)a.K) + a.eps);
+        }
+        cons_sync();
+        for (int nr = 0; nr < NR; ++nr) {
+            float* xd = xs + (size_t)nr * xsn;
+            const float inv = inv_s[nr];
+            for (int k = threadIdx.x; k < a.K; k += NCONS) {
+                float* p = xd + (k >> 6) * 68 + (k & 63);
+                *p = *p * __ldg(a.nw + k) * inv;
+            }
+        }
+        cons_sync();
+    }
     for (int i = threadIdx.x; i < NR * (a.K / 32); i += NCONS) {
         const int nr = i / (a.K / 32), sbk = i - nr * (a.K / 32);
         const float4* p = (const float4*)(xs + (size_t)nr * xsn + (sbk >> 1) * 68 + (sbk & 1) * 32);
@@ -433,7 +471,7 @@ extern "C" int sb_gv_supported(const sb_matrix* W, int n, int epi) {
 }
 
 extern "C" int sb_gv_gemm(const sb_matrix* W, const float* X, int ldx, int n, float* Y, int ldy,
-                          int epi, int* err, cudaStream_t st) {
+                          int epi, const float* norm_w, float eps, int* err, cudaStream_t st) {
     if (!sb_gv_supported(W, n, epi) || !X || !Y || !err || ldx < W->K ||
         (n > 1 && ldy < (epi == SB_EPI_SILU ? W->M / 2 : W->M)))
         return -1;
@@ -442,6 +480,8 @@ extern "C" int sb_gv_gemm(const sb_matrix* W, const float* X, int ldx, int n, fl
     a.X = X;
     a.Y = Y;
     a.err = err;
+    a.nw = norm_w;
+    a.eps = eps;
     a.ldx = ldx;
     a.ldy = ldy;
     a.M = W->M;

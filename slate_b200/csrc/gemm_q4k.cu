@@ -302,6 +302,7 @@ struct Args {
     int* cnt;                 // [tiles] arrival counters (zero between launches)
     int* err;
     int M, M_pad, K, n_rows, r_pad, ldy, epi, NT;
+    int one_pass;             // 1: x enters as its f16 rounding only (the lo part is not read)
 };
 
 // Epilogue of one finished 128x128 tile held in the drain threads' registers
@@ -572,9 +573,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         break;
                     }
                     unsigned char* st = bst + (size_t)s * STAGE_BYTES;
-                    bar_expect(&full[s], (uint32_t)(2 * B_BYTES));
+                    bar_expect(&full[s], (uint32_t)((a.one_pass ? 1 : 2) * B_BYTES));
                     tma_2d(st, &xmap_hi, &full[s], k * BK, n0);
-                    tma_2d(st + B_BYTES, &xmap_lo, &full[s], k * BK, n0);
+                    if (!a.one_pass) tma_2d(st + B_BYTES, &xmap_lo, &full[s], k * BK, n0);
                 }
                 cur.next();
             }
@@ -621,7 +622,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         mma_f16_ta(p1, at + 8u * kk, desc_sw128(bh + 32u * kk), idesc,
                                    (k > ks || kk > 0) ? 1u : 0u);
-                        mma_f16_ta(p1, at + 8u * kk, desc_sw128(bl + 32u * kk), idesc, 1u);
+                        if (!a.one_pass) mma_f16_ta(p1, at + 8u * kk, desc_sw128(bl + 32u * kk), idesc, 1u);
                     }
                     mma_commit(&empty[s]);
                 }
@@ -1094,9 +1095,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         break;
                     }
                     unsigned char* st = bst + (size_t)s * STAGE2_BYTES;
-                    if (leader) bar_expect(&full[s], (uint32_t)(2 * STAGE2_BYTES));
+                    if (leader) bar_expect(&full[s], (uint32_t)(a.one_pass ? 2 * B2_BYTES : 2 * STAGE2_BYTES));
                     tma_2d_2sm(st, &xmap_hi, &full[s], k * BK, n0);
-                    tma_2d_2sm(st + B2_BYTES, &xmap_lo, &full[s], k * BK, n0);
+                    if (!a.one_pass) tma_2d_2sm(st + B2_BYTES, &xmap_lo, &full[s], k * BK, n0);
                 }
                 cur.next();
             }
@@ -1142,7 +1143,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         mma2_ta(p1, at + 8u * kk, desc_sw128(bh + 32u * kk), idesc,
                                 (k > ks || kk > 0) ? 1u : 0u);
-                        mma2_ta(p1, at + 8u * kk, desc_sw128(bl + 32u * kk), idesc, 1u);
+                        if (!a.one_pass) mma2_ta(p1, at + 8u * kk, desc_sw128(bl + 32u * kk), idesc, 1u);
                     }
                     commit2(&empty[s]);
                 }
@@ -1348,6 +1349,7 @@ extern "C" int sb_q4_make_operand(sb_q4_operand* op, void* hi, void* lo, void* x
     op->r_pad = r_pad;
     op->K = K;
     op->ld16 = ld16;
+    op->one_pass = 0;
     const cuuint64_t nsb = (cuuint64_t)((K / 256 + 1) & ~1);
     for (int part = 0; part < 6; ++part) {
         // parts 0-1: x hi / lo, 64 x 128 boxes; 2-3: x hi / lo, 64 x 64 boxes;
@@ -1421,6 +1423,7 @@ extern "C" int sb_q4_gemm(const sb_matrix* W, const sb_q4_operand* X, int n_rows
     a.ldy = ldy;
     a.epi = epi;
     a.NT = (n_rows + BN - 1) / BN;
+    a.one_pass = X->one_pass;
     // the Q4_K rows as a 2-D byte tensor [M_pad][K/256 * 144], boxes of one
     // super-block x 128 rows (encoded per call; a captured graph keeps it)
     CUtensorMap wmap;

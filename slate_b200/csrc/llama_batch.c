@@ -173,6 +173,12 @@ static int step_norm(slate_llama_batch_t* b, sb_lane* L, const float* w, int n, 
     return sb_rmsnorm_rows(b->xn + ro, b->ld_x, b->x + ro, b->ld_x, w, n, b->D, b->eps, s);
 }
 
+/* Whether the GEMM after an RMSNorm takes the norm into its activation
+ * staging (the one-/two-row GEMV), so no RMSNorm launch precedes it. */
+static int norm_in_gemv(const slate_llama_batch_t* b, const sb_matrix* W, int n, int epi) {
+    return b->gv_on && n <= SB_GV_MAX_ROWS && W->K == b->D && sb_gv_supported(W, n, epi);
+}
+
 /* Whether the f32 LM head runs on the tensor cores as its f16 hi/lo pair: from
  * SB_TC_MIN_ROWS rows, and from 4 rows where the operand's row box is small
  * (an engine of at most 64 rows), since the CUDA-core GEMV is FMA-bound from
@@ -214,7 +220,7 @@ static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, con
     }
     /* one or two rows: the CUDA-core GEMV (gemm_gv.cu), weight streaming bound */
     if (b->gv_on && n <= SB_GV_MAX_ROWS && sb_gv_supported(W, n, epi))
-        return sb_gv_gemm(W, X, ldx, n, Y, ldy, epi, b->tc_err, s);
+        return sb_gv_gemm(W, X, ldx, n, Y, ldy, epi, NULL, 0.f, b->tc_err, s);
     /* a few rows: weight streaming bound, gemm_mv.cu */
     if (L->mv_ws && W->wtype == SB_WT_Q4K && n <= SB_MV_MAX_ROWS &&
         sb_mv_gemm(W, X, ldx, n, Y, ldy, epi, L->mv_ws, L->mv_cnt, s) == 0)
@@ -435,6 +441,16 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
     const int32_t* row_slot = b->row_slot + r0;
     const sb_layer* ly = &b->layers[l];
     if (part == 0) {
+        if (norm_in_gemv(b, &ly->wqkv, n, SB_EPI_STORE)) {
+            /* RMSNorm in the GEMV's staging of x, then RoPE + the KV append */
+            L->xn_split = 0;
+            rc |= sb_gv_gemm(&ly->wqkv, x, b->ld_x, n, qkv, b->ld_qkv, SB_EPI_STORE, ly->attn_norm,
+                             b->eps, b->tc_err, s);
+            rc |= sb_rope_append(qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, row_pos, row_slot,
+                                 b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
+                                 b->rope_cos, b->rope_sin, s);
+            return rc;
+        }
         rc |= step_norm(b, L, ly->attn_norm, n, s);
         if (qkv_rope_fused(b, L, n)) {
             /* RoPE and the KV append in the stream-K GEMM's output pass */
@@ -479,8 +495,16 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
     } else {
         rc |= step_gemm(b, L, &ly->wo, att, b->ld_att, IN_ATT, n, x, b->ld_x, res_epi, b->sp_wo, s);
         if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, x, (size_t)n * b->ld_x, s);
-        rc |= step_norm(b, L, ly->ffn_norm, n, s);
-        rc |= step_gemm(b, L, &ly->wgu, xn, b->ld_x, IN_XN, n, h, b->ld_h, SB_EPI_SILU, b->sp_gu, s);
+        if (norm_in_gemv(b, &ly->wgu, n, SB_EPI_SILU)) {
+            /* RMSNorm in the GEMV's staging of x */
+            L->xn_split = 0;
+            rc |= sb_gv_gemm(&ly->wgu, x, b->ld_x, n, h, b->ld_h, SB_EPI_SILU, ly->ffn_norm, b->eps,
+                             b->tc_err, s);
+        } else {
+            rc |= step_norm(b, L, ly->ffn_norm, n, s);
+            rc |= step_gemm(b, L, &ly->wgu, xn, b->ld_x, IN_XN, n, h, b->ld_h, SB_EPI_SILU, b->sp_gu,
+                            s);
+        }
         rc |= step_gemm(b, L, &ly->wdown, h, b->ld_h, IN_H, n, x, b->ld_x, res_epi, b->sp_dn, s);
         if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, x, (size_t)n * b->ld_x, s);
     }
@@ -606,8 +630,10 @@ static int layer_launches(const slate_llama_batch_t* b, const sb_lane* L, int n)
                                                                          SB_EPI_ROPE)
                         : 1 /* rope + append */ + gemm_launches(b, L, &l0->wqkv, n, SB_EPI_STORE,
                                                                 b->sp_qkv, 1);
+    const int norms = (norm_in_gemv(b, &l0->wqkv, n, SB_EPI_STORE) ? 0 : 1) +
+                      (norm_in_gemv(b, &l0->wgu, n, SB_EPI_SILU) ? 0 : 1);
     const int per_layer =
-        2 /* rmsnorm x2 */ + 2 /* attention */ + qkv +
+        norms /* rmsnorm */ + 2 /* attention */ + qkv +
         gemm_launches(b, L, &l0->wo, n, res_epi, b->sp_wo, L->op_a->ld16 >= b->Dq) +
         gemm_launches(b, L, &l0->wgu, n, SB_EPI_SILU, b->sp_gu, 1) +
         gemm_launches(b, L, &l0->wdown, n, res_epi, b->sp_dn, 0);
@@ -941,8 +967,9 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
              sb_cuda_check(cudaStreamSynchronize(b->stream), "head split")))
             goto fail;
         /* gemm_path 4: Q4_K weights on the exact-weight stream-K kernel (two f16
-         * passes, block scales per super-block) */
-        if (o->gemm_path == 4) {
+         * passes, block scales per super-block); 6: the same kernel with x
+         * rounded once to f16 (one pass) */
+        if (o->gemm_path == 4 || o->gemm_path == 6) {
             sb_q4_prepare();
             const int r_pad = (B + 127) / 128 * 128;
             const sb_tc_operand* src[3] = {&b->op_d, &b->op_f, &b->op_a};
@@ -956,6 +983,7 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
                     sb_q4_make_operand(dst[i], src[i]->hi, src[i]->lo, xh, xl, B, r_pad, src[i]->K,
                                        src[i]->K))
                     goto fail;
+                dst[i]->one_pass = o->gemm_path == 6;
             }
             int mp = l0->wqkv.M_pad;
             if (l0->wo.M_pad > mp) mp = l0->wo.M_pad;

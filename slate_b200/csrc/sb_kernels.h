@@ -68,15 +68,16 @@ typedef struct sb_matrix {
 /* One or two activation rows (gemm_gv.cu): Q4_K weights with K <= SB_GV_MAX_K,
  * M_pad % 128 == 0, on the CUDA cores (store / residual add / SiLU(gate)*up of
  * the interleaved gate|up weight), the weights streamed through shared memory
- * by bulk copies.  sb_gv_prepare() reads the SM count and opts the kernels
- * into their shared memory (per device, outside stream capture); a ring wait
- * that times out sets *err. */
+ * by bulk copies.  norm_w != NULL: X rows are RMSNorm-ed (weight norm_w[K],
+ * eps) as they are staged.  sb_gv_prepare() reads the SM count and opts the
+ * kernels into their shared memory (per device, outside stream capture); a
+ * ring wait that times out sets *err. */
 #define SB_GV_MAX_ROWS 2
 #define SB_GV_MAX_K 16384
 void sb_gv_prepare(void);
 int sb_gv_supported(const sb_matrix* W, int n, int epi);
 int sb_gv_gemm(const sb_matrix* W, const float* X, int ldx, int n, float* Y, int ldy, int epi,
-               int* err, cudaStream_t st);
+               const float* norm_w, float eps, int* err, cudaStream_t st);
 
 /* Small batches (gemm_mv.cu): Q4_K weights, 1..SB_MV_MAX_ROWS activation
  * rows, tensor cores through mma.sync, weights streamed once.  ws holds

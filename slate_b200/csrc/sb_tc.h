@@ -70,6 +70,7 @@ typedef struct sb_q4_operand {
     SB_ALIGN64 unsigned char xsmap_lo[128];
     void *hi, *lo, *xs_hi, *xs_lo;
     int rows, r_pad, K, ld16;
+    int one_pass;                            /* 1: the GEMM reads x's f16 rounding only */
 } sb_q4_operand;
 int sb_q4_make_operand(sb_q4_operand* op, void* hi, void* lo, void* xs_hi, void* xs_lo, int rows,
                        int r_pad, int K, int ld16);

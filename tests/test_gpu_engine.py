@@ -372,10 +372,10 @@ def test_scheduler_batches_concurrent_callers(sb, oracle, workdir):
 def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
     """The GEMM paths of the engine -- the default (0: the 3-pass split, on the
     stream-K kernel from 128 rows), the tile-per-CTA 3-pass kernel (3), the
-    exact-weight stream-K kernel (4), the 3-pass stream-K kernel (5; the
-    stream-K kernels with their STORE / residual ADD / fused SiLU*up epilogues)
-    and CUDA cores (1) -- each match the oracle on a 2-layer Q4_K model at batch
-    sizes with a partial second row tile."""
+    exact-weight stream-K kernel (4) and its one-pass mode (6), the 3-pass
+    stream-K kernel (5; the stream-K kernels with their STORE / residual ADD /
+    fused SiLU*up epilogues) and CUDA cores (1) -- each match the oracle on a
+    2-layer Q4_K model at batch sizes with a partial second row tile."""
     path = os.path.join(str(workdir), "paths_q4k.gguf")
     if not os.path.exists(path):
         sb.synth_gguf(path, n_layers=2, d_model=1024, ffn_hidden=2816, n_heads=16, n_kv_heads=4,
@@ -387,14 +387,15 @@ def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
     ref, _ = m.decode_many(feed)
     m.close()
     scale = np.abs(ref).max()
-    for gp in (0, 3, 4, 5, 1):
+    # (path, bound): x rounded once to f16 (path 6) carries ~2^-12 per element
+    for gp, tol in ((0, 1e-4), (3, 1e-4), (4, 1e-4), (5, 1e-4), (1, 1e-4), (6, 3e-3)):
         eng = make_engine(sb, path, max_batch=n_rows, gemm_path=gp)
         slots = [eng.open() for _ in range(n_rows)]
         for t in range(T):
             rc, out, lg = eng.step(slots, feed[:, t], want_logits=True)
             assert rc == 0, (gp, rc, sb.last_error())
             err = np.max(np.abs(lg - ref[:, t])) / scale
-            assert err < 1e-4, (gp, t, err)
+            assert err < tol, (gp, t, err)
         eng.close()
 
 

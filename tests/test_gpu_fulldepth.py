@@ -25,6 +25,8 @@ little above its measured error so that a regression shows:
     K/V element to f16, so this mode misses north_star's 1e-3 at full depth)
   * single-pass f16 GEMM (gemm_path 2, an opt-in speed mode): 1e-2 (measured
     6.5e-3; misses north_star's 2e-3 at full depth)
+  * exact f16 sc*q weights with x rounded once to f16 (gemm_path 6): 1e-2
+    (the x rounding alone, ~2^-12 per element)
 Greedy ids: the oracle's argmax, except near-ties (the oracle's own top-2 gap
 within the tolerance), of which at most ceil(tokens / 1000) are accepted per
 variant -- one in this test's 32 checked tokens.  The measured error and the
@@ -56,6 +58,7 @@ VARIANTS = [  # (name, kv_dtype, gemm_path, tolerance)
     ("f32kv_exact_weight_2pass", 0, 4, 1e-4),
     ("f16kv_default", 1, 0, 3e-3),
     ("f32kv_single_pass_f16", 0, 2, 1e-2),
+    ("f32kv_exact_weight_1pass", 0, 6, 1e-2),
 ]
 
 
