@@ -2,7 +2,8 @@
 // cores, bound by the weight stream from HBM.
 //
 //   Y[n][m] (op)= sum_k X[n][k] * W[m][k]      n < NR (1 or 2); op: store,
-//                                              residual add, SiLU(gate) * up
+//                                              residual add, SiLU(gate) * up,
+//                                              or store + RoPE + KV append
 //
 // A decode step of one or two sequences (the latency-bound regime of the
 // reference server, which decodes one token per session per step) multiplies
@@ -65,6 +66,8 @@ struct GvArgs {
     int* err;
     const float* nw;          // RMSNorm weight applied to X while it is staged (null: none)
     float eps;
+    sb_rope_args r;           // SB_EPI_ROPE: positions, page table, pool, RoPE tables
+    int* head_cnt;            // SB_EPI_ROPE: rows written per head (zero between launches)
     int ldx, ldy, M, K, nb;
     int RS, WPR, CH;          // rows per stage, warps per row, super-blocks per part
     int n_stages, NS;         // stages in the matrix, ring depth
@@ -148,6 +151,50 @@ __device__ __forceinline__ void nib4(uint32_t nb, float2& a, float2& b) {
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+__device__ __forceinline__ void put_kv(void* pool, int kv_dtype, size_t i, float v) {
+    if (kv_dtype == 1) ((__half*)pool)[i] = __float2half_rn(v);
+    else ((float*)pool)[i] = v;
+}
+
+// RoPE of head h of the fused Q|K|V rows (llama_infer.c:77-92, pairs (j, j +
+// hd/2) at the row's position) and the KV append (llama_infer.c:169-175): a
+// query head is rotated in place, a key head rotated into the pool, a value
+// head copied into it.  The rows were written by several CTAs: read through L2.
+template <int NR>
+__device__ void rope_head(const GvArgs& a, int h) {
+    const sb_rope_args& r = a.r;
+    const int half = r.hd / 2;
+    for (int t = threadIdx.x; t < NR * half; t += NCONS) {
+        const int nr = t / half, j = t - nr * half;
+        const int pos = r.row_pos[nr];
+        if (pos < 0) continue;
+        float* row = a.Y + (size_t)nr * a.ldy + (size_t)h * r.hd;
+        const float x0 = __ldcg(row + j), x1 = __ldcg(row + j + half);
+        if (h < r.nq) {
+            const float c = r.rope_cos[(size_t)pos * half + j], sn = r.rope_sin[(size_t)pos * half + j];
+            row[j] = x0 * c - x1 * sn;
+            row[j + half] = x0 * sn + x1 * c;
+            continue;
+        }
+        const int slot = r.row_slot[nr];
+        const int page = r.page_table[(size_t)slot * r.max_pages + pos / SB_PAGE_TOKENS];
+        if (page < 0 || page >= r.n_pages) continue;          // never allocated: skip, never fault
+        const size_t hs = (size_t)SB_PAGE_TOKENS * r.hd;
+        const size_t base = ((size_t)r.layer * r.n_pages + page) * 2 * r.nkv * hs +
+                            (size_t)(pos % SB_PAGE_TOKENS) * r.hd;
+        if (h < r.nq + r.nkv) {
+            const float c = r.rope_cos[(size_t)pos * half + j], sn = r.rope_sin[(size_t)pos * half + j];
+            const size_t o = base + (size_t)(h - r.nq) * hs;
+            put_kv(r.pool, r.kv_dtype, o + j, x0 * c - x1 * sn);
+            put_kv(r.pool, r.kv_dtype, o + j + half, x0 * sn + x1 * c);
+        } else {
+            const size_t o = base + (size_t)r.nkv * hs + (size_t)(h - r.nq - r.nkv) * hs;
+            put_kv(r.pool, r.kv_dtype, o + j, x0);
+            put_kv(r.pool, r.kv_dtype, o + j + half, x1);
+        }
+    }
+}
 
 template <int NR, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1) gv_kernel(const GvArgs a) {
@@ -392,6 +439,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) gv_kernel(const GvArgs a) {
             *y = EPI == SB_EPI_ADD ? *y + v : v;
         }
     }
+    if (EPI == SB_EPI_ROPE) {
+        // heads are 128-ish rows, written by two to four CTAs: the CTA that
+        // completes a head (per-head counters of rows written) rotates it
+        __shared__ int is_fin;
+        __threadfence();                  // this CTA's rows, before its counts
+        const int m0 = s0 * a.RS, m1 = min(a.M, s1 * a.RS);
+        for (int h = m0 / a.r.hd; m1 > m0 && h <= (m1 - 1) / a.r.hd; ++h) {
+            cons_sync();
+            if (threadIdx.x == 0) {
+                const int lo = max(m0, h * a.r.hd), hi = min(m1, (h + 1) * a.r.hd);
+                is_fin = atomicAdd(&a.head_cnt[h], hi - lo) + (hi - lo) == a.r.hd;
+                if (is_fin) __threadfence();   // the other CTAs' rows, after their counts
+            }
+            cons_sync();
+            if (is_fin) {
+                rope_head<NR>(a, h);
+                if (threadIdx.x == 0) a.head_cnt[h] = 0;   // every row of the head has counted
+            }
+        }
+    }
 }
 
 int g_sms = 0;
@@ -410,6 +477,7 @@ int dispatch(const GvArgs& a, size_t smem, int epi, cudaStream_t st) {
         case SB_EPI_STORE: return launch<NR, SB_EPI_STORE>(a, smem, st);
         case SB_EPI_ADD: return launch<NR, SB_EPI_ADD>(a, smem, st);
         case SB_EPI_SILU: return launch<NR, SB_EPI_SILU>(a, smem, st);
+        case SB_EPI_ROPE: return launch<NR, SB_EPI_ROPE>(a, smem, st);
     }
     return -1;
 }
@@ -440,6 +508,8 @@ extern "C" void sb_gv_prepare(void) {
     cudaFuncSetAttribute(gv_kernel<2, SB_EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaFuncSetAttribute(gv_kernel<2, SB_EPI_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaFuncSetAttribute(gv_kernel<2, SB_EPI_SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(gv_kernel<1, SB_EPI_ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(gv_kernel<2, SB_EPI_ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 // The ring depth that fits beside x for (n, K, M), 0 if fewer than 3 stages fit.
@@ -466,14 +536,20 @@ static int gv_ring(int n, int K, int M, int epi, size_t* smem_out, int* n_stages
 extern "C" int sb_gv_supported(const sb_matrix* W, int n, int epi) {
     return W && W->wtype == SB_WT_Q4K && n >= 1 && n <= SB_GV_MAX_ROWS && W->K % 256 == 0 &&
            W->K <= SB_GV_MAX_K && W->M_pad % 128 == 0 &&
-           (epi == SB_EPI_STORE || epi == SB_EPI_ADD || (epi == SB_EPI_SILU && W->M % 128 == 0)) &&
+           (epi == SB_EPI_STORE || epi == SB_EPI_ADD || epi == SB_EPI_ROPE ||
+            (epi == SB_EPI_SILU && W->M % 128 == 0)) &&
            gv_ring(n, W->K, W->M, epi, NULL, NULL, NULL) > 0;
 }
 
 extern "C" int sb_gv_gemm(const sb_matrix* W, const float* X, int ldx, int n, float* Y, int ldy,
-                          int epi, const float* norm_w, float eps, int* err, cudaStream_t st) {
+                          int epi, const float* norm_w, float eps, const sb_rope_args* rope,
+                          int* head_cnt, int* err, cudaStream_t st) {
     if (!sb_gv_supported(W, n, epi) || !X || !Y || !err || ldx < W->K ||
         (n > 1 && ldy < (epi == SB_EPI_SILU ? W->M / 2 : W->M)))
+        return -1;
+    if (epi == SB_EPI_ROPE &&
+        (!rope || !head_cnt || rope->hd % 2 || rope->hd / 2 > NCONS || rope->nq < 1 || rope->nkv < 1 ||
+         W->M != (rope->nq + 2 * rope->nkv) * rope->hd))
         return -1;
     GvArgs a;
     a.W = (const unsigned char*)W->data;
@@ -482,6 +558,8 @@ extern "C" int sb_gv_gemm(const sb_matrix* W, const float* X, int ldx, int n, fl
     a.err = err;
     a.nw = norm_w;
     a.eps = eps;
+    a.r = rope ? *rope : sb_rope_args{};
+    a.head_cnt = head_cnt;
     a.ldx = ldx;
     a.ldy = ldy;
     a.M = W->M;

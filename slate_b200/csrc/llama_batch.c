@@ -98,6 +98,7 @@ struct slate_llama_batch {
     sb_tc_operand op_d, op_f;      /* activations with K = d_model / ffn */
     float* tc_ws;
     int* tc_err;
+    int* head_cnt;                 /* per-head row counts of the GEMV's RoPE epilogue (zeroed) */
     int sp_qkv, sp_wo, sp_gu, sp_dn;
     sb_tc_weight head_tc;          /* f32 LM head as an f16 pair (hi set when used) */
     sb_tc_operand op_a;            /* attention output, K = nq*hd (tensor parallel: local heads) */
@@ -220,7 +221,7 @@ static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, con
     }
     /* one or two rows: the CUDA-core GEMV (gemm_gv.cu), weight streaming bound */
     if (b->gv_on && n <= SB_GV_MAX_ROWS && sb_gv_supported(W, n, epi))
-        return sb_gv_gemm(W, X, ldx, n, Y, ldy, epi, NULL, 0.f, b->tc_err, s);
+        return sb_gv_gemm(W, X, ldx, n, Y, ldy, epi, NULL, 0.f, NULL, NULL, b->tc_err, s);
     /* a few rows: weight streaming bound, gemm_mv.cu */
     if (L->mv_ws && W->wtype == SB_WT_Q4K && n <= SB_MV_MAX_ROWS &&
         sb_mv_gemm(W, X, ldx, n, Y, ldy, epi, L->mv_ws, L->mv_cnt, s) == 0)
@@ -441,14 +442,15 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
     const int32_t* row_slot = b->row_slot + r0;
     const sb_layer* ly = &b->layers[l];
     if (part == 0) {
-        if (norm_in_gemv(b, &ly->wqkv, n, SB_EPI_STORE)) {
-            /* RMSNorm in the GEMV's staging of x, then RoPE + the KV append */
+        if (norm_in_gemv(b, &ly->wqkv, n, SB_EPI_ROPE)) {
+            /* one launch: RMSNorm in the GEMV's staging of x, RoPE + the KV
+             * append in its epilogue */
+            const sb_rope_args ra = {row_pos, row_slot, b->page_table, b->pool, b->rope_cos,
+                                     b->rope_sin, b->n_pages, b->max_pages, l, b->kv_dtype,
+                                     b->nq, b->nkv, b->hd};
             L->xn_split = 0;
-            rc |= sb_gv_gemm(&ly->wqkv, x, b->ld_x, n, qkv, b->ld_qkv, SB_EPI_STORE, ly->attn_norm,
-                             b->eps, b->tc_err, s);
-            rc |= sb_rope_append(qkv, b->ld_qkv, n, b->nq, b->nkv, b->hd, row_pos, row_slot,
-                                 b->page_table, b->max_pages, b->pool, b->n_pages, l, b->kv_dtype,
-                                 b->rope_cos, b->rope_sin, s);
+            rc |= sb_gv_gemm(&ly->wqkv, x, b->ld_x, n, qkv, b->ld_qkv, SB_EPI_ROPE, ly->attn_norm,
+                             b->eps, &ra, b->head_cnt, b->tc_err, s);
             return rc;
         }
         rc |= step_norm(b, L, ly->attn_norm, n, s);
@@ -499,7 +501,7 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
             /* RMSNorm in the GEMV's staging of x */
             L->xn_split = 0;
             rc |= sb_gv_gemm(&ly->wgu, x, b->ld_x, n, h, b->ld_h, SB_EPI_SILU, ly->ffn_norm, b->eps,
-                             b->tc_err, s);
+                             NULL, NULL, b->tc_err, s);
         } else {
             rc |= step_norm(b, L, ly->ffn_norm, n, s);
             rc |= step_gemm(b, L, &ly->wgu, xn, b->ld_x, IN_XN, n, h, b->ld_h, SB_EPI_SILU, b->sp_gu,
@@ -625,12 +627,13 @@ static int gemm_launches(const slate_llama_batch_t* b, const sb_lane* L, const s
 static int layer_launches(const slate_llama_batch_t* b, const sb_lane* L, int n) {
     const sb_layer* l0 = &b->layers[0];
     const int res_epi = b->tp > 1 && b->rank != 0 ? SB_EPI_STORE : SB_EPI_ADD;
-    const int qkv = qkv_rope_fused(b, L, n)
+    const int qkv = norm_in_gemv(b, &l0->wqkv, n, SB_EPI_ROPE) ? 1
+                    : qkv_rope_fused(b, L, n)
                         ? (norm_splits(b, L, n) ? 0 : 1) + sb_sk_kernels(l0->wqkv.M_pad, l0->wqkv.K, n,
                                                                          SB_EPI_ROPE)
                         : 1 /* rope + append */ + gemm_launches(b, L, &l0->wqkv, n, SB_EPI_STORE,
                                                                 b->sp_qkv, 1);
-    const int norms = (norm_in_gemv(b, &l0->wqkv, n, SB_EPI_STORE) ? 0 : 1) +
+    const int norms = (norm_in_gemv(b, &l0->wqkv, n, SB_EPI_ROPE) ? 0 : 1) +
                       (norm_in_gemv(b, &l0->wgu, n, SB_EPI_SILU) ? 0 : 1);
     const int per_layer =
         norms /* rmsnorm */ + 2 /* attention */ + qkv +
@@ -897,9 +900,11 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
         b->d_io = (int32_t*)dalloc(b, (size_t)3 * B * 4);
         b->status = (int32_t*)dalloc(b, 16);
         b->tc_err = (int*)dalloc(b, 16);        /* pipeline-wait timeouts of any kernel */
+        b->head_cnt = (int*)dalloc(b, (size_t)(b->nq + 2 * b->nkv) * 4);
         if (!b->x || !b->xn || !b->att || !b->qkv || !b->h || !b->logits || !b->scratch ||
-            !b->row_pos || !b->row_slot || !b->d_io || !b->status || !b->tc_err ||
-            sb_cuda_check(cudaMemset(b->tc_err, 0, 16), "memset"))
+            !b->row_pos || !b->row_slot || !b->d_io || !b->status || !b->tc_err || !b->head_cnt ||
+            sb_cuda_check(cudaMemset(b->tc_err, 0, 16), "memset") ||
+            sb_cuda_check(cudaMemset(b->head_cnt, 0, (size_t)(b->nq + 2 * b->nkv) * 4), "memset"))
             goto fail;
         /* zero padding columns are part of the GEMM contract */
         if (sb_cuda_check(cudaMemset(b->x, 0, (size_t)B * b->ld_x * 4), "memset") ||
@@ -1228,8 +1233,10 @@ static int status_readback(slate_llama_batch_t* b) {
 static int status_code(slate_llama_batch_t* b) {
     const int32_t* h = b->h_io + 3 * b->max_batch;
     if (h[1]) {
-        /* a step that gave up may leave stream-K tile counters raised */
+        /* a step that gave up may leave stream-K tile counters and the
+         * GEMV's per-head counters raised */
         if (b->q4_cnt) cudaMemset(b->q4_cnt, 0, b->q4_cnt_n * 4);
+        if (b->head_cnt) cudaMemset(b->head_cnt, 0, (size_t)(b->nq + 2 * b->nkv) * 4);
         sb_set_error("tensor-core GEMM pipeline wait timed out (stage %d)", h[1]);
         return -5;
     }

@@ -69,7 +69,9 @@ typedef struct sb_matrix {
  * M_pad % 128 == 0, on the CUDA cores (store / residual add / SiLU(gate)*up of
  * the interleaved gate|up weight), the weights streamed through shared memory
  * by bulk copies.  norm_w != NULL: X rows are RMSNorm-ed (weight norm_w[K],
- * eps) as they are staged.  sb_gv_prepare() reads the SM count and opts the
+ * eps) as they are staged.  SB_EPI_ROPE (the fused Q|K|V weight): Y stored,
+ * then each head rotated / appended to the pool by the CTA that completes it
+ * (head_cnt: nq + 2 nkv zeroed ints, left zeroed).  sb_gv_prepare() reads the SM count and opts the
  * kernels into their shared memory (per device, outside stream capture); a
  * ring wait that times out sets *err. */
 #define SB_GV_MAX_ROWS 2
@@ -77,7 +79,8 @@ typedef struct sb_matrix {
 void sb_gv_prepare(void);
 int sb_gv_supported(const sb_matrix* W, int n, int epi);
 int sb_gv_gemm(const sb_matrix* W, const float* X, int ldx, int n, float* Y, int ldy, int epi,
-               const float* norm_w, float eps, int* err, cudaStream_t st);
+               const float* norm_w, float eps, const sb_rope_args* rope, int* head_cnt, int* err,
+               cudaStream_t st);
 
 /* Small batches (gemm_mv.cu): Q4_K weights, 1..SB_MV_MAX_ROWS activation
  * rows, tensor cores through mma.sync, weights streamed once.  ws holds
