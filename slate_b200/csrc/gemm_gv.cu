@@ -57,6 +57,7 @@ constexpr int NG = 2;                      // consumer groups
 constexpr int NCONS = 32 * CW * NG;        // consumer threads
 constexpr int NTHREADS = NCONS + 32;       // + the producer warp
 constexpr int MAX_NS = 12;
+constexpr int STATIC_SMEM = 1024;          // bound on the kernel's static shared memory
 constexpr uint64_t WAIT_NS = 2000000000ull;
 
 struct GvArgs {
@@ -501,6 +502,7 @@ extern "C" void sb_gv_prepare(void) {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&g_smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    g_smem_max -= STATIC_SMEM;          // the kernel's static shared memory comes on top
     const int smem = g_smem_max;
     cudaFuncSetAttribute(gv_kernel<1, SB_EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaFuncSetAttribute(gv_kernel<1, SB_EPI_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
