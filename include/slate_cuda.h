@@ -159,7 +159,7 @@ int slate_cuda_sample_rows(int32_t* out_tokens, const float* logits, int ld, int
  * Its scratch is one fixed device array per device of
  * SLATE_CUDA_NOALLOC_SCRATCH_FLOATS floats (8 MiB); a call needs
  * B * nq * ceil(max_pages * 16 / ct) * (hd + 2) of them, ct being the engine's
- * attention chunk for B rows (128 tokens below 4 rows up to 1024 from 16),
+ * attention chunk for B rows (64 tokens below 3 rows, 128 at 3, up to 1024 from 16),
  * doubled up to 1024 tokens until the partials fit, and is rejected with -1
  * when even 1024-token chunks do not fit.  All calls on a device share the
  * array, so calls that overlap on the GPU race: serialise them.  The first

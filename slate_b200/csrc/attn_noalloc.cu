@@ -11,7 +11,7 @@
 // Scratch: SLATE_CUDA_NOALLOC_SCRATCH_FLOATS floats of partial records plus
 // one error word.  A call needs B * n_heads * ceil(max_pages * 16 / ct) *
 // (head_dim + 2) floats, ct being the engine's attention chunk for B rows
-// (sb_attention_chunk_tokens: 128 tokens below 4 rows up to 1024 from 16),
+// (sb_attention_chunk_tokens: 64 tokens below 3 rows, 128 at 3, up to 1024 from 16),
 // doubled up to 1024 tokens until the partials fit; a request that does not
 // fit even with 1024-token chunks is rejected with -1 and a message before
 // any device work.  Every call on a device shares the one

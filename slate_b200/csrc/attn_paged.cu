@@ -410,7 +410,8 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     }
 }
 
-// Merge chunk partials: out = Σ_c o_c e^{m_c-M} / Σ_c l_c e^{m_c-M}.  With
+// Merge chunk partials: out = Σ_c o_c e^{m_c-M} / Σ_c l_c e^{m_c-M}, one warp
+// per (row, query head), the chunks' maxima and sums spread over its lanes.  With
 // hi != null the rows are also written as the f16 pair hi = f16(out), lo =
 // f16(out - hi) (row stride ld16) that the next tensor-core GEMM takes.
 template <int HD>
@@ -430,21 +431,46 @@ __global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ pa
     if (pos < 0) return;
     const int nch = (pos + ct) / ct;                      // ceil((pos + 1) / ct)
     const float* rec0 = part + ((size_t)b * nq + hq) * nchunk_max * (HD + 2);
+    // the chunks' maxima and weighted sums, spread over the lanes
     float M = -INFINITY;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, rec0[(size_t)c * (HD + 2)]);
+    for (int c = lane; c < nch; c += 32) M = fmaxf(M, rec0[(size_t)c * (HD + 2)]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     double L = 0.0;
-    for (int c = 0; c < nch; ++c) {
+    for (int c = lane; c < nch; c += 32) {
         const float* r = rec0 + (size_t)c * (HD + 2);
         L += (double)r[1] * (double)expf(r[0] - M);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
     const float invL = (float)(1.0 / L);
-    for (int d = lane; d < HD; d += 32) {
-        float acc = 0.f;
-        for (int c = 0; c < nch; ++c) {
-            const float* r = rec0 + (size_t)c * (HD + 2);
-            acc = fmaf(r[2 + d], expf(r[0] - M), acc);
+    // out[d] = sum_c o_c[d] e^{m_c - M}, chunks in order: lane c0 + j holds
+    // chunk c0 + j's weight, broadcast to the warp; the loads of successive
+    // chunks are independent of one another
+    constexpr int DPL = (HD + 31) / 32;
+    float acc[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+        const int cl = c0 + lane;
+        const float wl = cl < nch ? expf(rec0[(size_t)cl * (HD + 2)] - M) : 0.f;
+        const int cn = min(32, nch - c0);
+#pragma unroll 8
+        for (int j = 0; j < cn; ++j) {
+            const float wj = __shfl_sync(0xffffffffu, wl, j);
+            const float* r = rec0 + (size_t)(c0 + j) * (HD + 2) + 2;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) {
+                const int d = lane + 32 * i;
+                if (d < HD) acc[i] = fmaf(r[d], wj, acc[i]);
+            }
         }
-        const float o = acc * invL;
+    }
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+        const int d = lane + 32 * i;
+        if (d >= HD) break;
+        const float o = acc[i] * invL;
         att[(size_t)b * ld_att + (size_t)hq * HD + d] = o;
         if (hi) {
             const __half h = __float2half_rn(o);
@@ -576,7 +602,7 @@ int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
 
 extern "C" int sb_attention_chunk_tokens(int B) {
     return B >= 16 ? SB_ATTN_CHUNK : B >= 8 ? SB_ATTN_CHUNK / 2 : B >= 4 ? SB_ATTN_CHUNK / 4
-                                                                       : SB_ATTN_CHUNK / 8;
+                                   : B >= 3 ? SB_ATTN_CHUNK / 8 : SB_ATTN_CHUNK / 16;
 }
 
 extern "C" size_t sb_attention_scratch_rows(int B, int nq, int hd, int max_seq, int ct) {

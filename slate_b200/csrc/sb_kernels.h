@@ -156,8 +156,8 @@ int sb_rope_append(float* qkv, int ld, int B, int nq, int nkv, int hd, const int
  * faster per layer than 512, fewer per-CTA starts and partials, with ~10K
  * CTAs in flight; 4096 lost parallelism; at 16 rows 256-token chunks, 2.6
  * waves of CTAs, were slower than 1024), halving per halving of the rows down
- * to 128 tokens below 4 rows, so that a few sequences still fill about one
- * wave of CTAs.  sb_attention_scratch_rows() is the scratch of B rows at chunk ct;
+ * to 128 tokens at 3 rows and 64 below, so that a few sequences still fill
+ * one or more waves of CTAs whose pages are all in flight at once.  sb_attention_scratch_rows() is the scratch of B rows at chunk ct;
  * sb_attention_scratch_floats(max_batch) covers every B <= max_batch at its
  * own chunk (and any B <= max_batch at a longer chunk). */
 #define SB_ATTN_CHUNK 1024
