@@ -410,73 +410,62 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     }
 }
 
-// Merge chunk partials: out = Σ_c o_c e^{m_c-M} / Σ_c l_c e^{m_c-M}, one warp
-// per (row, query head), the chunks' maxima and sums spread over its lanes.  With
-// hi != null the rows are also written as the f16 pair hi = f16(out), lo =
-// f16(out - hi) (row stride ld16) that the next tensor-core GEMM takes.
+// Merge chunk partials: out = Σ_c o_c e^{m_c-M} / Σ_c l_c e^{m_c-M}, one CTA
+// per (row, query head): warp 0 forms the chunk weights e^{m_c-M} / L (the
+// chunks spread over its lanes), then thread d sums dim d over the chunks in
+// chunk order with independent loads.  With hi != null the rows are also
+// written as the f16 pair hi = f16(out), lo = f16(out - hi) (row stride ld16)
+// that the next tensor-core GEMM takes.
+constexpr int COMBINE_T = 128;            // threads per CTA: head_dim <= 128
+constexpr int COMBINE_MAXCH = 12288;      // chunk weights in the default 48 KB of shared memory
 template <int HD>
-__global__ void __launch_bounds__(128) attn_combine(const float* __restrict__ part, int B, int nq,
-                                                    const int32_t* __restrict__ row_pos,
-                                                    int nchunk_max, int ct, float* __restrict__ att,
-                                                    int ld_att, __half* __restrict__ hi,
-                                                    __half* __restrict__ lo, int ld16) {
+__global__ void __launch_bounds__(COMBINE_T) attn_combine(const float* __restrict__ part, int B, int nq,
+                                                          const int32_t* __restrict__ row_pos,
+                                                          int nchunk_max, int ct,
+                                                          float* __restrict__ att, int ld_att,
+                                                          __half* __restrict__ hi,
+                                                          __half* __restrict__ lo, int ld16) {
     sb_grid_release();   // the Wo GEMM may start its set-up
     sb_grid_wait();      // chunk partials: after the previous kernel (sb_pdl.h)
-    const int lane = threadIdx.x & 31;
-    const long w = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
-    const int hq = (int)(w % nq);
-    const int b = (int)(w / nq);
+    extern __shared__ float wch[];        // [nchunk_max] chunk weights
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int hq = (int)(blockIdx.x % nq);
+    const int b = (int)(blockIdx.x / nq);
     if (b >= B) return;
     const int pos = row_pos[b];
     if (pos < 0) return;
-    const int nch = (pos + ct) / ct;                      // ceil((pos + 1) / ct)
+    const int nch = min((pos + ct) / ct, nchunk_max);    // ceil((pos + 1) / ct)
     const float* rec0 = part + ((size_t)b * nq + hq) * nchunk_max * (HD + 2);
-    // the chunks' maxima and weighted sums, spread over the lanes
-    float M = -INFINITY;
-    for (int c = lane; c < nch; c += 32) M = fmaxf(M, rec0[(size_t)c * (HD + 2)]);
+    if (tid < 32) {
+        float M = -INFINITY;
+        for (int c = lane; c < nch; c += 32) M = fmaxf(M, rec0[(size_t)c * (HD + 2)]);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    double L = 0.0;
-    for (int c = lane; c < nch; c += 32) {
-        const float* r = rec0 + (size_t)c * (HD + 2);
-        L += (double)r[1] * (double)expf(r[0] - M);
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        double L = 0.0;
+        for (int c = lane; c < nch; c += 32) {
+            const float* r = rec0 + (size_t)c * (HD + 2);
+            const float e = expf(r[0] - M);
+            wch[c] = e;
+            L += (double)r[1] * (double)e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float invL = (float)(1.0 / L);
+        __syncwarp();
+        for (int c = lane; c < nch; c += 32) wch[c] *= invL;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    const float invL = (float)(1.0 / L);
-    // out[d] = sum_c o_c[d] e^{m_c - M}, chunks in order: lane c0 + j holds
-    // chunk c0 + j's weight, broadcast to the warp; the loads of successive
-    // chunks are independent of one another
-    constexpr int DPL = (HD + 31) / 32;
-    float acc[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-    for (int c0 = 0; c0 < nch; c0 += 32) {
-        const int cl = c0 + lane;
-        const float wl = cl < nch ? expf(rec0[(size_t)cl * (HD + 2)] - M) : 0.f;
-        const int cn = min(32, nch - c0);
+    __syncthreads();
+    const int d = tid;
+    if (d >= HD) return;
+    float acc = 0.f;
+    const float* r = rec0 + 2 + d;
 #pragma unroll 8
-        for (int j = 0; j < cn; ++j) {
-            const float wj = __shfl_sync(0xffffffffu, wl, j);
-            const float* r = rec0 + (size_t)(c0 + j) * (HD + 2) + 2;
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) {
-                const int d = lane + 32 * i;
-                if (d < HD) acc[i] = fmaf(r[d], wj, acc[i]);
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-        const int d = lane + 32 * i;
-        if (d >= HD) break;
-        const float o = acc[i] * invL;
-        att[(size_t)b * ld_att + (size_t)hq * HD + d] = o;
-        if (hi) {
-            const __half h = __float2half_rn(o);
-            hi[(size_t)b * ld16 + (size_t)hq * HD + d] = h;
-            if (lo) lo[(size_t)b * ld16 + (size_t)hq * HD + d] = __float2half_rn(o - __half2float(h));
-        }
+    for (int c = 0; c < nch; ++c) acc = fmaf(r[(size_t)c * (HD + 2)], wch[c], acc);
+    att[(size_t)b * ld_att + (size_t)hq * HD + d] = acc;
+    if (hi) {
+        const __half h = __float2half_rn(acc);
+        hi[(size_t)b * ld16 + (size_t)hq * HD + d] = h;
+        if (lo) lo[(size_t)b * ld16 + (size_t)hq * HD + d] = __float2half_rn(acc - __half2float(h));
     }
 }
 
@@ -508,7 +497,7 @@ int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
                       (const KT*)pool, n_pages, layer, nchunk, ct, scratch, err) != cudaSuccess)
         return -1;
     const long cw = (long)B * nq;
-    return sb_launch_pdl(attn_combine<HD>, dim3((unsigned)((cw + 3) / 4)), dim3(128), 0, st,
+    return sb_launch_pdl(attn_combine<HD>, dim3((unsigned)cw), dim3(COMBINE_T), (size_t)nchunk * 4, st,
                          (const float*)scratch, B, nq, row_pos, nchunk, ct, att, ld_att, hl.hi,
                          hl.lo, hl.ld16) == cudaSuccess
                ? 0
@@ -551,15 +540,15 @@ int launch_kt(int prepare, int hd, int G, float* att, int ld_att, const float* q
 
 int combine(int hd, const float* scratch, int B, int nq, const int32_t* row_pos, int nchunk,
             int ct, float* att, int ld_att, HiLo hl, cudaStream_t st) {
-    const unsigned grid = (unsigned)(((long)B * nq + 3) / 4);
+    const unsigned grid = (unsigned)((long)B * nq);
     switch (hd) {
         case 64:
-            return sb_launch_pdl(attn_combine<64>, dim3(grid), dim3(128), 0, st, scratch, B, nq,
+            return sb_launch_pdl(attn_combine<64>, dim3(grid), dim3(COMBINE_T), (size_t)nchunk * 4, st, scratch, B, nq,
                                  row_pos, nchunk, ct, att, ld_att, hl.hi, hl.lo, hl.ld16) == cudaSuccess
                        ? 0
                        : -1;
         case 128:
-            return sb_launch_pdl(attn_combine<128>, dim3(grid), dim3(128), 0, st, scratch, B, nq,
+            return sb_launch_pdl(attn_combine<128>, dim3(grid), dim3(COMBINE_T), (size_t)nchunk * 4, st, scratch, B, nq,
                                  row_pos, nchunk, ct, att, ld_att, hl.hi, hl.lo, hl.ld16) == cudaSuccess
                        ? 0
                        : -1;
@@ -577,6 +566,7 @@ int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
     if (ct <= 0) ct = sb_attention_chunk_tokens(B);
     if (ct < 16 || ct > SB_ATTN_CHUNK || ct % 16) return -1;
     const int nchunk = (max_seq + ct - 1) / ct;
+    if (nchunk > COMBINE_MAXCH) return -1;
     if (sb_attention_mma_supported(nq, nkv, hd, kv_dtype)) {
         if (prepare) {
             const int rc = sb_attention_mma(1, nullptr, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr,
