@@ -20,6 +20,10 @@ TP_MODELS = {
     # hd 64, 8 heads / 4 kv heads -> 4 / 2 per rank, ffn 512 per rank
     "small": dict(n_layers=2, d_model=512, ffn_hidden=1024, n_heads=8, n_kv_heads=4,
                   vocab=1000, max_seq=256, seed=31),
+    # 4 ranks need (n_heads / 4) * hd to be whole super-blocks: hd 64, 16 heads /
+    # 4 kv heads -> 4 / 1 per rank, ffn 256 per rank
+    "small4": dict(n_layers=2, d_model=1024, ffn_hidden=1024, n_heads=16, n_kv_heads=4,
+                   vocab=1000, max_seq=256, seed=33),
     # 8B head geometry (hd 128, 32 / 8 heads -> 16 / 4 per rank, group 4), 2 layers
     "8b_heads": dict(n_layers=2, d_model=4096, ffn_hidden=14336, n_heads=32, n_kv_heads=8,
                      vocab=4096, max_seq=512, theta_base=500000.0, seed=32),
@@ -87,8 +91,8 @@ def run_tp(path, feed, kv_dtype, tp=2, timeout=600):
 
 @pytest.mark.parametrize("name,kv_dtype,tol,tp", [
     ("small", 0, 1e-4, 2), ("small", 1, 2e-3, 2), ("8b_heads", 1, 2e-3, 2),
-    # 4 ranks: one kv head per rank (small), two (8B head geometry, group 4 kept whole)
-    ("small", 0, 1e-4, 4), ("8b_heads", 0, 1e-4, 4)])
+    # 4 ranks: one kv head per rank (small4), two (8B head geometry, group 4 kept whole)
+    ("small4", 0, 1e-4, 4), ("small4", 1, 2e-3, 4), ("8b_heads", 0, 1e-4, 4)])
 def test_tp_matches_oracle(sb, oracle, workdir, name, kv_dtype, tol, tp):
     if _gpu_count() < tp:
         pytest.skip(f"tensor parallelism over {tp} ranks needs {tp} GPUs")
