@@ -493,6 +493,14 @@ void geometry(int K, int& wpr, int& rs, int& ch, int& stage_bytes) {
     stage_bytes = rs * nb * 144;
 }
 
+template <int NR>
+void set_smem(int smem) {
+    cudaFuncSetAttribute(gv_kernel<NR, SB_EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(gv_kernel<NR, SB_EPI_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(gv_kernel<NR, SB_EPI_SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(gv_kernel<NR, SB_EPI_ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
 }  // namespace
 
 // SM count and the shared-memory opt-in of every instantiation (per device,
@@ -504,14 +512,10 @@ extern "C" void sb_gv_prepare(void) {
     cudaDeviceGetAttribute(&g_smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     g_smem_max -= STATIC_SMEM;          // the kernel's static shared memory comes on top
     const int smem = g_smem_max;
-    cudaFuncSetAttribute(gv_kernel<1, SB_EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(gv_kernel<1, SB_EPI_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(gv_kernel<1, SB_EPI_SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(gv_kernel<2, SB_EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(gv_kernel<2, SB_EPI_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(gv_kernel<2, SB_EPI_SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(gv_kernel<1, SB_EPI_ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(gv_kernel<2, SB_EPI_ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    set_smem<1>(smem);
+    set_smem<2>(smem);
+    set_smem<3>(smem);
+    set_smem<4>(smem);
 }
 
 // The ring depth that fits beside x for (n, K, M), 0 if fewer than 3 stages fit.
@@ -571,5 +575,11 @@ extern "C" int sb_gv_gemm(const sb_matrix* W, const float* X, int ldx, int n, fl
     size_t smem = 0;
     a.NS = gv_ring(n, a.K, a.M, epi, &smem, &a.n_stages, &a.max_local);
     if (a.NS <= 0) return -1;
-    return n == 1 ? dispatch<1>(a, smem, epi, st) : dispatch<2>(a, smem, epi, st);
+    switch (n) {
+        case 1: return dispatch<1>(a, smem, epi, st);
+        case 2: return dispatch<2>(a, smem, epi, st);
+        case 3: return dispatch<3>(a, smem, epi, st);
+        case 4: return dispatch<4>(a, smem, epi, st);
+    }
+    return -1;
 }

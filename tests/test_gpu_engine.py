@@ -368,7 +368,7 @@ def test_scheduler_batches_concurrent_callers(sb, oracle, workdir):
     m.close()
 
 
-@pytest.mark.parametrize("n_rows", [1, 2, 40, 150])
+@pytest.mark.parametrize("n_rows", [1, 2, 3, 40, 150])
 def test_gemm_paths_agree_with_oracle(sb, oracle, workdir, n_rows):
     """The GEMM paths of the engine -- the default (0: the 3-pass split, on the
     stream-K kernel from 128 rows), the tile-per-CTA 3-pass kernel (3), the
