@@ -514,8 +514,6 @@ extern "C" void sb_gv_prepare(void) {
     const int smem = g_smem_max;
     set_smem<1>(smem);
     set_smem<2>(smem);
-    set_smem<3>(smem);
-    set_smem<4>(smem);
 }
 
 // The ring depth that fits beside x for (n, K, M), 0 if fewer than 3 stages fit.
@@ -578,8 +576,6 @@ extern "C" int sb_gv_gemm(const sb_matrix* W, const float* X, int ldx, int n, fl
     switch (n) {
         case 1: return dispatch<1>(a, smem, epi, st);
         case 2: return dispatch<2>(a, smem, epi, st);
-        case 3: return dispatch<3>(a, smem, epi, st);
-        case 4: return dispatch<4>(a, smem, epi, st);
     }
     return -1;
 }

@@ -65,7 +65,7 @@ typedef struct sb_matrix {
 /* Y[n][·] (epi) X[n][0..K) · W[m][0..K)  for n < B.
  * X row stride ldx (floats); for f32 weights X must be zero in [K, ldw).
  * path: 0 = auto (GEMV for B <= 8, tiled otherwise), 1 = tiled only. */
-/* One to four activation rows (gemm_gv.cu): Q4_K weights with K <= SB_GV_MAX_K,
+/* One or two activation rows (gemm_gv.cu): Q4_K weights with K <= SB_GV_MAX_K,
  * M_pad % 128 == 0, on the CUDA cores (store / residual add / SiLU(gate)*up of
  * the interleaved gate|up weight), the weights streamed through shared memory
  * by bulk copies.  norm_w != NULL: X rows are RMSNorm-ed (weight norm_w[K],
@@ -74,7 +74,7 @@ typedef struct sb_matrix {
  * (head_cnt: nq + 2 nkv zeroed ints, left zeroed).  sb_gv_prepare() reads the SM count and opts the
  * kernels into their shared memory (per device, outside stream capture); a
  * ring wait that times out sets *err. */
-#define SB_GV_MAX_ROWS 4
+#define SB_GV_MAX_ROWS 2
 #define SB_GV_MAX_K 16384
 void sb_gv_prepare(void);
 int sb_gv_supported(const sb_matrix* W, int n, int epi);
