@@ -246,13 +246,15 @@ typedef struct slate_cuda_opts {
      * 32g + e holds element e of sub-block 2g low and of 2g + 1 high), repacked
      * to Slate's at upload, so real llama.cpp Q4_K files decode as intended. */
     int q4k_order;
-    /* 0 or 1: the whole batch as one chain of kernels.  2 (one GPU, stream-K
+    /* 0 or 1: the whole batch as one chain of kernels.  2 (stream-K
      * tensor-core GEMMs, max_batch >= 32): a decode step of more than
      * max_batch / 2 rows runs its layers as two independent halves of the
      * batch on two streams, the halves' attentions taking turns, so that one
      * half's attention (bound by HBM) can run beside the other half's
-     * projections (bound by the tensor cores).  Prompt-chunk steps always run
-     * as one chain. */
+     * projections (bound by the tensor cores).  With tensor parallelism each
+     * half's all-reduces use their own communicator (split from the group's at
+     * creation, a collective), so one half's all-reduce runs beside the other
+     * half's GEMMs.  Prompt-chunk steps always run as one chain. */
     int lanes;
 } slate_cuda_opts_t;
 

@@ -48,6 +48,7 @@ typedef struct sb_lane {
     float* mv_ws;                  /* small-batch GEMM partials and counters */
     int* mv_cnt;
     int r0;                        /* first row */
+    void* comm;                    /* NCCL communicator of this lane's all-reduces (tp > 1) */
     int xn_split, att_split;       /* enqueue time: the RMSNorm / attention wrote
                                       the f16 operand of the GEMM that follows */
 } sb_lane;
@@ -122,6 +123,7 @@ struct slate_llama_batch {
      * vocabulary of which the LM head holds rows [v0, v0 + V_l) */
     int tp, rank, V_l, v0, Dq;     /* Dq = nq * hd (local) */
     void* comm;                    /* NCCL communicator (tp > 1) */
+    void* comm2;                   /* the second lane's (split from comm; two lanes, tp > 1) */
     void *pairs, *pairs_all;       /* per-row (max, index) of this rank / of all ranks */
     float* logits_all;             /* [tp][max_batch][ld_logits], gathered on request */
     /* stochastic sampling (allocated on first use): per-row configs and RNG
@@ -496,7 +498,7 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
                                      s);
     } else {
         rc |= step_gemm(b, L, &ly->wo, att, b->ld_att, IN_ATT, n, x, b->ld_x, res_epi, b->sp_wo, s);
-        if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, x, (size_t)n * b->ld_x, s);
+        if (b->tp > 1) rc |= sb_tp_allreduce_sum(L->comm, x, (size_t)n * b->ld_x, s);
         if (norm_in_gemv(b, &ly->wgu, n, SB_EPI_SILU)) {
             /* RMSNorm in the GEMV's staging of x */
             L->xn_split = 0;
@@ -508,7 +510,7 @@ static int enqueue_part(slate_llama_batch_t* b, sb_lane* L, int l, int part, int
                             s);
         }
         rc |= step_gemm(b, L, &ly->wdown, h, b->ld_h, IN_H, n, x, b->ld_x, res_epi, b->sp_dn, s);
-        if (b->tp > 1) rc |= sb_tp_allreduce_sum(b->comm, x, (size_t)n * b->ld_x, s);
+        if (b->tp > 1) rc |= sb_tp_allreduce_sum(L->comm, x, (size_t)n * b->ld_x, s);
     }
     return rc;
 }
@@ -709,6 +711,7 @@ void slate_llama_batch_free(slate_llama_batch_t* b) {
     if (b->h_samp) cudaFreeHost(b->h_samp);
     if (b->h_rng) cudaFreeHost(b->h_rng);
     sb_tc_free_weight(&b->head_tc);
+    if (b->comm2) sb_tp_destroy(b->comm2);
     if (b->comm) sb_tp_destroy(b->comm);      /* after the graphs that hold its collectives */
     for (int i = 0; i < b->n_allocs; ++i) cudaFree(b->allocs[i]);
     free(b->allocs);
@@ -1024,8 +1027,14 @@ slate_llama_batch_t* slate_llama_batch_new_desc(const slate_llama_desc_t* m,
     b->full.op_a = &b->op_a;
     b->full.sk_ws = b->sk_ws;
     b->full.r0 = 0;
+    b->full.comm = b->comm;
     b->half_rows = b->max_batch / 2;
-    if (b->sk_on && b->tp == 1 && !b->q4_on && o->lanes == 2 && b->half_rows >= SB_TC_MIN_ROWS) {
+    if (b->sk_on && !b->q4_on && o->lanes == 2 && b->half_rows >= SB_TC_MIN_ROWS) {
+        /* tensor parallel: the second lane's all-reduces go through their own
+         * communicator on the second stream, beside the first lane's work */
+        if (b->tp > 1 && sb_tp_split(b->comm, b->rank, &b->comm2)) goto fail;
+        b->half[0].comm = b->comm;
+        b->half[1].comm = b->tp > 1 ? b->comm2 : NULL;
         const sb_tc_operand* fo[3] = {&b->op_d, &b->op_f, &b->op_a};
         for (int hh = 0; hh < 2; ++hh) {
             sb_lane* L = &b->half[hh];

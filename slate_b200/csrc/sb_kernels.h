@@ -227,6 +227,7 @@ int sb_tp_epilogue(const void* all_pairs, int T, int B, const int32_t* row_slot,
                    int32_t* out_tokens, cudaStream_t st);
 /* NCCL communicator of a tensor-parallel group (tp_nccl.c). */
 int sb_tp_init(void** comm, int nranks, int rank, const void* unique_id);
+int sb_tp_split(void* comm, int rank, void** out);
 void sb_tp_destroy(void* comm);
 int sb_tp_allreduce_sum(void* comm, float* buf, size_t n, cudaStream_t st);
 int sb_tp_allgather(void* comm, const void* send, void* recv, size_t bytes, cudaStream_t st);

@@ -28,6 +28,7 @@ static struct {
     ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
                                cudaStream_t);
     const char* (*error_string)(ncclResult_t);
+    ncclResult_t (*comm_split)(ncclComm_t, int, int, ncclComm_t*, ncclConfig_t*);   /* optional */
 } g_nccl;
 static pthread_once_t g_once = PTHREAD_ONCE_INIT;
 
@@ -41,6 +42,7 @@ static void nccl_open(void) {
     g_nccl.all_reduce = dlsym(h, "ncclAllReduce");
     g_nccl.all_gather = dlsym(h, "ncclAllGather");
     g_nccl.error_string = dlsym(h, "ncclGetErrorString");
+    g_nccl.comm_split = dlsym(h, "ncclCommSplit");
     g_nccl.ok = g_nccl.get_unique_id && g_nccl.comm_init_rank && g_nccl.comm_destroy &&
                 g_nccl.all_reduce && g_nccl.all_gather && g_nccl.error_string;
 }
@@ -76,6 +78,22 @@ int sb_tp_init(void** comm, int nranks, int rank, const void* id) {
     ncclComm_t c = NULL;
     int rc = nccl_check(g_nccl.comm_init_rank(&c, nranks, u, rank), "ncclCommInitRank");
     *comm = rc ? NULL : (void*)c;
+    return rc;
+}
+
+/* A second communicator over the same ranks (ncclCommSplit with one color, a
+ * collective: every rank calls it), for collectives issued on a second stream
+ * beside those of the first communicator. */
+int sb_tp_split(void* comm, int rank, void** out) {
+    *out = NULL;
+    if (!have_nccl()) return -5;
+    if (!g_nccl.comm_split) {
+        sb_set_error("ncclCommSplit not available in this NCCL: two lanes need it");
+        return -1;
+    }
+    ncclComm_t c = NULL;
+    int rc = nccl_check(g_nccl.comm_split((ncclComm_t)comm, 0, rank, &c, NULL), "ncclCommSplit");
+    *out = rc ? NULL : (void*)c;
     return rc;
 }
 

@@ -38,7 +38,7 @@ def _gpu_count():
         return 0
 
 
-def _rank_main(rank, tp, path, feed, kv_dtype, id_q, out_q):
+def _rank_main(rank, tp, path, feed, kv_dtype, id_q, out_q, lanes=1):
     """One TP rank: same calls on every rank; rank 0 reports logits and ids."""
     try:
         import slate_b200 as sb
@@ -50,7 +50,7 @@ def _rank_main(rank, tp, path, feed, kv_dtype, id_q, out_q):
             tp_id = id_q.get(timeout=120)
         n, T = feed.shape
         eng = sb.LlamaBatch(path, device=rank, max_batch=max(n, 2), kv_dtype=kv_dtype,
-                            tp_size=tp, tp_rank=rank, tp_id=tp_id)
+                            tp_size=tp, tp_rank=rank, tp_id=tp_id, lanes=lanes)
         slots = [eng.open() for _ in range(n)]
         logits, ids = [], []
         for t in range(T):
@@ -68,10 +68,10 @@ def _rank_main(rank, tp, path, feed, kv_dtype, id_q, out_q):
         out_q.put((rank, None, None, repr(e)))
 
 
-def run_tp(path, feed, kv_dtype, tp=2, timeout=600):
+def run_tp(path, feed, kv_dtype, tp=2, timeout=600, lanes=1):
     ctx = mp.get_context("spawn")
     id_q, out_q = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, tp, path, feed, kv_dtype, id_q, out_q))
+    procs = [ctx.Process(target=_rank_main, args=(r, tp, path, feed, kv_dtype, id_q, out_q, lanes))
              for r in range(tp)]
     for p in procs:
         p.start()
@@ -119,3 +119,35 @@ def test_tp_matches_oracle(sb, oracle, workdir, name, kv_dtype, tol, tp):
     # every rank picked the same greedy tokens
     for r in range(1, tp):
         assert np.array_equal(res[0][1], res[r][1])
+
+
+def test_tp_two_lanes_matches_oracle(sb, oracle, workdir):
+    """Two lanes under tensor parallelism (slate_cuda_opts_t.lanes = 2): the
+    batch's halves run on two streams and each half's all-reduces go through
+    its own communicator, split from the group's at creation.  72 rows (two
+    lanes of 36, stream-K GEMMs) on the small model at 2 ranks, f32 KV, against
+    the oracle at 1e-4 of scale."""
+    tp = 2
+    if _gpu_count() < tp:
+        pytest.skip(f"tensor parallelism over {tp} ranks needs {tp} GPUs")
+    mc = TP_MODELS["small"]
+    path = os.path.join(str(workdir), "tp_small.gguf")
+    if not os.path.exists(path):
+        sb.synth_gguf(path, q4k=True, **mc)
+    rng = np.random.default_rng(6)
+    n, T = 72, 8
+    feed = rng.integers(0, mc["vocab"], (n, T)).astype(np.int32)
+    res = run_tp(path, feed, 0, tp=tp, lanes=2)
+    m = oracle.open(path)
+    ref, _ = m.decode_many(feed)
+    m.close()
+    scale = np.abs(ref).max()
+    for r in range(tp):
+        lg, ids = res[r]
+        err = np.max(np.abs(lg - ref)) / scale
+        assert err <= 1e-4, (r, err)
+        for i in range(n):
+            for t in range(T):
+                ok, _ = greedy_agrees(int(ids[i, t]), ref[i, t], 1e-4 * scale)
+                assert ok, (r, i, t)
+    assert np.array_equal(res[0][1], res[1][1])
