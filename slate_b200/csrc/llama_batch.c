@@ -208,6 +208,16 @@ static int qkv_rope_fused(const slate_llama_batch_t* b, const sb_lane* L, int n)
            sb_sk_tiles(W->M_pad, n) <= sb_sk_tiles(b->layers[0].wgu.M_pad, n);
 }
 
+/* The lane's f16 operand for a GEMM input, chosen by what the input is (the
+ * RMSNorm output, the SwiGLU rows, the attention output) rather than by K:
+ * tensor-parallel shards can give two of them the same K (d_model = ffn / tp). */
+static const sb_tc_operand* lane_op(const sb_lane* L, int in, int K) {
+    if (in == IN_XN) return L->op_d;
+    if (in == IN_H) return L->op_f;
+    if (in == IN_ATT) return L->op_a;
+    return K == L->op_d->K ? L->op_d : K == L->op_f->K ? L->op_f : L->op_a;
+}
+
 /* One weight GEMM of the step on the path chosen for (weight, rows); X and Y
  * point at the lane's first row, in names the input (IN_*). */
 static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, const float* X,
@@ -229,14 +239,18 @@ static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, con
         sb_mv_gemm(W, X, ldx, n, Y, ldy, epi, L->mv_ws, L->mv_cnt, s) == 0)
         return 0;
     if (b->q4_on && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
-        const sb_q4_operand* op = W->K == b->q4_d.K ? &b->q4_d
+        const sb_q4_operand* op = in == IN_XN ? &b->q4_d : in == IN_H ? &b->q4_f
+                                  : in == IN_ATT ? &b->q4_a
+                                  : W->K == b->q4_d.K ? &b->q4_d
                                   : W->K == b->q4_f.K ? &b->q4_f : &b->q4_a;
+        if (op->K != W->K) return -1;
         int rc = sb_q4_split(X, ldx, n, op, s);
         return rc ? rc : sb_q4_gemm(W, op, n, Y, ldy, epi, b->q4_ws, b->q4_cnt, b->tc_err, s);
     }
-    const sb_tc_operand* op = W->K == L->op_d->K ? L->op_d : W->K == L->op_f->K ? L->op_f : L->op_a;
+    const sb_tc_operand* op = lane_op(L, in, W->K);
     const int pre = (have_d && op->hi == L->op_d->hi) || (have_a && op->hi == L->op_a->hi);
     if (uses_sk(b, L, W, n, epi)) {
+        if (op->K != W->K) return -1;
         /* the down GEMM's operand was written by the gate/up GEMM */
         int rc = (in == IN_H && b->sk_h) || pre ? 0 : sb_tc_split(X, ldx, n, op, s);
         const int fuse = epi == SB_EPI_SILU && b->sk_h;
@@ -244,6 +258,7 @@ static int step_gemm(slate_llama_batch_t* b, sb_lane* L, const sb_matrix* W, con
                                     fuse ? L->op_f->lo : NULL, L->op_f->ld16, NULL, b->tc_err, s);
     }
     if (b->tc_passes && W->wtype == SB_WT_Q4K && n >= SB_TC_MIN_ROWS && W->M_pad % 128 == 0) {
+        if (op->K != W->K) return -1;
         int rc = pre ? 0 : sb_tc_split(X, ldx, n, op, s);
         return rc ? rc : sb_tc_gemm(W, op, n, b->tc_passes, splits, b->tc_ws, Y, ldy, epi,
                                     b->tc_err, s);

@@ -121,12 +121,14 @@ def test_tp_matches_oracle(sb, oracle, workdir, name, kv_dtype, tol, tp):
         assert np.array_equal(res[0][1], res[r][1])
 
 
-def test_tp_two_lanes_matches_oracle(sb, oracle, workdir):
-    """Two lanes under tensor parallelism (slate_cuda_opts_t.lanes = 2): the
-    batch's halves run on two streams and each half's all-reduces go through
-    its own communicator, split from the group's at creation.  72 rows (two
-    lanes of 36, stream-K GEMMs) on the small model at 2 ranks, f32 KV, against
-    the oracle at 1e-4 of scale."""
+@pytest.mark.parametrize("n,lanes", [(140, 1), (72, 2)])
+def test_tp_stream_k_and_lanes_match_oracle(sb, oracle, workdir, n, lanes):
+    """Tensor parallelism at batch sizes that reach the stream-K GEMMs: 140 rows
+    in one chain, and two lanes (slate_cuda_opts_t.lanes = 2: the batch's halves
+    on two streams, each half's all-reduces through its own communicator, split
+    from the group's at creation) of 36 rows.  The small model at 2 ranks has
+    d_model = ffn / tp, so the GEMM operands must be picked by input, not by K.
+    f32 KV, against the oracle at 1e-4 of scale."""
     tp = 2
     if _gpu_count() < tp:
         pytest.skip(f"tensor parallelism over {tp} ranks needs {tp} GPUs")
@@ -135,9 +137,9 @@ def test_tp_two_lanes_matches_oracle(sb, oracle, workdir):
     if not os.path.exists(path):
         sb.synth_gguf(path, q4k=True, **mc)
     rng = np.random.default_rng(6)
-    n, T = 72, 8
+    T = 8
     feed = rng.integers(0, mc["vocab"], (n, T)).astype(np.int32)
-    res = run_tp(path, feed, 0, tp=tp, lanes=2)
+    res = run_tp(path, feed, 0, tp=tp, lanes=lanes)
     m = oracle.open(path)
     ref, _ = m.decode_many(feed)
     m.close()
