@@ -121,14 +121,16 @@ def test_tp_matches_oracle(sb, oracle, workdir, name, kv_dtype, tol, tp):
         assert np.array_equal(res[0][1], res[r][1])
 
 
-@pytest.mark.parametrize("n,lanes", [(140, 1), (72, 2)])
-def test_tp_stream_k_and_lanes_match_oracle(sb, oracle, workdir, n, lanes):
-    """Tensor parallelism at batch sizes that reach the stream-K GEMMs: 140 rows
-    in one chain, and two lanes (slate_cuda_opts_t.lanes = 2: the batch's halves
-    on two streams, each half's all-reduces through its own communicator, split
-    from the group's at creation) of 36 rows.  The small model at 2 ranks has
-    d_model = ffn / tp, so the GEMM operands must be picked by input, not by K.
-    f32 KV, against the oracle at 1e-4 of scale."""
+@pytest.mark.parametrize("n,lanes", [(2, 1), (140, 1), (72, 2)])
+def test_tp_batch_paths_match_oracle(sb, oracle, workdir, n, lanes):
+    """Tensor parallelism on each GEMM family: 2 rows (the GEMV, with the
+    RMSNorm in its staging and RoPE + KV append of the rank's heads in its
+    epilogue), 140 rows in one chain (stream-K), and two lanes
+    (slate_cuda_opts_t.lanes = 2: the batch's halves on two streams, each
+    half's all-reduces through its own communicator, split from the group's at
+    creation) of 36 rows.  The small model at 2 ranks has d_model = ffn / tp,
+    so the GEMM operands must be picked by input, not by K.  f32 KV, against the
+    oracle at 1e-4 of scale."""
     tp = 2
     if _gpu_count() < tp:
         pytest.skip(f"tensor parallelism over {tp} ranks needs {tp} GPUs")
