@@ -549,9 +549,9 @@ struct HiLo {
 
 // The merge of the chunk partials: a CTA per (row, query head) while there
 // are few such pairs (small batches, many chunks each), a warp per pair beyond
-// COMBINE_CTA_MAX of them (measured on B200 at the 8B shape, one chain of 20
-// steps: at 1 row 12.0 against 14.0 us per layer for chunk kernel + merge, at
-// 64 rows even, at 256 rows 0.711 against 0.708 ms).
+// COMBINE_CTA_MAX of them (chunk kernel + merge per layer on B200 at the 8B
+// shape, f32 KV: at 1 row 12.0 against 14.0 us, at 64 rows even, at 256 rows
+// 0.711 against 0.708 ms).
 #ifndef COMBINE_CTA_MAX
 #define COMBINE_CTA_MAX 2048
 #endif
