@@ -7,7 +7,7 @@
 //
 // One CTA per (row, kv_head, SB_ATTN_CHUNK-token chunk).  A producer warp streams the
 // chunk's pages with cp.async.bulk (TMA bulk copies, one for K and one for V,
-// completion on an mbarrier) into an 8-stage (f16) / 4-stage (f32) ring in
+// completion on an mbarrier) into a ring of ~64 KB (4-16 stages) in
 // shared memory.  Four consumer warps take pages round-robin; each handles
 // all G = n_heads / n_kv_heads query heads of the group, lane l holding
 // head_dim/32 consecutive dims, so every K/V byte crosses HBM once and shared
@@ -145,10 +145,13 @@ struct AttnShape {
     // STAGES a multiple of NW a stage always belongs to one warp, which waits
     // for its phases in order; otherwise a warp could wait two phases ahead of
     // another warp's pending use and the parity wait would alias.
-    static constexpr int STAGES = sizeof(KT) == 2 ? 8 : 4;
-    static_assert(STAGES % NW == 0, "each ring stage must belong to one consumer warp");
     static constexpr int HEAD_ELEMS = 16 * HD;
     static constexpr int HEAD_BYTES = HEAD_ELEMS * (int)sizeof(KT);
+    // about 64 KB of K/V in flight per CTA whatever the head size (8 KB pages
+    // of a 64-wide f32 head get 8 stages, 16 KB ones 4), a multiple of NW
+    static constexpr int STAGES_RAW = 65536 / (2 * HEAD_BYTES);
+    static constexpr int STAGES = STAGES_RAW >= 16 ? 16 : STAGES_RAW >= 8 ? 8 : 4;
+    static_assert(STAGES % NW == 0, "each ring stage must belong to one consumer warp");
     // scores are formed 8 tokens (half a page) at a time
     static constexpr int TOK = 8;
     static constexpr int NV = TOK * G;
