@@ -17,8 +17,12 @@
 // (running max / sum, expf, as the reference's max-subtracted softmax) and
 // accumulates p*V with probabilities broadcast through shared memory.  The
 // warps' (m, l, o) states are merged in the CTA, then across chunks by
-// attn_combine.  Waits are bounded (2 s); a timeout sets *err and the CTA
-// drains its copies before exiting.
+// attn_combine.  A prompt chunk (rows at consecutive positions of one
+// sequence, f32 K/V or any cache the tensor-core prefill kernel does not take)
+// runs the same kernel on tiles of four rows: each warp owns one row and reads
+// every page, so the chunk's K/V is streamed once per four rows.  Waits are
+// bounded (2 s); a timeout sets *err and the CTA drains its copies before
+// exiting.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -163,7 +167,12 @@ struct AttnShape {
     static constexpr size_t SMEM = RING > MERGE ? RING : MERGE;
 };
 
-template <int HD, int G, typename KT>
+// ROWS (prompt chunks): one CTA per (NW consecutive rows of one sequence,
+// kv_head, chunk).  Consumer warp w owns row b0 + w and every warp takes every
+// page of the chunk (the empty barrier counts NW arrivals), masking tokens past
+// its own row's position, so the chunk's K/V crosses HBM once for NW rows and
+// each warp writes its row's (m, l, o) partial without a CTA merge.
+template <int HD, int G, typename KT, bool ROWS>
 __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     const float* __restrict__ qkv, int ld_qkv, int B, int nq, int nkv,
     const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
@@ -183,22 +192,26 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     sb_grid_wait();      // q, positions, pages, the appended K/V: after the previous kernel (sb_pdl.h)
     // chunk-major order: every row's first chunk is scheduled first, and the
     // shorter (partial or empty) later chunks fill the last waves
-    const int chunk = blockIdx.x / (B * nkv);
-    const int rest = blockIdx.x % (B * nkv);
-    const int kvh = rest % nkv, b = rest / nkv;
-    if (b >= B) return;
-    const int pos = row_pos[b];
-    if (pos < 0) return;
-    const int ctx = pos + 1, t0 = chunk * ct;
+    const int nunit = ROWS ? (B + NW - 1) / NW : B;   // rows, or tiles of NW rows
+    const int chunk = blockIdx.x / (nunit * nkv);
+    const int rest = blockIdx.x % (nunit * nkv);
+    const int kvh = rest % nkv, unit = rest / nkv;
+    if (unit >= nunit) return;
+    const int b0 = ROWS ? unit * NW : unit;
+    int ctx = 0;                                      // the longest context of the unit's rows
+#pragma unroll
+    for (int w = 0; w < (ROWS ? NW : 1); ++w)
+        if (b0 + w < B) ctx = max(ctx, row_pos[b0 + w] + 1);
+    const int t0 = chunk * ct;
     if (t0 >= ctx) return;
     const int t1 = min(ctx, t0 + ct);
     const int npg = (t1 - t0 + 15) / 16;
-    const int slot = row_slot[b];
+    const int slot = row_slot[b0];
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
             bar_init(&full[s], 1);
-            bar_init(&empty[s], 1);
+            bar_init(&empty[s], ROWS ? NW : 1);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -240,24 +253,35 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
         }
     } else {
         // ---------------- consumers ----------------
+        // this warp's row and the end of its context inside the chunk
+        const int b = ROWS ? b0 + warp : b0;
+        int r1 = t1;
+        if (ROWS) {
+            r1 = b < B ? min(row_pos[b] + 1, t1) : 0;
+            if (r1 > t0 && row_slot[b] != slot) {     // rows of another sequence: not a prompt chunk
+                atomicCAS(err, 0, 8);
+                r1 = 0;
+            }
+        }
+        const bool live = r1 > t0;
 #pragma unroll
         for (int h = 0; h < G; ++h) {
             const float* qp = qkv + (size_t)b * ld_qkv + (size_t)(kvh * G + h) * HD + d0;
 #pragma unroll
             for (int i = 0; i < DPL; ++i) {
-                q[h][i] = dl ? qp[i] : 0.f;
+                q[h][i] = dl && live ? qp[i] : 0.f;
                 o[h][i] = 0.f;
             }
             m[h] = -INFINITY;
             l[h] = 0.f;
         }
         const float scale = 1.0f / sqrtf((float)HD);
-        for (int i = warp; i < npg; i += NW) {
+        for (int i = ROWS ? 0 : warp; i < npg; i += ROWS ? 1 : NW) {
             const int s = i % STAGES;
             if (!bar_wait(&full[s], (i / STAGES) & 1, err, 7)) break;
             const KT* kp0 = ring + (size_t)s * 2 * S::HEAD_ELEMS + d0;
             const KT* vp0 = kp0 + S::HEAD_ELEMS;
-            const int nval_page = min(16, t1 - (t0 + 16 * i));
+            const int nval_page = min(16, r1 - (t0 + 16 * i));   // <= 0: past this row's position
 #pragma unroll 1
             for (int half = 0; half < 2; ++half) {
                 const int nval = nval_page - TOK * half;   // valid tokens in this half (may be <= 0)
@@ -376,6 +400,25 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
         }
     }
     __syncthreads();                                  // ring drained: reuse it for the merge
+    if constexpr (ROWS) {
+        // each row's partial straight from its warp (the combine drops chunks
+        // at or past a row's position, so a row without tokens here writes none)
+        if (warp < NW && b0 + warp < B && t0 <= row_pos[b0 + warp]) {
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                float* out = part + (((size_t)(b0 + warp) * nq + kvh * G + h) * nchunk_max + chunk) *
+                                        (HD + 2);
+                if (lane == 0) {
+                    out[0] = m[h];
+                    out[1] = l[h];
+                }
+                if (dl)
+#pragma unroll
+                    for (int c = 0; c < DPL; ++c) out[2 + d0 + c] = o[h][c];
+            }
+        }
+        return;
+    }
     if (warp < NW) {
 #pragma unroll
         for (int h = 0; h < G; ++h) {
@@ -404,7 +447,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
             L += rec[1] * f;
             O += rec[2 + d] * f;
         }
-        float* out = part + (((size_t)b * nq + kvh * G + h) * nchunk_max + chunk) * (HD + 2);
+        float* out = part + (((size_t)b0 * nq + kvh * G + h) * nchunk_max + chunk) * (HD + 2);
         if (d == 0) {
             out[0] = M;
             out[1] = L;
@@ -573,35 +616,36 @@ int launch_combine(const float* scratch, int B, int nq, const int32_t* row_pos, 
 }
 
 template <int HD, int G, typename KT>
-int launch_g(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
-             int nkv, const int32_t* row_pos, const int32_t* row_slot, const int32_t* page_table,
-             int max_pages, const void* pool, int64_t n_pages, int layer, int nchunk, int ct,
-             float* scratch, int* err, HiLo hl, cudaStream_t st) {
+int launch_g(int prepare, int rows, float* att, int ld_att, const float* qkv, int ld_qkv, int B,
+             int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
+             const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages, int layer,
+             int nchunk, int ct, float* scratch, int* err, HiLo hl, cudaStream_t st) {
     using S = AttnShape<HD, G, KT>;
     if (prepare) {
-        cudaFuncSetAttribute(attn_chunk<HD, G, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)S::SMEM);
-        cudaFuncSetAttribute(attn_chunk<HD, G, KT>,
-                             cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        for (auto f : {attn_chunk<HD, G, KT, false>, attn_chunk<HD, G, KT, true>}) {
+            cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
+            cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        }
         return 0;
     }
-    const long ctas = (long)B * nkv * nchunk;
-    if (sb_launch_pdl(attn_chunk<HD, G, KT>, dim3((unsigned)ctas), dim3(32 * (NW + 1)), S::SMEM, st,
-                      qkv, ld_qkv, B, nq, nkv, row_pos, row_slot, page_table, max_pages,
-                      (const KT*)pool, n_pages, layer, nchunk, ct, scratch, err) != cudaSuccess)
+    const long ctas = (long)(rows ? (B + NW - 1) / NW : B) * nkv * nchunk;
+    if (sb_launch_pdl(rows ? attn_chunk<HD, G, KT, true> : attn_chunk<HD, G, KT, false>,
+                      dim3((unsigned)ctas), dim3(32 * (NW + 1)), S::SMEM, st, qkv, ld_qkv, B, nq,
+                      nkv, row_pos, row_slot, page_table, max_pages, (const KT*)pool, n_pages,
+                      layer, nchunk, ct, scratch, err) != cudaSuccess)
         return -1;
     return launch_combine<HD>(scratch, B, nq, row_pos, nchunk, ct, att, ld_att, hl, st);
 }
 
 template <int HD, typename KT>
-int launch_hd(int prepare, int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B,
+int launch_hd(int prepare, int rows, int G, float* att, int ld_att, const float* qkv, int ld_qkv, int B,
               int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
               const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
               int layer, int nchunk, int ct, float* scratch, int* err, HiLo hl, cudaStream_t st) {
     switch (G) {
 #define CASE(g)                                                                                  \
     case g:                                                                                      \
-        return launch_g<HD, g, KT>(prepare, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
+        return launch_g<HD, g, KT>(prepare, rows, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
                                    row_slot, page_table, max_pages, pool, n_pages, layer,        \
                                    nchunk, ct, scratch, err, hl, st);
         CASE(1) CASE(2) CASE(4) CASE(8)
@@ -611,14 +655,14 @@ int launch_hd(int prepare, int G, float* att, int ld_att, const float* qkv, int 
 }
 
 template <typename KT>
-int launch_kt(int prepare, int hd, int G, float* att, int ld_att, const float* qkv, int ld_qkv,
+int launch_kt(int prepare, int rows, int hd, int G, float* att, int ld_att, const float* qkv, int ld_qkv,
               int B, int nq, int nkv, const int32_t* row_pos, const int32_t* row_slot,
               const int32_t* page_table, int max_pages, const void* pool, int64_t n_pages,
               int layer, int nchunk, int ct, float* scratch, int* err, HiLo hl, cudaStream_t st) {
     switch (hd) {
 #define CASE(h)                                                                                  \
     case h:                                                                                      \
-        return launch_hd<h, KT>(prepare, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
+        return launch_hd<h, KT>(prepare, rows, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,       \
                                 row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,   \
                                 ct, scratch, err, hl, st);
         CASE(8) CASE(16) CASE(32) CASE(64) CASE(128)
@@ -636,8 +680,8 @@ int combine(int hd, const float* scratch, int B, int nq, const int32_t* row_pos,
     return -1;
 }
 
-int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, int B, int nq,
-             int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
+int dispatch(int prepare, int rows, float* att, int ld_att, const float* qkv, int ld_qkv, int B,
+             int nq, int nkv, int hd, const int32_t* row_pos, const int32_t* row_slot,
              const int32_t* page_table, int max_pages, const void* pool, const void* kvmap,
              int64_t n_pages, int layer, int kv_dtype, int max_seq, int ct, float* scratch,
              int* err, HiLo hl, cudaStream_t st) {
@@ -659,11 +703,13 @@ int dispatch(int prepare, float* att, int ld_att, const float* qkv, int ld_qkv, 
             return rc ? rc : combine(hd, scratch, B, nq, row_pos, nchunk, ct, att, ld_att, hl, st);
         }
     }
+    // a prompt chunk of fewer than NW rows gains nothing from row tiles
+    rows = rows && B >= NW;
     return kv_dtype == SLATE_KV_F16
-               ? launch_kt<__half>(prepare, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
+               ? launch_kt<__half>(prepare, rows, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
                                    row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,
                                    ct, scratch, err, hl, st)
-               : launch_kt<float>(prepare, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
+               : launch_kt<float>(prepare, rows, hd, G, att, ld_att, qkv, ld_qkv, B, nq, nkv, row_pos,
                                   row_slot, page_table, max_pages, pool, n_pages, layer, nchunk,
                                   ct, scratch, err, hl, st);
 }
@@ -689,7 +735,7 @@ extern "C" size_t sb_attention_scratch_floats(int max_batch, int nq, int hd, int
 }
 
 extern "C" int sb_attention_prepare(int nq, int nkv, int hd, int kv_dtype) {
-    return dispatch(1, nullptr, 0, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr, 0,
+    return dispatch(1, 0, nullptr, 0, nullptr, 0, 0, nq, nkv, hd, nullptr, nullptr, nullptr, 0,
                     nullptr, nullptr, 0, 0, kv_dtype, 0, SB_ATTN_CHUNK, nullptr, nullptr,
                     HiLo{nullptr, nullptr, 0}, 0);
 }
@@ -701,7 +747,7 @@ extern "C" int sb_attention_paged(float* att, int ld_att, const float* qkv, int 
                                   int64_t n_pages, int layer, int kv_dtype, int max_seq, int ct,
                                   float* scratch, int* err, cudaStream_t st) {
     if (B < 1 || !err) return -1;
-    return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
+    return dispatch(0, 0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
                     max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, ct, scratch, err,
                     HiLo{nullptr, nullptr, 0}, st);
 }
@@ -716,7 +762,7 @@ extern "C" int sb_attention_paged_prefill(float* att, int ld_att, const float* q
     if (B < 1 || !err || (hi && ld16 < nq * hd)) return -1;
     const HiLo hl{(__half*)hi, (__half*)lo, hi ? ld16 : 0};
     if (!kvmap || !sb_attention_mma_supported(nq, nkv, hd, kv_dtype))
-        return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
+        return dispatch(0, 1, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
                         max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, 0, scratch, err,
                         hl, st);
     const int nchunk = (max_seq + SB_ATTN_CHUNK - 1) / SB_ATTN_CHUNK;
@@ -735,7 +781,7 @@ extern "C" int sb_attention_paged_split(float* att, int ld_att, const float* qkv
                                         float* scratch, int* err, void* hi, void* lo, int ld16,
                                         cudaStream_t st) {
     if (B < 1 || !err || !hi || ld16 < nq * hd) return -1;
-    return dispatch(0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
+    return dispatch(0, 0, att, ld_att, qkv, ld_qkv, B, nq, nkv, hd, row_pos, row_slot, page_table,
                     max_pages, pool, kvmap, n_pages, layer, kv_dtype, max_seq, 0, scratch, err,
                     HiLo{(__half*)hi, (__half*)lo, ld16}, st);
 }
