@@ -4,8 +4,8 @@ pairs) on 2 and 4 GPUs, one process per rank, against the oracle's per-sequence
 sessions (src/loader/llama_infer.c semantics) on the same GGUF.
 
 Tolerances as the single-GPU engine tests: 1e-4 of the logit scale with f32 KV,
-2e-3 with f16 KV; greedy ids equal up to near-ties.  Runs at 2 and 4 ranks,
-each case skipped where the box has fewer GPUs."""
+2e-3 with f16 KV; greedy ids equal up to near-ties.  Runs at 2, 4 and 8
+ranks, each case skipped where the box has fewer GPUs."""
 import multiprocessing as mp
 import os
 
@@ -24,6 +24,9 @@ TP_MODELS = {
     # 4 kv heads -> 4 / 1 per rank, ffn 256 per rank
     "small4": dict(n_layers=2, d_model=1024, ffn_hidden=1024, n_heads=16, n_kv_heads=4,
                    vocab=1000, max_seq=256, seed=33),
+    # 8 ranks: hd 64, 32 heads / 8 kv heads -> 4 / 1 per rank, ffn 256 per rank
+    "small8": dict(n_layers=2, d_model=2048, ffn_hidden=2048, n_heads=32, n_kv_heads=8,
+                   vocab=1000, max_seq=256, seed=34),
     # 8B head geometry (hd 128, 32 / 8 heads -> 16 / 4 per rank, group 4), 2 layers
     "8b_heads": dict(n_layers=2, d_model=4096, ffn_hidden=14336, n_heads=32, n_kv_heads=8,
                      vocab=4096, max_seq=512, theta_base=500000.0, seed=32),
@@ -92,7 +95,9 @@ def run_tp(path, feed, kv_dtype, tp=2, timeout=600, lanes=1):
 @pytest.mark.parametrize("name,kv_dtype,tol,tp", [
     ("small", 0, 1e-4, 2), ("small", 1, 2e-3, 2), ("8b_heads", 1, 2e-3, 2),
     # 4 ranks: one kv head per rank (small4), two (8B head geometry, group 4 kept whole)
-    ("small4", 0, 1e-4, 4), ("small4", 1, 2e-3, 4), ("8b_heads", 0, 1e-4, 4)])
+    ("small4", 0, 1e-4, 4), ("small4", 1, 2e-3, 4), ("8b_heads", 0, 1e-4, 4),
+    # 8 ranks: one kv head and 256 FFN units per rank
+    ("small8", 0, 1e-4, 8)])
 def test_tp_matches_oracle(sb, oracle, workdir, name, kv_dtype, tol, tp):
     if _gpu_count() < tp:
         pytest.skip(f"tensor parallelism over {tp} ranks needs {tp} GPUs")
