@@ -34,6 +34,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import select
 import shutil
 import statistics
 import subprocess
@@ -205,8 +206,13 @@ class ClockSampler:
     def __enter__(self):
         if shutil.which("nvidia-smi"):
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                       "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                                       text=True)
+            # nvidia-smi takes a moment to start: wait (at most 5 s) for its first
+            # sample, taken before the timed region and left out of the summary,
+            # so that a short timed region is still sampled from its start
+            if select.select([self.p.stdout], [], [], 5.0)[0]:
+                self.p.stdout.readline()
         return self
 
     def __exit__(self, *a):
