@@ -198,15 +198,21 @@ __global__ void __launch_bounds__(32 * (NW + 1), G >= 8 ? 2 : 3) attn_chunk(
     const int kvh = rest % nkv, unit = rest / nkv;
     if (unit >= nunit) return;
     const int b0 = ROWS ? unit * NW : unit;
-    int ctx = 0;                                      // the longest context of the unit's rows
+    // the longest context of the unit's rows, and the sequence of its first row
+    // with a position (a row without one has no slot to trust)
+    int ctx = 0, slot = -1;
 #pragma unroll
-    for (int w = 0; w < (ROWS ? NW : 1); ++w)
-        if (b0 + w < B) ctx = max(ctx, row_pos[b0 + w] + 1);
+    for (int w = 0; w < (ROWS ? NW : 1); ++w) {
+        const int p = b0 + w < B ? row_pos[b0 + w] : -1;
+        if (p >= 0) {
+            ctx = max(ctx, p + 1);
+            if (slot < 0) slot = row_slot[b0 + w];
+        }
+    }
     const int t0 = chunk * ct;
-    if (t0 >= ctx) return;
+    if (t0 >= ctx) return;                            // also: no row with a position
     const int t1 = min(ctx, t0 + ct);
     const int npg = (t1 - t0 + 15) / 16;
-    const int slot = row_slot[b0];
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
